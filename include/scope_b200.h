@@ -1,0 +1,119 @@
+/*
+ * scope_b200.h -- C ABI of the B200 (sm_100a) decode-attention engine for
+ * physically partitioned KV caches.
+ *
+ * Every entry point:
+ *   - takes DEVICE pointers (the caller's CUDA allocations on the current
+ *     device) and plain sizes / strides (in ELEMENTS unless the name ends in
+ *     _bytes), and a cudaStream_t passed as `void* stream` (NULL = the legacy
+ *     default stream);
+ *   - launches asynchronously on that stream and never synchronises;
+ *   - returns WS_OK (0) or a WS_ERR_* code; ws_last_error() then returns a
+ *     message (thread-local).
+ * No entry point allocates device memory: callers pass a workspace whose
+ * size the matching *_workspace_size() returns.  A workspace must be zeroed
+ * once when it is allocated (its counters reset themselves after every
+ * launch) and must not be shared by launches that may overlap in time.
+ *
+ * bf16 tensors are passed as their 16-bit storage.  The reference interfaces
+ * each entry replaces are cited as path:line of the reference checkout.
+ */
+#ifndef SCOPE_B200_H
+#define SCOPE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes */
+#define WS_OK 0
+#define WS_ERR_INVALID_ARG 1   /* shape / pointer / alignment rejected on the host */
+#define WS_ERR_UNSUPPORTED 2   /* valid request this build has no kernel for     */
+#define WS_ERR_CUDA 3          /* a CUDA runtime call failed                      */
+#define WS_ERR_WORKSPACE 4     /* workspace missing or too small                  */
+#define WS_ERR_DEVICE 5        /* a kernel reported a device-side failure         */
+
+/* ---- element types */
+#define WS_DTYPE_BF16 0
+#define WS_DTYPE_F32 1
+#define WS_DTYPE_I8 2
+
+/* ---- GQA output modes (what the reference wrappers return) */
+#define WS_OUT_NORM_BF16 0   /* out bf16 normalised, max/sum bf16: fused_cpu_attn on bf16 (kernel/cpu_attn.cpp:631-634) */
+#define WS_OUT_UNNORM_F32 1  /* o fp32 NOT normalised, max/sum fp32: fused_cpu_attn_mla (kernel/cpu_attn.cpp:668-671)   */
+#define WS_OUT_NORM_F32 2    /* out fp32 normalised, max/sum fp32: fused_cpu_attn on fp32 (kernel/cpu_attn.cpp:635)     */
+
+const char* ws_last_error(void);
+int ws_version(void);
+
+/* Device-side status word: kernels whose bounded waits give up (they never
+ * spin forever) record WS_ERR_DEVICE there.  Returns the word for the current
+ * device and clears it (synchronises the given stream). */
+int ws_status_take(void* stream);
+
+/*
+ * GQA / MLA decode over one strided KV share.
+ * Replaces fused_cpu_attn (kernel/cpu_attn.cpp:572-636),
+ * fused_cpu_attn_mla (kernel/cpu_attn.cpp:638-672) and
+ * fused_cpu_attn_fp32 (kernel/cpu_attn.cpp:817-848).
+ *   q    [B_kv, G, Dk] contiguous (dtype bf16, or fp32 with dtype WS_DTYPE_F32)
+ *   k    element (b, t, d) at k + b*k_stride_b + t*k_stride_t + d   (Dk wide)
+ *   v    element (b, t, d) at v + b*v_stride_b + t*v_stride_t + d   (Dv wide)
+ *   out  [B_kv, G, Dv]; out_max, out_sum [B_kv, G]  (types per out_mode)
+ *   out_lse [B_kv, G] fp32, optional (NULL): max + log(sum)
+ * Constraints (bf16): 1 <= G <= 16; Dk, Dv multiples of 16 with
+ * (ceil64(Dk), ceil64(Dv)) in {(64,64), (128,128), (128,64), (192,128)};
+ * k, v 16-byte aligned, strides multiples of 8 elements.  L == 0 gives
+ * out = 0, max = -inf, sum = 0.
+ */
+int ws_gqa_decode(const void* q, const void* k, const void* v,
+                  int64_t k_stride_b, int64_t k_stride_t, int64_t v_stride_b, int64_t v_stride_t,
+                  int B_kv, int G, int Dk, int Dv, int L, float scale, int dtype, int out_mode,
+                  void* out, void* out_max, void* out_sum, float* out_lse,
+                  void* workspace, size_t workspace_bytes, void* stream);
+size_t ws_gqa_decode_workspace_size(int B_kv, int G, int Dv, int L);
+
+/*
+ * Ragged-batch GQA decode over up to 4 physically separate KV shares of every
+ * sequence, with the per-share partials merged by log-sum-exp inside the same
+ * launch.  Replaces the runtime's per-share fused_cpu_attn calls plus the
+ * Python merge (system/mixoffload.py:1263-1268, :1333-1334, :1456-1464;
+ * system/qwenoffload.py:1606-1617).
+ *   q        [B, Hkv*G, Dk] bf16 contiguous (head h = kvh*G + g)
+ *   share s: k_s, v_s token-major packed buffers [n_tok_s, Hkv, D] with
+ *            element (t, h, d) at k_s + t*k_stride_t + h*k_stride_h + d;
+ *            cu_seqlens_s [B+1] int32 DEVICE array of token offsets
+ *            (sequence b owns tokens [cu[b], cu[b+1]) of share s)
+ *   out      [B, Hkv*G, Dv] bf16 normalised;  out_lse [B, Hkv*G] fp32
+ */
+typedef struct ws_kv_share {
+    const void* k;
+    const void* v;
+    const int32_t* cu_seqlens;   /* device, [B+1] */
+    int64_t n_tok;               /* rows of the packed buffers */
+    int64_t k_stride_t, k_stride_h, v_stride_t, v_stride_h;
+} ws_kv_share;
+
+int ws_gqa_decode_shares(const void* q, int B, int Hkv, int G, int Dk, int Dv, float scale,
+                         const ws_kv_share* shares, int n_shares,
+                         void* out, float* out_lse, void* workspace, size_t workspace_bytes, void* stream);
+size_t ws_gqa_decode_shares_workspace_size(int B, int Hkv, int G, int Dv, int n_shares);
+
+/*
+ * Log-sum-exp merge of P partial attention results (the cross-GPU combine of
+ * a sequence-sharded KV cache, and the runtime merges it replaces:
+ * system/qwenoffload.py:1606-1617 lse form).
+ *   o_parts   [P, R, D] fp32 normalised partials;  lse_parts [P, R] fp32
+ *   out       [R, D] in out_dtype (WS_DTYPE_BF16 or WS_DTYPE_F32);  out_lse [R] fp32 (optional)
+ * Rows whose partials are all -inf give out = 0, lse = -inf.
+ */
+int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D,
+                 void* out, int out_dtype, float* out_lse, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SCOPE_B200_H */

@@ -1,0 +1,162 @@
+"""Drop-in for the reference's `cpu_attn_ext` / `cpu_attn_tile_ext` modules.
+
+The reference builds these with ``kernel/build.py:8-26`` /
+``kernel/build_tile.py`` and binds them at ``kernel/cpu_attn.cpp:1024-1054``.
+Same attribute names, positional/keyword signatures, output dtypes and
+normalisation; the tensors are CUDA tensors instead of CPU tensors and every
+call runs the sm_100a kernels of libscope_b200.so on the current stream.
+There is no CPU fallback: a CPU tensor raises RuntimeError.
+
+    ext = scope_b200.build()
+    out, mx, sm = ext.fused_cpu_attn(q, k, v, scale)
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, stream_ptr, workspaces
+
+_num_threads = [0]
+
+
+def _require_cuda(name: str, *ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name}: expected tensors")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name}: scope_b200 ops take CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{name}: all tensors must be on the same device")
+    return dev
+
+
+def _gqa_common(name, q, k, v):
+    dev = _require_cuda(name, q, k, v)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise RuntimeError(f"{name}: q, k, v must be 3-D ([B_kv, G, D], [B_kv, L, D], [B_kv, L, Dv])")
+    if not q.is_contiguous():
+        raise RuntimeError("q must be contiguous")
+    if k.stride(2) != 1 or v.stride(2) != 1:
+        raise RuntimeError(f"{name}: k and v must have unit stride on the head dim")
+    B, G, Dk = q.shape
+    if k.shape[0] != B or v.shape[0] != B or k.shape[2] != Dk or k.shape[1] != v.shape[1]:
+        raise RuntimeError(f"{name}: shape mismatch between q, k, v")
+    return dev, B, G, Dk, k.shape[1], v.shape[2]
+
+
+def _run_gqa(q, k, v, scale, dtype_code, out_mode, out, mx, sm, lse):
+    dev = q.device
+    B, G, Dk = q.shape
+    L, Dv = k.shape[1], v.shape[2]
+    L_ = lib()
+    with torch.cuda.device(dev):
+        nbytes = L_.ws_gqa_decode_workspace_size(B, G, Dv, L)
+        ws = workspaces.get(nbytes, dev)
+        rc = L_.ws_gqa_decode(ptr(q), ptr(k), ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+                              B, G, Dk, Dv, L, float(scale), dtype_code, out_mode,
+                              ptr(out), ptr(mx), ptr(sm), ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
+    check(rc, "ws_gqa_decode")
+
+
+def fused_cpu_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float):
+    """GQA decode (kernel/cpu_attn.cpp:572-636).
+
+    q [B_kv, G, D] contiguous, k/v [B_kv, L, D] with any strides on dims 0-1;
+    fp32 or bf16 (all three alike); D % 16 == 0.
+    Returns (out [B_kv, G, D] normalised, max [B_kv, G, 1], sum [B_kv, G, 1]),
+    all bf16 for bf16 inputs and fp32 for fp32 inputs, like the reference.
+    """
+    if q.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("q must be float32 or bfloat16")
+    if k.dtype != q.dtype:
+        raise RuntimeError("k dtype must match q")
+    if v.dtype != q.dtype:
+        raise RuntimeError("v dtype must match q")
+    dev, B, G, D, L, Dv = _gqa_common("fused_cpu_attn", q, k, v)
+    if D % 16 != 0:
+        raise RuntimeError("head_dim must be multiple of 16 for AVX512")
+    if Dv != D:
+        raise RuntimeError("fused_cpu_attn: k and v head dims must match (use fused_cpu_attn_mla)")
+    if q.dtype == torch.bfloat16:
+        out = torch.empty(B, G, D, dtype=torch.bfloat16, device=dev)
+        mx = torch.empty(B, G, 1, dtype=torch.bfloat16, device=dev)
+        sm = torch.empty(B, G, 1, dtype=torch.bfloat16, device=dev)
+        _run_gqa(q, k, v, scale, _lib.WS_DTYPE_BF16, _lib.WS_OUT_NORM_BF16, out, mx, sm, None)
+    else:
+        out = torch.empty(B, G, D, dtype=torch.float32, device=dev)
+        mx = torch.empty(B, G, 1, dtype=torch.float32, device=dev)
+        sm = torch.empty(B, G, 1, dtype=torch.float32, device=dev)
+        _run_gqa(q, k, v, scale, _lib.WS_DTYPE_F32, _lib.WS_OUT_NORM_F32, out, mx, sm, None)
+    return out, mx, sm
+
+
+def fused_cpu_attn_mla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float):
+    """Decode with k_head_dim != v_head_dim allowed (kernel/cpu_attn.cpp:638-672).
+
+    bf16 only.  Returns fp32 (o NOT normalised [B_kv, G, Dv], max [B_kv, G, 1],
+    sum [B_kv, G, 1]) like the reference; o / sum is the attention output and
+    max + log(sum) its log-sum-exp.
+    """
+    if q.dtype != torch.bfloat16:
+        raise RuntimeError("fused_cpu_attn_mla requires bf16 inputs")
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError("fused_cpu_attn_mla requires bf16 inputs")
+    dev, B, G, Dk, L, Dv = _gqa_common("fused_cpu_attn_mla", q, k, v)
+    out = torch.empty(B, G, Dv, dtype=torch.float32, device=dev)
+    mx = torch.empty(B, G, 1, dtype=torch.float32, device=dev)
+    sm = torch.empty(B, G, 1, dtype=torch.float32, device=dev)
+    _run_gqa(q, k, v, scale, _lib.WS_DTYPE_BF16, _lib.WS_OUT_UNNORM_F32, out, mx, sm, None)
+    return out, mx, sm
+
+
+def fused_cpu_attn_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float):
+    """fp32 decode (kernel/cpu_attn.cpp:817-848): (out normalised, max, sum), all fp32."""
+    for t in (q, k, v):
+        if t.dtype != torch.float32:
+            raise RuntimeError("fused_cpu_attn_fp32 requires float32 inputs")
+    dev, B, G, D, L, Dv = _gqa_common("fused_cpu_attn_fp32", q, k, v)
+    out = torch.empty(B, G, D, dtype=torch.float32, device=dev)
+    mx = torch.empty(B, G, 1, dtype=torch.float32, device=dev)
+    sm = torch.empty(B, G, 1, dtype=torch.float32, device=dev)
+    _run_gqa(q, k, v, scale, _lib.WS_DTYPE_F32, _lib.WS_OUT_NORM_F32, out, mx, sm, None)
+    return out, mx, sm
+
+
+def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float):
+    """GQA decode returning (out bf16 [B_kv, G, Dv] normalised, lse fp32 [B_kv, G]).
+
+    The fp32 log-sum-exp (max + log sum) is what the LSE merges consume; the
+    reference's bf16 fused_cpu_attn rounds max and sum to bf16 (~1e-2 LSE error).
+    """
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError("gqa_decode requires bf16 inputs")
+    dev, B, G, Dk, L, Dv = _gqa_common("gqa_decode", q, k, v)
+    out = torch.empty(B, G, Dv, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, G, dtype=torch.float32, device=dev)
+    _run_gqa(q, k, v, scale, _lib.WS_DTYPE_BF16, _lib.WS_OUT_NORM_BF16, out, None, None, lse)
+    return out, lse
+
+
+def set_num_threads(n: int) -> None:
+    """Kept for API compatibility (kernel/cpu_attn.cpp:1046-1050).  The GPU
+    kernels size their grids from the SM count; the value is only remembered."""
+    _num_threads[0] = int(n)
+
+
+def get_num_threads() -> int:
+    """Last value given to set_num_threads, else the device's SM count."""
+    if _num_threads[0] > 0:
+        return _num_threads[0]
+    if torch.cuda.is_available():
+        return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return 1
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,215 @@
+// extern "C" entry points of libscope_b200.so: argument checks, tensor-map
+// encoding and launch.  Declarations and contracts: include/scope_b200.h.
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "ws_internal.h"
+
+namespace ws {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char* msg) {
+    snprintf(g_err, sizeof(g_err), "%s", msg ? msg : "");
+    return code;
+}
+
+int device_sm_count() {
+    static int cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+// Kernel-side failure word (bounded waits that gave up).  One per device.
+__device__ int g_status_word;
+
+int* device_status_word() {
+    static int* cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!cache[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_status_word) != cudaSuccess) return nullptr;
+        cache[dev] = static_cast<int*>(ptr);
+    }
+    return cache[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D bf16 tensor map over a KV buffer whose element (tok, row, d) sits at
+// base + tok*stride_tok + row*stride_row + d.  The box is 64 dims x box_tok
+// tokens x 1 row, 128-byte swizzled; the two outer dimensions are ordered by
+// increasing stride, and *tok_in_dim2 says where the token axis ended up.
+int make_kv_map(CUtensorMap* map, const void* base, int64_t stride_tok, int64_t stride_row, int D, int64_t n_tok,
+                int64_t n_rows, int box_tok, int* tok_in_dim2) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(WS_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+    if (reinterpret_cast<uintptr_t>(base) % 16) return set_error(WS_ERR_INVALID_ARG, "KV base must be 16-byte aligned");
+    // strides of size-1 axes are irrelevant: normalise them so that ordering works
+    if (n_rows == 1) stride_row = stride_tok * n_tok;
+    if (n_tok == 1) stride_tok = (n_rows == 1 ? D : stride_row * n_rows);
+    if (stride_tok <= 0 || stride_row <= 0) return set_error(WS_ERR_INVALID_ARG, "KV strides must be positive");
+    if ((stride_tok * 2) % 16 || (stride_row * 2) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "KV strides must be multiples of 8 elements (16 bytes)");
+    cuuint64_t dims[3];
+    cuuint64_t strides[2];
+    cuuint32_t box[3];
+    const cuuint32_t es[3] = {1, 1, 1};
+    dims[0] = (cuuint64_t)D;
+    box[0] = 64;
+    if (stride_tok <= stride_row) {
+        *tok_in_dim2 = 0;
+        dims[1] = n_tok; dims[2] = n_rows;
+        strides[0] = stride_tok * 2; strides[1] = stride_row * 2;
+        box[1] = box_tok; box[2] = 1;
+    } else {
+        *tok_in_dim2 = 1;
+        dims[1] = n_rows; dims[2] = n_tok;
+        strides[0] = stride_row * 2; strides[1] = stride_tok * 2;
+        box[1] = 1; box[2] = box_tok;
+    }
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+        return set_error(WS_ERR_INVALID_ARG, buf);
+    }
+    return WS_OK;
+}
+
+}  // namespace ws
+
+using namespace ws;
+
+extern "C" {
+
+const char* ws_last_error(void) { return g_err; }
+
+int ws_version(void) { return 100; }
+
+int ws_status_take(void* stream) {
+    int* w = device_status_word();
+    if (!w) return set_error(WS_ERR_CUDA, "status word unavailable");
+    int h = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(&h, w, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaMemsetAsync(w, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+        return set_error(WS_ERR_CUDA, "status word read failed");
+    return h == 0 ? WS_OK : WS_ERR_DEVICE;
+}
+
+size_t ws_gqa_decode_workspace_size(int B_kv, int G, int Dv, int L) {
+    const int64_t tiles = (int64_t)B_kv * ((L + 63) / 64);
+    const int nctas = (int)std::min<int64_t>(device_sm_count(), std::max<int64_t>(tiles, 1));
+    return gqa_workspace_bytes(G, Dv, B_kv, B_kv, nctas);
+}
+
+int ws_gqa_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_t,
+                  int64_t v_stride_b, int64_t v_stride_t, int B_kv, int G, int Dk, int Dv, int L, float scale,
+                  int dtype, int out_mode, void* out, void* out_max, void* out_sum, float* out_lse, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+    if (B_kv < 0 || G < 1 || L < 0 || Dk < 1 || Dv < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");
+    if (B_kv == 0) return WS_OK;
+    if (!q || !out || (L > 0 && (!k || !v))) return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    if (out_mode < WS_OUT_NORM_BF16 || out_mode > WS_OUT_NORM_F32) return set_error(WS_ERR_INVALID_ARG, "bad out_mode");
+    if ((out_max == nullptr) != (out_sum == nullptr)) return set_error(WS_ERR_INVALID_ARG, "out_max/out_sum: both or neither");
+    if (dtype == WS_DTYPE_F32) {
+        if (out_mode == WS_OUT_NORM_BF16) return set_error(WS_ERR_INVALID_ARG, "fp32 inputs cannot use WS_OUT_NORM_BF16");
+        if (Dk != Dv) return set_error(WS_ERR_UNSUPPORTED, "fp32 path needs Dk == Dv");
+        return gqa_f32_launch(q, k, v, k_stride_b, k_stride_t, v_stride_b, v_stride_t, B_kv, G, Dk, L, scale, out_mode,
+                              out, out_max, out_sum, out_lse, workspace, workspace_bytes,
+                              static_cast<cudaStream_t>(stream));
+    }
+    if (dtype != WS_DTYPE_BF16) return set_error(WS_ERR_INVALID_ARG, "dtype must be bf16 or fp32");
+    GqaLaunch a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.q_row_stride = (int64_t)G * Dk;
+    a.G = G; a.Dk = Dk; a.Dv = Dv; a.scale = scale;
+    a.varlen = 0;
+    a.n_rows = B_kv; a.L = L;
+    a.nshare = 1;
+    a.shares[0].k = k; a.shares[0].v = v;
+    a.shares[0].n_tok = L; a.shares[0].n_rows = B_kv;
+    a.shares[0].k_stride_tok = k_stride_t; a.shares[0].k_stride_row = k_stride_b;
+    a.shares[0].v_stride_tok = v_stride_t; a.shares[0].v_stride_row = v_stride_b;
+    a.out_mode = out_mode;
+    a.out = out; a.out_max = out_max; a.out_sum = out_sum; a.out_lse = out_lse;
+    a.out_row_stride = (int64_t)G * Dv; a.ml_row_stride = G;
+    a.workspace = workspace; a.workspace_bytes = workspace_bytes;
+    a.status = device_status_word();
+    a.stream = stream;
+    return gqa_launch(a);
+}
+
+size_t ws_gqa_decode_shares_workspace_size(int B, int Hkv, int G, int Dv, int n_shares) {
+    return gqa_workspace_bytes(G, Dv, B * Hkv * n_shares, B * Hkv, device_sm_count());
+}
+
+int ws_gqa_decode_shares(const void* q, int B, int Hkv, int G, int Dk, int Dv, float scale, const ws_kv_share* shares,
+                         int n_shares, void* out, float* out_lse, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+    if (B < 0 || Hkv < 1 || G < 1 || n_shares < 1 || n_shares > 4) return set_error(WS_ERR_INVALID_ARG, "bad shape");
+    if (B == 0) return WS_OK;
+    if (!q || !out || !shares) return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    GqaLaunch a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.q_row_stride = (int64_t)G * Dk;
+    a.G = G; a.Dk = Dk; a.Dv = Dv; a.scale = scale;
+    a.varlen = 1;
+    a.B = B; a.Hkv = Hkv;
+    a.nshare = n_shares;
+    for (int s = 0; s < n_shares; ++s) {
+        if (!shares[s].cu_seqlens) return set_error(WS_ERR_INVALID_ARG, "share without cu_seqlens");
+        if (shares[s].n_tok > 0 && (!shares[s].k || !shares[s].v)) return set_error(WS_ERR_INVALID_ARG, "share without k/v");
+        if (shares[s].n_tok > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "share longer than 2^31 tokens");
+        a.shares[s].k = shares[s].k; a.shares[s].v = shares[s].v;
+        a.shares[s].cu_seqlens = shares[s].cu_seqlens;
+        a.shares[s].n_tok = shares[s].n_tok; a.shares[s].n_rows = Hkv;
+        a.shares[s].k_stride_tok = shares[s].k_stride_t; a.shares[s].k_stride_row = shares[s].k_stride_h;
+        a.shares[s].v_stride_tok = shares[s].v_stride_t; a.shares[s].v_stride_row = shares[s].v_stride_h;
+    }
+    a.out_mode = WS_OUT_NORM_BF16;
+    a.out = out; a.out_max = nullptr; a.out_sum = nullptr; a.out_lse = out_lse;
+    a.out_row_stride = (int64_t)G * Dv; a.ml_row_stride = G;
+    a.workspace = workspace; a.workspace_bytes = workspace_bytes;
+    a.status = device_status_word();
+    a.stream = stream;
+    return gqa_launch(a);
+}
+
+int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out, int out_dtype,
+                 float* out_lse, void* stream) {
+    if (P < 1 || R < 0 || D < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");
+    if (R == 0) return WS_OK;
+    if (!o_parts || !lse_parts || !out) return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    if (out_dtype != WS_DTYPE_BF16 && out_dtype != WS_DTYPE_F32) return set_error(WS_ERR_INVALID_ARG, "bad out dtype");
+    return lse_merge_launch(o_parts, lse_parts, P, R, D, out, out_dtype, out_lse, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

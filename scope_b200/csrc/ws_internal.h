@@ -1,0 +1,64 @@
+// Host-side internals shared by the .cu files of libscope_b200.so.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <algorithm>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/scope_b200.h"
+
+namespace ws {
+
+int set_error(int code, const char* msg);
+int device_sm_count();
+int make_kv_map(CUtensorMap* map, const void* base, int64_t stride_tok, int64_t stride_row, int D, int64_t n_tok,
+                int64_t n_rows, int box_tok, int* tok_in_dim2);
+int* device_status_word();
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct KvShare {
+    const void* k;
+    const void* v;
+    const int* cu_seqlens;      // varlen only
+    int64_t n_tok, n_rows;      // TMA extents: tokens, rows (kv rows or kv heads)
+    int64_t k_stride_tok, k_stride_row, v_stride_tok, v_stride_row;   // elements
+};
+
+struct GqaLaunch {
+    const void* q;
+    int64_t q_row_stride;
+    int G, Dk, Dv;
+    float scale;
+    int varlen;
+    int n_rows, L;              // dense
+    int B, Hkv;                 // varlen
+    int nshare;
+    KvShare shares[4];
+    int out_mode;
+    void* out;
+    void* out_max;
+    void* out_sum;
+    float* out_lse;
+    int64_t out_row_stride, ml_row_stride;
+    void* workspace;
+    size_t workspace_bytes;
+    int* status;
+    void* stream;
+};
+
+int gqa_launch(const GqaLaunch& a);
+size_t gqa_workspace_bytes(int G, int Dv, int nseg, int n_groups, int nctas);
+size_t gqa_slot_bytes(int G, int Dv);
+
+int gqa_f32_launch(const void* q, const void* k, const void* v, int64_t k_sb, int64_t k_st, int64_t v_sb,
+                   int64_t v_st, int B_kv, int G, int D, int L, float scale, int out_mode, void* out, void* out_max,
+                   void* out_sum, float* out_lse, void* workspace, size_t workspace_bytes, cudaStream_t st);
+
+int lse_merge_launch(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out,
+                     int out_dtype, float* out_lse, cudaStream_t st);
+
+}  // namespace ws

@@ -1,0 +1,208 @@
+"""GPU parity of the GQA / MLA(non-absorbed) decode against the oracle and
+the reference's golden outputs.
+
+Tolerances (from the north star): bf16 outputs max-abs 2e-2, fp32 LSE 1e-3.
+The kernels compute in fp32 from bf16 operands; the oracle in float64.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import scope_b200
+
+pytestmark = pytest.mark.gpu
+
+TOL_OUT = 2e-2
+TOL_LSE = 1e-3
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def ext():
+    return scope_b200.build()
+
+
+def bits_to_bf16(bits, device=DEV):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def rand_bf16(*shape, gen):
+    return torch.randn(*shape, generator=gen).bfloat16()
+
+
+def oracle_of(q, k, v, scale):
+    return oracle.gqa_decode(oracle.bf16_bits(q.cpu()), oracle.bf16_bits(k.cpu()), oracle.bf16_bits(v.cpu()), scale)
+
+
+def test_golden_qwen3(ext, golden):
+    g = golden("gqa_qwen3_bf16")
+    q, k, v = (bits_to_bf16(g[n]) for n in ("q", "k", "v"))
+    sc = float(g["scale"])
+    o, m, s = ext.fused_cpu_attn_mla(q, k, v, sc)
+    torch.cuda.synchronize()
+    o, m, s = o.cpu().numpy(), m.cpu().numpy(), s.cpu().numpy()
+    assert np.abs(o / s - g["mla_o"] / g["mla_sum"]).max() < TOL_OUT / 10
+    assert np.abs((m + np.log(s)) - (g["mla_max"] + np.log(g["mla_sum"]))).max() < TOL_LSE
+    po, pm, ps = ext.fused_cpu_attn(q, k, v, sc)
+    assert po.dtype == torch.bfloat16 and pm.dtype == torch.bfloat16 and pm.shape == (4, 8, 1)
+    ref_pub = oracle.bits_to_f32(g["pub_out"])
+    assert np.abs(po.float().cpu().numpy() - ref_pub).max() < TOL_OUT
+
+
+def test_golden_strided(ext, golden):
+    g = golden("gqa_strided_bf16")
+    q = bits_to_bf16(g["q"])
+    kc, vc = bits_to_bf16(g["k_cache"]), bits_to_bf16(g["v_cache"])
+    o, m, s = ext.fused_cpu_attn_mla(q, kc.permute(1, 0, 2), vc.permute(1, 0, 2), float(g["scale"]))
+    o, s, m = o.cpu().numpy(), s.cpu().numpy(), m.cpu().numpy()
+    assert np.abs(o / s - g["mla_o"] / g["mla_sum"]).max() < TOL_OUT / 10
+    assert np.abs((m + np.log(s)) - (g["mla_max"] + np.log(g["mla_sum"]))).max() < TOL_LSE
+
+
+def test_golden_mla_192_128(ext, golden):
+    g = golden("mla_nonabsorbed_bf16")
+    q, k, v = (bits_to_bf16(g[n]) for n in ("q", "k", "v"))
+    o, m, s = ext.fused_cpu_attn_mla(q, k, v, float(g["scale"]))
+    o, m, s = o.cpu().numpy(), m.cpu().numpy(), s.cpu().numpy()
+    assert o.shape == (8, 1, 128)
+    assert np.abs(o / s - g["mla_o"] / g["mla_sum"]).max() < TOL_OUT / 10
+    assert np.abs((m + np.log(s)) - (g["mla_max"] + np.log(g["mla_sum"]))).max() < TOL_LSE
+
+
+def test_golden_fp32(ext, golden):
+    g = golden("gqa_fp32")
+    q, k, v = (torch.from_numpy(g[n]).to(DEV) for n in ("q", "k", "v"))
+    for fn, pre in ((ext.fused_cpu_attn, "pub"), (ext.fused_cpu_attn_fp32, "abl")):
+        o, m, s = fn(q, k, v, float(g["scale"]))
+        assert o.dtype == torch.float32
+        assert np.abs(o.cpu().numpy() - g[pre + "_out"]).max() < 1e-4
+        assert np.abs(m.cpu().numpy() - g[pre + "_max"]).max() < 1e-5
+        assert np.allclose(s.cpu().numpy(), g[pre + "_sum"], rtol=1e-4)
+
+
+@pytest.mark.parametrize("B,G,D,L", [
+    (1, 8, 128, 4096),     # cfg1 shape (Qwen3-30B-A3B layer: 32 q heads / 4 kv heads -> B_kv = 4 rows)
+    (4, 8, 128, 4096),
+    (3, 8, 128, 1), (2, 8, 128, 15), (2, 8, 128, 16), (2, 8, 128, 63), (2, 8, 128, 64), (2, 8, 128, 65),
+    (5, 4, 128, 1000), (7, 1, 128, 333), (2, 16, 128, 777), (3, 2, 64, 129), (300, 8, 128, 40),
+    (2, 12, 128, 2049),
+])
+def test_random_shapes(ext, B, G, D, L):
+    gen = torch.Generator().manual_seed(1000 + B * 7 + G * 13 + L)
+    Bkv = B * (4 if (B, L) == (1, 4096) else 1)
+    q = rand_bf16(Bkv, G, D, gen=gen)
+    k = rand_bf16(Bkv, L, D, gen=gen)
+    v = rand_bf16(Bkv, L, D, gen=gen)
+    sc = D ** -0.5
+    ro, rm, rs = oracle_of(q, k, v, sc)
+    out, lse = scope_b200.cpu_attn.gqa_decode(q.to(DEV), k.to(DEV), v.to(DEV), sc)
+    assert np.abs(out.float().cpu().numpy() - ro).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < TOL_LSE
+    o, m, s = ext.fused_cpu_attn_mla(q.to(DEV), k.to(DEV), v.to(DEV), sc)
+    assert np.abs(m.cpu().numpy()[..., 0] - rm).max() < TOL_LSE
+    assert np.allclose(s.cpu().numpy()[..., 0], rs, rtol=1e-3)
+
+
+def test_token_major_cache_view(ext):
+    """[L, Hkv, D] token-major buffer seen per head: strides (D, Hkv*D) on (b, t)."""
+    gen = torch.Generator().manual_seed(5)
+    L, Hkv, G, D = 3000, 4, 8, 128
+    kc = rand_bf16(L, Hkv, D, gen=gen)
+    vc = rand_bf16(L, Hkv, D, gen=gen)
+    q = rand_bf16(Hkv, G, D, gen=gen)
+    ro, rm, rs = oracle.gqa_decode_strided_buffer(oracle.bf16_bits(q), oracle.bf16_bits(kc), oracle.bf16_bits(vc),
+                                                  L, (D, Hkv * D), (D, Hkv * D), D, D ** -0.5)
+    out, lse = scope_b200.cpu_attn.gqa_decode(q.to(DEV), kc.to(DEV).permute(1, 0, 2), vc.to(DEV).permute(1, 0, 2),
+                                              D ** -0.5)
+    assert np.abs(out.float().cpu().numpy() - ro).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < TOL_LSE
+
+
+def test_empty_kv(ext):
+    q = torch.randn(2, 8, 128, device=DEV).bfloat16()
+    k = torch.empty(2, 0, 128, device=DEV, dtype=torch.bfloat16)
+    o, m, s = ext.fused_cpu_attn_mla(q, k, k, 0.1)
+    assert torch.all(o == 0) and torch.all(torch.isneginf(m)) and torch.all(s == 0)
+
+
+def test_repeat_calls_reuse_workspace(ext):
+    """Counters in the workspace reset themselves: many launches stay correct."""
+    gen = torch.Generator().manual_seed(9)
+    q = rand_bf16(4, 8, 128, gen=gen).to(DEV)
+    k = rand_bf16(4, 8192, 128, gen=gen).to(DEV)
+    v = rand_bf16(4, 8192, 128, gen=gen).to(DEV)
+    first, lse0 = scope_b200.cpu_attn.gqa_decode(q, k, v, 0.088)
+    for _ in range(20):
+        out, lse = scope_b200.cpu_attn.gqa_decode(q, k, v, 0.088)
+    assert torch.equal(out, first) and torch.equal(lse, lse0)
+
+
+def test_shares_ragged_two_way(ext):
+    """cfg2-style ragged batch, each sequence split into two physical shares."""
+    gen = torch.Generator().manual_seed(2)
+    B, Hkv, G, D = 5, 8, 4, 128
+    lens = [1024, 77, 3000, 1, 2500]
+    r = 0.25
+    L0 = [int(r * L) for L in lens]
+    L1 = [L - a for L, a in zip(lens, L0)]
+    q = rand_bf16(B, Hkv * G, D, gen=gen)
+    ks = [rand_bf16(L, Hkv, D, gen=gen) for L in lens]
+    vs = [rand_bf16(L, Hkv, D, gen=gen) for L in lens]
+
+    def pack(part):
+        k = torch.cat([kk[a:b] for kk, (a, b) in zip(ks, part)], 0)
+        v = torch.cat([vv[a:b] for vv, (a, b) in zip(vs, part)], 0)
+        cu = torch.tensor([0] + list(np.cumsum([b - a for a, b in part])), dtype=torch.int32)
+        return scope_b200.Share(k.to(DEV), v.to(DEV), cu.to(DEV))
+
+    s0 = pack([(0, a) for a in L0])
+    s1 = pack([(a, L) for a, L in zip(L0, lens)])
+    out, lse = scope_b200.gqa_decode_shares(q.to(DEV), [s0, s1], D ** -0.5)
+    out, lse = out.float().cpu().numpy(), lse.cpu().numpy()
+    for b in range(B):
+        qb = q[b].view(Hkv, G, D)
+        kb = ks[b].permute(1, 0, 2)
+        vb = vs[b].permute(1, 0, 2)
+        ro, rm, rs = oracle_of(qb, kb.contiguous(), vb.contiguous(), D ** -0.5)
+        assert np.abs(out[b].reshape(Hkv, G, D) - ro).max() < TOL_OUT, b
+        assert np.abs(lse[b].reshape(Hkv, G) - (rm + np.log(rs))).max() < TOL_LSE, b
+
+
+def test_lse_merge_kernel():
+    rng = np.random.default_rng(3)
+    P, R, D = 3, 100, 128
+    o = rng.standard_normal((P, R, D))
+    lse = rng.standard_normal((P, R)) * 3
+    lse[1, :10] = -np.inf
+    lse[:, 50] = -np.inf
+    ro, rl = oracle.lse_merge(o, lse)
+    out, ol = scope_b200.lse_merge(torch.tensor(o, dtype=torch.float32, device=DEV),
+                                   torch.tensor(lse, dtype=torch.float32, device=DEV), torch.float32)
+    out, ol = out.cpu().numpy(), ol.cpu().numpy()
+    assert np.abs(out - ro).max() < 1e-5
+    fin = np.isfinite(rl)
+    assert np.abs(ol[fin] - rl[fin]).max() < 1e-5
+    assert np.all(np.isneginf(ol[~fin])) and np.all(out[~fin] == 0)
+
+
+def test_split_merge_equals_unsplit_large(ext):
+    """Size-independent property at a long context: attention over [0, L) equals
+    the LSE merge of attention over [0, L/2) and [L/2, L)."""
+    gen = torch.Generator(device=DEV).manual_seed(4)
+    Bkv, G, D, L = 16, 8, 128, 131072
+    q = torch.randn(Bkv, G, D, device=DEV, generator=gen).bfloat16()
+    k = torch.randn(Bkv, L, D, device=DEV, generator=gen).bfloat16()
+    v = torch.randn(Bkv, L, D, device=DEV, generator=gen).bfloat16()
+    sc = D ** -0.5
+    full_o, full_m, full_s = ext.fused_cpu_attn_mla(q, k, v, sc)
+    parts = [ext.fused_cpu_attn_mla(q, k[:, a:a + L // 2], v[:, a:a + L // 2], sc) for a in (0, L // 2)]
+    o_parts = torch.stack([(po / ps).view(-1, D) for po, pm, ps in parts])
+    l_parts = torch.stack([(pm + ps.log()).view(-1) for po, pm, ps in parts])
+    mo, ml = scope_b200.lse_merge(o_parts, l_parts, torch.float32)
+    assert (mo - (full_o / full_s).view(-1, D)).abs().max().item() < 1e-4
+    assert (ml - (full_m + full_s.log()).view(-1)).abs().max().item() < 1e-4
+    # one row against the oracle at full length
+    ro, rm, rs = oracle_of(q[:1].cpu(), k[:1].cpu(), v[:1].cpu(), sc)
+    assert np.abs((full_o[:1] / full_s[:1]).cpu().numpy() - ro).max() < TOL_OUT
+    assert np.abs((full_m[:1] + full_s[:1].log()).cpu().numpy()[..., 0] - (rm + np.log(rs))).max() < TOL_LSE
