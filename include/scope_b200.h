@@ -77,6 +77,30 @@ int ws_gqa_decode(const void* q, const void* k, const void* v,
 size_t ws_gqa_decode_workspace_size(int B_kv, int G, int Dv, int L);
 
 /*
+ * ws_gqa_decode without a workspace argument.  No counterpart in the
+ * reference: it is for callers that can pass their inputs and outputs but no
+ * other device memory -- e.g. a server whose memory manager has already
+ * reserved the GPU's HBM for its KV-cache pool, or a plugin host that passes
+ * only tensors -- and for whom cudaMalloc would fail or stall the decode loop.
+ * The kernel's scratch is a built-in 4 MiB array per device (see
+ * ws_gqa_decode_noalloc_max_scratch), held by every GPU that loads this
+ * library until the process exits.  Same arguments and results as
+ * ws_gqa_decode with dtype WS_DTYPE_BF16.
+ *   - Shapes whose scratch (ws_gqa_decode_workspace_size) exceeds the array
+ *     are rejected with WS_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's device address; make it
+ *     before any stream capture.
+ *   - All calls on a device share the array: calls that may overlap on the
+ *     GPU race.  Issue them in order on one stream.
+ * Allocates nothing (no cudaMalloc, cudaFree or allocating library call).
+ */
+int ws_gqa_decode_noalloc(const void* q, const void* k, const void* v,
+                          int64_t k_stride_b, int64_t k_stride_t, int64_t v_stride_b, int64_t v_stride_t,
+                          int B_kv, int G, int Dk, int Dv, int L, float scale, int out_mode,
+                          void* out, void* out_max, void* out_sum, float* out_lse, void* stream);
+size_t ws_gqa_decode_noalloc_max_scratch(void);
+
+/*
  * Ragged-batch GQA decode over up to 4 physically separate KV shares of every
  * sequence, with the per-share partials merged by log-sum-exp inside the same
  * launch.  Replaces the runtime's per-share fused_cpu_attn calls plus the
