@@ -5,14 +5,16 @@
 
 One JSON line on rank 0.  `value` is whole-job throughput in TB/s of
 algorithmic bytes (KV read once + q + outputs, summed over ranks) divided by
-the device-timed step (max over ranks), inputs resident in HBM.  `e2e` is the
-same metric through the public API with the step's host buffers copied in
-(H2D of q and of the new token's K/V, D2H of out + lse) inside the timed
-region.  The KV cache itself is device-resident state, as the reference's
-InplaceKVCache is host-resident state appended one token per step
-(system/qwenoffload.py:100-122).
+the device-timed step (CUDA events, max over ranks), inputs resident in HBM
+and larger than L2 (small workloads rotate over enough copies of their inputs
+to exceed L2).  `e2e` is the same metric through the public API with the
+step's host buffers copied in (H2D of q and of the new token's K/V) and the
+result copied out (D2H of out + lse) inside the timed region.  The KV cache
+itself is device-resident state, as the reference's InplaceKVCache is
+host-resident state appended one token per step (system/qwenoffload.py:100-122).
 
-Workloads:
+Workloads (the default is the one the metric's
+1/2/4/8-GPU scaling is quoted on):
   cfg1  GQA Qwen3 layer, B=1, L=4096
   cfg2  GQA Mixtral layer, B=16, ragged L in [1024, 32768], two shares merged by LSE
   cfg4  GQA Qwen3, B=32, L=131072 sequence-sharded over N GPUs (default)
@@ -21,7 +23,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -35,6 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode-attn µs/step and achieved HBM TB/s (frac of peak) at 1/2/4/8 B200 vs CPU"
+L2_BYTES = 126 * 2 ** 20
 
 
 # ----------------------------------------------------------------- helpers
@@ -78,6 +80,7 @@ class ClockSampler:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(self.idx)], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
         except Exception:
             self.proc = None
         return self
@@ -112,10 +115,8 @@ class ClockSampler:
 
 
 def dist_info():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), \
+        int(os.environ.get("LOCAL_RANK", "0"))
 
 
 def max_over_ranks(x, world):
@@ -133,34 +134,90 @@ def barrier(world):
         dist.barrier()
 
 
+def bf16_randn(shape, gen, device):
+    return torch.randn(*shape, device=device, dtype=torch.bfloat16, generator=gen)
+
+
+def median_time(fn, budget_s, max_calls, warm=1):
+    for _ in range(warm):
+        fn()
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max_calls and (time.perf_counter() - t_start) < budget_s:
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def load_cpu_ref(module="cpu_attn_ext"):
+    """The reference's own extension from oracle/_ref on all host cores, or None."""
+    import oracle
+    if not oracle.ref_available():
+        return None
+    try:
+        ref = oracle.load_ref(module)
+    except Exception:
+        return None
+    n = os.cpu_count() or 1
+    ref.set_num_threads(n)
+    torch.set_num_threads(n)
+    return ref
+
+
 # --------------------------------------------------------------- workloads
-class GqaLongCtx:
-    """cfg4: Qwen3 shape, B=32, 32 q heads / 4 kv heads, D=128, L=131072 per
-    sequence, KV sharded contiguously over the ranks: rank r holds tokens
-    [r*L/N, (r+1)*L/N) of every (sequence, kv-head) row."""
+class Workload:
+    """Common harness: kernel(i) is the dominant launch on input copy i,
+    step(i) the full decode step, e2e_step(i) the step through the public API
+    with host buffers.  `copies` input sets rotate so that the bytes touched
+    between two uses of one set exceed L2."""
 
-    name = "cfg4"
-    workload = "gqa_longctx_qwen3_b32_l131072_sharded"
+    name = ""
+    workload = ""
+    copies = 1
+    graph = False
+    kernel_name = ""
 
-    def __init__(self, world, rank, B=32, H=32, Hkv=4, D=128, L=131072):
+    def kernel_bytes(self):
+        raise NotImplementedError
+
+    def step_bytes(self):
+        return self.kernel_bytes()
+
+
+class GqaDense(Workload):
+    """Dense GQA decode through ws_gqa_decode over [B*Hkv, L, D] rows.
+
+    cfg4 (default): Qwen3 shape, B=32, 32 q heads / 4 kv heads, D=128,
+    L=131072, KV sharded contiguously over the ranks -- rank r holds tokens
+    [r*L/N, (r+1)*L/N) of every (sequence, kv-head) row; partials are
+    exchanged with NCCL all_gather and merged with ws_lse_merge.
+    cfg1: the same layer shape at B=1, L=4096 on one GPU."""
+
+    kernel_name = "gqa_decode_kernel<128,128,1,4>"
+
+    def __init__(self, world, rank, name, B, H, Hkv, D, L, seed):
         from scope_b200 import _lib
+        self.name = name
         self.world, self.rank = world, rank
         self.B, self.H, self.Hkv, self.D, self.L = B, H, Hkv, D, L
         self.G = H // Hkv
         assert L % world == 0
         self.Lloc = L // world
         self.scale = D ** -0.5
+        self.workload = (f"gqa_qwen3_b{B}_l{L}" + ("_sharded" if name == "cfg4" else ""))
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.dev = dev
-        g = torch.Generator(device=dev).manual_seed(4000 + rank)
         rows = B * Hkv
-        self.k = torch.randn(rows, self.Lloc, D, device=dev, dtype=torch.bfloat16, generator=g)
-        self.v = torch.randn(rows, self.Lloc, D, device=dev, dtype=torch.bfloat16, generator=g)
-        gq = torch.Generator(device=dev).manual_seed(4)
-        self.q = torch.randn(B, H, D, device=dev, dtype=torch.bfloat16, generator=gq)
+        per_copy = 2 * rows * self.Lloc * D * 2
+        self.copies = max(1, -(-3 * L2_BYTES // per_copy)) if per_copy < 3 * L2_BYTES else 1
+        self.graph = per_copy < 64 * 2 ** 20
+        g = torch.Generator(device=dev).manual_seed(seed + rank)
+        self.k = [bf16_randn((rows, self.Lloc, D), g, dev) for _ in range(self.copies)]
+        self.v = [bf16_randn((rows, self.Lloc, D), g, dev) for _ in range(self.copies)]
+        gq = torch.Generator(device=dev).manual_seed(seed)
+        self.q = bf16_randn((B, H, D), gq, dev)
         self.qv = self.q.view(rows, self.G, D)
-        self.lib = _lib.lib()
-        self._lib = _lib
+        self.lib, self._lib = _lib.lib(), _lib
         if world == 1:
             self.out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(B, H, dtype=torch.float32, device=dev)
@@ -173,7 +230,6 @@ class GqaLongCtx:
             self.lse = torch.empty(B * H, dtype=torch.float32, device=dev)
         nbytes = self.lib.ws_gqa_decode_workspace_size(rows, self.G, D, self.Lloc)
         self.ws = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=dev)
-        # host buffers for the end-to-end step
         self.q_host = torch.randn(B, H, D).bfloat16().pin_memory()
         self.knew_host = torch.randn(rows, D).bfloat16().pin_memory()
         self.vnew_host = torch.randn(rows, D).bfloat16().pin_memory()
@@ -181,39 +237,33 @@ class GqaLongCtx:
         self.lse_host = torch.empty(B * H, dtype=torch.float32).pin_memory()
         self.kernels_per_step = 1 if world == 1 else 2
 
-    # algorithmic bytes of one local kernel launch, and of one step summed over ranks
     def kernel_bytes(self):
         rows = self.B * self.Hkv
-        kv = 2 * rows * self.Lloc * self.D * 2
-        q = self.B * self.H * self.D * 2
-        out = self.B * self.H * (self.D * (2 if self.world == 1 else 4) + 4)
-        return kv + q + out
+        return (2 * rows * self.Lloc * self.D * 2 + self.B * self.H * self.D * 2
+                + self.B * self.H * (self.D * (2 if self.world == 1 else 4) + 4))
 
     def step_bytes(self):
-        kv = 2 * self.B * self.Hkv * self.L * self.D * 2
-        return kv + self.B * self.H * self.D * 2 + self.B * self.H * (self.D * 2 + 4)
+        return (2 * self.B * self.Hkv * self.L * self.D * 2 + self.B * self.H * self.D * 2
+                + self.B * self.H * (self.D * 2 + 4))
 
-    def kernel(self):
-        L_ = self.lib
+    def kernel(self, i):
+        L_, c = self.lib, i % self.copies
+        k, v = self.k[c], self.v[c]
         st = torch.cuda.current_stream().cuda_stream
         rows = self.B * self.Hkv
         if self.world == 1:
-            rc = L_.ws_gqa_decode(self.qv.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.k.stride(0),
-                                  self.k.stride(1), self.v.stride(0), self.v.stride(1), rows, self.G, self.D, self.D,
-                                  self.Lloc, self.scale, self._lib.WS_DTYPE_BF16, self._lib.WS_OUT_NORM_BF16,
-                                  self.out.data_ptr(), None, None, self.lse.data_ptr(), self.ws.data_ptr(),
-                                  self.ws.numel(), st)
+            out, lse, mode = self.out, self.lse, self._lib.WS_OUT_NORM_BF16
         else:
-            rc = L_.ws_gqa_decode(self.qv.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.k.stride(0),
-                                  self.k.stride(1), self.v.stride(0), self.v.stride(1), rows, self.G, self.D, self.D,
-                                  self.Lloc, self.scale, self._lib.WS_DTYPE_BF16, self._lib.WS_OUT_NORM_F32,
-                                  self.part_o.data_ptr(), None, None, self.part_l.data_ptr(), self.ws.data_ptr(),
-                                  self.ws.numel(), st)
+            out, lse, mode = self.part_o, self.part_l, self._lib.WS_OUT_NORM_F32
+        rc = L_.ws_gqa_decode(self.qv.data_ptr(), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                              v.stride(0), v.stride(1), rows, self.G, self.D, self.D, self.Lloc, self.scale,
+                              self._lib.WS_DTYPE_BF16, mode, out.data_ptr(), None, None, lse.data_ptr(),
+                              self.ws.data_ptr(), self.ws.numel(), st)
         if rc != 0:
             raise RuntimeError(L_.ws_last_error().decode())
 
-    def step(self):
-        self.kernel()
+    def step(self, i):
+        self.kernel(i)
         if self.world > 1:
             import torch.distributed as dist
             from scope_b200 import lse_merge
@@ -221,86 +271,260 @@ class GqaLongCtx:
             dist.all_gather_into_tensor(self.all_l.view(-1), self.part_l.view(-1))
             lse_merge(self.all_o, self.all_l, torch.bfloat16, out=self.out, out_lse=self.lse)
 
-    def e2e_step(self):
-        # H2D: this step's query, and the new token's K/V row appended to the last shard
+    def e2e_step(self, i):
+        c = i % self.copies
         self.q.copy_(self.q_host, non_blocking=True)
-        if self.rank == self.world - 1:
-            self.k[:, self.Lloc - 1].copy_(self.knew_host, non_blocking=True)
-            self.v[:, self.Lloc - 1].copy_(self.vnew_host, non_blocking=True)
-        self.step()
+        if self.rank == self.world - 1:   # the new token lands in the last shard
+            self.k[c][:, self.Lloc - 1].copy_(self.knew_host, non_blocking=True)
+            self.v[c][:, self.Lloc - 1].copy_(self.vnew_host, non_blocking=True)
+        self.step(i)
         if self.rank == 0:
             self.out_host.copy_(self.out.view(-1), non_blocking=True)
             self.lse_host.copy_(self.lse.view(-1), non_blocking=True)
 
     def e2e_bytes(self):
-        h2d = self.world * self.q.numel() * 2 + 2 * self.knew_host.numel() * 2
-        d2h = self.out.numel() * 2 + self.lse.numel() * 4
-        return h2d, d2h
+        return (self.world * self.q.numel() * 2 + 2 * self.knew_host.numel() * 2,
+                self.out.numel() * 2 + self.lse.numel() * 4)
 
     def config(self):
         return {"workload": self.workload, "batch": self.B, "q_heads": self.H, "kv_heads": self.Hkv,
                 "head_dim": self.D, "kv_len": self.L, "kv_len_per_gpu": self.Lloc,
-                "parallelism": f"seq-shard{self.world}", "l2": "inputs > L2 (KV 8.6 GB total)",
+                "parallelism": f"seq-shard{self.world}",
+                "l2": (f"inputs {2 * self.B * self.Hkv * self.Lloc * self.D * 2 / 1e9:.2f} GB per GPU > L2"
+                       if self.copies == 1 else f"{self.copies} rotating input copies > 3x L2"),
+                "timing": "cuda-graph replay" if self.graph else "stream launches",
                 "exchange": "nccl all_gather of (o fp32, lse) + lse_merge kernel" if self.world > 1 else "none"}
 
-    # reference CPU sample: same op (fused_cpu_attn, B_kv = 128 rows), shorter KV
-    def cpu_sample(self, L_s=4096):
-        return dict(rows=self.B * self.Hkv, G=self.G, D=self.D, L=L_s)
+    def cpu_reference(self, budget_s, max_calls, warm=1):
+        return cpu_ref_dense(self.B, self.Hkv, self.G, self.D, self.L, budget_s, max_calls, warm)
 
 
-def cpu_reference_time(sample, budget_s=10.0, max_calls=200, warm=1, kind_pref="reference"):
-    """Time the reference's own CPU kernel (oracle/_ref) -- or the oracle port
-    when the compiled reference cannot run here -- on a bounded sample.
-    Returns (bytes_per_second, dict)."""
+class GqaShares(Workload):
+    """cfg2: Mixtral layer shape, B=16, 32 q heads / 8 kv heads (G=4), D=128,
+    ragged per-sequence KV lengths ~ U[1024, 32768] (seed 2), each sequence's
+    KV split at r in {0.25, 0.5, 0.75} into two physical shares (share 0 =
+    tokens [0, floor(r*L)), share 1 = the rest), one launch of
+    ws_gqa_decode_shares decodes both and merges them by LSE."""
+
+    name = "cfg2"
+    kernel_name = "gqa_decode_kernel<128,128,1,4> (2 shares)"
+
+    def __init__(self, world, rank, B=16, H=32, Hkv=8, D=128, seed=2):
+        import scope_b200
+        self.world, self.rank = world, rank
+        self.B, self.H, self.Hkv, self.D = B, H, Hkv, D
+        self.G = H // Hkv
+        self.scale = D ** -0.5
+        self.lens, self.ratio, self.L0, self.L1 = cfg2_geometry(B, seed)
+        self.workload = f"gqa_mixtral_b{B}_ragged_1024_32768_two_shares"
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.q = bf16_randn((B, H, D), g, dev)
+        self.total_tokens = int(self.lens.sum())
+        # each share is the reference's cache layout: [B*Hkv, capacity, D] rows per
+        # (sequence, kv-head), valid tokens [0, len) (system/qwenoffload.py:59-141)
+        cap0, cap1 = int(self.L0.max()), int(self.L1.max())
+        self.k0, self.v0 = bf16_randn((B * Hkv, cap0, D), g, dev), bf16_randn((B * Hkv, cap0, D), g, dev)
+        self.k1, self.v1 = bf16_randn((B * Hkv, cap1, D), g, dev), bf16_randn((B * Hkv, cap1, D), g, dev)
+        n0 = torch.tensor(self.L0, dtype=torch.int32, device=dev)
+        n1 = torch.tensor(self.L1, dtype=torch.int32, device=dev)
+        self.shares = [scope_b200.Share(self.k0, self.v0, seqlens=n0), scope_b200.Share(self.k1, self.v1, seqlens=n1)]
+        self.out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+        self.q_host = torch.randn(B, H, D).bfloat16().pin_memory()
+        self.out_host = torch.empty(B, H, D, dtype=torch.bfloat16).pin_memory()
+        self.lse_host = torch.empty(B, H, dtype=torch.float32).pin_memory()
+        self.copies = 1
+        self.graph = True
+        self.kernels_per_step = 1
+        self._decode = scope_b200.gqa_decode_shares
+
+    def kernel_bytes(self):
+        return 2 * self.total_tokens * self.Hkv * self.D * 2 + self.B * self.H * (self.D * 2 * 2 + 4)
+
+    def kernel(self, i):
+        self._decode(self.q, self.shares, self.scale, out=self.out, lse=self.lse)
+
+    step = kernel
+
+    def e2e_step(self, i):
+        self.q.copy_(self.q_host, non_blocking=True)
+        self._decode(self.q, self.shares, self.scale, out=self.out, lse=self.lse)
+        self.out_host.copy_(self.out, non_blocking=True)
+        self.lse_host.copy_(self.lse, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.q.numel() * 2, self.out.numel() * 2 + self.lse.numel() * 4
+
+    def config(self):
+        return {"workload": self.workload, "batch": self.B, "q_heads": self.H, "kv_heads": self.Hkv,
+                "head_dim": self.D, "kv_len_sum": int(self.lens.sum()), "kv_len_min": int(self.lens.min()),
+                "kv_len_max": int(self.lens.max()), "share_ratios": [float(r) for r in self.ratio],
+                "layout": "two padded shares [B*Hkv, cap, D] per sequence split",
+                "parallelism": "single-gpu", "l2": f"inputs {self.kernel_bytes() / 1e9:.2f} GB > L2",
+                "timing": "cuda-graph replay"}
+
+    def cpu_reference(self, budget_s, max_calls, warm=1):
+        return cpu_ref_shares(self.B, self.H, self.Hkv, self.D, budget_s, max_calls, warm)
+
+
+# ------------------------------------------------- reference CPU measurements
+def cfg2_geometry(B=16, seed=2):
+    """Seeded ragged lengths ~ U[1024, 32768] and share ratios in {.25, .5, .75}."""
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(1024, 32768, size=B, endpoint=True)
+    ratio = rng.choice([0.25, 0.5, 0.75], size=B)
+    L0 = np.floor(ratio * lens).astype(np.int64)
+    return lens, ratio, L0, lens - L0
+
+
+def cpu_ref_dense(B, Hkv, G, D, L, budget_s, max_calls, warm=1):
+    """The reference's fused_cpu_attn on all host cores over B*Hkv rows
+    (long rows are sampled at L=4096 tokens).  Returns (bytes/s, info)."""
     import oracle
-    rows, G, D, L = sample["rows"], sample["G"], sample["D"], sample["L"]
+    rows = B * Hkv
+    L = min(L, 4096)
     torch.manual_seed(11)
-    ncores = os.cpu_count() or 1
     q = torch.randn(rows, G, D).bfloat16()
     k = torch.randn(rows, L, D).bfloat16()
     v = torch.randn(rows, L, D).bfloat16()
     nbytes = 2 * rows * L * D * 2 + rows * G * D * 2 + rows * G * (D * 2 + 4)
-    kind = "port"
-    if kind_pref == "reference" and oracle.ref_available():
-        try:
-            ref = oracle.load_ref("cpu_attn_ext")
-            ref.set_num_threads(ncores)
-            torch.set_num_threads(ncores)
-            fn = lambda: ref.fused_cpu_attn(q, k, v, D ** -0.5)  # noqa: E731
-            kind = "reference"
-        except Exception:
-            kind = "port"
-    if kind == "port":
+    ref = load_cpu_ref()
+    if ref is not None:
+        kind, fn = "reference", (lambda: ref.fused_cpu_attn(q, k, v, D ** -0.5))
+    else:
         qb, kb, vb = oracle.bf16_bits(q), oracle.bf16_bits(k), oracle.bf16_bits(v)
-        fn = lambda: oracle.gqa_decode(qb, kb, vb, D ** -0.5)  # noqa: E731
-    for _ in range(warm):
-        fn()
-    times = []
-    t_start = time.perf_counter()
-    while len(times) < max_calls and (time.perf_counter() - t_start) < budget_s:
-        t0 = time.perf_counter()
-        fn()
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return nbytes / t, {"kind": kind, "cores": ncores, "calls": len(times), "sec_per_call": t,
+        kind, fn = "port", (lambda: oracle.gqa_decode(qb, kb, vb, D ** -0.5))
+    t, n = median_time(fn, budget_s, max_calls, warm)
+    return nbytes / t, {"kind": kind, "cores": os.cpu_count() or 1, "calls": n, "sec_per_call": t,
                         "sample": f"fused_cpu_attn bf16, B_kv={rows}, G={G}, D={D}, L={L} "
-                                  f"({nbytes / 1e6:.0f} MB algorithmic per call)"}
+                                  f"({nbytes / 1e6:.1f} MB per call)"}
 
 
-WORKLOADS = {"cfg4": GqaLongCtx}
+def cpu_ref_shares(B, H, Hkv, D, budget_s, max_calls, warm=1):
+    """cfg2 on the host: per sequence and share the reference's fused_cpu_attn
+    (bf16), then the runtime's merge (system/mixoffload.py:1333-1334,
+    :1456-1464) in torch.  Returns (bytes/s, info)."""
+    import oracle
+    G = H // Hkv
+    lens, ratio, L0, L1 = cfg2_geometry(B)
+    torch.manual_seed(12)
+    q = torch.randn(B, H, D).bfloat16()
+    ks0 = [torch.randn(Hkv, int(a), D).bfloat16() for a in L0]
+    vs0 = [torch.randn(Hkv, int(a), D).bfloat16() for a in L0]
+    ks1 = [torch.randn(Hkv, int(a), D).bfloat16() for a in L1]
+    vs1 = [torch.randn(Hkv, int(a), D).bfloat16() for a in L1]
+    nbytes = 2 * int(lens.sum()) * Hkv * D * 2 + B * H * (D * 2 * 2 + 4)
+    ref = load_cpu_ref()
+
+    def one(kb, vb, qb):
+        if ref is not None:
+            o, m, s = ref.fused_cpu_attn(qb, kb, vb, D ** -0.5)
+            return o.float() * s.float(), m.float(), s.float()
+        o, m, s = oracle.gqa_decode(oracle.bf16_bits(qb), oracle.bf16_bits(kb), oracle.bf16_bits(vb), D ** -0.5)
+        return torch.from_numpy(o * s[..., None]), torch.from_numpy(m)[..., None], torch.from_numpy(s)[..., None]
+
+    def run():
+        for b in range(B):
+            qb = q[b].view(Hkv, G, D)
+            o0, m0, s0 = one(ks0[b], vs0[b], qb)
+            o1, m1, s1 = one(ks1[b], vs1[b], qb)
+            M = torch.maximum(m0, m1)
+            w0, w1 = torch.exp(m0 - M), torch.exp(m1 - M)
+            _ = (o0 * w0 + o1 * w1) / (w0 * s0 + w1 * s1).clamp(min=1e-3)
+
+    t, n = median_time(run, budget_s, max_calls, warm)
+    return nbytes / t, {"kind": "reference" if ref is not None else "port", "cores": os.cpu_count() or 1,
+                        "calls": n, "sec_per_call": t,
+                        "sample": f"full cfg2 step ({nbytes / 1e9:.2f} GB): per sequence and share "
+                                  "fused_cpu_attn + torch LSE merge"}
+
+
+def cpu_reference_for(name, args, budget_s, max_calls, warm):
+    if name == "cfg4":
+        return cpu_ref_dense(32, 4, 8, 128, args.kv_len or 131072, budget_s, max_calls, warm), \
+            "gqa_qwen3_b32_l131072_sharded"
+    if name == "cfg1":
+        return cpu_ref_dense(1, 4, 8, 128, args.kv_len or 4096, budget_s, max_calls, warm), "gqa_qwen3_b1_l4096"
+    if name == "cfg2":
+        return cpu_ref_shares(16, 32, 8, 128, budget_s, max_calls, warm), \
+            "gqa_mixtral_b16_ragged_1024_32768_two_shares"
+    raise ValueError(name)
+
+
+def make_workload(name, world, rank, args):
+    if name == "cfg4":
+        return GqaDense(world, rank, "cfg4", 32, 32, 4, 128, args.kv_len or 131072, 4000)
+    if name == "cfg1":
+        return GqaDense(world, rank, "cfg1", 1, 32, 4, 128, args.kv_len or 4096, 1000)
+    if name == "cfg2":
+        return GqaShares(world, rank)
+    raise ValueError(name)
+
+
+WORKLOADS = ("cfg1", "cfg2", "cfg4")
 
 
 # -------------------------------------------------------------------- main
-def time_loop(fn, steps, warmup, world):
-    for _ in range(warmup):
-        fn()
+def make_runner(wl, fn):
+    """Returns run(n) that issues n steps.  Small workloads are captured once
+    (one pass over all input copies) in a CUDA graph and replayed."""
+    if not wl.graph:
+        state = {"i": 0}
+
+        def run(n):
+            for _ in range(n):
+                fn(state["i"])
+                state["i"] += 1
+        return run, 1
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    per = max(wl.copies, 8)
+    with torch.cuda.stream(s):
+        for i in range(per):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(per):
+            fn(i)
+
+    def run(n):
+        for _ in range(max(1, n // per)):
+            g.replay()
+    run.graph = g
+    return run, per
+
+
+def time_steps(wl, fn, steps, warmup, world):
+    run, per = make_runner(wl, fn)
+    run(max(warmup, per))
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n = max(steps // per, 1) * per
+    e0.record()
+    run(n)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / 1e3 / n, world), n
+
+
+def time_e2e(wl, steps, warmup, world):
+    """Public-API steps with host buffers; no graph (a user calls the API)."""
+    for i in range(warmup):
+        wl.e2e_step(i)
     barrier(world)
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(steps):
-        fn()
+    for i in range(steps):
+        wl.e2e_step(i)
     e1.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -308,19 +532,18 @@ def time_loop(fn, steps, warmup, world):
 
 
 def run_reference_arm(args):
+    """The reference's own CPU kernel on this host's cores, one bounded sample
+    of the workload per step.  Touches no GPU and loads nothing of scope_b200."""
     world, rank, _ = dist_info()
     if rank != 0:
         return
-    wl = WORKLOADS[args.workload]
-    # one step = one reference call on a bounded sample of the workload (same rows, shorter KV)
-    sample = {"rows": 128, "G": 8, "D": 128, "L": 2048}
-    bps, info = cpu_reference_time(sample, budget_s=1e9, max_calls=args.steps, warm=args.warmup)
+    (bps, info), workload = cpu_reference_for(args.workload, args, budget_s=1e9, max_calls=args.steps,
+                                              warm=args.warmup)
     value = bps / 1e12
-    line = {"metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus, "steps": args.steps,
+    line = {"metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus, "steps": info["calls"],
             "warmup": args.warmup, "ms_per_step": info["sec_per_call"] * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": wl.workload, "sample": info["sample"]},
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": workload, "sample": info["sample"]},
             "cpu_baseline": {"value": value, "unit": "TB/s", "cores": info["cores"], "kind": info["kind"],
                              "sample": info["sample"]},
             "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -332,7 +555,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cfg4", choices=WORKLOADS)
+    ap.add_argument("--kv-len", type=int, default=0, help="override KV length (profiling on a small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -351,18 +575,15 @@ def main():
                                 device_id=torch.device("cuda", local))
     import scope_b200
     scope_b200.build()
-    wl = WORKLOADS[args.workload](world, rank)
+    wl = make_workload(args.workload, world, rank, args)
 
-    # 1) dominant kernel alone (roofline)
-    t_kernel = time_loop(wl.kernel, args.steps, args.warmup, world)
-    # 2) full step, device-resident inputs (value)
-    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    t_kernel, _ = time_steps(wl, wl.kernel, args.steps, args.warmup, world)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = int(vis.split(",")[local]) if vis else local
     with ClockSampler(gpu_index) as clk:
-        t_step = time_loop(wl.step, args.steps, args.warmup, world)
+        t_step, n_timed = time_steps(wl, wl.step, args.steps, args.warmup, world)
     clocks = clk.summary()
-    # 3) end to end through the public path with host buffers
-    t_e2e = time_loop(wl.e2e_step, args.steps, args.warmup, world)
+    t_e2e = time_e2e(wl, min(args.steps, 500), args.warmup, world)
 
     hbm, peak_src = peaks()
     kb = wl.kernel_bytes()
@@ -371,22 +592,22 @@ def main():
     h2d, d2h = wl.e2e_bytes()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        bps, info = cpu_reference_time(wl.cpu_sample())
+        bps, info = wl.cpu_reference(budget_s=10.0, max_calls=200)
         cpu = {"value": bps / 1e12, "unit": "TB/s", "cores": info["cores"], "kind": info["kind"],
-               "sample": info["sample"] + f"; median of {info['calls']} calls"}
+               "sample": info["sample"] + f"; median of {info['calls']} calls",
+               "us_per_call": info["sec_per_call"] * 1e6}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": t_step * 1e3, "us_per_step": t_step * 1e6,
+                "warmup": args.warmup, "timed_steps": n_timed, "ms_per_step": t_step * 1e3, "us_per_step": t_step * 1e6,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded N(0,1) q/k/v)", "config": wl.config(),
                 "e2e": {"value": wl.step_bytes() / t_e2e / 1e12, "unit": "TB/s", "us_per_step": t_e2e * 1e6,
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                             "frac": achieved / hbm, "peak_source": peak_src,
-                             "kernel": "gqa_decode_kernel<128,128,1,4>", "kernel_us": t_kernel * 1e6,
-                             "algorithmic_bytes_per_launch": kb,
+                             "frac": achieved / hbm, "peak_source": peak_src, "kernel": wl.kernel_name,
+                             "kernel_us": t_kernel * 1e6, "algorithmic_bytes_per_launch": kb,
                              "traffic": profile_traffic(f"gqa_decode_{wl.name}")},
-                "gpu_launches": wl.kernels_per_step * args.steps,
+                "gpu_launches": wl.kernels_per_step * n_timed,
                 "clocks": clocks, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -107,17 +107,21 @@ size_t ws_gqa_decode_noalloc_max_scratch(void);
  * Python merge (system/mixoffload.py:1263-1268, :1333-1334, :1456-1464;
  * system/qwenoffload.py:1606-1617).
  *   q        [B, Hkv*G, Dk] bf16 contiguous (head h = kvh*G + g)
- *   share s: k_s, v_s token-major packed buffers [n_tok_s, Hkv, D] with
- *            element (t, h, d) at k_s + t*k_stride_t + h*k_stride_h + d;
- *            cu_seqlens_s [B+1] int32 DEVICE array of token offsets
- *            (sequence b owns tokens [cu[b], cu[b+1]) of share s)
+ *   share s, one of two layouts (element (t, r, d) at k_s + t*k_stride_t + r*k_stride_h + d):
+ *     packed:  cu_seqlens_s [B+1] int32 DEVICE token offsets, seqlens_s = NULL;
+ *              r = kv head, sequence b owns tokens [cu[b], cu[b+1]); n_tok = total tokens
+ *              (e.g. [n_tok, Hkv, D] token-major or [Hkv, n_tok, D] head-major)
+ *     padded:  seqlens_s [B] int32 DEVICE token counts, cu_seqlens_s = NULL;
+ *              r = b*Hkv + kv head, tokens [0, seqlens[b]) of a row of capacity n_tok
+ *              (the reference's [B*Hkv, max_seq, D] cache, system/qwenoffload.py:59-141)
  *   out      [B, Hkv*G, Dv] bf16 normalised;  out_lse [B, Hkv*G] fp32
  */
 typedef struct ws_kv_share {
     const void* k;
     const void* v;
-    const int32_t* cu_seqlens;   /* device, [B+1] */
-    int64_t n_tok;               /* rows of the packed buffers */
+    const int32_t* cu_seqlens;   /* device, [B+1] (packed) or NULL */
+    const int32_t* seqlens;      /* device, [B] (padded) or NULL */
+    int64_t n_tok;               /* packed: total tokens; padded: row capacity */
     int64_t k_stride_t, k_stride_h, v_stride_t, v_stride_h;
 } ws_kv_share;
 

@@ -12,7 +12,8 @@ import threading
 import torch
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libscope_b200.so")
+# SCOPE_B200_LIB selects another build of the same library (e.g. a tuned variant).
+LIB_PATH = os.environ.get("SCOPE_B200_LIB") or os.path.join(PKG, "libscope_b200.so")
 
 WS_OK = 0
 WS_ERR_INVALID_ARG = 1
@@ -38,7 +39,7 @@ _sz = ctypes.c_size_t
 
 class KvShare(ctypes.Structure):
     """Mirror of `ws_kv_share` (include/scope_b200.h)."""
-    _fields_ = [("k", _V), ("v", _V), ("cu_seqlens", _V), ("n_tok", _i64),
+    _fields_ = [("k", _V), ("v", _V), ("cu_seqlens", _V), ("seqlens", _V), ("n_tok", _i64),
                 ("k_stride_t", _i64), ("k_stride_h", _i64), ("v_stride_t", _i64), ("v_stride_h", _i64)]
 
 

@@ -123,6 +123,7 @@ int ws_status_take(void* stream) {
 }
 
 size_t ws_gqa_decode_workspace_size(int B_kv, int G, int Dv, int L) {
+    B_kv = std::min(B_kv, kMaxGroupsPerLaunch);   // larger calls run in chunks of rows
     const int64_t tiles = (int64_t)B_kv * ((L + 63) / 64);
     const int nctas = (int)std::min<int64_t>(device_sm_count(), std::max<int64_t>(tiles, 1));
     return gqa_workspace_bytes(G, Dv, B_kv, B_kv, nctas);
@@ -145,6 +146,24 @@ int ws_gqa_decode(const void* q, const void* k, const void* v, int64_t k_stride_
                               static_cast<cudaStream_t>(stream));
     }
     if (dtype != WS_DTYPE_BF16) return set_error(WS_ERR_INVALID_ARG, "dtype must be bf16 or fp32");
+    if (B_kv > kMaxGroupsPerLaunch) {
+        // rows are independent: run them in chunks that fit the counter header
+        const size_t ob = out_mode == WS_OUT_NORM_BF16 ? 2 : 4;
+        for (int r0 = 0; r0 < B_kv; r0 += kMaxGroupsPerLaunch) {
+            const int n = std::min(kMaxGroupsPerLaunch, B_kv - r0);
+            const int rc = ws_gqa_decode(
+                static_cast<const uint16_t*>(q) + (int64_t)r0 * G * Dk,
+                static_cast<const uint16_t*>(k) + (int64_t)r0 * k_stride_b,
+                static_cast<const uint16_t*>(v) + (int64_t)r0 * v_stride_b, k_stride_b, k_stride_t, v_stride_b,
+                v_stride_t, n, G, Dk, Dv, L, scale, dtype, out_mode,
+                static_cast<uint8_t*>(out) + (size_t)r0 * G * Dv * ob,
+                out_max ? static_cast<uint8_t*>(out_max) + (size_t)r0 * G * ob : nullptr,
+                out_sum ? static_cast<uint8_t*>(out_sum) + (size_t)r0 * G * ob : nullptr,
+                out_lse ? out_lse + (size_t)r0 * G : nullptr, workspace, workspace_bytes, stream);
+            if (rc != WS_OK) return rc;
+        }
+        return WS_OK;
+    }
     GqaLaunch a;
     memset(&a, 0, sizeof(a));
     a.q = q;
@@ -185,12 +204,17 @@ int ws_gqa_decode_shares(const void* q, int B, int Hkv, int G, int Dk, int Dv, f
     a.B = B; a.Hkv = Hkv;
     a.nshare = n_shares;
     for (int s = 0; s < n_shares; ++s) {
-        if (!shares[s].cu_seqlens) return set_error(WS_ERR_INVALID_ARG, "share without cu_seqlens");
+        const bool padded = shares[s].seqlens != nullptr;
+        if (!padded && !shares[s].cu_seqlens)
+            return set_error(WS_ERR_INVALID_ARG, "share needs cu_seqlens (packed) or seqlens (padded)");
+        if (padded && shares[s].cu_seqlens)
+            return set_error(WS_ERR_INVALID_ARG, "share: give cu_seqlens or seqlens, not both");
         if (shares[s].n_tok > 0 && (!shares[s].k || !shares[s].v)) return set_error(WS_ERR_INVALID_ARG, "share without k/v");
         if (shares[s].n_tok > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "share longer than 2^31 tokens");
         a.shares[s].k = shares[s].k; a.shares[s].v = shares[s].v;
         a.shares[s].cu_seqlens = shares[s].cu_seqlens;
-        a.shares[s].n_tok = shares[s].n_tok; a.shares[s].n_rows = Hkv;
+        a.shares[s].seqlens = shares[s].seqlens;
+        a.shares[s].n_tok = shares[s].n_tok; a.shares[s].n_rows = padded ? (int64_t)B * Hkv : Hkv;
         a.shares[s].k_stride_tok = shares[s].k_stride_t; a.shares[s].k_stride_row = shares[s].k_stride_h;
         a.shares[s].v_stride_tok = shares[s].v_stride_t; a.shares[s].v_stride_row = shares[s].v_stride_h;
     }

@@ -32,6 +32,9 @@ constexpr int kTile = 64;        // tokens per TMA tile
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxShares = 4;
+// Most pieces one group can have: one per CTA plus one per extra share.  The
+// host caps the grid at kMaxPieces - kMaxShares CTAs.
+constexpr int kMaxPieces = 160;
 
 struct GqaMaps {
     CUtensorMap k[kMaxShares];
@@ -46,7 +49,8 @@ struct GqaParams {
     int varlen;                // 0: dense rows, 1: ragged shares
     int n_rows, L;             // dense
     int B, Hkv, nshare;        // varlen
-    const int* cu[kMaxShares]; // varlen: cumulative token offsets per share, [B+1]
+    const int* cu[kMaxShares]; // varlen, packed share: cumulative token offsets [B+1]
+    const int* lens[kMaxShares];  // varlen, padded share: tokens per sequence [B] (rows b*Hkv + h)
     int tok_in_dim2[kMaxShares];
     int has_map[kMaxShares];
     int n_groups;
@@ -80,8 +84,11 @@ struct GqaCfg {
     static constexpr int STAGE_BYTES = (KBOX + VBOX) * BOX_BYTES;
     static constexpr int RED_FLOATS = kConsumerWarps * NG * (DVP + 2);
     static constexpr int SLOT_FLOATS = NG * DVP + 2 * NG;
+    // merge of a group's pieces: slot list, per-piece (weight, l), group (M, L)
+    static constexpr int COMB_BYTES = kMaxPieces * 4 + 2 * kMaxPieces * NG * 4 + 2 * NG * 4;
     static constexpr size_t fixed_smem() {
-        return 1024 /*align slack*/ + size_t(STAGES) * STAGE_BYTES + RED_FLOATS * 4 + 2 * STAGES * 8 + 64;
+        return 1024 /*align slack*/ + size_t(STAGES) * STAGE_BYTES + RED_FLOATS * 4 + 2 * STAGES * 8 + 64 +
+               COMB_BYTES;
     }
 };
 
@@ -91,7 +98,11 @@ struct SegTable {
     const int* pre;   // varlen: exclusive prefix of tiles per sequence, [B+1] in smem
     int tpr;          // dense: tiles per row
 
-    __device__ __forceinline__ int seq_len(int s, int b) const { return __ldg(p->cu[s] + b + 1) - __ldg(p->cu[s] + b); }
+    // Tokens of sequence b in share s: a packed share gives offsets, a padded
+    // share (one capacity-sized row per (sequence, kv-head)) gives lengths.
+    __device__ __forceinline__ int seq_len(int s, int b) const {
+        return p->lens[s] ? __ldg(p->lens[s] + b) : __ldg(p->cu[s] + b + 1) - __ldg(p->cu[s] + b);
+    }
 
     __device__ __forceinline__ int64_t total() const {
         return p->varlen ? (int64_t)pre[p->B] : (int64_t)p->n_rows * tpr;
@@ -125,7 +136,15 @@ struct SegTable {
             base += ts;
         }
         s.j = (b * p->Hkv + h) * p->nshare + sh;
-        s.map = sh; s.y = h; s.x0 = __ldg(p->cu[sh] + b); s.len = seq_len(sh, b);
+        s.map = sh;
+        if (p->lens[sh]) {
+            s.y = b * p->Hkv + h;
+            s.x0 = 0;
+        } else {
+            s.y = h;
+            s.x0 = __ldg(p->cu[sh] + b);
+        }
+        s.len = seq_len(sh, b);
         s.group = b * p->Hkv + h; s.t0 = base;
         return s;
     }
@@ -207,10 +226,14 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
     float* red = reinterpret_cast<float*>(smem + size_t(STAGES) * C::STAGE_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(red + C::RED_FLOATS);
     int* flags = reinterpret_cast<int*>(bars + 2 * STAGES);
-    int* pre = flags + 16;
+    int* pslot = flags + 16;                                          // [kMaxPieces]
+    float* pw = reinterpret_cast<float*>(pslot + kMaxPieces);         // [kMaxPieces][NG]
+    float* pl = pw + kMaxPieces * NG;                                 // [kMaxPieces][NG]
+    float* gml = pl + kMaxPieces * NG;                                // [2][NG]
+    int* pre = reinterpret_cast<int*>(gml + 2 * NG);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nctas = gridDim.x, cta = blockIdx.x;
+    const int grid_ctas = gridDim.x, cta = blockIdx.x;
 
     SegTable tab;
     tab.p = &p;
@@ -241,8 +264,12 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
     __syncthreads();
 
     const int64_t total = tab.total();
-    const int64_t t_begin = split_start(cta, total, nctas);
-    const int64_t t_end = split_start(cta + 1, total, nctas);
+    // Tiles are split over min(grid, total) CTAs so that every working CTA
+    // owns at least one tile: the piece bookkeeping counts one piece per CTA
+    // between a segment's first and last owner.  Surplus CTAs own nothing.
+    const int nctas = total < 1 ? 1 : (total < grid_ctas ? (int)total : grid_ctas);
+    const int64_t t_begin = cta < nctas ? split_start(cta, total, nctas) : total;
+    const int64_t t_end = cta < nctas ? split_start(cta + 1, total, nctas) : total;
     const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[STAGES]);
 
     if (warp == kConsumerWarps) {
@@ -254,14 +281,19 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                     tma_prefetch_desc(&maps.v[s]);
                 }
             int64_t i = 0;
+            Seg sg;
+            int64_t seg_end = -1;   // first tile after the current segment
+            int stage = 0;
+            uint32_t use = 0;
             for (int64_t t = t_begin; t < t_end; ++t, ++i) {
-                const int stage = (int)(i % STAGES);
-                const uint32_t use = (uint32_t)(i / STAGES);
                 if (use > 0 && !mbar_wait_bounded(empty0 + 8 * stage, (use & 1) ^ 1)) {
                     atomicExch(p.status, kDevTimeout);
                     break;
                 }
-                const Seg sg = tab.of_tile(t);
+                if (t >= seg_end) {
+                    sg = tab.of_tile(t);
+                    seg_end = sg.t0 + (sg.len + kTile - 1) / kTile;
+                }
                 const int x = sg.x0 + (int)(t - sg.t0) * kTile;
                 const int c1 = p.tok_in_dim2[sg.map] ? sg.y : x;
                 const int c2 = p.tok_in_dim2[sg.map] ? x : sg.y;
@@ -273,6 +305,10 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
 #pragma unroll
                 for (int vb = 0; vb < C::VBOX; ++vb)
                     tma_load_3d(dst + (C::KBOX + vb) * C::BOX_BYTES, &maps.v[sg.map], fb, vb * 64, c1, c2);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    ++use;
+                }
             }
         }
         return;
@@ -280,8 +316,8 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
 
     // --------------------------------------------------------------- consumers
     const int ctid = tid;   // 0..127
-    // Empty groups (no tokens at all): written once, by CTA group % nctas.
-    for (int g = cta; g < p.n_groups; g += nctas) {
+    // Empty groups (no tokens at all): written once, by CTA group % grid.
+    for (int g = cta; g < p.n_groups; g += grid_ctas) {
         if (tab.pieces(g, total, nctas) == 0) {
             for (int e = ctid; e < p.G * p.Dv; e += kConsumerWarps * 32)
                 store_final(p, g, e / p.Dv, e % p.Dv, 0.f, -INFINITY, 0.f);
@@ -396,36 +432,90 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
             named_bar_sync(1, kConsumerWarps * 32);
             if (flags[1]) {
                 __threadfence();
-                // enumerate this group's pieces: segments of the group, CTAs spanning each
-                const int nseg_g = p.varlen ? p.nshare : 1;
-                const int j0 = p.varlen ? sg.group * p.nshare : sg.group;
-                for (int e = ctid; e < NG * DVP; e += kConsumerWarps * 32) {
-                    const int grp = e / DVP, d = e - grp * DVP;
-                    if (grp >= p.G || d >= p.Dv) continue;
+                // This CTA filed the group's last piece: merge all of them.
+                // (1) list the pieces -- for each segment of the group, the CTAs spanning it
+                if (ctid == 0) {
+                    const int nseg_g = p.varlen ? p.nshare : 1;
+                    const int j0 = p.varlen ? sg.group * p.nshare : sg.group;
+                    int n = 0;
+                    for (int js = 0; js < nseg_g; ++js) {
+                        int64_t t0, nt_;
+                        tab.seg_tiles(sg.group, js, t0, nt_);
+                        if (nt_ == 0) continue;
+                        const int64_t c0 = split_owner(t0, total, nctas), c1 = split_owner(t0 + nt_ - 1, total, nctas);
+                        for (int64_t c = c0; c <= c1 && n < kMaxPieces; ++c) pslot[n++] = (int)(c + j0 + js);
+                    }
+                    flags[2] = n;
+                }
+                named_bar_sync(1, kConsumerWarps * 32);
+                const int npc = flags[2];
+                // (2) every piece's (m, l) per query group, in parallel
+                for (int x = ctid; x < npc * NG; x += kConsumerWarps * 32) {
+                    const float* pp = p.ws_part + (int64_t)pslot[x / NG] * C::SLOT_FLOATS + NG * DVP;
+                    pw[x] = __ldcg(pp + x % NG);
+                    pl[x] = __ldcg(pp + NG + x % NG);
+                }
+                named_bar_sync(1, kConsumerWarps * 32);
+                // (3) per query group: global max, piece weights, total sum
+                if (ctid < NG) {
                     float M = -INFINITY;
-                    for (int js = 0; js < nseg_g; ++js) {
-                        int64_t t0, nt_;
-                        tab.seg_tiles(sg.group, js, t0, nt_);
-                        if (nt_ == 0) continue;
-                        const int64_t c0 = split_owner(t0, total, nctas), c1 = split_owner(t0 + nt_ - 1, total, nctas);
-                        for (int64_t c = c0; c <= c1; ++c)
-                            M = fmaxf(M, __ldcg(p.ws_part + (c + j0 + js) * C::SLOT_FLOATS + NG * DVP + grp));
-                    }
+                    for (int k = 0; k < npc; ++k) M = fmaxf(M, pw[k * NG + ctid]);
                     const float Mu = (M == -INFINITY) ? 0.f : M;
-                    float acc = 0.f, L = 0.f;
-                    for (int js = 0; js < nseg_g; ++js) {
-                        int64_t t0, nt_;
-                        tab.seg_tiles(sg.group, js, t0, nt_);
-                        if (nt_ == 0) continue;
-                        const int64_t c0 = split_owner(t0, total, nctas), c1 = split_owner(t0 + nt_ - 1, total, nctas);
-                        for (int64_t c = c0; c <= c1; ++c) {
-                            const float* pp = p.ws_part + (c + j0 + js) * C::SLOT_FLOATS;
-                            const float wt = ex2(__ldcg(pp + NG * DVP + grp) - Mu);
-                            acc += wt * __ldcg(pp + e);
-                            L += wt * __ldcg(pp + NG * DVP + NG + grp);
-                        }
+                    float L = 0.f;
+                    for (int k = 0; k < npc; ++k) {
+                        const float w = ex2(pw[k * NG + ctid] - Mu);
+                        pw[k * NG + ctid] = w;
+                        L += w * pl[k * NG + ctid];
                     }
-                    store_final(p, sg.group, grp, d, acc, M, L);
+                    gml[ctid] = M;
+                    gml[NG + ctid] = L;
+                }
+                named_bar_sync(1, kConsumerWarps * 32);
+                // (4) weighted sum of the pieces' o: each thread owns CPT float4 chunks and
+                //     keeps KB pieces' loads in flight per chunk (the loads are latency-bound)
+                {
+                    constexpr int NCH = NG * DVP / 4;
+                    constexpr int CPT = (NCH + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
+                    constexpr int KB = CPT >= 4 ? 4 : 16 / (2 * CPT);
+                    float4 acc[CPT];
+#pragma unroll
+                    for (int c = 0; c < CPT; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int k0 = 0; k0 < npc; k0 += KB) {
+                        float4 v[CPT][KB];
+#pragma unroll
+                        for (int u = 0; u < KB; ++u)
+#pragma unroll
+                            for (int c = 0; c < CPT; ++c) {
+                                const int ch = ctid + c * kConsumerWarps * 32;
+                                v[c][u] = (k0 + u < npc && ch < NCH)
+                                              ? __ldcg(reinterpret_cast<const float4*>(
+                                                    p.ws_part + (int64_t)pslot[k0 + u] * C::SLOT_FLOATS + ch * 4))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                        for (int u = 0; u < KB; ++u)
+#pragma unroll
+                            for (int c = 0; c < CPT; ++c) {
+                                const int ch = ctid + c * kConsumerWarps * 32;
+                                if (k0 + u < npc && ch < NCH) {
+                                    const float w = pw[(k0 + u) * NG + (ch * 4) / DVP];
+                                    acc[c].x += w * v[c][u].x; acc[c].y += w * v[c][u].y;
+                                    acc[c].z += w * v[c][u].z; acc[c].w += w * v[c][u].w;
+                                }
+                            }
+                    }
+#pragma unroll
+                    for (int c = 0; c < CPT; ++c) {
+                        const int ch = ctid + c * kConsumerWarps * 32;
+                        if (ch >= NCH) continue;
+                        const int e = ch * 4, grp = e / DVP, d = e - grp * DVP;
+                        if (grp >= p.G || d >= p.Dv) continue;
+                        const float M = gml[grp], L = gml[NG + grp];
+                        store_final(p, sg.group, grp, d, acc[c].x, M, L);
+                        if (d + 1 < p.Dv) store_final(p, sg.group, grp, d + 1, acc[c].y, M, L);
+                        if (d + 2 < p.Dv) store_final(p, sg.group, grp, d + 2, acc[c].z, M, L);
+                        if (d + 3 < p.Dv) store_final(p, sg.group, grp, d + 3, acc[c].w, M, L);
+                    }
                 }
                 if (ctid == 0) p.ws_cnt[sg.group] = 0;   // ready for the next launch
             }
@@ -434,17 +524,19 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
     };
 
     reset_state();
-    int64_t i = 0;
-    for (int64_t t = t_begin; t < t_end; ++t, ++i) {
-        const Seg sg = tab.of_tile(t);
-        if (sg.j != cur.j) {
+    int64_t seg_end = -1;   // first tile after the current segment
+    int stage = 0;
+    uint32_t use = 0;
+    for (int64_t t = t_begin; t < t_end; ++t) {
+        if (t >= seg_end) {
+            const Seg sg = tab.of_tile(t);
             if (cur.j >= 0) flush(cur);
             cur = sg;
+            seg_end = sg.t0 + (sg.len + kTile - 1) / kTile;
             load_q(sg.group);
             reset_state();
         }
-        const int stage = (int)(i % STAGES);
-        const uint32_t use = (uint32_t)(i / STAGES);
+        const Seg& sg = cur;
         if (!mbar_wait_bounded(full0 + 8 * stage, use & 1)) {
             atomicExch(p.status, kDevTimeout);
             break;
@@ -505,6 +597,11 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                 pb[nt][1] = movmatrix_t(pack_bf16(pbm[0], pbm[1]));
             }
             // ---- O^T += V^T . P^T
+            // Rows past the segment's end may hold anything (unused cache
+            // capacity); P is 0 there but 0 * NaN is not, so those V entries are
+            // zeroed.  a0/a1 carry tokens 2c, 2c+1 and a2/a3 tokens 2c+8, 2c+9.
+            const uint32_t vm01 = (2 * cq < nv ? 0x0000ffffu : 0u) | (2 * cq + 1 < nv ? 0xffff0000u : 0u);
+            const uint32_t vm23 = (2 * cq + 8 < nv ? 0x0000ffffu : 0u) | (2 * cq + 9 < nv ? 0xffff0000u : 0u);
 #pragma unroll
             for (int ii = 0; ii < DVP / 16; ++ii) {
                 const int d0 = ii * 16;
@@ -512,12 +609,17 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                 const int chunk = ((d0 & 63) >> 3) + (lq & 1);
                 uint32_t a0, a1, a2, a3;
                 ldsm_x4_t(vbase + (d0 >> 6) * C::BOX_BYTES + swz128(row, chunk), a0, a1, a2, a3);
+                a0 &= vm01; a1 &= vm01; a2 &= vm23; a3 &= vm23;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_bf16_16816(o[ii][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * stage);
+        if (++stage == STAGES) {
+            stage = 0;
+            ++use;
+        }
     }
     if (cur.j >= 0) flush(cur);
 }
@@ -591,6 +693,7 @@ int gqa_launch(const GqaLaunch& a) {
     for (int s = 0; s < a.nshare; ++s) {
         const KvShare& sh = a.shares[s];
         p.cu[s] = sh.cu_seqlens;
+        p.lens[s] = sh.seqlens;
         if (sh.n_tok == 0 || sh.n_rows == 0) continue;   // nothing to map; no tile will reference it
         const int tmk = make_kv_map(&maps.k[s], sh.k, sh.k_stride_tok, sh.k_stride_row, a.Dk, sh.n_tok, sh.n_rows,
                                     kTile, &p.tok_in_dim2[s]);
@@ -604,7 +707,7 @@ int gqa_launch(const GqaLaunch& a) {
         p.has_map[s] = 1;
     }
 
-    int nsm = device_sm_count();
+    const int nsm = std::min(device_sm_count(), kMaxPieces - kMaxShares);
     int64_t total_tiles;
     int nctas;
     if (!a.varlen) {
@@ -614,19 +717,22 @@ int gqa_launch(const GqaLaunch& a) {
         nctas = nsm;
         total_tiles = -1;
     }
+    if (p.n_groups > kMaxGroupsPerLaunch)
+        return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: more than 65536 output row groups in one launch");
     const int nseg = a.varlen ? a.B * a.Hkv * a.nshare : a.n_rows;
     const size_t need = gqa_workspace_bytes(a.G, a.Dv, nseg, p.n_groups, nctas);
     if (a.workspace_bytes < need || (need && !a.workspace))
         return set_error(WS_ERR_WORKSPACE, "gqa_decode: workspace too small (see ws_gqa_workspace_size)");
     p.ws_cnt = static_cast<int*>(a.workspace);
-    p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + align_up(size_t(p.n_groups) * 4, 256));
+    p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
     const size_t extra_smem = a.varlen ? size_t(a.B + 1) * 4 : 0;
     (void)total_tiles;
     return dispatch(maps, p, a.Dk, a.Dv, nctas, extra_smem, static_cast<cudaStream_t>(a.stream));
 }
 
 size_t gqa_workspace_bytes(int G, int Dv, int nseg, int n_groups, int nctas) {
-    return align_up(size_t(n_groups) * 4, 256) + size_t(nseg + nctas) * gqa_slot_bytes(G, Dv);
+    (void)n_groups;
+    return kCounterHeaderBytes + size_t(nseg + nctas) * gqa_slot_bytes(G, Dv);
 }
 
 }  // namespace ws

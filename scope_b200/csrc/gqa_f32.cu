@@ -179,7 +179,8 @@ int gqa_f32_launch(const void* q, const void* k, const void* v, int64_t k_sb, in
     // splits: enough blocks to cover the SMs twice, at most one per 256 tokens
     const int nsm = device_sm_count();
     int splits = std::max(1, std::min((L + 255) / 256, (2 * nsm + B_kv - 1) / B_kv));
-    const size_t cnt_bytes = align_up(size_t(B_kv) * 4, 256);
+    if (B_kv > kMaxGroupsPerLaunch) return set_error(WS_ERR_UNSUPPORTED, "fp32 path: more than 65536 rows in one launch");
+    const size_t cnt_bytes = kCounterHeaderBytes;
     const size_t slots_fit = workspace_bytes > cnt_bytes ? (workspace_bytes - cnt_bytes) / (size_t(slot_floats) * 4) : 0;
     while (splits > 1 && size_t(B_kv) * splits > slots_fit) --splits;
     if (splits > 1 && !workspace) splits = 1;

@@ -76,7 +76,7 @@ int ws_gqa_decode_noalloc(const void* q, const void* k, const void* v, int64_t k
     void* scratch = scratch_address();
     if (!scratch) return set_error(WS_ERR_CUDA, "ws_gqa_decode_noalloc: cudaGetSymbolAddress failed");
     // the merge counters (one int per output row group) must start at zero
-    const size_t counters = align_up(size_t(B_kv) * 4, 256);
+    const size_t counters = std::min(align_up(size_t(B_kv) * 4, 256), kCounterHeaderBytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (cudaMemsetAsync(scratch, 0, counters, st) != cudaSuccess)
         return set_error(WS_ERR_CUDA, "ws_gqa_decode_noalloc: clearing the scratch counters failed");

@@ -20,10 +20,19 @@ int* device_status_word();
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Every workspace starts with a fixed header of merge counters (one int per
+// output row group, group g at index g) and the partial results follow it.
+// Because the header never moves, a workspace can be shared by launches of
+// any shapes: counters are touched only by the merge tickets, which return
+// them to zero, and partials never land on them.
+constexpr size_t kCounterHeaderBytes = size_t(256) << 10;
+constexpr int kMaxGroupsPerLaunch = int(kCounterHeaderBytes / 4);
+
 struct KvShare {
     const void* k;
     const void* v;
-    const int* cu_seqlens;      // varlen only
+    const int* cu_seqlens;      // varlen, packed share
+    const int* seqlens;         // varlen, padded share
     int64_t n_tok, n_rows;      // TMA extents: tokens, rows (kv rows or kv heads)
     int64_t k_stride_tok, k_stride_row, v_stride_tok, v_stride_row;   // elements
 };

@@ -17,17 +17,30 @@ from ._lib import KvShare, check, lib, ptr, stream_ptr, workspaces
 
 
 class Share:
-    """One physical KV share of a ragged batch.
+    """One physical KV share of a ragged batch, in one of two layouts.
 
-    k, v: token-major packed buffers [n_tok, Hkv, D] bf16 (any strides on the
-    first two dims, unit stride on D); cu_seqlens: int32 [B+1] on the same
-    device -- sequence b owns tokens [cu[b], cu[b+1]) of this share.
+    packed -- ``Share(k, v, cu_seqlens=cu)``: k, v [n_tok, Hkv, D] bf16 (any
+        strides on the first two dims, e.g. a token-major buffer or the
+        transpose of a head-major [Hkv, n_tok, D] one); cu int32 [B+1]:
+        sequence b owns tokens [cu[b], cu[b+1]).
+    padded -- ``Share(k, v, seqlens=lens)``: k, v [B*Hkv, cap, D] bf16, one
+        capacity-sized row per (sequence, kv-head) like the reference's
+        InplaceKVCache (system/qwenoffload.py:59-141); lens int32 [B]: tokens
+        [0, lens[b]) of rows b*Hkv .. b*Hkv+Hkv-1 are valid.
+    Length arrays live on the same device as k and v.
     """
 
-    __slots__ = ("k", "v", "cu_seqlens")
+    __slots__ = ("k", "v", "cu_seqlens", "seqlens")
 
-    def __init__(self, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor):
-        self.k, self.v, self.cu_seqlens = k, v, cu_seqlens
+    def __init__(self, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor | None = None,
+                 seqlens: torch.Tensor | None = None):
+        if (cu_seqlens is None) == (seqlens is None):
+            raise ValueError("Share: give exactly one of cu_seqlens (packed) or seqlens (padded)")
+        self.k, self.v, self.cu_seqlens, self.seqlens = k, v, cu_seqlens, seqlens
+
+    @property
+    def padded(self) -> bool:
+        return self.seqlens is not None
 
 
 def gqa_decode_shares(q: torch.Tensor, shares: Sequence[Share], scale: float,
@@ -43,29 +56,39 @@ def gqa_decode_shares(q: torch.Tensor, shares: Sequence[Share], scale: float,
     if not 1 <= len(shares) <= 4:
         raise RuntimeError("gqa_decode_shares: 1 to 4 shares")
     B, H, Dk = q.shape
-    Hkv = shares[0].k.shape[1]
-    Dv = shares[0].v.shape[2]
-    if H % Hkv:
+    s0 = shares[0]
+    Hkv = s0.k.shape[0] // B if s0.padded else s0.k.shape[1]
+    Dv = s0.v.shape[2]
+    if Hkv < 1 or H % Hkv:
         raise RuntimeError("gqa_decode_shares: query heads must be a multiple of KV heads")
     G = H // Hkv
     dev = q.device
     arr = (KvShare * len(shares))()
     for i, s in enumerate(shares):
-        for t in (s.k, s.v, s.cu_seqlens):
+        lens = s.seqlens if s.padded else s.cu_seqlens
+        for t in (s.k, s.v, lens):
             if not t.is_cuda or t.device != dev:
                 raise RuntimeError("gqa_decode_shares: all tensors must be on q's device")
         if s.k.dtype != torch.bfloat16 or s.v.dtype != torch.bfloat16:
             raise RuntimeError("gqa_decode_shares: k/v must be bf16")
-        if s.k.dim() != 3 or s.v.dim() != 3 or s.k.shape[1] != Hkv or s.v.shape[1] != Hkv:
-            raise RuntimeError("gqa_decode_shares: k/v must be [n_tok, Hkv, D] with the same Hkv")
-        if s.k.shape[2] != Dk or s.v.shape[2] != Dv or s.k.shape[0] != s.v.shape[0]:
+        if s.k.dim() != 3 or s.v.dim() != 3 or s.k.shape[2] != Dk or s.v.shape[2] != Dv:
+            raise RuntimeError("gqa_decode_shares: k/v must be 3-D with head dims Dk / Dv")
+        if s.k.shape[:2] != s.v.shape[:2]:
             raise RuntimeError("gqa_decode_shares: k/v shape mismatch")
         if s.k.stride(2) != 1 or s.v.stride(2) != 1:
             raise RuntimeError("gqa_decode_shares: unit stride on the head dim required")
-        if s.cu_seqlens.dtype != torch.int32 or s.cu_seqlens.numel() != B + 1:
-            raise RuntimeError("gqa_decode_shares: cu_seqlens must be int32 [B+1]")
-        arr[i] = KvShare(ptr(s.k), ptr(s.v), ptr(s.cu_seqlens), s.k.shape[0],
-                         s.k.stride(0), s.k.stride(1), s.v.stride(0), s.v.stride(1))
+        if lens.dtype != torch.int32:
+            raise RuntimeError("gqa_decode_shares: length arrays must be int32")
+        if s.padded:
+            if s.k.shape[0] != B * Hkv or lens.numel() != B:
+                raise RuntimeError("gqa_decode_shares: padded share must be [B*Hkv, cap, D] with seqlens [B]")
+            arr[i] = KvShare(ptr(s.k), ptr(s.v), None, ptr(lens), s.k.shape[1],
+                             s.k.stride(1), s.k.stride(0), s.v.stride(1), s.v.stride(0))
+        else:
+            if s.k.shape[1] != Hkv or lens.numel() != B + 1:
+                raise RuntimeError("gqa_decode_shares: packed share must be [n_tok, Hkv, D] with cu_seqlens [B+1]")
+            arr[i] = KvShare(ptr(s.k), ptr(s.v), ptr(lens), None, s.k.shape[0],
+                             s.k.stride(0), s.k.stride(1), s.v.stride(0), s.v.stride(1))
     if out is None:
         out = torch.empty(B, H, Dv, dtype=torch.bfloat16, device=dev)
     if lse is None:

@@ -138,26 +138,40 @@ def test_repeat_calls_reuse_workspace(ext):
     assert torch.equal(out, first) and torch.equal(lse, lse0)
 
 
-def test_shares_ragged_two_way(ext):
-    """cfg2-style ragged batch, each sequence split into two physical shares."""
+@pytest.mark.parametrize("layout", ["token_major", "head_major", "padded"])
+def test_shares_ragged_two_way(ext, layout):
+    """cfg2-style ragged batch, each sequence split into two physical shares,
+    in the packed token-major, packed head-major and padded (reference cache) layouts."""
     gen = torch.Generator().manual_seed(2)
     B, Hkv, G, D = 5, 8, 4, 128
     lens = [1024, 77, 3000, 1, 2500]
     r = 0.25
     L0 = [int(r * L) for L in lens]
-    L1 = [L - a for L, a in zip(lens, L0)]
     q = rand_bf16(B, Hkv * G, D, gen=gen)
     ks = [rand_bf16(L, Hkv, D, gen=gen) for L in lens]
     vs = [rand_bf16(L, Hkv, D, gen=gen) for L in lens]
 
-    def pack(part):
-        k = torch.cat([kk[a:b] for kk, (a, b) in zip(ks, part)], 0)
-        v = torch.cat([vv[a:b] for vv, (a, b) in zip(vs, part)], 0)
-        cu = torch.tensor([0] + list(np.cumsum([b - a for a, b in part])), dtype=torch.int32)
-        return scope_b200.Share(k.to(DEV), v.to(DEV), cu.to(DEV))
+    def make(part):
+        n = [b - a for a, b in part]
+        if layout == "padded":
+            cap = max(max(n), 1) + 3
+            k = torch.full((B * Hkv, cap, D), float("nan")).bfloat16()   # unused capacity is never read
+            v = torch.full((B * Hkv, cap, D), float("nan")).bfloat16()
+            for bi, (a, b2) in enumerate(part):
+                k[bi * Hkv:(bi + 1) * Hkv, :b2 - a] = ks[bi][a:b2].permute(1, 0, 2)
+                v[bi * Hkv:(bi + 1) * Hkv, :b2 - a] = vs[bi][a:b2].permute(1, 0, 2)
+            return scope_b200.Share(k.to(DEV), v.to(DEV), seqlens=torch.tensor(n, dtype=torch.int32).to(DEV))
+        k = torch.cat([kk[a:b2] for kk, (a, b2) in zip(ks, part)], 0)
+        v = torch.cat([vv[a:b2] for vv, (a, b2) in zip(vs, part)], 0)
+        cu = torch.tensor([0] + list(np.cumsum(n)), dtype=torch.int32).to(DEV)
+        if layout == "head_major":
+            kd = k.permute(1, 0, 2).contiguous().to(DEV).permute(1, 0, 2)
+            vd = v.permute(1, 0, 2).contiguous().to(DEV).permute(1, 0, 2)
+            return scope_b200.Share(kd, vd, cu_seqlens=cu)
+        return scope_b200.Share(k.to(DEV), v.to(DEV), cu_seqlens=cu)
 
-    s0 = pack([(0, a) for a in L0])
-    s1 = pack([(a, L) for a, L in zip(L0, lens)])
+    s0 = make([(0, a) for a in L0])
+    s1 = make([(a, L) for a, L in zip(L0, lens)])
     out, lse = scope_b200.gqa_decode_shares(q.to(DEV), [s0, s1], D ** -0.5)
     out, lse = out.float().cpu().numpy(), lse.cpu().numpy()
     for b in range(B):
@@ -167,6 +181,22 @@ def test_shares_ragged_two_way(ext):
         ro, rm, rs = oracle_of(qb, kb.contiguous(), vb.contiguous(), D ** -0.5)
         assert np.abs(out[b].reshape(Hkv, G, D) - ro).max() < TOL_OUT, b
         assert np.abs(lse[b].reshape(Hkv, G) - (rm + np.log(rs))).max() < TOL_LSE, b
+
+
+def test_shares_one_empty_share(ext):
+    """A sequence whose second share is empty, and a batch of all-empty rows."""
+    gen = torch.Generator().manual_seed(3)
+    B, Hkv, G, D = 2, 2, 8, 128
+    q = rand_bf16(B, Hkv * G, D, gen=gen).to(DEV)
+    k = rand_bf16(B * Hkv, 300, D, gen=gen)
+    v = rand_bf16(B * Hkv, 300, D, gen=gen)
+    sA = scope_b200.Share(k.to(DEV), v.to(DEV), seqlens=torch.tensor([300, 0], dtype=torch.int32, device=DEV))
+    sB = scope_b200.Share(k.to(DEV), v.to(DEV), seqlens=torch.tensor([0, 0], dtype=torch.int32, device=DEV))
+    out, lse = scope_b200.gqa_decode_shares(q, [sA, sB], D ** -0.5)
+    ro, rm, rs = oracle_of(q[0].view(Hkv, G, D).cpu(), k[:Hkv], v[:Hkv], D ** -0.5)
+    assert np.abs(out[0].float().cpu().numpy().reshape(Hkv, G, D) - ro).max() < TOL_OUT
+    assert np.abs(lse[0].cpu().numpy().reshape(Hkv, G) - (rm + np.log(rs))).max() < TOL_LSE
+    assert torch.all(out[1] == 0) and torch.all(torch.isneginf(lse[1]))
 
 
 def test_lse_merge_kernel():
