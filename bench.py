@@ -17,6 +17,7 @@ Workloads (the default is the one the metric's
 1/2/4/8-GPU scaling is quoted on):
   cfg1  GQA Qwen3 layer, B=1, L=4096
   cfg2  GQA Mixtral layer, B=16, ragged L in [1024, 32768], two shares merged by LSE
+  cfg3  absorbed MLA, DeepSeek-V2-Lite: B=8, 16 heads, latent 512 + rope 64, S=16384
   cfg4  GQA Qwen3, B=32, L=131072 sequence-sharded over N GPUs (default)
 """
 from __future__ import annotations
@@ -369,6 +370,72 @@ class GqaShares(Workload):
         return cpu_ref_shares(self.B, self.H, self.Hkv, self.D, budget_s, max_calls, warm)
 
 
+class Mla(Workload):
+    """cfg3: absorbed MLA, DeepSeek-V2-Lite shape: B=8, 16 heads sharing one
+    latent KV of 512 + 64 rope dims, S=16384, scale 1/sqrt(192); output
+    [8*16, 512] bf16 normalised + fp32 LSE (ws_mla_decode: the tcgen05 split-KV
+    kernel and its merge kernel)."""
+
+    name = "cfg3"
+    kernel_name = "mla_decode_kernel (tcgen05) + mla_merge_kernel"
+    profile_name = "mla_decode_cfg3"
+
+    def __init__(self, world, rank, B=8, nH=16, S=16384, seed=3):
+        from scope_b200 import cpu_attn
+        self.world, self.rank = world, rank
+        self.B, self.nH, self.S = B, nH, S
+        self.scale = 192 ** -0.5
+        self.workload = f"mla_absorbed_ds2lite_b{B}_h{nH}_s{S}"
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(seed)
+        per_copy = B * S * (512 + 64) * 2
+        self.copies = max(1, -(-3 * L2_BYTES // per_copy))
+        self.graph = True
+        self.c = [bf16_randn((B, S, 512), g, dev) for _ in range(self.copies)]
+        self.p = [bf16_randn((B, S, 64), g, dev) for _ in range(self.copies)]
+        self.qp = bf16_randn((B * nH, 512), g, dev)
+        self.qpe = bf16_randn((B * nH, 64), g, dev)
+        self._decode = cpu_attn.mla_decode
+        self.qp_host = torch.randn(B * nH, 512).bfloat16().pin_memory()
+        self.qpe_host = torch.randn(B * nH, 64).bfloat16().pin_memory()
+        self.cnew_host = torch.randn(B, 512).bfloat16().pin_memory()
+        self.pnew_host = torch.randn(B, 64).bfloat16().pin_memory()
+        self.out_host = torch.empty(B * nH, 512, dtype=torch.bfloat16).pin_memory()
+        self.lse_host = torch.empty(B * nH, dtype=torch.float32).pin_memory()
+        self.kernels_per_step = 2
+
+    def kernel_bytes(self):
+        return self.B * self.S * (512 + 64) * 2 + self.B * self.nH * (576 * 2 + 512 * 2 + 4)
+
+    def kernel(self, i):
+        c = i % self.copies
+        self.out, self.lse = self._decode(self.qp, self.qpe, self.c[c], self.p[c], self.scale)
+
+    step = kernel
+
+    def e2e_step(self, i):
+        c = i % self.copies
+        self.qp.copy_(self.qp_host, non_blocking=True)
+        self.qpe.copy_(self.qpe_host, non_blocking=True)
+        self.c[c][:, self.S - 1].copy_(self.cnew_host, non_blocking=True)   # the new token's latent
+        self.p[c][:, self.S - 1].copy_(self.pnew_host, non_blocking=True)
+        out, lse = self._decode(self.qp, self.qpe, self.c[c], self.p[c], self.scale)
+        self.out_host.copy_(out, non_blocking=True)
+        self.lse_host.copy_(lse, non_blocking=True)
+
+    def e2e_bytes(self):
+        return ((self.qp_host.numel() + self.qpe_host.numel() + self.cnew_host.numel() + self.pnew_host.numel()) * 2,
+                self.out_host.numel() * 2 + self.lse_host.numel() * 4)
+
+    def config(self):
+        return {"workload": self.workload, "batch": self.B, "heads": self.nH, "kv_lora_rank": 512, "rope_dims": 64,
+                "kv_len": self.S, "parallelism": "single-gpu",
+                "l2": f"{self.copies} rotating input copies > 3x L2", "timing": "cuda-graph replay"}
+
+    def cpu_reference(self, budget_s, max_calls, warm=1):
+        return cpu_ref_mla(self.B, self.nH, self.S, budget_s, max_calls, warm)
+
+
 # ------------------------------------------------- reference CPU measurements
 def cfg2_geometry(B=16, seed=2):
     """Seeded ragged lengths ~ U[1024, 32768] and share ratios in {.25, .5, .75}."""
@@ -441,6 +508,27 @@ def cpu_ref_shares(B, H, Hkv, D, budget_s, max_calls, warm=1):
                                   "fused_cpu_attn + torch LSE merge"}
 
 
+def cpu_ref_mla(B, nH, S, budget_s, max_calls, warm=1):
+    """The reference's fused_cpu_attn_mla_compressed on all host cores (full cfg3)."""
+    import oracle
+    torch.manual_seed(13)
+    qp = torch.randn(B * nH, 512).bfloat16()
+    qpe = torch.randn(B * nH, 64).bfloat16()
+    c = torch.randn(B, S, 512).bfloat16()
+    p = torch.randn(B, S, 64).bfloat16()
+    nbytes = B * S * 576 * 2 + B * nH * (576 * 2 + 512 * 4 + 8)
+    ref = load_cpu_ref()
+    if ref is not None:
+        kind, fn = "reference", (lambda: ref.fused_cpu_attn_mla_compressed(qp, qpe, c, p, 192 ** -0.5))
+    else:
+        bits = [oracle.bf16_bits(t) for t in (qp, qpe, c, p)]
+        kind, fn = "port", (lambda: oracle.mla_compressed(*bits, 192 ** -0.5))
+    t, n = median_time(fn, budget_s, max_calls, warm)
+    return nbytes / t, {"kind": kind, "cores": os.cpu_count() or 1, "calls": n, "sec_per_call": t,
+                        "sample": f"fused_cpu_attn_mla_compressed, B={B}, nH={nH}, S={S} (full cfg3, "
+                                  f"{nbytes / 1e6:.1f} MB per call)"}
+
+
 def cpu_reference_for(name, args, budget_s, max_calls, warm):
     if name == "cfg4":
         return cpu_ref_dense(32, 4, 8, 128, args.kv_len or 131072, budget_s, max_calls, warm), \
@@ -450,6 +538,8 @@ def cpu_reference_for(name, args, budget_s, max_calls, warm):
     if name == "cfg2":
         return cpu_ref_shares(16, 32, 8, 128, budget_s, max_calls, warm), \
             "gqa_mixtral_b16_ragged_1024_32768_two_shares"
+    if name == "cfg3":
+        return cpu_ref_mla(8, 16, 16384, budget_s, max_calls, warm), "mla_absorbed_ds2lite_b8_h16_s16384"
     raise ValueError(name)
 
 
@@ -460,10 +550,12 @@ def make_workload(name, world, rank, args):
         return GqaDense(world, rank, "cfg1", 1, 32, 4, 128, args.kv_len or 4096, 1000)
     if name == "cfg2":
         return GqaShares(world, rank)
+    if name == "cfg3":
+        return Mla(world, rank, S=args.kv_len or 16384)
     raise ValueError(name)
 
 
-WORKLOADS = ("cfg1", "cfg2", "cfg4")
+WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4")
 
 
 # -------------------------------------------------------------------- main
@@ -606,7 +698,8 @@ def main():
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "peak_source": peak_src, "kernel": wl.kernel_name,
                              "kernel_us": t_kernel * 1e6, "algorithmic_bytes_per_launch": kb,
-                             "traffic": profile_traffic(f"gqa_decode_{wl.name}")},
+                             "traffic": profile_traffic(wl.profile_name if hasattr(wl, "profile_name")
+                                                        else f"gqa_decode_{wl.name}")},
                 "gpu_launches": wl.kernels_per_step * n_timed,
                 "clocks": clocks, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

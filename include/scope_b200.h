@@ -131,6 +131,23 @@ int ws_gqa_decode_shares(const void* q, int B, int Hkv, int G, int Dk, int Dv, f
 size_t ws_gqa_decode_shares_workspace_size(int B, int Hkv, int G, int Dv, int n_shares);
 
 /*
+ * Absorbed-MLA decode: many heads over one shared latent KV (V = the latent).
+ * Replaces fused_cpu_attn_mla_compressed (kernel/cpu_attn.cpp:852-1022).
+ *   q_proj [B*nH, 512], q_pe [B*nH, 64], c_kv [B, S, 512], k_pe [B, S, 64]:
+ *   bf16, contiguous, 16-byte aligned.
+ *   score(h, t) = scale * (q_proj[h].c_kv[t] + q_pe[h].k_pe[t]);  o[h] = sum_t softmax * c_kv[t]
+ *   out_mode WS_OUT_UNNORM_F32: out [B*nH, 512] fp32 NOT normalised + out_max, out_sum
+ *     [B*nH] fp32 (the reference's outputs); WS_OUT_NORM_BF16 / _F32: out normalised.
+ *   out_lse [B*nH] fp32 optional (NULL).  out_max/out_sum may be NULL.
+ * Two launches on the stream: the tcgen05 split-KV kernel and its merge
+ * (a programmatic dependent launch).  This build supports nH == 16.
+ */
+int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
+                  float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse,
+                  void* workspace, size_t workspace_bytes, void* stream);
+size_t ws_mla_decode_workspace_size(int B, int nH, int S);
+
+/*
  * Log-sum-exp merge of P partial attention results (the cross-GPU combine of
  * a sequence-sharded KV cache, and the runtime merges it replaces:
  * system/qwenoffload.py:1606-1617 lse form).

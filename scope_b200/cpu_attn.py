@@ -128,6 +128,57 @@ def fused_cpu_attn_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale
     return out, mx, sm
 
 
+def _run_mla(q_proj, q_pe, c_kv, k_pe, scale, out_mode, out, mx, sm, lse):
+    dev = _require_cuda("fused_cpu_attn_mla_compressed", q_proj, q_pe, c_kv, k_pe)
+    for t in (q_proj, q_pe, c_kv, k_pe):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError("fused_cpu_attn_mla_compressed requires bf16 inputs")
+        if not t.is_contiguous():
+            raise RuntimeError("q_proj, q_pe, c_kv and k_pe must be contiguous")
+    B, S, CLR = c_kv.shape
+    if B == 0 or q_proj.shape[0] % B:
+        raise RuntimeError("q_proj rows must be a multiple of the batch")
+    nH = q_proj.shape[0] // B
+    if not (q_proj.shape[1] == 512 and q_pe.shape[1] == 64 and CLR == 512 and k_pe.shape[2] == 64):
+        raise RuntimeError("expected q_proj [B*nH, 512], q_pe [B*nH, 64], c_kv [B, S, 512], k_pe [B, S, 64]")
+    if q_pe.shape[0] != B * nH or k_pe.shape[0] != B or k_pe.shape[1] != S:
+        raise RuntimeError("shape mismatch between q_proj, q_pe, c_kv, k_pe")
+    L_ = lib()
+    with torch.cuda.device(dev):
+        ws = workspaces.get(L_.ws_mla_decode_workspace_size(B, nH, S), dev)
+        rc = L_.ws_mla_decode(ptr(q_proj), ptr(q_pe), ptr(c_kv), ptr(k_pe), B, nH, S, float(scale), out_mode,
+                              ptr(out), ptr(mx), ptr(sm), ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
+    check(rc, "ws_mla_decode")
+
+
+def fused_cpu_attn_mla_compressed(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor,
+                                  k_pe: torch.Tensor, scale: float):
+    """Absorbed MLA decode (kernel/cpu_attn.cpp:852-1022).
+
+    q_proj [B*nH, 512], q_pe [B*nH, 64], c_kv [B, S, 512], k_pe [B, S, 64], bf16.
+    Returns fp32 (o NOT normalised [B*nH, 512], max [B*nH], sum [B*nH]) like the
+    reference; o / sum[:, None] is the attention output over the latent.
+    """
+    B, S, _ = c_kv.shape
+    R = q_proj.shape[0]
+    dev = c_kv.device
+    out = torch.empty(R, 512, dtype=torch.float32, device=dev)
+    mx = torch.empty(R, dtype=torch.float32, device=dev)
+    sm = torch.empty(R, dtype=torch.float32, device=dev)
+    _run_mla(q_proj, q_pe, c_kv, k_pe, scale, _lib.WS_OUT_UNNORM_F32, out, mx, sm, None)
+    return out, mx, sm
+
+
+def mla_decode(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_pe: torch.Tensor, scale: float):
+    """Absorbed MLA decode returning (out bf16 [B*nH, 512] normalised, lse fp32 [B*nH])."""
+    R = q_proj.shape[0]
+    dev = c_kv.device
+    out = torch.empty(R, 512, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(R, dtype=torch.float32, device=dev)
+    _run_mla(q_proj, q_pe, c_kv, k_pe, scale, _lib.WS_OUT_NORM_BF16, out, None, None, lse)
+    return out, lse
+
+
 def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float):
     """GQA decode returning (out bf16 [B_kv, G, Dv] normalised, lse fp32 [B_kv, G]).
 

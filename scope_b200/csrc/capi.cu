@@ -227,6 +227,19 @@ int ws_gqa_decode_shares(const void* q, int B, int Hkv, int G, int Dk, int Dv, f
     return gqa_launch(a);
 }
 
+size_t ws_mla_decode_workspace_size(int B, int nH, int S) { return mla_workspace_bytes(B, nH, S); }
+
+int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
+                  float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (B < 0 || nH < 1 || S < 0) return set_error(WS_ERR_INVALID_ARG, "mla_decode: bad shape");
+    if (B == 0) return WS_OK;
+    if (!q_proj || !q_pe || !out || (S > 0 && (!c_kv || !k_pe))) return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    if (out_mode < WS_OUT_NORM_BF16 || out_mode > WS_OUT_NORM_F32) return set_error(WS_ERR_INVALID_ARG, "bad out_mode");
+    return mla_launch(q_proj, q_pe, c_kv, k_pe, B, nH, S, scale, out_mode, out, out_max, out_sum, out_lse, workspace,
+                      workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out, int out_dtype,
                  float* out_lse, void* stream) {
     if (P < 1 || R < 0 || D < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");

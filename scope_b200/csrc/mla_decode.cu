@@ -1,0 +1,646 @@
+// Absorbed-MLA decode on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Replaces fused_cpu_attn_mla_compressed (kernel/cpu_attn.cpp:852-1022):
+//   score(h, t) = scale * (q_proj[h] . c[t] + q_pe[h] . p[t])   (576-dim dot)
+//   o[h]        = sum_t softmax(score)[h, t] * c[t]              (V = the 512 latent)
+// for nH heads of one sequence sharing one latent KV.
+//
+// One persistent CTA per SM walks an even share of the flattened (batch,
+// 128-token tile) space.  Warp roles (320 threads):
+//   warp 8      producer: TMA loads of each tile -- the latent as four 32 KB
+//               "pairs" (two 64-dim SWIZZLE_128B boxes of 128 tokens) through
+//               a 5-slot ring, the 64-dim rope box through a 2-slot ring, and
+//               the batch's queries (576 x nH) when a new batch starts;
+//   warp 9      one thread issues the MMAs; the warp owns the TMEM allocation:
+//                 S^T[128 tok x nH]  = [C | P](tile) . [Q_proj | Q_pe]^T  (A K-major)
+//                 O^T[512 x nH]      = C(tile)^T . P^T                   (A MN-major:
+//                 the same swizzled latent tile, read along the other axis)
+//               S and O are double-buffered in TMEM (10*nH of 256 columns);
+//   warps 0-3   softmax: thread = token (TMEM lane); per-head tile max by warp
+//               shuffles + shared memory, online rescale factors, P in bf16
+//               written K-major (swizzled) for the second MMA;
+//   warps 4-7   correction: thread = latent dim (TMEM lane) x 4 blocks; loads
+//               each tile's fresh O^T from TMEM and accumulates
+//               acc = acc * alpha + O in registers.
+// At a batch boundary the CTA files one piece (o, m, l) per head into
+// workspace slot cta + batch; mla_merge_kernel (launched as a programmatic
+// dependent) merges a batch's pieces by log-sum-exp into the outputs.
+// Every mbarrier wait is bounded (2 s) and a timeout aborts the CTA cleanly
+// (status word set, TMEM freed).
+#include <cstdio>
+
+#include "common.cuh"
+#include "ws_internal.h"
+
+namespace ws {
+
+namespace mla {
+
+constexpr int NH = 16;          // heads per sequence (MMA N)
+constexpr int CLR = 512;        // latent (kv_lora_rank)
+constexpr int QRD = 64;         // rope dims
+constexpr int TT = 128;         // tokens per tile (MMA M of the first product)
+constexpr int NP = 5;           // latent pair slots
+constexpr int NE = 2;           // rope slots
+constexpr int PAIR_BYTES = 2 * TT * 128;    // 32 KB
+constexpr int BOX_BYTES = TT * 128;         // 16 KB
+constexpr int QBOX_BYTES = NH * 128;        // 2 KB
+constexpr int PBUF_BYTES = 2 * NH * 128;    // P^T of one tile: 2 K-boxes of 64 tokens
+constexpr int TMEM_COLS = 256;
+constexpr int S_COL = 0;                    // S[j] at j*NH
+constexpr int O_COL = 2 * NH;               // O[j] at O_COL + j*4*NH
+constexpr int kThreads = 320;
+constexpr int SLOT_FLOATS = NH * CLR + 2 * NH;
+
+constexpr int OFF_PAIRS = 0;
+constexpr int OFF_PE = OFF_PAIRS + NP * PAIR_BYTES;
+constexpr int OFF_Q = OFF_PE + NE * BOX_BYTES;
+constexpr int OFF_P = OFF_Q + 9 * QBOX_BYTES;
+constexpr int OFF_MISC = OFF_P + 2 * PBUF_BYTES;
+// barriers
+constexpr int B_PAIR_FULL = 0, B_PAIR_EMPTY = NP, B_PE_FULL = 2 * NP, B_PE_EMPTY = 2 * NP + NE,
+              B_Q_FULL = 2 * NP + 2 * NE, B_Q_EMPTY = B_Q_FULL + 1, B_S_FULL = B_Q_EMPTY + 1,
+              B_S_EMPTY = B_S_FULL + 2, B_P_FULL = B_S_EMPTY + 2, B_P_EMPTY = B_P_FULL + 2,
+              B_O_FULL = B_P_EMPTY + 2, B_O_EMPTY = B_O_FULL + 2, B_ALPHA = B_O_EMPTY + 2,
+              B_ST_FULL = B_ALPHA + 4, B_ST_EMPTY = B_ST_FULL + 1, B_RED = B_ST_EMPTY + 1, B_LRED = B_RED + 2,
+              B_DONE = B_LRED + 1, NBARS = B_DONE + 1;
+constexpr int MISC_BYTES = NBARS * 8 + (2 * 4 * NH + 4 * NH + 2 * NH + 4 * NH) * 4 + 64;
+constexpr size_t SMEM_BYTES = 1024 + OFF_MISC + MISC_BYTES;
+static_assert(SMEM_BYTES <= 227 * 1024, "MLA shared-memory plan exceeds 227 KB");
+
+struct Maps {
+    CUtensorMap c;     // c_kv  [B, S, 512]   dims (512, S, B)
+    CUtensorMap pe;    // k_pe  [B, S, 64]    dims (64, S, B)
+    CUtensorMap q;     // q_proj [B*nH, 512]  dims (512, B*nH, 1)
+    CUtensorMap qpe;   // q_pe   [B*nH, 64]   dims (64, B*nH, 1)
+};
+
+struct Params {
+    int B, S, tpb;          // batches, tokens, tiles per batch
+    float scale_log2;       // softmax scale * log2(e)
+    int c_tok_in_dim2, pe_tok_in_dim2;   // tensor-map axis order (see make_kv_map)
+    float* ws_part;         // pieces, slot = cta + batch
+    int* status;
+};
+
+struct Smem {
+    uint8_t* base;
+    uint64_t* bars;
+    float* red;      // [2][4][NH] per-warp tile maxima
+    float* alpha;    // [4][NH] per-tile rescale factors for the correction warps
+    float* stats;    // [2][NH] segment (m, l)
+    float* lred;     // [4][NH] per-warp partial sums
+    uint32_t* tmem_holder;
+    volatile int* abort_flag;
+};
+
+__device__ __forceinline__ uint32_t bar(const Smem& s, int i) { return smem_u32(&s.bars[i]); }
+
+// Bounded wait that also gives up as soon as another role aborted the CTA.
+__device__ __forceinline__ bool wait_bar(const Smem& s, uint32_t b, uint32_t parity, int* status) {
+    if (mbar_try_wait(b, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(b, parity)) return true;
+        if (*s.abort_flag) return false;
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+            *s.abort_flag = 1;
+            atomicExch(status, kDevTimeout);
+            return false;
+        }
+    }
+}
+
+// 16 per-thread values -> each lane ends with the warp-wide max (or sum) of every entry.
+__device__ __forceinline__ void warp_allmax16(float* v) {
+#pragma unroll
+    for (int h = 0; h < NH; ++h)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v[h] = fmaxf(v[h], __shfl_xor_sync(0xffffffffu, v[h], o));
+}
+__device__ __forceinline__ void warp_allsum16(float* v) {
+#pragma unroll
+    for (int h = 0; h < NH; ++h)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v[h] += __shfl_xor_sync(0xffffffffu, v[h], o);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem s;
+    s.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    s.bars = reinterpret_cast<uint64_t*>(s.base + OFF_MISC);
+    s.red = reinterpret_cast<float*>(s.bars + NBARS);
+    s.alpha = s.red + 2 * 4 * NH;
+    s.stats = s.alpha + 4 * NH;
+    s.lred = s.stats + 2 * NH;
+    s.tmem_holder = reinterpret_cast<uint32_t*>(s.lred + 4 * NH);
+    s.abort_flag = reinterpret_cast<volatile int*>(s.tmem_holder + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cta = blockIdx.x;
+    const int64_t total = (int64_t)p.B * p.tpb;
+    const int nctas = total < 1 ? 1 : (total < (int64_t)gridDim.x ? (int)total : (int)gridDim.x);
+    const int64_t t_begin = cta < nctas ? split_start(cta, total, nctas) : total;
+    const int64_t t_end = cta < nctas ? split_start(cta + 1, total, nctas) : total;
+
+    if (tid == 0) {
+        for (int i = 0; i < NP; ++i) {
+            mbar_init(bar(s, B_PAIR_FULL + i), 1);
+            mbar_init(bar(s, B_PAIR_EMPTY + i), 1);
+        }
+        for (int i = 0; i < NE; ++i) {
+            mbar_init(bar(s, B_PE_FULL + i), 1);
+            mbar_init(bar(s, B_PE_EMPTY + i), 1);
+        }
+        mbar_init(bar(s, B_Q_FULL), 1);
+        mbar_init(bar(s, B_Q_EMPTY), 1);
+        for (int j = 0; j < 2; ++j) {
+            mbar_init(bar(s, B_S_FULL + j), 1);
+            mbar_init(bar(s, B_S_EMPTY + j), 4);
+            mbar_init(bar(s, B_P_FULL + j), 4);
+            mbar_init(bar(s, B_P_EMPTY + j), 1);
+            mbar_init(bar(s, B_O_FULL + j), 1);
+            mbar_init(bar(s, B_O_EMPTY + j), 4);
+        }
+        for (int j = 0; j < 4; ++j) mbar_init(bar(s, B_ALPHA + j), 1);
+        mbar_init(bar(s, B_ST_FULL), 1);
+        mbar_init(bar(s, B_ST_EMPTY), 4);
+        mbar_init(bar(s, B_RED), 4);
+        mbar_init(bar(s, B_RED + 1), 4);
+        mbar_init(bar(s, B_LRED), 4);
+        mbar_init(bar(s, B_DONE), 1);
+        *s.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 9) tmem_alloc(smem_u32(s.tmem_holder), TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *s.tmem_holder;
+    pdl_launch_dependents();
+
+    const uint32_t pairs = smem_u32(s.base + OFF_PAIRS), pes = smem_u32(s.base + OFF_PE);
+    const uint32_t qs = smem_u32(s.base + OFF_Q), ps = smem_u32(s.base + OFF_P);
+
+    if (warp == 8) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0 && t_begin < t_end) {
+            tma_prefetch_desc(&maps.c);
+            tma_prefetch_desc(&maps.pe);
+            tma_prefetch_desc(&maps.q);
+            tma_prefetch_desc(&maps.qpe);
+            int seg = -1, qn = 0;
+            int64_t i = 0;
+            int b = (int)(t_begin / p.tpb);
+            int tl = (int)(t_begin - (int64_t)b * p.tpb);
+            for (int64_t t = t_begin; t < t_end; ++t, ++i) {
+                if (b != seg) {
+                    if (qn > 0 && !wait_bar(s, bar(s, B_Q_EMPTY), (qn - 1) & 1, p.status)) break;
+                    mbar_arrive_expect_tx(bar(s, B_Q_FULL), 9 * QBOX_BYTES);
+                    for (int kb = 0; kb < 8; ++kb)
+                        tma_load_3d(qs + kb * QBOX_BYTES, &maps.q, bar(s, B_Q_FULL), kb * 64, b * NH, 0);
+                    tma_load_3d(qs + 8 * QBOX_BYTES, &maps.qpe, bar(s, B_Q_FULL), 0, b * NH, 0);
+                    ++qn;
+                    seg = b;
+                }
+                bool ok = true;
+                for (int pr = 0; pr < 4 && ok; ++pr) {
+                    const int64_t n = 4 * i + pr;
+                    const int sl = (int)(n % NP);
+                    const uint32_t u = (uint32_t)(n / NP);
+                    if (u > 0 && !wait_bar(s, bar(s, B_PAIR_EMPTY + sl), (u - 1) & 1, p.status)) ok = false;
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(bar(s, B_PAIR_FULL + sl), PAIR_BYTES);
+                    const int c1 = p.c_tok_in_dim2 ? b : tl * TT, c2 = p.c_tok_in_dim2 ? tl * TT : b;
+                    tma_load_3d(pairs + sl * PAIR_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr, c1, c2);
+                    tma_load_3d(pairs + sl * PAIR_BYTES + BOX_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr + 64,
+                                c1, c2);
+                }
+                if (!ok) break;
+                const int e = (int)(i % NE);
+                const uint32_t ue = (uint32_t)(i / NE);
+                if (ue > 0 && !wait_bar(s, bar(s, B_PE_EMPTY + e), (ue - 1) & 1, p.status)) break;
+                mbar_arrive_expect_tx(bar(s, B_PE_FULL + e), BOX_BYTES);
+                tma_load_3d(pes + e * BOX_BYTES, &maps.pe, bar(s, B_PE_FULL + e), 0,
+                            p.pe_tok_in_dim2 ? b : tl * TT, p.pe_tok_in_dim2 ? tl * TT : b);
+                if (++tl == p.tpb) {
+                    tl = 0;
+                    ++b;
+                }
+            }
+            if (*s.abort_flag) {
+                // leave no bulk copy in flight into this CTA's shared memory:
+                // wait (bounded) for the last load issued into every slot
+                const int64_t np_issued = 4 * i + 4, ne_issued = i + 1;
+                for (int sl = 0; sl < NP; ++sl) {
+                    int64_t n = np_issued - 1 - ((np_issued - 1 - sl) % NP + NP) % NP;
+                    if (n >= 0) mbar_wait_bounded(bar(s, B_PAIR_FULL + sl), (uint32_t)(n / NP) & 1, 200000000ull);
+                }
+                for (int e = 0; e < NE; ++e) {
+                    int64_t n = ne_issued - 1 - ((ne_issued - 1 - e) % NE + NE) % NE;
+                    if (n >= 0) mbar_wait_bounded(bar(s, B_PE_FULL + e), (uint32_t)(n / NE) & 1, 200000000ull);
+                }
+                if (qn > 0) mbar_wait_bounded(bar(s, B_Q_FULL), (qn - 1) & 1, 200000000ull);
+            }
+        }
+    } else if (warp == 9) {
+        // ------------------------------------------------------------- MMA issue
+        if (lane == 0 && t_begin < t_end) {
+            const uint32_t id1 = idesc_bf16_f32(TT, NH, false, false);
+            const uint32_t id2 = idesc_bf16_f32(128, NH, true, false);
+            int seg = -1, qn = 0;
+            int64_t i = 0;
+            int b = (int)(t_begin / p.tpb);
+            int tl = (int)(t_begin - (int64_t)b * p.tpb);
+            for (int64_t t = t_begin; t < t_end; ++t, ++i) {
+                const int j = (int)(i & 1);
+                const uint32_t us = (uint32_t)(i >> 1);
+                if (b != seg) {
+                    if (!wait_bar(s, bar(s, B_Q_FULL), qn & 1, p.status)) break;
+                    ++qn;
+                    seg = b;
+                }
+                if (us > 0 && !wait_bar(s, bar(s, B_S_EMPTY + j), (us - 1) & 1, p.status)) break;
+                tc_fence_after();
+                // S^T = [C | P] . [Q_proj | Q_pe]^T  (K = 576 in 36 steps of 16)
+                bool ok = true;
+                for (int pr = 0; pr < 4; ++pr) {
+                    const int64_t n = 4 * i + pr;
+                    const int sl = (int)(n % NP);
+                    if (!wait_bar(s, bar(s, B_PAIR_FULL + sl), (uint32_t)(n / NP) & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int half = 0; half < 2; ++half)
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_bf16(tbase + S_COL + j * NH,
+                                      sdesc_sw128(pairs + sl * PAIR_BYTES + half * BOX_BYTES + kk * 32, 16, 1024),
+                                      sdesc_sw128(qs + (2 * pr + half) * QBOX_BYTES + kk * 32, 16, 1024), id1,
+                                      (pr | half | kk) != 0);
+                }
+                if (!ok) break;
+                const int e = (int)(i % NE);
+                if (!wait_bar(s, bar(s, B_PE_FULL + e), (uint32_t)(i / NE) & 1, p.status)) break;
+                tc_fence_after();
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(tbase + S_COL + j * NH, sdesc_sw128(pes + e * BOX_BYTES + kk * 32, 16, 1024),
+                              sdesc_sw128(qs + 8 * QBOX_BYTES + kk * 32, 16, 1024), id1, 1);
+                umma_commit(bar(s, B_S_FULL + j));
+                umma_commit(bar(s, B_PE_EMPTY + e));
+                const bool seg_end = (t + 1 == t_end) || (tl + 1 == p.tpb);
+                if (seg_end) umma_commit(bar(s, B_Q_EMPTY));
+                // O^T = C^T . P^T  (M = 512 in 4 blocks, K = 128 tokens in 8 steps)
+                if (!wait_bar(s, bar(s, B_P_FULL + j), us & 1, p.status)) break;
+                if (us > 0 && !wait_bar(s, bar(s, B_O_EMPTY + j), (us - 1) & 1, p.status)) break;
+                tc_fence_after();
+                for (int mb = 0; mb < 4; ++mb) {
+                    const int64_t n = 4 * i + mb;
+                    const int sl = (int)(n % NP);
+                    for (int ks = 0; ks < 8; ++ks)
+                        umma_bf16(tbase + O_COL + j * 4 * NH + mb * NH,
+                                  sdesc_sw128(pairs + sl * PAIR_BYTES + ks * 2048, BOX_BYTES, 1024),
+                                  sdesc_sw128(ps + j * PBUF_BYTES + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), id2,
+                                  ks > 0);
+                    umma_commit(bar(s, B_PAIR_EMPTY + sl));
+                }
+                umma_commit(bar(s, B_O_FULL + j));
+                umma_commit(bar(s, B_P_EMPTY + j));
+                if (++tl == p.tpb) {
+                    tl = 0;
+                    ++b;
+                }
+            }
+            // every MMA this thread issued has finished before TMEM is freed
+            umma_commit(bar(s, B_DONE));
+            mbar_wait_bounded(bar(s, B_DONE), 0, 1000000000ull);
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------------------- softmax
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float m_run[NH], l_run[NH];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+            m_run[h] = -INFINITY;
+            l_run[h] = 0.f;
+        }
+        int sn = 0;
+        int64_t i = 0;
+        int b = (int)(t_begin / (p.tpb > 0 ? p.tpb : 1));
+        int tl = (int)(t_begin - (int64_t)b * p.tpb);
+        for (int64_t t = t_begin; t < t_end; ++t, ++i) {
+            const int j = (int)(i & 1);
+            const uint32_t us = (uint32_t)(i >> 1);
+            if (!wait_bar(s, bar(s, B_S_FULL + j), us & 1, p.status)) break;
+            tc_fence_after();
+            float x[NH];
+            tmem_ld16(tbase + lane_base + S_COL + j * NH, x);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(s, B_S_EMPTY + j));
+            const int k = warp * 32 + lane;   // token within the tile
+            const bool valid = tl * TT + k < p.S;
+            float mx[NH];
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+                x[h] = valid ? x[h] * p.scale_log2 : -INFINITY;
+                mx[h] = x[h];
+            }
+            warp_allmax16(mx);
+            // exchange the four warps' maxima through shared memory; the
+            // exchange barrier is an mbarrier so that its wait is bounded too
+            float* red = s.red + (int)(i & 1) * 4 * NH;
+            if (lane == 0)
+#pragma unroll
+                for (int h = 0; h < NH; ++h) red[warp * NH + h] = mx[h];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(s, B_RED + (int)(i & 1)));
+            if (!wait_bar(s, bar(s, B_RED + (int)(i & 1)), us & 1, p.status)) break;
+            float alpha[NH], pv[NH];
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+                const float mt = fmaxf(fmaxf(red[h], red[NH + h]), fmaxf(red[2 * NH + h], red[3 * NH + h]));
+                const float mn = fmaxf(m_run[h], mt);
+                const float mu = (mn == -INFINITY) ? 0.f : mn;
+                alpha[h] = ex2(m_run[h] - mu);
+                pv[h] = ex2(x[h] - mu);
+                l_run[h] = l_run[h] * alpha[h] + pv[h];
+                m_run[h] = mn;
+            }
+            if (us > 0 && !wait_bar(s, bar(s, B_P_EMPTY + j), (us - 1) & 1, p.status)) break;
+            // P^T for the second MMA: K-major (rows = heads, 64 tokens per 128-B row)
+            uint8_t* pb = s.base + OFF_P + j * PBUF_BYTES + (k >> 6) * 2048;
+            const int kc = (k & 63) >> 3, ke = (k & 7) * 2;
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+                *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((kc ^ (h & 7)) << 4) + ke) =
+                    __float2bfloat16_rn(pv[h]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(s, B_P_FULL + j));
+            if (warp == 0 && lane == 0) {
+#pragma unroll
+                for (int h = 0; h < NH; ++h) s.alpha[(i & 3) * NH + h] = alpha[h];
+                mbar_arrive(bar(s, B_ALPHA + (int)(i & 3)));
+            }
+            const bool seg_end = (t + 1 == t_end) || (tl + 1 == p.tpb);
+            if (seg_end) {
+                float lsum[NH];
+#pragma unroll
+                for (int h = 0; h < NH; ++h) lsum[h] = l_run[h];
+                warp_allsum16(lsum);
+                if (lane == 0)
+#pragma unroll
+                    for (int h = 0; h < NH; ++h) s.lred[warp * NH + h] = lsum[h];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(s, B_LRED));
+                if (!wait_bar(s, bar(s, B_LRED), sn & 1, p.status)) break;
+                if (warp == 0 && lane == 0) {
+                    if (sn > 0 && !wait_bar(s, bar(s, B_ST_EMPTY), (sn - 1) & 1, p.status)) {
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < NH; ++h) {
+                            s.stats[h] = m_run[h];
+                            s.stats[NH + h] = s.lred[h] + s.lred[NH + h] + s.lred[2 * NH + h] + s.lred[3 * NH + h];
+                        }
+                        mbar_arrive(bar(s, B_ST_FULL));
+                    }
+                }
+                ++sn;
+#pragma unroll
+                for (int h = 0; h < NH; ++h) {
+                    m_run[h] = -INFINITY;
+                    l_run[h] = 0.f;
+                }
+            }
+            if (++tl == p.tpb) {
+                tl = 0;
+                ++b;
+            }
+        }
+    } else {
+        // ---------------------------------------------------------- correction
+        const int q4 = warp - 4;
+        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+        float acc[4][NH];
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb)
+#pragma unroll
+            for (int h = 0; h < NH; ++h) acc[mb][h] = 0.f;
+        int sn = 0;
+        int64_t i = 0;
+        int b = (int)(t_begin / (p.tpb > 0 ? p.tpb : 1));
+        int tl = (int)(t_begin - (int64_t)b * p.tpb);
+        for (int64_t t = t_begin; t < t_end; ++t, ++i) {
+            const int j = (int)(i & 1);
+            const uint32_t us = (uint32_t)(i >> 1);
+            if (!wait_bar(s, bar(s, B_O_FULL + j), us & 1, p.status)) break;
+            tc_fence_after();
+            float o[4][NH];
+#pragma unroll
+            for (int mb = 0; mb < 4; ++mb) tmem_ld16(tbase + lane_base + O_COL + j * 4 * NH + mb * NH, o[mb]);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(s, B_O_EMPTY + j));
+            if (!wait_bar(s, bar(s, B_ALPHA + (int)(i & 3)), (uint32_t)(i >> 2) & 1, p.status)) break;
+            const float* al = s.alpha + (i & 3) * NH;
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+                const float a = al[h];
+#pragma unroll
+                for (int mb = 0; mb < 4; ++mb) acc[mb][h] = fmaf(acc[mb][h], a, o[mb][h]);
+            }
+            const bool seg_end = (t + 1 == t_end) || (tl + 1 == p.tpb);
+            if (seg_end) {
+                if (!wait_bar(s, bar(s, B_ST_FULL), sn & 1, p.status)) break;
+                float* part = p.ws_part + (int64_t)(cta + b) * SLOT_FLOATS;
+#pragma unroll
+                for (int h = 0; h < NH; ++h)
+#pragma unroll
+                    for (int mb = 0; mb < 4; ++mb) part[h * CLR + mb * 128 + q4 * 32 + lane] = acc[mb][h];
+                if (q4 == 0 && lane < NH) {
+                    part[NH * CLR + lane] = s.stats[lane];
+                    part[NH * CLR + NH + lane] = s.stats[NH + lane];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(s, B_ST_EMPTY));
+                ++sn;
+#pragma unroll
+                for (int mb = 0; mb < 4; ++mb)
+#pragma unroll
+                    for (int h = 0; h < NH; ++h) acc[mb][h] = 0.f;
+            }
+            if (++tl == p.tpb) {
+                tl = 0;
+                ++b;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 9) tmem_dealloc(tbase, TMEM_COLS);
+}
+
+struct MergeParams {
+    int B, S, tpb, nctas;
+    const float* ws_part;
+    int out_mode;
+    void* out;
+    float* out_max;
+    float* out_sum;
+    float* out_lse;
+};
+
+// One warp per (batch, head) output row: log-sum-exp merge of the batch's pieces.
+__global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
+    pdl_wait_primary();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= p.B * NH) return;
+    const int b = row / NH, h = row - b * NH;
+    int c0 = 0, c1 = -1;
+    if (p.tpb > 0) {
+        const int64_t total = (int64_t)p.B * p.tpb;
+        const int64_t t0 = (int64_t)b * p.tpb;
+        c0 = (int)split_owner(t0, total, p.nctas);
+        c1 = (int)split_owner(t0 + p.tpb - 1, total, p.nctas);
+    }
+    float M = -INFINITY;
+    for (int c = c0; c <= c1; ++c) M = fmaxf(M, __ldg(p.ws_part + (int64_t)(c + b) * SLOT_FLOATS + NH * CLR + h));
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
+    float4 acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = c0; c <= c1; ++c) {
+        const float* pp = p.ws_part + (int64_t)(c + b) * SLOT_FLOATS;
+        const float w = ex2(__ldg(pp + NH * CLR + h) - Mu);
+        L += w * __ldg(pp + NH * CLR + NH + h);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(pp + h * CLR + k * 128 + lane * 4));
+            acc[k].x += w * v.x; acc[k].y += w * v.y; acc[k].z += w * v.z; acc[k].w += w * v.w;
+        }
+    }
+    const bool empty = !(L > 0.f);
+    const float mnat = empty ? -INFINITY : M * kLn2;
+    if (p.out_mode == WS_OUT_UNNORM_F32) {
+        float* o = static_cast<float*>(p.out) + (int64_t)row * CLR;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) *reinterpret_cast<float4*>(o + k * 128 + lane * 4) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[k];
+    } else {
+        const float inv = empty ? 0.f : 1.f / L;
+        if (p.out_mode == WS_OUT_NORM_F32) {
+            float* o = static_cast<float*>(p.out) + (int64_t)row * CLR;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<float4*>(o + k * 128 + lane * 4) =
+                    make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
+        } else {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * CLR;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(acc[k].x * inv, acc[k].y * inv);
+                __nv_bfloat162 hi = __floats2bfloat162_rn(acc[k].z * inv, acc[k].w * inv);
+                *reinterpret_cast<__nv_bfloat162*>(o + k * 128 + lane * 4) = lo;
+                *reinterpret_cast<__nv_bfloat162*>(o + k * 128 + lane * 4 + 2) = hi;
+            }
+        }
+    }
+    if (lane == 0) {
+        if (p.out_max) p.out_max[row] = mnat;
+        if (p.out_sum) p.out_sum[row] = empty ? 0.f : L;
+        if (p.out_lse) p.out_lse[row] = empty ? -INFINITY : mnat + logf(L);
+    }
+}
+
+}  // namespace mla
+
+size_t mla_workspace_bytes(int B, int nH, int S) {
+    (void)S;
+    const int nsm = device_sm_count();
+    return kCounterHeaderBytes + size_t(nsm + B) * mla::SLOT_FLOATS * 4 + (nH > 0 ? 0 : 0);
+}
+
+int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
+               float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
+               size_t workspace_bytes, cudaStream_t st) {
+    using namespace mla;
+    if (nH != NH) return set_error(WS_ERR_UNSUPPORTED, "mla_decode: this build supports 16 heads per sequence");
+    if (B < 0 || S < 0) return set_error(WS_ERR_INVALID_ARG, "mla_decode: bad shape");
+    if (B == 0) return WS_OK;
+    const int tpb = (S + TT - 1) / TT;
+    const int64_t total = (int64_t)B * tpb;
+    const int nsm = device_sm_count();
+    const int nctas = (int)std::max<int64_t>(1, std::min<int64_t>(nsm, total));
+    const size_t need = kCounterHeaderBytes + size_t(nctas + B) * SLOT_FLOATS * 4;
+    if (workspace_bytes < need || !workspace)
+        return set_error(WS_ERR_WORKSPACE, "mla_decode: workspace too small (see ws_mla_decode_workspace_size)");
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterHeaderBytes);
+    if (total > 0) {
+        Maps maps;
+        memset(&maps, 0, sizeof(maps));
+        int fc = 0, fpe = 0, fq = 0, rc;
+        if ((rc = make_kv_map(&maps.c, c_kv, CLR, (int64_t)S * CLR, CLR, S, B, TT, &fc)) != WS_OK) return rc;
+        if ((rc = make_kv_map(&maps.pe, k_pe, QRD, (int64_t)S * QRD, QRD, S, B, TT, &fpe)) != WS_OK) return rc;
+        if ((rc = make_kv_map(&maps.q, q_proj, CLR, (int64_t)B * NH * CLR, CLR, (int64_t)B * NH, 1, NH, &fq)) != WS_OK)
+            return rc;
+        if (fq) return set_error(WS_ERR_INVALID_ARG, "mla_decode: unexpected query layout");
+        if ((rc = make_kv_map(&maps.qpe, q_pe, QRD, (int64_t)B * NH * QRD, QRD, (int64_t)B * NH, 1, NH, &fq)) != WS_OK)
+            return rc;
+        if (fq) return set_error(WS_ERR_INVALID_ARG, "mla_decode: unexpected query layout");
+        Params prm;
+        prm.c_tok_in_dim2 = fc;
+        prm.pe_tok_in_dim2 = fpe;
+        prm.B = B;
+        prm.S = S;
+        prm.tpb = tpb;
+        prm.scale_log2 = scale * kLog2e;
+        prm.ws_part = part;
+        prm.status = device_status_word();
+        static int configured_dev = -1;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (configured_dev != dev) {
+            if (cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)SMEM_BYTES) != cudaSuccess)
+                return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for mla_decode_kernel");
+            configured_dev = dev;
+        }
+        mla_decode_kernel<<<nctas, kThreads, SMEM_BYTES, st>>>(maps, prm);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+    }
+    MergeParams mp;
+    mp.B = B;
+    mp.S = S;
+    mp.tpb = tpb;
+    mp.nctas = nctas;
+    mp.ws_part = part;
+    mp.out_mode = out_mode;
+    mp.out = out;
+    mp.out_max = out_max;
+    mp.out_sum = out_sum;
+    mp.out_lse = out_lse;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((B * NH + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = total > 0 ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, mla_merge_kernel, mp);
+    if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+    return WS_OK;
+}
+
+}  // namespace ws

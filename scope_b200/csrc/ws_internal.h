@@ -67,6 +67,11 @@ int gqa_f32_launch(const void* q, const void* k, const void* v, int64_t k_sb, in
                    int64_t v_st, int B_kv, int G, int D, int L, float scale, int out_mode, void* out, void* out_max,
                    void* out_sum, float* out_lse, void* workspace, size_t workspace_bytes, cudaStream_t st);
 
+size_t mla_workspace_bytes(int B, int nH, int S);
+int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
+               float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
+               size_t workspace_bytes, cudaStream_t st);
+
 int lse_merge_launch(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out,
                      int out_dtype, float* out_lse, cudaStream_t st);
 

@@ -1,0 +1,98 @@
+"""GPU parity of the absorbed-MLA decode (tcgen05) against the oracle and the
+reference's golden outputs (fused_cpu_attn_mla_compressed,
+kernel/cpu_attn.cpp:852-1022).  Tolerances: normalised output max-abs 2e-2,
+LSE 1e-3, max 1e-3."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import scope_b200
+
+pytestmark = pytest.mark.gpu
+
+TOL_OUT = 2e-2
+TOL_LSE = 1e-3
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def ext():
+    return scope_b200.build()
+
+
+def bits_to_bf16(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(DEV)
+
+
+def rand_inputs(B, S, nH=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    qp = torch.randn(B * nH, 512, generator=g).bfloat16()
+    qpe = torch.randn(B * nH, 64, generator=g).bfloat16()
+    c = torch.randn(B, S, 512, generator=g).bfloat16()
+    p = torch.randn(B, S, 64, generator=g).bfloat16()
+    return qp, qpe, c, p
+
+
+def check_against_oracle(ext, qp, qpe, c, p, scale):
+    o, m, s = ext.fused_cpu_attn_mla_compressed(qp.to(DEV), qpe.to(DEV), c.to(DEV), p.to(DEV), scale)
+    torch.cuda.synchronize()
+    ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, c, p)), scale)
+    o, m, s = o.cpu().numpy(), m.cpu().numpy(), s.cpu().numpy()
+    assert np.abs(o / s[:, None] - ro / rs[:, None]).max() < TOL_OUT
+    assert np.abs((m + np.log(s)) - (rm + np.log(rs))).max() < TOL_LSE
+    assert np.abs(m - rm).max() < TOL_LSE
+
+
+def test_golden(ext, golden):
+    g = golden("mla_compressed")
+    qp, qpe, c, p = (bits_to_bf16(g[n]) for n in ("q_proj", "q_pe", "c_kv", "k_pe"))
+    o, m, s = ext.fused_cpu_attn_mla_compressed(qp, qpe, c, p, float(g["scale"]))
+    assert o.shape == (32, 512) and m.shape == (32,) and s.shape == (32,)
+    assert o.dtype == torch.float32
+    o, m, s = o.cpu().numpy(), m.cpu().numpy(), s.cpu().numpy()
+    assert np.abs(o / s[:, None] - g["o"] / g["sum"][:, None]).max() < TOL_OUT / 10
+    assert np.abs((m + np.log(s)) - (g["max"] + np.log(g["sum"]))).max() < TOL_LSE
+    assert np.abs(m - g["max"]).max() < TOL_LSE
+
+
+@pytest.mark.parametrize("B,S", [(2, 1), (2, 127), (2, 128), (2, 129), (3, 700), (1, 4096), (8, 2000),
+                                 (300, 100), (37, 257)])
+def test_random_shapes(ext, B, S):
+    qp, qpe, c, p = rand_inputs(B, S, seed=B * 1000 + S)
+    check_against_oracle(ext, qp, qpe, c, p, 192 ** -0.5)
+
+
+def test_empty_sequence(ext):
+    qp, qpe, c, p = rand_inputs(2, 0)
+    o, m, s = ext.fused_cpu_attn_mla_compressed(qp.to(DEV), qpe.to(DEV), c.to(DEV), p.to(DEV), 0.07)
+    assert torch.all(o == 0) and torch.all(torch.isneginf(m)) and torch.all(s == 0)
+
+
+def test_normalised_bf16_path(ext):
+    qp, qpe, c, p = rand_inputs(4, 1500, seed=7)
+    out, lse = scope_b200.cpu_attn.mla_decode(qp.to(DEV), qpe.to(DEV), c.to(DEV), p.to(DEV), 192 ** -0.5)
+    assert out.dtype == torch.bfloat16
+    ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, c, p)), 192 ** -0.5)
+    assert np.abs(out.float().cpu().numpy() - ro / rs[:, None]).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < TOL_LSE
+
+
+def test_cfg3_size(ext):
+    """The DeepSeek-V2-Lite benchmark shape (B=8, 16 heads, S=16384): two rows
+    against the oracle, all rows against the split/merge property."""
+    qp, qpe, c, p = rand_inputs(8, 16384, seed=3)
+    sc = 192 ** -0.5
+    qp_d, qpe_d, c_d, p_d = qp.to(DEV), qpe.to(DEV), c.to(DEV), p.to(DEV)
+    o, m, s = ext.fused_cpu_attn_mla_compressed(qp_d, qpe_d, c_d, p_d, sc)
+    ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp[:16], qpe[:16], c[:1], p[:1])), sc)
+    on = (o / s[:, None]).cpu().numpy()
+    assert np.abs(on[:16] - ro / rs[:, None]).max() < TOL_OUT
+    assert np.abs((m + s.log()).cpu().numpy()[:16] - (rm + np.log(rs))).max() < TOL_LSE
+    halves = [ext.fused_cpu_attn_mla_compressed(qp_d, qpe_d, c_d[:, a:a + 8192].contiguous(),
+                                                p_d[:, a:a + 8192].contiguous(), sc) for a in (0, 8192)]
+    parts_o = torch.stack([ho / hs[:, None] for ho, hm, hs in halves])
+    parts_l = torch.stack([hm + hs.log() for ho, hm, hs in halves])
+    mo, ml = scope_b200.lse_merge(parts_o, parts_l, torch.float32)
+    assert (mo - o / s[:, None]).abs().max().item() < 1e-3
+    assert (ml - (m + s.log())).abs().max().item() < 1e-3
