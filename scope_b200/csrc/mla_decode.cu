@@ -6,17 +6,20 @@
 // for nH heads of one sequence sharing one latent KV.
 //
 // One persistent CTA per SM walks an even share of the flattened (batch,
-// 128-token tile) space.  Warp roles (320 threads):
-//   warp 8      producer: TMA loads of each tile -- the latent as four 32 KB
-//               "pairs" (two 64-dim SWIZZLE_128B boxes of 128 tokens) through
-//               a 5-slot ring, the 64-dim rope box through a 2-slot ring, and
-//               the batch's queries (576 x nH) when a new batch starts;
-//   warp 9      one thread issues the MMAs; the warp owns the TMEM allocation:
-//                 S^T[128 tok x nH]  = [C | P](tile) . [Q_proj | Q_pe]^T  (A K-major)
+// token tile) space.  Warp roles (352 threads):
+//   warp 8      producer: TMA loads of each tile (128 tokens; 64 with
+//               WS_MLA_TILE=64) -- the latent as four "pairs" (two 64-dim
+//               SWIZZLE_128B boxes) through a 5-slot ring (11 for 64-token
+//               tiles), the 64-dim rope box through a 2-slot ring, and the
+//               batch's queries (576 x nH) when a new batch starts;
+//   warps 9-10  one thread each issues the MMAs (warp 9 the first product of
+//               every tile, warp 10 the second); warp 9 owns the TMEM allocation:
+//                 S^T[tile x nH]     = [C | P](tile) . [Q_proj | Q_pe]^T  (A K-major)
 //                 O^T[512 x nH]      = C(tile)^T . P^T                   (A MN-major:
 //                 the same swizzled latent tile, read along the other axis)
 //               S and O are double-buffered in TMEM (10*nH of 256 columns);
-//   warps 0-3   softmax: thread = token (TMEM lane); per-head tile max by warp
+//   warps 0-3   softmax: lanes 0-15 of each warp = a token (the M=64 TMEM
+//               layout puts tile row 16w+r in lane 32w+r); per-head tile max by warp
 //               shuffles + shared memory, online rescale factors, P in bf16
 //               written K-major (swizzled) for the second MMA;
 //   warps 4-7   correction: thread = latent dim (TMEM lane) x 4 blocks; loads
@@ -39,17 +42,21 @@ namespace mla {
 constexpr int NH = 16;          // heads per sequence (MMA N)
 constexpr int CLR = 512;        // latent (kv_lora_rank)
 constexpr int QRD = 64;         // rope dims
-constexpr int TT = 128;         // tokens per tile (MMA M of the first product)
-constexpr int NP = 5;           // latent pair slots
-constexpr int NE = 2;           // rope slots
-constexpr int PAIR_BYTES = 2 * TT * 128;    // 32 KB
-constexpr int BOX_BYTES = TT * 128;         // 16 KB
+#ifndef WS_MLA_TILE
+#define WS_MLA_TILE 128
+#endif
+constexpr int TT = WS_MLA_TILE;  // tokens per tile (MMA M of the first product: 64 or 128)
+static_assert(TT == 64 || TT == 128, "MLA tile must be 64 or 128 tokens");
+constexpr int NP = TT == 64 ? 11 : 5;   // latent pair slots (4 per tile)
+constexpr int NE = TT == 64 ? 3 : 2;    // rope slots
+constexpr int BOX_BYTES = TT * 128;         // 8 KB: 64 dims x 64 tokens
+constexpr int PAIR_BYTES = 2 * BOX_BYTES;   // 16 KB: 128 latent dims x 64 tokens
 constexpr int QBOX_BYTES = NH * 128;        // 2 KB
-constexpr int PBUF_BYTES = 2 * NH * 128;    // P^T of one tile: 2 K-boxes of 64 tokens
+constexpr int PBUF_BYTES = (TT / 64) * NH * 128;   // P^T of one tile: one K-box per 64 tokens
 constexpr int TMEM_COLS = 256;
 constexpr int S_COL = 0;                    // S[j] at j*NH
 constexpr int O_COL = 2 * NH;               // O[j] at O_COL + j*4*NH
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int SLOT_FLOATS = NH * CLR + 2 * NH;
 
 constexpr int OFF_PAIRS = 0;
@@ -63,7 +70,7 @@ constexpr int B_PAIR_FULL = 0, B_PAIR_EMPTY = NP, B_PE_FULL = 2 * NP, B_PE_EMPTY
               B_S_EMPTY = B_S_FULL + 2, B_P_FULL = B_S_EMPTY + 2, B_P_EMPTY = B_P_FULL + 2,
               B_O_FULL = B_P_EMPTY + 2, B_O_EMPTY = B_O_FULL + 2, B_ALPHA = B_O_EMPTY + 2,
               B_ST_FULL = B_ALPHA + 4, B_ST_EMPTY = B_ST_FULL + 1, B_RED = B_ST_EMPTY + 1, B_LRED = B_RED + 2,
-              B_DONE = B_LRED + 1, NBARS = B_DONE + 1;
+              B_DONE = B_LRED + 1, B_DONE2 = B_DONE + 1, NBARS = B_DONE2 + 1;
 constexpr int MISC_BYTES = NBARS * 8 + (2 * 4 * NH + 4 * NH + 2 * NH + 4 * NH) * 4 + 64;
 constexpr size_t SMEM_BYTES = 1024 + OFF_MISC + MISC_BYTES;
 static_assert(SMEM_BYTES <= 227 * 1024, "MLA shared-memory plan exceeds 227 KB");
@@ -171,6 +178,7 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
         mbar_init(bar(s, B_RED + 1), 4);
         mbar_init(bar(s, B_LRED), 4);
         mbar_init(bar(s, B_DONE), 1);
+        mbar_init(bar(s, B_DONE2), 1);
         *s.abort_flag = 0;
         fence_mbar_init();
     }
@@ -245,34 +253,34 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
                 if (qn > 0) mbar_wait_bounded(bar(s, B_Q_FULL), (qn - 1) & 1, 200000000ull);
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == 9 || warp == 10) {
         // ------------------------------------------------------------- MMA issue
+        // Two issuing threads: warp 9 runs the first product of every tile,
+        // warp 10 the second, so freeing a tile's ring slots (after its second
+        // product) never waits behind the next tile's loads.
         if (lane == 0 && t_begin < t_end) {
             const uint32_t id1 = idesc_bf16_f32(TT, NH, false, false);
             const uint32_t id2 = idesc_bf16_f32(128, NH, true, false);
-            int seg = -1, qn = 0;
-            int64_t i = 0;
-            int b = (int)(t_begin / p.tpb);
-            int tl = (int)(t_begin - (int64_t)b * p.tpb);
-            for (int64_t t = t_begin; t < t_end; ++t, ++i) {
+            const int64_t n_tiles = t_end - t_begin;
+            int q_seg = -1, qn = 0;
+            bool ok = true;
+            auto gemm1 = [&](int64_t i) -> bool {
+                const int64_t t = t_begin + i;
+                const int b = (int)(t / p.tpb), tl = (int)(t - (int64_t)b * p.tpb);
                 const int j = (int)(i & 1);
                 const uint32_t us = (uint32_t)(i >> 1);
-                if (b != seg) {
-                    if (!wait_bar(s, bar(s, B_Q_FULL), qn & 1, p.status)) break;
+                if (b != q_seg) {
+                    if (!wait_bar(s, bar(s, B_Q_FULL), qn & 1, p.status)) return false;
                     ++qn;
-                    seg = b;
+                    q_seg = b;
                 }
-                if (us > 0 && !wait_bar(s, bar(s, B_S_EMPTY + j), (us - 1) & 1, p.status)) break;
+                if (us > 0 && !wait_bar(s, bar(s, B_S_EMPTY + j), (us - 1) & 1, p.status)) return false;
                 tc_fence_after();
                 // S^T = [C | P] . [Q_proj | Q_pe]^T  (K = 576 in 36 steps of 16)
-                bool ok = true;
                 for (int pr = 0; pr < 4; ++pr) {
                     const int64_t n = 4 * i + pr;
                     const int sl = (int)(n % NP);
-                    if (!wait_bar(s, bar(s, B_PAIR_FULL + sl), (uint32_t)(n / NP) & 1, p.status)) {
-                        ok = false;
-                        break;
-                    }
+                    if (!wait_bar(s, bar(s, B_PAIR_FULL + sl), (uint32_t)(n / NP) & 1, p.status)) return false;
                     tc_fence_after();
                     for (int half = 0; half < 2; ++half)
                         for (int kk = 0; kk < 4; ++kk)
@@ -281,41 +289,46 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
                                       sdesc_sw128(qs + (2 * pr + half) * QBOX_BYTES + kk * 32, 16, 1024), id1,
                                       (pr | half | kk) != 0);
                 }
-                if (!ok) break;
                 const int e = (int)(i % NE);
-                if (!wait_bar(s, bar(s, B_PE_FULL + e), (uint32_t)(i / NE) & 1, p.status)) break;
+                if (!wait_bar(s, bar(s, B_PE_FULL + e), (uint32_t)(i / NE) & 1, p.status)) return false;
                 tc_fence_after();
                 for (int kk = 0; kk < 4; ++kk)
                     umma_bf16(tbase + S_COL + j * NH, sdesc_sw128(pes + e * BOX_BYTES + kk * 32, 16, 1024),
                               sdesc_sw128(qs + 8 * QBOX_BYTES + kk * 32, 16, 1024), id1, 1);
                 umma_commit(bar(s, B_S_FULL + j));
                 umma_commit(bar(s, B_PE_EMPTY + e));
-                const bool seg_end = (t + 1 == t_end) || (tl + 1 == p.tpb);
-                if (seg_end) umma_commit(bar(s, B_Q_EMPTY));
-                // O^T = C^T . P^T  (M = 512 in 4 blocks, K = 128 tokens in 8 steps)
-                if (!wait_bar(s, bar(s, B_P_FULL + j), us & 1, p.status)) break;
-                if (us > 0 && !wait_bar(s, bar(s, B_O_EMPTY + j), (us - 1) & 1, p.status)) break;
+                if (t + 1 == t_end || tl + 1 == p.tpb) umma_commit(bar(s, B_Q_EMPTY));
+                return true;
+            };
+            auto gemm2 = [&](int64_t i) -> bool {
+                const int j = (int)(i & 1);
+                const uint32_t us = (uint32_t)(i >> 1);
+                // O^T = C^T . P^T  (M = 512 in 4 blocks of 128, K = 64 tokens in 4 steps)
+                if (!wait_bar(s, bar(s, B_P_FULL + j), us & 1, p.status)) return false;
+                if (us > 0 && !wait_bar(s, bar(s, B_O_EMPTY + j), (us - 1) & 1, p.status)) return false;
                 tc_fence_after();
                 for (int mb = 0; mb < 4; ++mb) {
-                    const int64_t n = 4 * i + mb;
-                    const int sl = (int)(n % NP);
-                    for (int ks = 0; ks < 8; ++ks)
+                    const int sl = (int)((4 * i + mb) % NP);
+                    for (int ks = 0; ks < TT / 16; ++ks)
                         umma_bf16(tbase + O_COL + j * 4 * NH + mb * NH,
                                   sdesc_sw128(pairs + sl * PAIR_BYTES + ks * 2048, BOX_BYTES, 1024),
-                                  sdesc_sw128(ps + j * PBUF_BYTES + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), id2,
-                                  ks > 0);
+                                  sdesc_sw128(ps + j * PBUF_BYTES + (ks >> 2) * (NH * 128) + (ks & 3) * 32, 16, 1024),
+                                  id2, ks > 0);
                     umma_commit(bar(s, B_PAIR_EMPTY + sl));
                 }
                 umma_commit(bar(s, B_O_FULL + j));
                 umma_commit(bar(s, B_P_EMPTY + j));
-                if (++tl == p.tpb) {
-                    tl = 0;
-                    ++b;
-                }
+                return true;
+            };
+            if (warp == 9) {
+                for (int64_t i = 0; ok && i < n_tiles; ++i) ok = gemm1(i);
+            } else {
+                for (int64_t i = 0; ok && i < n_tiles; ++i) ok = gemm2(i);
             }
             // every MMA this thread issued has finished before TMEM is freed
-            umma_commit(bar(s, B_DONE));
-            mbar_wait_bounded(bar(s, B_DONE), 0, 1000000000ull);
+            const uint32_t done = bar(s, warp == 9 ? B_DONE : B_DONE2);
+            umma_commit(done);
+            mbar_wait_bounded(done, 0, 1000000000ull);
         }
     } else if (warp < 4) {
         // ------------------------------------------------------------- softmax
@@ -341,8 +354,10 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(s, B_S_EMPTY + j));
-            const int k = warp * 32 + lane;   // token within the tile
-            const bool valid = tl * TT + k < p.S;
+            // M=128: tile row r sits in TMEM lane r.  M=64: tile row 16*warp + r
+            // sits in lane 32*warp + r (lanes 16-31 of each warp are unused).
+            const int k = TT == 128 ? warp * 32 + lane : warp * 16 + (lane & 15);   // token within the tile
+            const bool valid = (TT == 128 || lane < 16) && tl * TT + k < p.S;
             float mx[NH];
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
@@ -371,13 +386,15 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
                 m_run[h] = mn;
             }
             if (us > 0 && !wait_bar(s, bar(s, B_P_EMPTY + j), (us - 1) & 1, p.status)) break;
-            // P^T for the second MMA: K-major (rows = heads, 64 tokens per 128-B row)
-            uint8_t* pb = s.base + OFF_P + j * PBUF_BYTES + (k >> 6) * 2048;
-            const int kc = (k & 63) >> 3, ke = (k & 7) * 2;
+            // P^T for the second MMA: K-major (rows = heads, the tile's 64 tokens per 128-B row)
+            if (TT == 128 || lane < 16) {
+                uint8_t* pb = s.base + OFF_P + j * PBUF_BYTES + (k >> 6) * (NH * 128);
+                const int kc = (k & 63) >> 3, ke = (k & 7) * 2;
 #pragma unroll
-            for (int h = 0; h < NH; ++h)
-                *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((kc ^ (h & 7)) << 4) + ke) =
-                    __float2bfloat16_rn(pv[h]);
+                for (int h = 0; h < NH; ++h)
+                    *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((kc ^ (h & 7)) << 4) + ke) =
+                        __float2bfloat16_rn(pv[h]);
+            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(s, B_P_FULL + j));
@@ -497,63 +514,81 @@ struct MergeParams {
     float* out_lse;
 };
 
-// One warp per (batch, head) output row: log-sum-exp merge of the batch's pieces.
+// Log-sum-exp merge of a batch's pieces.  One warp per (batch, head, quarter
+// of the 512 latent dims); lane k first fetches piece k's (m, l), the warp
+// reduces them, then every lane accumulates one float4 of the quarter over
+// all pieces with eight loads in flight.
 __global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
     pdl_wait_primary();
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= p.B * NH) return;
+    if (wid >= p.B * NH * 4) return;
+    const int row = wid >> 2, quarter = wid & 3;
     const int b = row / NH, h = row - b * NH;
-    int c0 = 0, c1 = -1;
+    int c0 = 0, npc = 0;
     if (p.tpb > 0) {
         const int64_t total = (int64_t)p.B * p.tpb;
         const int64_t t0 = (int64_t)b * p.tpb;
         c0 = (int)split_owner(t0, total, p.nctas);
-        c1 = (int)split_owner(t0 + p.tpb - 1, total, p.nctas);
+        npc = (int)split_owner(t0 + p.tpb - 1, total, p.nctas) - c0 + 1;
     }
+    const float* base = p.ws_part + (int64_t)(c0 + b) * SLOT_FLOATS;
+    // pass 1: global max and sum over the pieces (32 pieces per round)
     float M = -INFINITY;
-    for (int c = c0; c <= c1; ++c) M = fmaxf(M, __ldg(p.ws_part + (int64_t)(c + b) * SLOT_FLOATS + NH * CLR + h));
+    for (int k0 = 0; k0 < npc; k0 += 32) {
+        const int k = k0 + lane;
+        const float m = k < npc ? __ldg(base + (int64_t)k * SLOT_FLOATS + NH * CLR + h) : -INFINITY;
+        M = fmaxf(M, m);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float Mu = (M == -INFINITY) ? 0.f : M;
     float L = 0.f;
-    float4 acc[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c = c0; c <= c1; ++c) {
-        const float* pp = p.ws_part + (int64_t)(c + b) * SLOT_FLOATS;
-        const float w = ex2(__ldg(pp + NH * CLR + h) - Mu);
-        L += w * __ldg(pp + NH * CLR + NH + h);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(pp + h * CLR + k * 128 + lane * 4));
-            acc[k].x += w * v.x; acc[k].y += w * v.y; acc[k].z += w * v.z; acc[k].w += w * v.w;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int off = h * CLR + quarter * 128 + lane * 4;
+    for (int k0 = 0; k0 < npc; k0 += 32) {
+        const int kl = k0 + lane;
+        float wl = 0.f;
+        if (kl < npc) {
+            const float* pp = base + (int64_t)kl * SLOT_FLOATS;
+            wl = ex2(__ldg(pp + NH * CLR + h) - Mu);
+            L += wl * __ldg(pp + NH * CLR + NH + h);
         }
-    }
-    const bool empty = !(L > 0.f);
-    const float mnat = empty ? -INFINITY : M * kLn2;
-    if (p.out_mode == WS_OUT_UNNORM_F32) {
-        float* o = static_cast<float*>(p.out) + (int64_t)row * CLR;
+        const int n = min(32, npc - k0);
+        for (int u0 = 0; u0 < n; u0 += 8) {
+            float4 v[8];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) *reinterpret_cast<float4*>(o + k * 128 + lane * 4) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[k];
-    } else {
-        const float inv = empty ? 0.f : 1.f / L;
-        if (p.out_mode == WS_OUT_NORM_F32) {
-            float* o = static_cast<float*>(p.out) + (int64_t)row * CLR;
+            for (int u = 0; u < 8; ++u)
+                v[u] = (u0 + u < n) ? __ldg(reinterpret_cast<const float4*>(base + (int64_t)(k0 + u0 + u) * SLOT_FLOATS + off))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                *reinterpret_cast<float4*>(o + k * 128 + lane * 4) =
-                    make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
-        } else {
-            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * CLR;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                __nv_bfloat162 lo = __floats2bfloat162_rn(acc[k].x * inv, acc[k].y * inv);
-                __nv_bfloat162 hi = __floats2bfloat162_rn(acc[k].z * inv, acc[k].w * inv);
-                *reinterpret_cast<__nv_bfloat162*>(o + k * 128 + lane * 4) = lo;
-                *reinterpret_cast<__nv_bfloat162*>(o + k * 128 + lane * 4 + 2) = hi;
+            for (int u = 0; u < 8; ++u) {
+                const float w = __shfl_sync(0xffffffffu, wl, (u0 + u) & 31);
+                if (u0 + u < n) {
+                    acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
+                }
             }
         }
     }
-    if (lane == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    const bool empty = !(L > 0.f);
+    const float mnat = empty ? -INFINITY : M * kLn2;
+    const int64_t oi = (int64_t)row * CLR + quarter * 128 + lane * 4;
+    if (p.out_mode == WS_OUT_UNNORM_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc;
+    } else {
+        const float inv = empty ? 0.f : 1.f / L;
+        if (p.out_mode == WS_OUT_NORM_F32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        } else {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
+            *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+            *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+        }
+    }
+    if (lane == 0 && quarter == 0) {
         if (p.out_max) p.out_max[row] = mnat;
         if (p.out_sum) p.out_sum[row] = empty ? 0.f : L;
         if (p.out_lse) p.out_lse[row] = empty ? -INFINITY : mnat + logf(L);
@@ -629,7 +664,7 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
     mp.out_sum = out_sum;
     mp.out_lse = out_lse;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((B * NH + 7) / 8));
+    cfg.gridDim = dim3((unsigned)((B * NH * 4 + 7) / 8));
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
