@@ -19,6 +19,8 @@ Workloads (the default is the one the metric's
   cfg2  GQA Mixtral layer, B=16, ragged L in [1024, 32768], two shares merged by LSE
   cfg3  absorbed MLA, DeepSeek-V2-Lite: B=8, 16 heads, latent 512 + rope 64, S=16384
   cfg4  GQA Qwen3, B=32, L=131072 sequence-sharded over N GPUs (default)
+  cfg5  CSA sparse decode, DeepSeek-V4 style: bs=16, 64 heads, 65536 int8
+        entries, top-2048 gather, entry-sharded over N GPUs
 """
 from __future__ import annotations
 
@@ -436,6 +438,131 @@ class Mla(Workload):
         return cpu_ref_mla(self.B, self.nH, self.S, budget_s, max_calls, warm)
 
 
+class Csa(Workload):
+    """cfg5: CSA sparse decode (DeepSeek-V4 style), bs=16, 64 heads over a
+    512-wide latent, nc=65536 int8 entries with one fp32 scale each, top-2048
+    sorted unique ids per sequence, bf16 q, scale 1/sqrt(512); out bf16
+    normalised + fp32 LSE (ws_csa_decode).  With N GPUs rank r holds entries
+    [r*nc/N, (r+1)*nc/N) of every sequence, attends to the ids that fall in
+    its shard (rebased locally), and the fp32 partials are exchanged with NCCL
+    all_gather and merged with ws_lse_merge.
+
+    The entries one step touches (16.8 MB, or 1/N of it per rank) fit in L2,
+    so L2 is flushed (a 256 MB write) before every timed step and each step is
+    timed with its own CUDA-event pair."""
+
+    name = "cfg5"
+    kernel_name = "csa_decode_kernel<64,false> (tcgen05, cluster/DSMEM merge)"
+    profile_name = "csa_decode_cfg5"
+    flush_l2 = True
+
+    def __init__(self, world, rank, bs=16, nH=64, nc=65536, k=2048, seed=5):
+        from scope_b200 import _lib
+        self.world, self.rank = world, rank
+        self.bs, self.nH, self.nc, self.k = bs, nH, nc, k
+        self.scale = 512 ** -0.5
+        self.workload = f"csa_ds4_b{bs}_h{nH}_nc{nc}_top{k}_int8"
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.lo, self.hi = nc * rank // world, nc * (rank + 1) // world
+        ncl = self.hi - self.lo
+        g = torch.Generator(device=dev).manual_seed(seed + 17 * rank)
+        self.kv = torch.empty(bs, ncl, 512, dtype=torch.int8, device=dev)
+        for b in range(bs):   # round(N(0,1) * 32) clipped to +-127, per sequence to bound the temporary
+            self.kv[b] = (torch.randn(ncl, 512, generator=g, device=dev) * 32).round_().clamp_(-127, 127)
+        self.kv_scales = torch.rand(bs, ncl, generator=g, device=dev) * 0.04 + 0.01
+        gi = torch.Generator().manual_seed(seed)
+        self.idx = torch.stack([torch.randperm(nc, generator=gi)[:k].sort().values for _ in range(bs)]).int().to(dev)
+        self.n_local = int(((self.idx >= self.lo) & (self.idx < self.hi)).sum())
+        gq = torch.Generator(device=dev).manual_seed(seed + 1)
+        self.q = torch.randn(bs, nH, 512, generator=gq, device=dev).bfloat16()
+        self.lib, self._lib = _lib.lib(), _lib
+        if world == 1:
+            self.out = torch.empty(bs, nH, 512, dtype=torch.bfloat16, device=dev)
+            self.lse = torch.empty(bs, nH, dtype=torch.float32, device=dev)
+        else:
+            self.part_o = torch.empty(bs * nH, 512, dtype=torch.float32, device=dev)
+            self.part_l = torch.empty(bs * nH, dtype=torch.float32, device=dev)
+            self.all_o = torch.empty(world, bs * nH, 512, dtype=torch.float32, device=dev)
+            self.all_l = torch.empty(world, bs * nH, dtype=torch.float32, device=dev)
+            self.out = torch.empty(bs * nH, 512, dtype=torch.bfloat16, device=dev)
+            self.lse = torch.empty(bs * nH, dtype=torch.float32, device=dev)
+        self.flush_buf = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+        self.q_host = torch.randn(bs, nH, 512).bfloat16().pin_memory()
+        self.idx_host = self.idx.cpu().pin_memory()
+        self.out_host = torch.empty(bs * nH * 512, dtype=torch.bfloat16).pin_memory()
+        self.lse_host = torch.empty(bs * nH, dtype=torch.float32).pin_memory()
+        self.kernels_per_step = 1 if world == 1 else 2
+
+    def flush(self, i):
+        self.flush_buf.fill_(i & 0xff)
+
+    def kernel_bytes(self):
+        out_b = 2 * 512 if self.world == 1 else 4 * 512
+        return (self.n_local * (512 + 4 + 4) + self.bs * self.nH * (512 * 2 + out_b + 4))
+
+    def step_bytes(self):
+        return self.bs * self.k * (512 + 4 + 4) + self.bs * self.nH * (512 * 2 + 512 * 2 + 4)
+
+    def kernel(self, i):
+        L_ = self.lib
+        st = torch.cuda.current_stream().cuda_stream
+        if self.world == 1:
+            out, lse, odt, mode, lo = self.out, self.lse, self._lib.WS_DTYPE_BF16, self._lib.WS_CSA_IDX_ALL, 0
+        else:
+            out, lse, odt, mode, lo = (self.part_o, self.part_l, self._lib.WS_DTYPE_F32,
+                                       self._lib.WS_CSA_IDX_SORTED_SHARD, self.lo)
+        rc = L_.ws_csa_decode(self.q.data_ptr(), self._lib.WS_DTYPE_BF16, self.bs, self.nH, 512, self.kv.data_ptr(),
+                              self._lib.WS_DTYPE_I8, self.kv_scales.data_ptr(), self.kv.shape[1], lo,
+                              self.idx.data_ptr(), self.k, mode, 0, 0, self.scale, out.data_ptr(), odt,
+                              lse.data_ptr(), st)
+        if rc != 0:
+            raise RuntimeError(L_.ws_last_error().decode())
+
+    def step(self, i):
+        self.kernel(i)
+        if self.world > 1:
+            import torch.distributed as dist
+            from scope_b200 import lse_merge
+            dist.all_gather_into_tensor(self.all_o.view(-1), self.part_o.view(-1))
+            dist.all_gather_into_tensor(self.all_l.view(-1), self.part_l.view(-1))
+            lse_merge(self.all_o, self.all_l, torch.bfloat16, out=self.out, out_lse=self.lse)
+
+    def e2e_step(self, i):
+        """Through the public API: q and the step's top-k ids come from host
+        memory, out and lse go back to it."""
+        from scope_b200 import csa_attn, lse_merge
+        self.q.copy_(self.q_host, non_blocking=True)
+        self.idx.copy_(self.idx_host, non_blocking=True)
+        if self.world == 1:
+            out, lse = csa_attn.csa_sparse_decode(self.q, self.kv, self.idx, self.scale, self.kv_scales)
+        else:
+            import torch.distributed as dist
+            po, pl = csa_attn.csa_sparse_decode(self.q, self.kv, self.idx, self.scale, self.kv_scales,
+                                                shard_lo=self.lo, idx_mode="sorted_shard", out_dtype=torch.float32)
+            dist.all_gather_into_tensor(self.all_o.view(-1), po.view(-1))
+            dist.all_gather_into_tensor(self.all_l.view(-1), pl.view(-1))
+            out, lse = lse_merge(self.all_o, self.all_l, torch.bfloat16)
+        if self.rank == 0:
+            self.out_host.copy_(out.view(-1), non_blocking=True)
+            self.lse_host.copy_(lse.view(-1), non_blocking=True)
+
+    def e2e_bytes(self):
+        return (self.world * (self.q_host.numel() * 2 + self.idx_host.numel() * 4),
+                self.out_host.numel() * 2 + self.lse_host.numel() * 4)
+
+    def config(self):
+        return {"workload": self.workload, "batch": self.bs, "heads": self.nH, "kv_lora_rank": 512,
+                "n_compressed": self.nc, "topk": self.k, "kv_dtype": "int8 + fp32 scale per entry",
+                "entries_per_gpu": self.hi - self.lo, "selected_entries_this_rank": self.n_local,
+                "parallelism": f"entry-shard{self.world}",
+                "l2": "256 MB L2 flush before every step; per-step CUDA-event timing",
+                "timing": "stream launches, per-step events",
+                "exchange": "nccl all_gather of (o fp32, lse) + lse_merge kernel" if self.world > 1 else "none"}
+
+    def cpu_reference(self, budget_s, max_calls, warm=1):
+        return cpu_ref_csa(self.bs, self.nH, self.nc, self.k, budget_s, max_calls, warm)
+
+
 # ------------------------------------------------- reference CPU measurements
 def cfg2_geometry(B=16, seed=2):
     """Seeded ragged lengths ~ U[1024, 32768] and share ratios in {.25, .5, .75}."""
@@ -529,6 +656,36 @@ def cpu_ref_mla(B, nH, S, budget_s, max_calls, warm=1):
                                   f"{nbytes / 1e6:.1f} MB per call)"}
 
 
+def cpu_ref_csa(bs, nH, nc, k, budget_s, max_calls, warm=1):
+    """cfg5 on the host: the reference's indexer_attn_cpu (csa_attn.cpp:1819-1883)
+    on all cores over a bf16 copy of the dequantised entries (int8 * scale,
+    made outside the timing), fp32 q, the same sorted top-k ids.  Full cfg5
+    step; bytes are the workload's algorithmic bytes."""
+    import oracle
+    torch.manual_seed(15)
+    kv = torch.empty(bs, nc, 512, dtype=torch.bfloat16)
+    sc = torch.rand(bs, nc) * 0.04 + 0.01
+    for b in range(bs):
+        kv[b] = ((torch.randn(nc, 512) * 32).round_().clamp_(-127, 127) * sc[b, :, None]).bfloat16()
+    g = torch.Generator().manual_seed(5)
+    idx = torch.stack([torch.randperm(nc, generator=g)[:k].sort().values for _ in range(bs)]).int()
+    q = torch.randn(bs, nH, 512).bfloat16().float()
+    o = torch.empty(bs, nH, 512)
+    lse = torch.empty(bs, nH)
+    nbytes = bs * k * (512 + 4 + 4) + bs * nH * (512 * 2 + 512 * 2 + 4)
+    ref = load_cpu_ref("csa_attn_kernel")
+    n = os.cpu_count() or 1
+    if ref is not None:
+        kind, fn = "reference", (lambda: ref.indexer_attn_cpu(q, kv, idx, 512 ** -0.5, o, lse, n))
+    else:
+        qn, kvn, idn = q.numpy(), oracle.bf16_bits(kv), idx.numpy()
+        kind, fn = "port", (lambda: oracle.csa_attend(qn, kvn, 512 ** -0.5, idx=idn))
+    t, calls = median_time(fn, budget_s, max_calls, warm)
+    return nbytes / t, {"kind": kind, "cores": n, "calls": calls, "sec_per_call": t,
+                        "sample": f"indexer_attn_cpu, bs={bs}, nH={nH}, nc={nc}, k={k} on bf16 dequantised "
+                                  f"entries (full cfg5 step, {nbytes / 1e6:.1f} MB algorithmic)"}
+
+
 def cpu_reference_for(name, args, budget_s, max_calls, warm):
     if name == "cfg4":
         return cpu_ref_dense(32, 4, 8, 128, args.kv_len or 131072, budget_s, max_calls, warm), \
@@ -540,6 +697,8 @@ def cpu_reference_for(name, args, budget_s, max_calls, warm):
             "gqa_mixtral_b16_ragged_1024_32768_two_shares"
     if name == "cfg3":
         return cpu_ref_mla(8, 16, 16384, budget_s, max_calls, warm), "mla_absorbed_ds2lite_b8_h16_s16384"
+    if name == "cfg5":
+        return cpu_ref_csa(16, 64, 65536, 2048, budget_s, max_calls, warm), "csa_ds4_b16_h64_nc65536_top2048_int8"
     raise ValueError(name)
 
 
@@ -552,10 +711,12 @@ def make_workload(name, world, rank, args):
         return GqaShares(world, rank)
     if name == "cfg3":
         return Mla(world, rank, S=args.kv_len or 16384)
+    if name == "cfg5":
+        return Csa(world, rank, nc=args.kv_len or 65536)
     raise ValueError(name)
 
 
-WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4")
+WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5")
 
 
 # -------------------------------------------------------------------- main
@@ -590,7 +751,28 @@ def make_runner(wl, fn):
     return run, per
 
 
+def time_steps_flushed(wl, fn, steps, warmup, world):
+    """One CUDA-event pair per step, with an L2 flush (untimed) before each."""
+    for i in range(warmup):
+        wl.flush(i)
+        fn(i)
+    barrier(world)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i, (a, b) in enumerate(evs):
+        wl.flush(i)
+        a.record()
+        fn(i)
+        b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    total = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    return max_over_ranks(total / steps, world), steps
+
+
 def time_steps(wl, fn, steps, warmup, world):
+    if getattr(wl, "flush_l2", False):
+        return time_steps_flushed(wl, fn, steps, warmup, world)
     run, per = make_runner(wl, fn)
     run(max(warmup, per))
     barrier(world)
@@ -608,6 +790,8 @@ def time_steps(wl, fn, steps, warmup, world):
 
 def time_e2e(wl, steps, warmup, world):
     """Public-API steps with host buffers; no graph (a user calls the API)."""
+    if getattr(wl, "flush_l2", False):
+        return time_steps_flushed(wl, wl.e2e_step, steps, warmup, world)[0]
     for i in range(warmup):
         wl.e2e_step(i)
     barrier(world)

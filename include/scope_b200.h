@@ -147,6 +147,50 @@ int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const 
                   void* workspace, size_t workspace_bytes, void* stream);
 size_t ws_mla_decode_workspace_size(int B, int nH, int S);
 
+/* ---- CSA index modes (ws_csa_decode with an id list) */
+#define WS_CSA_IDX_ALL 0            /* every id must lie in this buffer's range; others are skipped and
+                                       reported as WS_ERR_DEVICE by ws_status_take */
+#define WS_CSA_IDX_SORTED_SHARD 1   /* ids ascending per sequence; only those in this buffer's range count */
+#define WS_CSA_IDX_SHARD 2          /* ids in any order; those outside this buffer's range are skipped */
+
+/*
+ * CSA decode: nq query rows per sequence over a shared 512-wide latent KV
+ * (K = V), gathered by a top-k id list or over a dense id range.
+ * Replaces indexer_attn_cpu (kernel/cpu_attn_ds4_ext/csa_attn.cpp:1819-1883),
+ * fused_csa_attn (:200-281) and fused_csa_attn_range (:1587-1656); int8 KV
+ * with one fp32 scale per entry is the storage of the int8 family
+ * (value = int8 * scale, csa_attn.cpp:1338-1344), attended without quantising q.
+ *   q        [bs, nq, 512], q_dtype WS_DTYPE_F32 or WS_DTYPE_BF16, contiguous
+ *   kv       [bs, nc, 512], kv_dtype WS_DTYPE_BF16 or WS_DTYPE_I8, contiguous;
+ *            row j of sequence b holds entry id shard_lo + j (shard_lo = 0
+ *            for an unsharded cache)
+ *   kv_scales [bs, nc] fp32 (WS_DTYPE_I8 only)
+ *   idx      [bs, k] int32 entry ids (duplicates attend twice, as the
+ *            reference does), idx_mode one of WS_CSA_IDX_*; or idx = NULL:
+ *            attend ids [kv_begin, kv_end) (clipped to this buffer's range)
+ *   score = scale * q . value;  out [bs, nq, 512] normalised in out_dtype
+ *   (WS_DTYPE_F32 or WS_DTYPE_BF16), out_lse [bs, nq] fp32 (may be NULL).
+ * A row with no entry gives out = 0, lse = -inf (the partial of an empty
+ * shard).  One launch, no workspace.
+ */
+int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void* kv, int kv_dtype,
+                  const float* kv_scales, int64_t nc, int64_t shard_lo, const int32_t* idx, int k, int idx_mode,
+                  int64_t kv_begin, int64_t kv_end, float scale, void* out, int out_dtype, float* out_lse,
+                  void* stream);
+
+/*
+ * Per-row quantisers of the CSA int8 family, bit-exact with the reference:
+ * ws_csa_kv_quantize_s8 replaces kv_quantize_bf16_to_int8
+ * (kernel/cpu_attn_ds4_ext/csa_attn.cpp:1203-1233) and ws_csa_q_quantize_u8
+ * replaces q_quantize_fp32_to_u8 (:1175-1201).
+ *   kv [rows, hd] bf16 -> out int8 [rows, hd], scales fp32 [rows], sums int32 [rows]
+ *   q  [rows, hd] fp32 -> out uint8 [rows, hd] (value + 128), scales fp32 [rows]
+ * hd % 8 == 0; all pointers 16-byte aligned.
+ */
+int ws_csa_kv_quantize_s8(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
+                          void* stream);
+int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float* scales, void* stream);
+
 /*
  * Log-sum-exp merge of P partial attention results (the cross-GPU combine of
  * a sequence-sharded KV cache, and the runtime merges it replaces:

@@ -19,7 +19,8 @@ from . import cpu_attn as _cpu_attn
 from ._lib import LIB_PATH, ScopeError, lib
 from .ops import Share, gqa_decode_shares, lse_merge
 
-__all__ = ["build", "build_tile", "build_csa_attn", "lib", "ScopeError", "Share", "gqa_decode_shares", "lse_merge"]
+__all__ = ["build", "build_tile", "build_csa_attn", "lib", "ScopeError", "Share", "gqa_decode_shares", "lse_merge",
+           "status_take"]
 
 
 def _ensure_library(verbose: bool = False) -> None:
@@ -50,3 +51,14 @@ def build_csa_attn():
     lib()
     from . import csa_attn as _csa_attn
     return _csa_attn
+
+
+def status_take(device=None) -> int:
+    """Read and clear the device status word of ``device`` (synchronises its
+    current stream): 0 when no kernel reported a problem since the last call,
+    else WS_ERR_DEVICE (5): a bounded wait gave up, or a CSA id outside the
+    KV buffer was skipped."""
+    import torch
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        return int(lib().ws_status_take(torch.cuda.current_stream(dev).cuda_stream))

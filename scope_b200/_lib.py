@@ -30,6 +30,10 @@ WS_OUT_NORM_BF16 = 0
 WS_OUT_UNNORM_F32 = 1
 WS_OUT_NORM_F32 = 2
 
+WS_CSA_IDX_ALL = 0
+WS_CSA_IDX_SORTED_SHARD = 1
+WS_CSA_IDX_SHARD = 2
+
 _V = ctypes.c_void_p
 _i = ctypes.c_int
 _i64 = ctypes.c_int64
@@ -60,6 +64,10 @@ SIGNATURES = {
     "ws_gqa_decode_noalloc_max_scratch": (_sz, []),
     "ws_mla_decode": (_i, [_V, _V, _V, _V, _i, _i, _i, _f, _i, _V, _V, _V, _V, _V, _sz, _V]),
     "ws_mla_decode_workspace_size": (_sz, [_i, _i, _i]),
+    "ws_csa_kv_quantize_s8": (_i, [_V, _i64, _i, _V, _V, _V, _V]),
+    "ws_csa_q_quantize_u8": (_i, [_V, _i64, _i, _V, _V, _V]),
+    "ws_csa_decode": (_i, [_V, _i, _i, _i, _i, _V, _i, _V, _i64, _i64, _V, _i, _i, _i64, _i64, _f, _V, _i, _V,
+                           _V]),
 }
 
 _lib = None

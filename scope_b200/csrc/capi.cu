@@ -240,6 +240,67 @@ int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const 
                       workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void* kv, int kv_dtype,
+                  const float* kv_scales, int64_t nc, int64_t shard_lo, const int32_t* idx, int k, int idx_mode,
+                  int64_t kv_begin, int64_t kv_end, float scale, void* out, int out_dtype, float* out_lse,
+                  void* stream) {
+    if (bs < 0 || nq < 1 || nc < 0 || shard_lo < 0) return set_error(WS_ERR_INVALID_ARG, "csa_decode: bad shape");
+    if (hd != 512) return set_error(WS_ERR_UNSUPPORTED, "csa_decode: this build supports a 512-wide latent");
+    if (q_dtype != WS_DTYPE_F32 && q_dtype != WS_DTYPE_BF16) return set_error(WS_ERR_INVALID_ARG, "csa_decode: q dtype");
+    if (kv_dtype != WS_DTYPE_BF16 && kv_dtype != WS_DTYPE_I8) return set_error(WS_ERR_INVALID_ARG, "csa_decode: kv dtype");
+    if (out_dtype != WS_DTYPE_F32 && out_dtype != WS_DTYPE_BF16) return set_error(WS_ERR_INVALID_ARG, "csa_decode: out dtype");
+    if (idx && (k < 0 || idx_mode < WS_CSA_IDX_ALL || idx_mode > WS_CSA_IDX_SHARD))
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode: bad k or idx_mode");
+    if (!idx && kv_end < kv_begin) return set_error(WS_ERR_INVALID_ARG, "csa_decode: kv_end < kv_begin");
+    if (nc > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "csa_decode: nc > 2^31 - 1");
+    if (bs == 0) return WS_OK;
+    if (!q || !out || (nc > 0 && !kv) || (kv_dtype == WS_DTYPE_I8 && nc > 0 && !kv_scales))
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode: null pointer");
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv) | reinterpret_cast<uintptr_t>(out)) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode: q, kv and out must be 16-byte aligned");
+    CsaLaunch a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.q_f32 = q_dtype == WS_DTYPE_F32;
+    a.bs = bs;
+    a.nq = nq;
+    a.kv = kv;
+    a.kv_i8 = kv_dtype == WS_DTYPE_I8;
+    a.kv_scales = kv_scales;
+    a.nc_local = nc;
+    a.shard_lo = shard_lo;
+    a.idx = idx;
+    a.k = idx ? k : 0;
+    a.window = idx_mode;
+    a.dense_begin = kv_begin;
+    a.dense_end = kv_end;
+    a.scale = scale;
+    a.out = out;
+    a.out_f32 = out_dtype == WS_DTYPE_F32;
+    a.out_lse = out_lse;
+    a.stream = stream;
+    return csa_launch(a);
+}
+
+int ws_csa_kv_quantize_s8(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
+                          void* stream) {
+    if (rows < 0 || hd < 8 || hd % 8) return set_error(WS_ERR_INVALID_ARG, "csa_kv_quantize: bad shape");
+    if (rows == 0) return WS_OK;
+    if (!kv || !out || !scales || !sums) return set_error(WS_ERR_INVALID_ARG, "csa_kv_quantize: null pointer");
+    if ((reinterpret_cast<uintptr_t>(kv) | reinterpret_cast<uintptr_t>(out)) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "csa_kv_quantize: kv and out must be 16-byte aligned");
+    return csa_kv_quantize_launch(kv, rows, hd, out, scales, sums, static_cast<cudaStream_t>(stream));
+}
+
+int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float* scales, void* stream) {
+    if (rows < 0 || hd < 8 || hd % 8) return set_error(WS_ERR_INVALID_ARG, "csa_q_quantize: bad shape");
+    if (rows == 0) return WS_OK;
+    if (!q || !out || !scales) return set_error(WS_ERR_INVALID_ARG, "csa_q_quantize: null pointer");
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "csa_q_quantize: q and out must be 16-byte aligned");
+    return csa_q_quantize_launch(q, rows, hd, out, scales, static_cast<cudaStream_t>(stream));
+}
+
 int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out, int out_dtype,
                  float* out_lse, void* stream) {
     if (P < 1 || R < 0 || D < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");

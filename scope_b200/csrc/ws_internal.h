@@ -72,6 +72,30 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
                float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
                size_t workspace_bytes, cudaStream_t st);
 
+struct CsaLaunch {
+    const void* q;
+    int q_f32;
+    int bs, nq;
+    const void* kv;
+    int kv_i8;
+    const float* kv_scales;
+    int64_t nc_local, shard_lo;   // the buffer holds entries [shard_lo, shard_lo + nc_local)
+    const int* idx;               // [bs, k] or null for the dense range
+    int k, window;
+    int64_t dense_begin, dense_end;
+    float scale;
+    void* out;
+    int out_f32;
+    float* out_lse;
+    void* stream;
+};
+
+int csa_launch(const CsaLaunch& a);
+int csa_cluster_size(int64_t entries_per_seq);
+int csa_kv_quantize_launch(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
+                           cudaStream_t st);
+int csa_q_quantize_launch(const float* q, int64_t rows, int hd, void* out, float* scales, cudaStream_t st);
+
 int lse_merge_launch(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out,
                      int out_dtype, float* out_lse, cudaStream_t st);
 
