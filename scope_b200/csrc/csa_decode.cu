@@ -1,5 +1,5 @@
-// CSA sparse decode (DeepSeek-V4 style): many query rows of one sequence
-// attend over a shared 512-dim latent KV (K = V), either over the entries a
+// CSA sparse decode (DeepSeek-V4 style): the query rows of one sequence
+// attend over a shared 512-wide latent KV (K = V), either over the entries a
 // top-k id list selects (gather) or over a contiguous id range (dense), with
 // the KV stored bf16 or int8 with one fp32 scale per entry.
 //
@@ -8,19 +8,29 @@
 // int8-entry storage of the int8 family (values = int8 * scale, :1338-1344)
 // without quantising the query.
 //
-// One thread-block cluster per (sequence, group of <= 64 query rows).  Its CS
-// CTAs split the sequence's selected entries evenly; each CTA
-//   * gathers its entries 128 at a time straight from global memory into a
-//     128-byte-swizzled bf16 tile (int8 -> bf16 is exact for |v| <= 127; the
-//     per-entry scale is folded into the scores and into P instead),
-//   * S^T[128 x NQ] = K . Q^T and O^T[512 x NQ] += K^T . P^T on tcgen05 with
-//     the accumulators in TMEM (the same smem tile read K-major, then MN-major),
-//   * keeps a lazily updated running max per query row: O in TMEM is rescaled
-//     only when a row's max grows by more than 2^8, which keeps P <= 256 and the
-//     result exact because m, l and O always refer to the same max;
-// then the cluster merges its CS partials through distributed shared memory:
+// One thread-block cluster per (sequence, group of query rows); its CS CTAs
+// split the sequence's selected entries evenly.  Inside a CTA, warp roles:
+//   * gather warps (3): resolve entry ids to rows of this buffer (512 at a
+//     time), load each 64-entry tile's rows straight from global memory into
+//     registers (two tiles in flight for int8) and write them as a
+//     128-byte-swizzled bf16 tile into a 2-slot ring (int8 -> bf16 is exact;
+//     the per-entry scale is folded into the scores and into P instead);
+//   * MMA warp (1): S[heads x 64] = Q . K^T (M=64, heads on TMEM lanes, two S
+//     buffers) and O^T[512 x heads] += K^T . P^T (M=128), tcgen05 with the
+//     accumulators in TMEM;
+//   * softmax warps (4): one thread per head owns that head's running max and
+//     sum and reads its 64 scores from its own TMEM lane, so the per-tile max
+//     and sum need no cross-thread reduction; the max is updated lazily (O is
+//     rescaled in TMEM only when a head's max grows by more than 2^8, which
+//     keeps P <= 256 and is exact because m, l and O always share one max).
+// Then the cluster merges its CS partials through distributed shared memory:
 // CTA r reduces query rows [r*NQ/CS, (r+1)*NQ/CS) by log-sum-exp over the
 // peers' (m, l, O) and writes the output.  No workspace, one launch.
+//
+// Every wait is bounded: a wait that gives up records kDevTimeout in the
+// status word and sets a CTA-wide abort flag, after which the remaining waits
+// return at once and no more products are issued, so every role still reaches
+// the final barriers.
 #include <cstdio>
 
 #include "common.cuh"
@@ -29,31 +39,68 @@
 namespace ws {
 namespace csa {
 
-constexpr int HD = 512;          // latent width
-constexpr int TT = 128;          // entries per tile (MMA M of the first product)
-constexpr int kThreads = 256;
-constexpr int KBOX = TT * 128;   // 16 KB: 64 dims x 128 entries
-constexpr float kLazy = 8.f;     // rescale O only when a row max grows by more than 2^8
+constexpr int HD = 512;                  // latent width
+constexpr int TT = 64;                   // entries per tile
+constexpr int KBOX = TT * 128;           // 8 KB: 64 dims x 64 entries, 128-byte swizzled
+constexpr int KSLOT = 8 * KBOX;          // 64 KB: one bf16 tile of 512 dims
+constexpr int CHUNK = 512;               // entries resolved to rows at a time (8 tiles)
+// 8 warps (two per SM sub-partition, so up to 255 registers a thread)
+constexpr int kSmWarps = 4, kGaWarps = 3;
+constexpr int kGaThreads = 32 * kGaWarps;
+constexpr int kMmaWarp = kSmWarps + kGaWarps;
+constexpr int kThreads = 32 * (kMmaWarp + 1);   // 256
+constexpr int kGaRows = (TT + kGaWarps - 1) / kGaWarps;   // tile rows per gather warp (22)
+constexpr int kResolve = (CHUNK + kGaThreads - 1) / kGaThreads;   // entries per gather thread per chunk
+constexpr float kLazy = 8.f;             // rescale O only when a head's max grows by more than 2^8
+constexpr int kMaxCs = 8;
+constexpr int BAR_SOFTMAX = 1, BAR_GATHER = 2;  // named barriers (0 is __syncthreads)
 
-// QSPLIT: an fp32 query is held as bf16 hi + lo parts (q - hi rounded again)
-// and the first product runs on both, so the scores keep ~16 mantissa bits of
-// the query instead of 8.
-template <int NQ, bool QSPLIT>
+// mbarriers
+enum { B_KFULL = 0, B_KEMPTY = 2, B_SFULL = 4, B_SEMPTY = 6, B_PFULL = 8, B_ODONE = 9, NBARS = 10 };
+
+// QSPLIT: an fp32 query is held as bf16 hi + lo parts (lo = q - hi, rounded
+// again) and the first product runs on both, so the scores keep ~16 mantissa
+// bits of the query; 32 query rows per group then.  A bf16 query: 64 rows.
+template <bool QSPLIT>
 struct Cfg {
-    static constexpr int QBOX = NQ * 128;            // 64 dims x NQ query rows
-    static constexpr int PBOX = NQ * 128;            // 64 entries x NQ rows
-    static constexpr int OFF_K = 0;                  // 8 K boxes; reused for the O partial [NQ][512] fp32
-    static constexpr int OFF_Q = 8 * KBOX;           // hi part, then (QSPLIT) lo part
-    static constexpr int OFF_P = OFF_Q + (QSPLIT ? 2 : 1) * 8 * QBOX;
-    static constexpr int OFF_MISC = OFF_P + 2 * PBOX;
-    // misc: scale[TT], row[TT] (int), red[4][NQ], m_used, alpha, m_new, m_fin, l_fin [NQ each],
-    //       lred[4][NQ], wgt[NQ][8], rinv[NQ], rlse[NQ]
-    static constexpr int MISC_WORDS = 2 * TT + 4 * NQ + 5 * NQ + 4 * NQ + 8 * NQ + 2 * NQ;
-    static constexpr size_t SMEM = 1024 + OFF_MISC + MISC_WORDS * 4 + 64;
-    static constexpr int TMEM_COLS = NQ == 64 ? 512 : (NQ == 32 ? 256 : 128);
-    static constexpr int S_COL = 0, O_COL = NQ;
-    static_assert(NQ * HD * 4 <= 8 * KBOX, "O partial must fit in the K tile");
+    static constexpr int NQ = QSPLIT ? 32 : 64;
+    static constexpr int QBOX = NQ * 128;                  // 64 dims x NQ rows
+    static constexpr int OFF_K = 0;                        // K ring; the O partial [NQ][512] fp32 at the end
+    static constexpr int OFF_Q = 2 * KSLOT;
+    static constexpr int QBYTES = (QSPLIT ? 2 : 1) * 8 * QBOX;
+    // the M=64 product reads 64 rows from each box start: for 32-row boxes the
+    // extra rows are the next box (garbage rows of S nobody reads); the last
+    // box reads into this pad
+    static constexpr int QPAD = QSPLIT ? 4096 : 0;
+    static constexpr int OFF_P = OFF_Q + QBYTES + QPAD;    // P [NQ rows x 64 entries], K-major
+    static constexpr int OFF_MISC = OFF_P + NQ * 128;
+    // misc, in 4-byte words
+    static constexpr int W_CROW = 0;                       // [CHUNK] local row of each entry, -1 = none
+    static constexpr int W_CSC = W_CROW + CHUNK;           // [CHUNK] value scale of each entry
+    static constexpr int W_F = W_CSC + CHUNK;              // [2][TT] score factor: scale * softmax scale * log2(e)
+    static constexpr int W_BIAS = W_F + 2 * TT;            // [2][TT] 0, or -inf where there is no entry
+    static constexpr int W_PSC = W_BIAS + 2 * TT;          // [2][TT] value scale folded into P
+    static constexpr int W_ALPHA = W_PSC + 2 * TT;         // [2][64] per-head rescale factor, by tile parity
+    static constexpr int W_NEED = W_ALPHA + 128;           // [2][4] per-warp "some head rescales"
+    static constexpr int W_MFIN = W_NEED + 8;              // [64] this CTA's final max (log2 units)
+    static constexpr int W_LFIN = W_MFIN + 64;             // [64] and sum
+    static constexpr int W_WGT = W_LFIN + 64;              // [64][8] merge weights of the peers
+    static constexpr int W_RINV = W_WGT + 64 * 8;          // [64] 1 / L
+    static constexpr int W_RLSE = W_RINV + 64;             // [64]
+    static constexpr int W_QEXP = W_RLSE + 64;             // [64] per-head query exponent (fp16 products)
+    static constexpr int W_TEXP = W_QEXP + 64;             // [2] value-scale exponent of the tile in each slot
+    static constexpr int W_WMAX = W_TEXP + 2;              // [4] per-gather-warp max value scale of a chunk
+    static constexpr int W_FLAGS = W_WMAX + 4;             // [0] abort, [1] TMEM base
+    static constexpr int W_BARS = W_FLAGS + 4;
+    static constexpr int MISC_WORDS = W_BARS + 2 * NBARS;
+    static constexpr size_t SMEM = 1024 + OFF_MISC + MISC_WORDS * 4;
+    static constexpr int S_COL = 0;                        // two S buffers of TT columns
+    static constexpr int O_COL = 2 * TT;                   // O^T: 4 blocks of NQ columns (128 dims each)
+    static constexpr int TMEM_COLS = 512;
+    static_assert(O_COL + 4 * NQ <= TMEM_COLS, "TMEM budget");
+    static_assert(NQ * HD * 4 <= 2 * KSLOT, "O partial must fit in the K ring");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert((W_BARS & 1) == 0, "mbarrier alignment");
 };
 
 struct Params {
@@ -91,36 +138,55 @@ __device__ __forceinline__ int lower_bound_ids(const int* ids, int n, int64_t v)
     return lo;
 }
 
-template <int NQ, bool QSPLIT>
+__device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, volatile int* abort, int* status) {
+    if (*abort) return;
+    if (!mbar_wait_bounded(bar, parity)) {
+        *abort = 1;
+        atomicExch(status, kDevTimeout);
+    }
+}
+
+// KV_I8: int8 entries; both products then run in fp16 (int8 -> fp16 is exact
+// and takes two byte permutes and one packed subtract per four values).  The
+// query is scaled per head by a power of two so its largest element sits in
+// [2^14, 2^15) (no fp16 overflow, elements above 2^-28 of it exact), and the
+// value scales folded into P are scaled per 512-entry chunk by a power of two
+// so that P <= 256.  bf16 entries: bf16 products, no scaling.
+template <bool KV_I8, bool QSPLIT>
 __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p) {
-    using C = Cfg<NQ, QSPLIT>;
-    constexpr int kMaxCs = 8;
+    using C = Cfg<QSPLIT>;
+    constexpr int NQ = C::NQ;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* misc = reinterpret_cast<float*>(sm + C::OFF_MISC);
-    float* s_scale = misc;                 // [TT]   per-entry value scale (1 for bf16)
-    int* s_row = reinterpret_cast<int*>(s_scale + TT);   // [TT] local row, -1 = no entry
-    float* s_red = reinterpret_cast<float*>(s_row + TT); // [4][NQ] per-warp tile max
-    float* s_mused = s_red + 4 * NQ;       // [NQ]   running max (log2 units)
-    float* s_alpha = s_mused + NQ;         // [NQ]   rescale factor of this tile
-    float* s_mnew = s_alpha + NQ;          // [NQ]   running max after this tile
-    float* s_mfin = s_mnew + NQ;           // [NQ]   this CTA's final (m, l)
-    float* s_lfin = s_mfin + NQ;           // [NQ]
-    float* s_lred = s_lfin + NQ;           // [4][NQ]
-    float* s_wgt = s_lred + 4 * NQ;        // [NQ][8] merge weights of the peers
-    float* s_rinv = s_wgt + 8 * NQ;        // [NQ]   1 / L
-    float* s_rlse = s_rinv + NQ;           // [NQ]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s_rlse + NQ);
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2);
-    int* s_flags = reinterpret_cast<int*>(tmem_holder + 1);   // [0] abort, [1] rescale
+    uint32_t* misc = reinterpret_cast<uint32_t*>(sm + C::OFF_MISC);
+    int* s_crow = reinterpret_cast<int*>(misc + C::W_CROW);
+    float* s_csc = reinterpret_cast<float*>(misc + C::W_CSC);
+    float* s_f = reinterpret_cast<float*>(misc + C::W_F);
+    float* s_bias = reinterpret_cast<float*>(misc + C::W_BIAS);
+    float* s_psc = reinterpret_cast<float*>(misc + C::W_PSC);
+    float* s_alpha = reinterpret_cast<float*>(misc + C::W_ALPHA);
+    int* s_need = reinterpret_cast<int*>(misc + C::W_NEED);
+    float* s_mfin = reinterpret_cast<float*>(misc + C::W_MFIN);
+    float* s_lfin = reinterpret_cast<float*>(misc + C::W_LFIN);
+    float* s_wgt = reinterpret_cast<float*>(misc + C::W_WGT);
+    float* s_rinv = reinterpret_cast<float*>(misc + C::W_RINV);
+    float* s_rlse = reinterpret_cast<float*>(misc + C::W_RLSE);
+    int* s_qexp = reinterpret_cast<int*>(misc + C::W_QEXP);
+    int* s_texp = reinterpret_cast<int*>(misc + C::W_TEXP);
+    float* s_wmax = reinterpret_cast<float*>(misc + C::W_WMAX);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(misc + C::W_FLAGS);
+    uint32_t* s_tmem = misc + C::W_FLAGS + 1;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(misc + C::W_BARS);
+    const uint32_t bar0 = smem_u32(bars);
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank = (int)cluster_ctarank(), CS = (int)cluster_nctarank();
     const int seq = blockIdx.y / p.ngroups, grp = blockIdx.y - seq * p.ngroups;
-    const int row0 = grp * NQ;                                   // first query row of this group
+    const int row0 = grp * NQ;                       // first query row of this group
     const int nrows = min(NQ, p.nq - row0);
     const int* ids = p.idx ? p.idx + (int64_t)seq * p.k : nullptr;
-    const int64_t kv_seq = (int64_t)seq * p.nc_local;            // first row of this sequence
+    const int64_t kv_seq = (int64_t)seq * p.nc_local;   // first row of this sequence
 
     // ---- this CTA's share of the sequence's entries: positions in ids (gather) or ids (dense)
     int64_t e_begin, e_end;
@@ -145,241 +211,461 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
 
     const uint32_t kbase = smem_u32(sm + C::OFF_K), qbase = smem_u32(sm + C::OFF_Q), pbase = smem_u32(sm + C::OFF_P);
     if (tid == 0) {
-        mbar_init(smem_u32(&bars[0]), 1);
-        mbar_init(smem_u32(&bars[1]), 1);
-        s_flags[0] = 0;
-        s_flags[1] = 0;
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(BAR(B_KFULL + i), kGaThreads);
+            mbar_init(BAR(B_KEMPTY + i), 1);
+            mbar_init(BAR(B_SFULL + i), 1);
+            mbar_init(BAR(B_SEMPTY + i), kSmWarps);
+        }
+        mbar_init(BAR(B_PFULL), kSmWarps);
+        mbar_init(BAR(B_ODONE), 1);
+        *s_abort = 0;
+        s_qexp[0] = 0;   // largest |q| of the group (float bits), for the fp16 query scale
         fence_mbar_init();
     }
-    if (tid < NQ) s_mused[tid] = -INFINITY;
-    // ---- queries -> K-major swizzled bf16 (rows past nrows are zero)
-    for (int j = tid; j < NQ * (HD / 8); j += kThreads) {
-        const int r = j / (HD / 8), c = j - r * (HD / 8);   // 8 dims per 16-byte chunk
-        uint4 v = make_uint4(0, 0, 0, 0), vlo = make_uint4(0, 0, 0, 0);
-        if (r < nrows) {
-            const int64_t off = ((int64_t)seq * p.nq + row0 + r) * HD + c * 8;
-            if (p.q_f32) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + off));
-                const float4 b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + off + 4));
-                const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                uint32_t hi[4], lo[4];
+    if (warp == kMmaWarp) tmem_alloc(smem_u32(s_tmem), C::TMEM_COLS);
+    __syncthreads();
+
+    // ---- queries -> registers (TPR threads per row); converted after the entry ids are resolved, so
+    //      the two sets of loads are in flight together
+    constexpr int TPR = kThreads / NQ, DPT = HD / TPR;   // DPT dims per thread: 128 (bf16 q) or 64 (fp32 q)
+    static_assert(DPT % 8 == 0 && DPT * TPR == HD, "query split");
+    const int r = tid / TPR, part = tid - r * TPR;
+    const bool ok = r < nrows;
+    const int64_t qoff = ((int64_t)seq * p.nq + row0 + (ok ? r : 0)) * HD + part * DPT;
+    constexpr int QL = DPT * (QSPLIT ? 4 : 2) / 16;     // 16-byte loads per thread (16)
+    uint4 qraw[QL];
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.q) +
+                                                          qoff * (QSPLIT ? 4 : 2));
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    hi[u] = pack_bf16(f[2 * u], f[2 * u + 1]);
-                    const float h0 = __uint_as_float(hi[u] << 16), h1 = __uint_as_float(hi[u] & 0xffff0000u);
-                    lo[u] = pack_bf16(f[2 * u] - h0, f[2 * u + 1] - h1);
-                }
-                v = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                vlo = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            } else {
-                v = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) + off));
+        for (int j = 0; j < QL; ++j) qraw[j] = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+    }
+    // ---- entry ids -> local rows and value scales, CHUNK entries at a time (gather warps)
+    const int gtid = tid - 32 * kSmWarps;   // 0..95 in the gather warps
+    auto resolve_chunk = [&](int64_t cbase) {
+        int64_t id[kResolve];
+        int row[kResolve];
+#pragma unroll
+        for (int u = 0; u < kResolve; ++u) {
+            const int j = gtid + u * kGaThreads;
+            const int64_t e = cbase + j;
+            id[u] = (j < CHUNK && e < e_end) ? (ids ? (int64_t)__ldg(ids + e) : e) : INT64_MIN;
+        }
+#pragma unroll
+        for (int u = 0; u < kResolve; ++u) {
+            row[u] = -1;
+            if (id[u] != INT64_MIN) {
+                if (id[u] >= p.shard_lo && id[u] < p.shard_hi) row[u] = (int)(id[u] - p.shard_lo);
+                else if (p.window == WS_CSA_IDX_ALL) atomicExch(p.status, kDevBadIndex);   // skipped, and reported
             }
         }
-        *reinterpret_cast<uint4*>(sm + C::OFF_Q + (c >> 3) * C::QBOX + swz(r, c & 7)) = v;
-        if (QSPLIT) *reinterpret_cast<uint4*>(sm + C::OFF_Q + (8 + (c >> 3)) * C::QBOX + swz(r, c & 7)) = vlo;
+        float sc[kResolve];
+#pragma unroll
+        for (int u = 0; u < kResolve; ++u)
+            sc[u] = row[u] >= 0 ? (KV_I8 ? __ldg(p.kv_scales + kv_seq + row[u]) : 1.f) : 0.f;
+        float mx = 0.f;
+#pragma unroll
+        for (int u = 0; u < kResolve; ++u) {
+            const int j = gtid + u * kGaThreads;
+            if (j < CHUNK) {
+                s_crow[j] = row[u];
+                s_csc[j] = sc[u];
+                mx = fmaxf(mx, sc[u]);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) s_wmax[warp - kSmWarps] = mx;
+    };
+    if (warp >= kSmWarps && warp < kMmaWarp && ntiles > 0) resolve_chunk(e_begin);
+
+    // ---- queries -> K-major swizzled fp16 / bf16 tile (rows past nrows are zero)
+    float v[DPT];
+#pragma unroll
+    for (int j = 0; j < QL; ++j) {
+        const uint32_t w[4] = {qraw[j].x, qraw[j].y, qraw[j].z, qraw[j].w};
+        if (QSPLIT) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[4 * j + u] = __uint_as_float(w[u]);
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                v[8 * j + 2 * u] = __uint_as_float(w[u] << 16);
+                v[8 * j + 2 * u + 1] = __uint_as_float(w[u] & 0xffff0000u);
+            }
+        }
     }
-    if (warp == 0) tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+    if (KV_I8) {   // fp16 products: the group's q * 2^-qe has its largest magnitude in [2^14, 2^15)
+        float mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) mx = fmaxf(mx, fabsf(v[j]));
+#pragma unroll
+        for (int o = 1; o < TPR; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (part == 0 && mx > 0.f) atomicMax(&s_qexp[0], __float_as_int(mx));   // non-negative: int order
+        __syncthreads();
+        const int mb = s_qexp[0];
+        const int qe = mb > 0 ? min(max(((mb >> 23) & 0xff) - 127 - 14, -126), 113) : 0;
+        const float sq = __int_as_float((127 - qe) << 23);
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) v[j] *= sq;   // exact: a power of two
+        if (tid == 0) s_qexp[1] = qe;
+    }
+#pragma unroll
+    for (int j = 0; j < DPT / 8; ++j) {
+        const int c8 = part * (DPT / 8) + j;   // 8-dim chunk index 0..63
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float a = v[8 * j + 2 * u], b = v[8 * j + 2 * u + 1];
+            if (KV_I8) {
+                const __half2 h = __floats2half2_rn(a, b);
+                hi[u] = *reinterpret_cast<const uint32_t*>(&h);
+                const float2 hf = __half22float2(h);
+                const __half2 l2 = __floats2half2_rn(a - hf.x, b - hf.y);
+                lo[u] = *reinterpret_cast<const uint32_t*>(&l2);
+            } else {
+                hi[u] = pack_bf16(a, b);
+                lo[u] = pack_bf16(a - __uint_as_float(hi[u] << 16), b - __uint_as_float(hi[u] & 0xffff0000u));
+            }
+        }
+        *reinterpret_cast<uint4*>(sm + C::OFF_Q + (c8 >> 3) * C::QBOX + swz(r, c8 & 7)) =
+            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        if (QSPLIT)
+            *reinterpret_cast<uint4*>(sm + C::OFF_Q + (8 + (c8 >> 3)) * C::QBOX + swz(r, c8 & 7)) =
+                make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+
+
+    cp_async_wait_all();
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tbase = *tmem_holder;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    constexpr uint32_t id1 = idesc_bf16_f32(TT, NQ, false, false);
-    constexpr uint32_t id2 = idesc_bf16_f32(128, NQ, true, false);
+    const uint32_t tbase = *s_tmem;
+    // S = Q . K^T and O^T += K^T . P^T
+    constexpr uint32_t id1 = KV_I8 ? idesc_f16_f32(64, TT, false, false) : idesc_bf16_f32(64, TT, false, false);
+    constexpr uint32_t id2 = KV_I8 ? idesc_f16_f32(128, NQ, true, false) : idesc_bf16_f32(128, NQ, true, false);
 
-    float l_run[NQ];
-#pragma unroll
-    for (int h = 0; h < NQ; ++h) l_run[h] = 0.f;
-
-    for (int t = 0; t < ntiles; ++t) {
-        // ---- resolve this tile's entries to local rows
-        const int64_t ebase = e_begin + (int64_t)t * TT;
-        if (tid < TT) {
-            const int64_t e = ebase + tid;
-            int row = -1;
-            float sc = 0.f;
-            if (e < e_end) {
-                const int64_t id = ids ? (int64_t)__ldg(ids + e) : e;
-                if (id >= p.shard_lo && id < p.shard_hi) {
-                    row = (int)(id - p.shard_lo);
-                    sc = p.kv_i8 ? __ldg(p.kv_scales + kv_seq + row) : 1.f;
-                } else if (p.window == WS_CSA_IDX_ALL) {
-                    atomicExch(p.status, kDevBadIndex);   // skipped, and reported
-                }
+    if (warp >= kSmWarps && warp < kMmaWarp) {
+        // ================================================================ gather
+        // score factor per unit value scale: softmax scale * log2(e), times 2^qe for the scaled fp16 query
+        const float fscale = KV_I8 ? p.scale_log2 * __int_as_float((127 + s_qexp[1]) << 23) : p.scale_log2;
+        // publish tile t's per-entry factors (thread gtid < TT owns entry gtid) and signal the MMA warp
+        auto publish = [&](int t, float sc, int ex) {   // ex: the chunk's value-scale exponent
+            const int slot = t & 1;
+            if (gtid < TT) {
+                const bool ok = sc >= 0.f;
+                s_f[slot * TT + gtid] = ok ? sc * fscale : 0.f;
+                s_bias[slot * TT + gtid] = ok ? 0.f : -INFINITY;
+                s_psc[slot * TT + gtid] = ok ? sc * __int_as_float((127 - ex) << 23) : 0.f;
             }
-            s_row[tid] = row;
-            s_scale[tid] = sc;
-        }
-        __syncthreads();
-        // ---- gather into the bf16 K tile (zero rows where there is no entry); all loads first
-        if (p.kv_i8) {
+            if (gtid == 0) s_texp[slot] = ex;
+            fence_proxy_async_smem();
+            mbar_arrive(BAR(B_KFULL + slot));
+        };
+        auto next_chunk = [&](int t) {   // tile t starts a new chunk
+            named_bar_sync(BAR_GATHER, kGaThreads);
+            resolve_chunk(e_begin + (int64_t)t * TT);
+            named_bar_sync(BAR_GATHER, kGaThreads);
+        };
+        auto chunk_exp = [&]() {   // ceil(log2(largest value scale of the current chunk)), in [-126, 126]
+            const float mx = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), s_wmax[2]);
+            if (!(mx > 0.f)) return 0;
+            const int b = __float_as_int(mx);
+            return min(max(((b >> 23) & 0xff) - 127 + ((b & 0x7fffff) != 0), -126), 126);
+        };
+        auto entry_scale = [&](int t) {  // this thread's entry of tile t: its scale, or -1 when none
+            const int off = (t * TT) % CHUNK + gtid;
+            return (gtid < TT && s_crow[off] >= 0) ? s_csc[off] : -1.f;
+        };
+        auto wait_slot = [&](int t) {
+            if (t >= 2) wait_bar(BAR(B_KEMPTY + (t & 1)), ((t >> 1) + 1) & 1, s_abort, p.status);
+        };
+        if (KV_I8) {
             const int8_t* kv = static_cast<const int8_t*>(p.kv);
-            const int c = tid & 31, rb = tid >> 5;               // 32 chunks of 16 int8 per row
-            int4 raw[16];
+            const int c = lane, rb = warp - kSmWarps;   // 32 chunks of 16 int8 per row; rows rb + 3i
+            auto load = [&](int4 (&r)[kGaRows], int t) {
+                const int off = (t * TT) % CHUNK;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int row = s_row[rb + 8 * i];
-                raw[i] = row >= 0 ? __ldg(reinterpret_cast<const int4*>(kv + (kv_seq + row) * HD + c * 16))
-                                  : make_int4(0, 0, 0, 0);
+                for (int i = 0; i < kGaRows; ++i) {
+                    const int rr = rb + kGaWarps * i;
+                    const int row = rr < TT ? s_crow[off + rr] : -1;
+                    r[i] = row >= 0 ? __ldg(reinterpret_cast<const int4*>(kv + (kv_seq + row) * HD + c * 16))
+                                    : make_int4(0, 0, 0, 0);
+                }
+            };
+            auto store = [&](const int4 (&r)[kGaRows], int t, float sc, int ex) {
+                wait_slot(t);
+                uint8_t* box = sm + C::OFF_K + (t & 1) * KSLOT + (c >> 2) * KBOX;   // 64 dims per box
+                const __half2 bias2 = __floats2half2_rn(1152.f, 1152.f);          // 1024 + 128
+#pragma unroll
+                for (int i = 0; i < kGaRows; ++i) {
+                    const int rr = rb + kGaWarps * i;
+                    if (rr >= TT) continue;
+                    const uint32_t src[4] = {(uint32_t)r[i].x, (uint32_t)r[i].y, (uint32_t)r[i].z, (uint32_t)r[i].w};
+                    uint32_t w[8];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        // byte b -> fp16 bits 0x6400 | (b + 128) = 1024 + b + 128, then subtract 1152: exact b
+                        const uint32_t x = src[u] ^ 0x80808080u;
+                        const uint32_t lo = __byte_perm(x, 0x64646464u, 0x4140);
+                        const uint32_t hi = __byte_perm(x, 0x64646464u, 0x4342);
+                        const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias2);
+                        const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias2);
+                        w[2 * u] = *reinterpret_cast<const uint32_t*>(&a);
+                        w[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&b);
+                    }
+                    *reinterpret_cast<uint4*>(box + swz(rr, (c & 3) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(box + swz(rr, (c & 3) * 2 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+                publish(t, sc, ex);
+            };
+            // two tiles in flight: the next tile's loads are issued before this tile is converted
+            int4 ra[kGaRows], rb2[kGaRows];
+            float sca = 0.f, scb = 0.f;
+            int exa = 0, exb = 0;
+            if (ntiles > 0) {
+                sca = entry_scale(0);
+                exa = chunk_exp();
+                load(ra, 0);
             }
-            uint8_t* box = sm + C::OFF_K + (c >> 2) * KBOX;      // 16 dims per chunk; 64 dims per box
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int r = rb + 8 * i;
-                const int8_t* b8 = reinterpret_cast<const int8_t*>(&raw[i]);
-                uint32_t w[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) w[u] = pack_bf16((float)b8[2 * u], (float)b8[2 * u + 1]);
-                *reinterpret_cast<uint4*>(box + swz(r, (c & 3) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4*>(box + swz(r, (c & 3) * 2 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+            for (int t = 0; t < ntiles; t += 2) {
+                if (t + 1 < ntiles) {
+                    if (((t + 1) * TT) % CHUNK == 0) next_chunk(t + 1);
+                    scb = entry_scale(t + 1);
+                    exb = chunk_exp();
+                    load(rb2, t + 1);
+                }
+                store(ra, t, sca, exa);
+                if (t + 1 >= ntiles) break;
+                if (t + 2 < ntiles) {
+                    if (((t + 2) * TT) % CHUNK == 0) next_chunk(t + 2);
+                    sca = entry_scale(t + 2);
+                    exa = chunk_exp();
+                    load(ra, t + 2);
+                }
+                store(rb2, t + 1, scb, exb);
             }
         } else {
             const __nv_bfloat16* kv = static_cast<const __nv_bfloat16*>(p.kv);
-            const int c = tid & 63, rb = tid >> 6;               // 64 chunks of 8 bf16 per row
+            const int rb = warp - kSmWarps;   // 64 chunks of 8 bf16 per row: lane and lane + 32; rows rb + 3i
+            for (int t = 0; t < ntiles; ++t) {
+                if (t > 0 && (t * TT) % CHUNK == 0) next_chunk(t);
+                const float sc = entry_scale(t);
+                const int off = (t * TT) % CHUNK;
+                uint4 v[2 * kGaRows];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint4 v[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int row = s_row[rb + 4 * (half * 16 + i)];
-                    v[i] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(kv + (kv_seq + row) * HD + c * 8))
-                                    : make_uint4(0, 0, 0, 0);
+                for (int i = 0; i < kGaRows; ++i) {
+                    const int rr = rb + kGaWarps * i;
+                    const int row = rr < TT ? s_crow[off + rr] : -1;
+                    const __nv_bfloat16* src = kv + (kv_seq + max(row, 0)) * HD;
+                    v[2 * i] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(src + lane * 8)) : make_uint4(0, 0, 0, 0);
+                    v[2 * i + 1] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(src + (lane + 32) * 8))
+                                            : make_uint4(0, 0, 0, 0);
                 }
+                wait_slot(t);
+                uint8_t* slot = sm + C::OFF_K + (t & 1) * KSLOT;
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    *reinterpret_cast<uint4*>(sm + C::OFF_K + (c >> 3) * KBOX + swz(rb + 4 * (half * 16 + i), c & 7)) =
-                        v[i];
+                for (int i = 0; i < kGaRows; ++i) {
+                    const int rr = rb + kGaWarps * i;
+                    if (rr >= TT) continue;
+                    *reinterpret_cast<uint4*>(slot + (lane >> 3) * KBOX + swz(rr, lane & 7)) = v[2 * i];
+                    *reinterpret_cast<uint4*>(slot + (4 + (lane >> 3)) * KBOX + swz(rr, lane & 7)) = v[2 * i + 1];
+                }
+                publish(t, sc, 0);
             }
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        // ---- S^T = K . Q^T
-        if (tid == 0) {
-            for (int part = 0; part < (QSPLIT ? 2 : 1); ++part)
-                for (int kb = 0; kb < 8; ++kb)
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16(tbase + C::S_COL, sdesc_sw128(kbase + kb * KBOX + kk * 32, 16, 1024),
-                                  sdesc_sw128(qbase + (part * 8 + kb) * C::QBOX + kk * 32, 16, 1024), id1,
-                                  (part | kb | kk) != 0);
-            umma_commit(smem_u32(&bars[0]));
+    } else if (warp == kMmaWarp) {
+        // ================================================================ MMA issue (lane 0)
+        // Issue whichever product is ready: the second product of the oldest
+        // tile first (it frees a K slot and lets the next P be written), else
+        // the first product of the next tile.
+        int g1 = 0, g2 = 0;   // next tile for the first / second product
+        uint64_t t_last = globaltimer_ns();
+        while (g2 < ntiles) {
+            int choice = 0;
+            if (lane == 0) {
+                if (*s_abort) {
+                    choice = 3;
+                } else if (g2 < g1 && mbar_try_wait(BAR(B_PFULL), g2 & 1)) {
+                    choice = 2;
+                } else if (g1 < ntiles && mbar_try_wait(BAR(B_KFULL + (g1 & 1)), (g1 >> 1) & 1) &&
+                           (g1 < 2 || mbar_try_wait(BAR(B_SEMPTY + (g1 & 1)), ((g1 >> 1) + 1) & 1))) {
+                    choice = 1;
+                } else if (globaltimer_ns() - t_last > 2000000000ull) {
+                    *s_abort = 1;
+                    atomicExch(p.status, kDevTimeout);
+                    choice = 3;
+                }
+            }
+            choice = __shfl_sync(0xffffffffu, choice, 0);
+            if (choice == 3) break;
+            if (choice == 0) continue;
+            tc_fence_after();
+            if (lane == 0) {
+                t_last = globaltimer_ns();
+                if (choice == 1) {
+                    const int slot = g1 & 1;
+                    const uint32_t kb_base = kbase + slot * KSLOT;
+                    for (int part = 0; part < (QSPLIT ? 2 : 1); ++part)
+                        for (int kb = 0; kb < 8; ++kb)
+                            for (int kk = 0; kk < 4; ++kk)
+                                umma_bf16(tbase + C::S_COL + slot * TT,
+                                          sdesc_sw128(qbase + (part * 8 + kb) * C::QBOX + kk * 32, 16, 1024),
+                                          sdesc_sw128(kb_base + kb * KBOX + kk * 32, 16, 1024), id1,
+                                          (part | kb | kk) != 0);
+                    umma_commit(BAR(B_SFULL + slot));
+                } else {
+                    const uint32_t ks_base = kbase + (g2 & 1) * KSLOT;
+                    for (int mb = 0; mb < 4; ++mb)
+                        for (int ks = 0; ks < TT / 16; ++ks)
+                            umma_bf16(tbase + C::O_COL + mb * NQ,
+                                      sdesc_sw128(ks_base + (2 * mb) * KBOX + ks * 2048, KBOX, 1024),
+                                      sdesc_sw128(pbase + ks * 32, 16, 1024), id2, (g2 > 0 || ks > 0) ? 1u : 0u);
+                    umma_commit(BAR(B_KEMPTY + (g2 & 1)));
+                    umma_commit(BAR(B_ODONE));
+                }
+            }
+            if (choice == 1) ++g1; else ++g2;
+            __syncwarp();
         }
-        if (!mbar_wait_bounded(smem_u32(&bars[0]), t & 1)) {
-            s_flags[0] = 1;
-            atomicExch(p.status, kDevTimeout);
-        }
-        tc_fence_after();
-        // ---- softmax over the tile (warps 0-3: thread = entry row)
-        float x[NQ];
-        float sc = 0.f;
-        if (warp < 4) {
+    } else {
+        // ================================================================ softmax (thread = head)
+        const int h = warp * 16 + lane;
+        const bool own = lane < 16 && h < NQ;
+        const bool active = own && h < nrows;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        int eref = 0;   // value-scale exponent O is accumulated in (the largest chunk exponent so far)
+        for (int t = 0; t < ntiles; ++t) {
+            const int sb = t & 1;
+            wait_bar(BAR(B_SFULL + sb), (t >> 1) & 1, s_abort, p.status);
+            tc_fence_after();
+            // this tile's chunk exponent: O and l are rescaled when it grows, P is scaled down when it is smaller
+            const int ex = s_texp[sb];
+            float alpha = 1.f, g = 1.f;   // alpha: factor on O (and, its max part, on l); g: on P
+            int need = 0;
+            if (t == 0) {
+                eref = ex;
+            } else if (ex > eref) {
+                alpha = __int_as_float((127 + max(eref - ex, -126)) << 23);
+                need = 1;
+                eref = ex;
+            } else if (ex < eref) {
+                g = __int_as_float((127 + max(ex - eref, -126)) << 23);
+            }
+            float am = 1.f;   // the max part of alpha
+            float x[TT];
 #pragma unroll
-            for (int cb = 0; cb < NQ / 16; ++cb) tmem_ld16(tbase + lane_base + C::S_COL + cb * 16, x + cb * 16);
+            for (int j = 0; j < TT / 16; ++j) tmem_ld16(tbase + lane_base + C::S_COL + sb * TT + j * 16, x + j * 16);
             tmem_wait_ld();
-            const int r = warp * 32 + lane;
-            sc = s_scale[r];
-            const float f = sc * p.scale_log2;
-            const bool valid = s_row[r] >= 0;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(BAR(B_SEMPTY + sb));
+            if (active) {
+                const float4* f4 = reinterpret_cast<const float4*>(s_f + sb * TT);
+                const float4* b4 = reinterpret_cast<const float4*>(s_bias + sb * TT);
+                float mt0 = -INFINITY, mt1 = -INFINITY;
 #pragma unroll
-            for (int h = 0; h < NQ; ++h) {
-                x[h] = valid ? x[h] * f : -INFINITY;
-                float mx = x[h];
+                for (int j = 0; j < TT / 4; ++j) {
+                    const float4 f = f4[j], b = b4[j];
+                    x[4 * j] = fmaf(x[4 * j], f.x, b.x);
+                    x[4 * j + 1] = fmaf(x[4 * j + 1], f.y, b.y);
+                    x[4 * j + 2] = fmaf(x[4 * j + 2], f.z, b.z);
+                    x[4 * j + 3] = fmaf(x[4 * j + 3], f.w, b.w);
+                    mt0 = fmaxf(mt0, fmaxf(x[4 * j], x[4 * j + 1]));
+                    mt1 = fmaxf(mt1, fmaxf(x[4 * j + 2], x[4 * j + 3]));
+                }
+                const float mt = fmaxf(mt0, mt1);
+                const bool grow = mt > m + kLazy;   // also true when m == -inf and mt is finite
+                const float mn = grow ? mt : m;
+                if (grow) {
+                    am = ex2(m - mn);               // 0 when m == -inf
+                    need |= m != -INFINITY;
+                }
+                alpha *= am;
+                m = mn;
+                const float4* s4 = reinterpret_cast<const float4*>(s_psc + sb * TT);
+                const float mneg = mn == -INFINITY ? 0.f : -mn;   // with mn == -inf every x is -inf: p = 0
+                float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                if (lane == 0) s_red[warp * NQ + h] = mx;
+                for (int j = 0; j < TT / 4; ++j) {
+                    const float4 s = s4[j];
+                    const float p0 = ex2(x[4 * j] + mneg), p1 = ex2(x[4 * j + 1] + mneg);
+                    const float p2 = ex2(x[4 * j + 2] + mneg), p3 = ex2(x[4 * j + 3] + mneg);
+                    ls0 += p0 + p1;
+                    ls1 += p2 + p3;
+                    x[4 * j] = p0 * s.x;            // the value scale folded into P
+                    x[4 * j + 1] = p1 * s.y;
+                    x[4 * j + 2] = p2 * s.z;
+                    x[4 * j + 3] = p3 * s.w;
+                }
+                if (g != 1.f) {
+#pragma unroll
+                    for (int j = 0; j < TT; ++j) x[j] *= g;
+                }
+                l = l * am + (ls0 + ls1);
             }
-        }
-        tc_fence_before();
-        __syncthreads();
-        // new running max per row (lazy), rescale factor, P
-        if (warp < 4) {
-            int need_any = 0;
+            if (own) s_alpha[sb * 64 + h] = alpha;
+            need = __any_sync(0xffffffffu, need);
+            if (lane == 0) s_need[sb * 4 + warp] = need;
+            named_bar_sync(BAR_SOFTMAX, 32 * kSmWarps);
+            const int any = s_need[sb * 4] | s_need[sb * 4 + 1] | s_need[sb * 4 + 2] | s_need[sb * 4 + 3];
+            if (t > 0) {
+                // the previous second product has finished: O is stable and P may be rewritten
+                wait_bar(BAR(B_ODONE), (t - 1) & 1, s_abort, p.status);
+                tc_fence_after();
+                if (any) {   // O *= alpha per head (column); this warp's 32 dims of each 128-dim block
+                    for (int mb = 0; mb < 4; ++mb)
 #pragma unroll
-            for (int h = 0; h < NQ; ++h) {
-                const float mt = fmaxf(fmaxf(s_red[h], s_red[NQ + h]), fmaxf(s_red[2 * NQ + h], s_red[3 * NQ + h]));
-                const float mo = s_mused[h];
-                const bool need = mt > mo + kLazy;   // also true when mo == -inf and mt is finite
-                const float mn = need ? mt : mo;
-                const float alpha = need ? ex2(mo - mn) : 1.f;
-                need_any |= (need && mo != -INFINITY) ? 1 : 0;
-                const float pv = (mn == -INFINITY) ? 0.f : ex2(x[h] - mn);
-                l_run[h] = l_run[h] * alpha + pv;
-                x[h] = pv * sc;                     // the value scale folded into P
-                if (tid == 0) {
-                    s_alpha[h] = alpha;
-                    s_mnew[h] = mn;
+                        for (int cb = 0; cb < NQ / 16; ++cb) {
+                            float v[16];
+                            const uint32_t ta = tbase + lane_base + C::O_COL + mb * NQ + cb * 16;
+                            tmem_ld16(ta, v);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int u = 0; u < 16; ++u) v[u] *= s_alpha[sb * 64 + cb * 16 + u];
+                            tmem_st16(ta, v);
+                        }
+                    tmem_wait_st();
                 }
             }
-            // P^T, K-major: rows = query rows, 64 entries per 128-byte row, two boxes
-            const int r = warp * 32 + lane;
-            uint8_t* pb = sm + C::OFF_P + (r >> 6) * C::PBOX;
-            const int kc = (r & 63) >> 3, ke = (r & 7) * 2;
+            if (own) {   // this head's P row: 64 entries, 8 swizzled 16-byte chunks (zeros when inactive)
+                uint8_t* prow = sm + C::OFF_P + h * 128;
 #pragma unroll
-            for (int h = 0; h < NQ; ++h)
-                *reinterpret_cast<__nv_bfloat16*>(pb + h * 128 + ((kc ^ (h & 7)) << 4) + ke) = __float2bfloat16_rn(x[h]);
-            if (tid == 0) s_flags[1] = need_any;
-        }
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (tid < NQ) s_mused[tid] = s_mnew[tid];
-        if (s_flags[1] && t > 0 && warp < 4) {
-            // O (previous tiles) *= alpha per query row; the previous second product has completed
-            for (int mb = 0; mb < 4; ++mb)
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t w4[4] = {0u, 0u, 0u, 0u};
+                    if (active) {
 #pragma unroll
-                for (int cb = 0; cb < NQ / 16; ++cb) {
-                    float v[16];
-                    const uint32_t ta = tbase + lane_base + C::O_COL + mb * NQ + cb * 16;
-                    tmem_ld16(ta, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int u = 0; u < 16; ++u) v[u] *= s_alpha[cb * 16 + u];
-                    tmem_st16(ta, v);
+                        for (int u = 0; u < 4; ++u) {
+                            if (KV_I8) {
+                                const __half2 hp = __floats2half2_rn(x[8 * j + 2 * u], x[8 * j + 2 * u + 1]);
+                                w4[u] = *reinterpret_cast<const uint32_t*>(&hp);
+                            } else {
+                                w4[u] = pack_bf16(x[8 * j + 2 * u], x[8 * j + 2 * u + 1]);
+                            }
+                        }
+                    }
+                    const uint4 w = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    *reinterpret_cast<uint4*>(prow + ((j ^ (h & 7)) << 4)) = w;
                 }
-            tmem_wait_st();
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(BAR(B_PFULL));
         }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        // ---- O^T += K^T . P^T
-        if (tid == 0) {
-            for (int mb = 0; mb < 4; ++mb)
-                for (int ks = 0; ks < TT / 16; ++ks)
-                    umma_bf16(tbase + C::O_COL + mb * NQ,
-                              sdesc_sw128(kbase + (2 * mb) * KBOX + ks * 2048, KBOX, 1024),
-                              sdesc_sw128(pbase + (ks >> 2) * C::PBOX + (ks & 3) * 32, 16, 1024), id2,
-                              (t > 0 || ks > 0) ? 1u : 0u);
-            umma_commit(smem_u32(&bars[1]));
+        if (own) {
+            s_mfin[h] = (active && ntiles > 0 && !*s_abort) ? m : -INFINITY;
+            s_lfin[h] = (active && ntiles > 0 && !*s_abort) ? l : 0.f;
         }
-        if (!mbar_wait_bounded(smem_u32(&bars[1]), t & 1)) {
-            s_flags[0] = 1;
-            atomicExch(p.status, kDevTimeout);
-        }
-        tc_fence_after();
-        __syncthreads();
-        if (s_flags[0]) break;
-    }
-
-    // ---- this CTA's partial: (m, l) per row and O -> shared memory (over the K tile)
-    if (warp < 4) {
-#pragma unroll
-        for (int h = 0; h < NQ; ++h) {
-            float v = l_run[h];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) s_lred[warp * NQ + h] = v;
-        }
-    }
-    __syncthreads();
-    const bool have = ntiles > 0 && !s_flags[0];
-    if (tid < NQ) {
-        s_mfin[tid] = have ? s_mused[tid] : -INFINITY;
-        s_lfin[tid] = have ? s_lred[tid] + s_lred[NQ + tid] + s_lred[2 * NQ + tid] + s_lred[3 * NQ + tid] : 0.f;
-    }
-    float* o_part = reinterpret_cast<float*>(sm + C::OFF_K);   // [NQ][512]
-    if (have) {
-        if (warp < 4)
+        // ---- this CTA's O partial -> shared memory [NQ][512] (over the K ring, which no one reads any more)
+        float* o_part = reinterpret_cast<float*>(sm + C::OFF_K);
+        if (ntiles > 0) {
+            wait_bar(BAR(B_ODONE), (ntiles - 1) & 1, s_abort, p.status);
+            tc_fence_after();
+            const float oscale = __int_as_float((127 + eref) << 23);   // undo the value-scale exponent
             for (int mb = 0; mb < 4; ++mb)
 #pragma unroll
                 for (int cb = 0; cb < NQ / 16; ++cb) {
@@ -387,19 +673,23 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                     tmem_ld16(tbase + lane_base + C::O_COL + mb * NQ + cb * 16, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int u = 0; u < 16; ++u) o_part[(cb * 16 + u) * HD + mb * 128 + warp * 32 + lane] = v[u];
+                    for (int u = 0; u < 16; ++u)
+                        o_part[(cb * 16 + u) * HD + mb * 128 + warp * 32 + lane] = v[u] * oscale;
                 }
-    } else {
-        for (int j = tid; j < NQ * HD; j += kThreads) o_part[j] = 0.f;
+        } else {
+            for (int j = tid; j < NQ * HD; j += 32 * kSmWarps) o_part[j] = 0.f;
+        }
     }
+#undef BAR
     tc_fence_before();
     __syncthreads();
     cluster_sync();
 
-    // ---- merge the cluster's partials: this CTA owns rows [rank*RPC, (rank+1)*RPC)
-    const int RPC = NQ / CS;
+    // ---- merge the cluster's partials: this CTA owns rows [r_lo, r_lo + RPC)
+    const float* o_part = reinterpret_cast<const float*>(sm + C::OFF_K);
+    const int r_lo = rank * NQ / CS, RPC = (rank + 1) * NQ / CS - r_lo;
     if (tid < RPC) {
-        const int h = rank * RPC + tid;
+        const int h = r_lo + tid;
         float M = -INFINITY;
         float mc[kMaxCs];
 #pragma unroll
@@ -419,52 +709,120 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
         s_rlse[tid] = empty ? -INFINITY : M * kLn2 + logf(L);
     }
     __syncthreads();
-    for (int j = tid; j < RPC * (HD / 4); j += kThreads) {
-        const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
-        const int h = rank * RPC + hl;
-        if (h >= nrows) continue;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = 0; c < CS; ++c) {
-            const float w = s_wgt[hl * 8 + c];
-            if (w == 0.f) continue;
-            const float4 v = dsmem_ld_f32x4(dsmem_addr(smem_u32(o_part + h * HD + d4 * 4), c));
-            acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+    // two float4 of every peer in flight per thread
+    for (int j0 = tid; j0 < RPC * (HD / 4); j0 += 2 * kThreads) {
+        float4 v[2][kMaxCs];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int j = j0 + u * kThreads;
+            if (j >= RPC * (HD / 4)) continue;
+            const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
+            const uint32_t src = smem_u32(o_part + (r_lo + hl) * HD + d4 * 4);
+#pragma unroll
+            for (int c = 0; c < kMaxCs; ++c)
+                if (c < CS && s_wgt[hl * 8 + c] != 0.f) v[u][c] = dsmem_ld_f32x4(dsmem_addr(src, c));
         }
-        const float inv = s_rinv[hl];
-        const int64_t oi = ((int64_t)seq * p.nq + row0 + h) * HD + d4 * 4;
-        if (p.out_f32) {
-            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
-                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        } else {
-            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
-            *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-            *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int j = j0 + u * kThreads;
+            if (j >= RPC * (HD / 4)) continue;
+            const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
+            const int h = r_lo + hl;
+            if (h >= nrows) continue;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int c = 0; c < kMaxCs; ++c) {
+                const float w = c < CS ? s_wgt[hl * 8 + c] : 0.f;
+                if (w == 0.f) continue;
+                acc.x = fmaf(w, v[u][c].x, acc.x); acc.y = fmaf(w, v[u][c].y, acc.y);
+                acc.z = fmaf(w, v[u][c].z, acc.z); acc.w = fmaf(w, v[u][c].w, acc.w);
+            }
+            const float inv = s_rinv[hl];
+            const int64_t oi = ((int64_t)seq * p.nq + row0 + h) * HD + d4 * 4;
+            if (p.out_f32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
+                    make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            } else {
+                __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
+                *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+                *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+            }
         }
     }
-    if (tid < RPC && rank * RPC + tid < nrows && p.out_lse)
-        p.out_lse[(int64_t)seq * p.nq + row0 + rank * RPC + tid] = s_rlse[tid];
+    if (tid < RPC && r_lo + tid < nrows && p.out_lse)
+        p.out_lse[(int64_t)seq * p.nq + row0 + r_lo + tid] = s_rlse[tid];
     // peers keep their shared memory until every CTA of the cluster has read it
     cluster_sync();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tbase, C::TMEM_COLS);
+    if (warp == kMmaWarp) tmem_dealloc(tbase, C::TMEM_COLS);
 }
 
-template <int NQ, bool QSPLIT>
-static int launch(const Params& p, int bs, int cs, cudaStream_t st) {
-    auto kfn = csa_decode_kernel<NQ, QSPLIT>;
+// Clusters of `cs` CTAs of this kernel that the device runs at once.
+template <bool KV_I8, bool QSPLIT>
+static int max_active_clusters(int cs) {
+    static int cached[kMaxCs + 1] = {};   // for the device last asked about
+    static int cached_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cached_dev != dev) {
+        for (int& v : cached) v = 0;
+        cached_dev = dev;
+    }
+    int& slot = cached[cs];
+    if (slot == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(cs, 1, 1);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Cfg<QSPLIT>::SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = cs;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, csa_decode_kernel<KV_I8, QSPLIT>, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            return 1;   // not cached: asked again next time
+        }
+        slot = n;
+    }
+    return slot;
+}
+
+template <bool KV_I8, bool QSPLIT>
+static int launch(const Params& p, int bs, int64_t entries_per_seq, cudaStream_t st) {
+    auto kfn = csa_decode_kernel<KV_I8, QSPLIT>;
     static int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
-        if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<NQ, QSPLIT>::SMEM) !=
+        if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<QSPLIT>::SMEM) !=
             cudaSuccess)
             return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for csa_decode_kernel");
         configured_dev = dev;
     }
+    // CTAs per cluster: the fewest tile-times, counting waves of clusters the
+    // device cannot run at once and one tile-time per wave for the merge.
+    const int64_t clusters = (int64_t)bs * p.ngroups;
+    int cs = 1;
+    int64_t best = INT64_MAX;
+    for (int c = 1; c <= kMaxCs; ++c) {
+        if (c > 1 && entries_per_seq <= (int64_t)(c - 1) * TT) break;   // some CTA would get no full tile
+        const int64_t active = max_active_clusters<KV_I8, QSPLIT>(c);
+        const int64_t waves = (clusters + active - 1) / active;
+        const int64_t tiles = (entries_per_seq + (int64_t)c * TT - 1) / ((int64_t)c * TT);
+        const int64_t cost = waves * (tiles + 1);
+        if (cost < best) {
+            best = cost;
+            cs = c;
+        }
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(cs, (unsigned)(bs * p.ngroups), 1);
+    cfg.gridDim = dim3(cs, (unsigned)clusters, 1);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg<NQ, QSPLIT>::SMEM;
+    cfg.dynamicSmemBytes = Cfg<QSPLIT>::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -479,12 +837,6 @@ static int launch(const Params& p, int bs, int cs, cudaStream_t st) {
 
 }  // namespace csa
 
-int csa_cluster_size(int64_t entries_per_seq) {
-    int cs = 1;
-    while (cs < 8 && entries_per_seq > (int64_t)cs * 256) cs *= 2;
-    return cs;
-}
-
 int csa_launch(const CsaLaunch& a) {
     using namespace csa;
     Params p;
@@ -492,10 +844,9 @@ int csa_launch(const CsaLaunch& a) {
     p.q = a.q;
     p.q_f32 = a.q_f32;
     p.nq = a.nq;
-    // query rows per cluster: 64 for a bf16 query, 32 for an fp32 query (its hi/lo parts)
-    const int NQ = a.nq <= 16 ? 16 : (a.nq <= 32 || a.q_f32 ? 32 : 64);
+    const int NQ = a.q_f32 ? Cfg<true>::NQ : Cfg<false>::NQ;
     p.ngroups = (a.nq + NQ - 1) / NQ;
-    if ((int64_t)a.bs * p.ngroups > 65535) return set_error(WS_ERR_UNSUPPORTED, "csa_decode: bs * ceil(nq/64) > 65535");
+    if ((int64_t)a.bs * p.ngroups > 65535) return set_error(WS_ERR_UNSUPPORTED, "csa_decode: too many query groups");
     p.kv = a.kv;
     p.kv_i8 = a.kv_i8;
     p.kv_scales = a.kv_scales;
@@ -512,13 +863,12 @@ int csa_launch(const CsaLaunch& a) {
     p.out_f32 = a.out_f32;
     p.out_lse = a.out_lse;
     p.status = device_status_word();
-    // CTAs per sequence: about 256 entries each, at most 8 (one portable cluster)
-    const int cs = csa_cluster_size(a.idx ? (int64_t)a.k : p.dense_end - p.dense_begin);
+    // entries one sequence selects (a sharded sorted list selects about k * nc_local / nc; k bounds it)
+    const int64_t per_seq = a.idx ? (int64_t)a.k : p.dense_end - p.dense_begin;
     cudaStream_t st = static_cast<cudaStream_t>(a.stream);
-    if (a.q_f32) return NQ == 16 ? launch<16, true>(p, a.bs, cs, st) : launch<32, true>(p, a.bs, cs, st);
-    if (NQ == 16) return launch<16, false>(p, a.bs, cs, st);
-    if (NQ == 32) return launch<32, false>(p, a.bs, cs, st);
-    return launch<64, false>(p, a.bs, cs, st);
+    if (a.kv_i8)
+        return a.q_f32 ? launch<true, true>(p, a.bs, per_seq, st) : launch<true, false>(p, a.bs, per_seq, st);
+    return a.q_f32 ? launch<false, true>(p, a.bs, per_seq, st) : launch<false, false>(p, a.bs, per_seq, st);
 }
 
 }  // namespace ws
