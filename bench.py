@@ -509,6 +509,8 @@ class Csa(Workload):
             self.all_l = torch.empty(world, bs * nH, dtype=torch.float32, device=dev)
             self.out = torch.empty(bs * nH, 512, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(bs * nH, dtype=torch.float32, device=dev)
+        self.ws = torch.zeros(self.lib.ws_csa_decode_workspace_size(bs, nH, self._lib.WS_DTYPE_BF16),
+                              dtype=torch.uint8, device=dev)
         self.q_host = torch.randn(bs, nH, 512).bfloat16().pin_memory()
         self.idx_host = self.idx[0].cpu().pin_memory()
         self.out_host = torch.empty(bs * nH * 512, dtype=torch.bfloat16).pin_memory()
@@ -541,7 +543,7 @@ class Csa(Workload):
         rc = L_.ws_csa_decode(self.q[c].data_ptr(), self._lib.WS_DTYPE_BF16, self.bs, self.nH, 512, kv.data_ptr(),
                               self._lib.WS_DTYPE_I8, self.kv_scales[kvc].data_ptr(), kv.shape[1], lo,
                               self.idx[c].data_ptr(), self.k, mode, 0, 0, self.scale, out.data_ptr(), odt,
-                              lse.data_ptr(), st)
+                              lse.data_ptr(), self.ws.data_ptr(), self.ws.numel(), st)
         if rc != 0:
             raise RuntimeError(L_.ws_last_error().decode())
 

@@ -171,12 +171,15 @@ size_t ws_mla_decode_workspace_size(int B, int nH, int S);
  *   score = scale * q . value;  out [bs, nq, 512] normalised in out_dtype
  *   (WS_DTYPE_F32 or WS_DTYPE_BF16), out_lse [bs, nq] fp32 (may be NULL).
  * A row with no entry gives out = 0, lse = -inf (the partial of an empty
- * shard).  One launch, no workspace.
+ * shard).  One launch; the workspace (ws_csa_decode_workspace_size bytes,
+ * 16-byte aligned, no zeroing needed) carries the partials the CTAs of a
+ * sequence exchange.
  */
 int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void* kv, int kv_dtype,
                   const float* kv_scales, int64_t nc, int64_t shard_lo, const int32_t* idx, int k, int idx_mode,
                   int64_t kv_begin, int64_t kv_end, float scale, void* out, int out_dtype, float* out_lse,
-                  void* stream);
+                  void* workspace, size_t workspace_bytes, void* stream);
+size_t ws_csa_decode_workspace_size(int bs, int nq, int q_dtype);
 
 /*
  * Per-row quantisers of the CSA int8 family, bit-exact with the reference:

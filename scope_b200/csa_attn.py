@@ -6,7 +6,8 @@ and ignored), same output dtypes (fp32 normalised ``o``, fp32 ``lse``), same
 in-place behaviour for the ``_bsq*`` / ``_inplace`` / ``indexer_attn_cpu``
 variants.  Every attention entry runs the one tcgen05 CSA kernel of
 libscope_b200.so (``ws_csa_decode``): bf16 or int8+scale entries, gathered by
-top-k ids or over a dense range.  There is no CPU path: CPU tensors raise.
+top-k ids or over a dense range; its workspace comes from the per-stream pool.
+There is no CPU path: CPU tensors raise.
 
 Arithmetic differences from the reference, all toward the exact result:
   * the query is rounded to bf16 inside the kernel (fp32 accumulation);
@@ -20,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import check, lib, ptr, stream_ptr
+from ._lib import check, lib, ptr, stream_ptr, workspaces
 from .cpu_attn import _require_cuda, get_num_threads, set_num_threads  # noqa: F401
 
 HD = 512
@@ -76,9 +77,11 @@ def _launch(q, kv, scale, out, lse, *, idx=None, kv_scales=None, kv_range=None, 
     if bs == 0 or nq == 0:
         return
     with torch.cuda.device(dev):
-        rc = lib().ws_csa_decode(ptr(q), q_code, bs, nq, hd, ptr(kv), kv_code, ptr(kv_scales), nc, int(shard_lo),
-                                 ptr(idx), k, _IDX_MODES[idx_mode], int(kv_s), int(kv_e), float(scale),
-                                 ptr(out), out_code, ptr(lse), stream_ptr(dev))
+        L_ = lib()
+        ws = workspaces.get(L_.ws_csa_decode_workspace_size(bs, nq, q_code), dev)
+        rc = L_.ws_csa_decode(ptr(q), q_code, bs, nq, hd, ptr(kv), kv_code, ptr(kv_scales), nc, int(shard_lo),
+                              ptr(idx), k, _IDX_MODES[idx_mode], int(kv_s), int(kv_e), float(scale),
+                              ptr(out), out_code, ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
     check(rc, "ws_csa_decode")
 
 

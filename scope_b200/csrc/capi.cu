@@ -240,10 +240,14 @@ int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const 
                       workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+size_t ws_csa_decode_workspace_size(int bs, int nq, int q_dtype) {
+    return csa_workspace_bytes(std::max(bs, 0), std::max(nq, 1), q_dtype == WS_DTYPE_F32);
+}
+
 int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void* kv, int kv_dtype,
                   const float* kv_scales, int64_t nc, int64_t shard_lo, const int32_t* idx, int k, int idx_mode,
                   int64_t kv_begin, int64_t kv_end, float scale, void* out, int out_dtype, float* out_lse,
-                  void* stream) {
+                  void* workspace, size_t workspace_bytes, void* stream) {
     if (bs < 0 || nq < 1 || nc < 0 || shard_lo < 0) return set_error(WS_ERR_INVALID_ARG, "csa_decode: bad shape");
     if (hd != 512) return set_error(WS_ERR_UNSUPPORTED, "csa_decode: this build supports a 512-wide latent");
     if (q_dtype != WS_DTYPE_F32 && q_dtype != WS_DTYPE_BF16) return set_error(WS_ERR_INVALID_ARG, "csa_decode: q dtype");
@@ -278,6 +282,8 @@ int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void
     a.out = out;
     a.out_f32 = out_dtype == WS_DTYPE_F32;
     a.out_lse = out_lse;
+    a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes;
     a.stream = stream;
     return csa_launch(a);
 }

@@ -316,3 +316,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 }  // namespace ws
+
+namespace ws {
+// Store to shared memory of another CTA of the cluster (address from dsmem_addr).
+__device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+}  // namespace ws

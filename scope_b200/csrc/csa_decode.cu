@@ -23,9 +23,10 @@
 //     and sum need no cross-thread reduction; the max is updated lazily (O is
 //     rescaled in TMEM only when a head's max grows by more than 2^8, which
 //     keeps P <= 256 and is exact because m, l and O always share one max).
-// Then the cluster merges its CS partials through distributed shared memory:
-// CTA r reduces query rows [r*NQ/CS, (r+1)*NQ/CS) by log-sum-exp over the
-// peers' (m, l, O) and writes the output.  No workspace, one launch.
+// Then the cluster merges its CS partials: each CTA writes (m, l, O) of every
+// head to its slot of a workspace (L2), and after one cluster barrier CTA r
+// reduces query rows [r*NQ/CS, (r+1)*NQ/CS) by log-sum-exp over the CS slots
+// and writes the output.  One launch.
 //
 // Every wait is bounded: a wait that gives up records kDevTimeout in the
 // status word and sets a CTA-wide abort flag, after which the remaining waits
@@ -82,9 +83,7 @@ struct Cfg {
     static constexpr int W_PSC = W_BIAS + 2 * TT;          // [2][TT] value scale folded into P
     static constexpr int W_ALPHA = W_PSC + 2 * TT;         // [2][64] per-head rescale factor, by tile parity
     static constexpr int W_NEED = W_ALPHA + 128;           // [2][4] per-warp "some head rescales"
-    static constexpr int W_MFIN = W_NEED + 8;              // [64] this CTA's final max (log2 units)
-    static constexpr int W_LFIN = W_MFIN + 64;             // [64] and sum
-    static constexpr int W_WGT = W_LFIN + 64;              // [64][8] merge weights of the peers
+    static constexpr int W_WGT = W_NEED + 8;               // [64][8] merge weights of the cluster's partials
     static constexpr int W_RINV = W_WGT + 64 * 8;          // [64] 1 / L
     static constexpr int W_RLSE = W_RINV + 64;             // [64]
     static constexpr int W_QEXP = W_RLSE + 64;             // [64] per-head query exponent (fp16 products)
@@ -121,6 +120,7 @@ struct Params {
     void* out;
     int out_f32;
     float* out_lse;
+    float* ws;                // [clusters][8 slots][NQ * 512 + 2 * NQ] partials exchanged through L2
     int* status;
 };
 
@@ -166,8 +166,6 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     float* s_psc = reinterpret_cast<float*>(misc + C::W_PSC);
     float* s_alpha = reinterpret_cast<float*>(misc + C::W_ALPHA);
     int* s_need = reinterpret_cast<int*>(misc + C::W_NEED);
-    float* s_mfin = reinterpret_cast<float*>(misc + C::W_MFIN);
-    float* s_lfin = reinterpret_cast<float*>(misc + C::W_LFIN);
     float* s_wgt = reinterpret_cast<float*>(misc + C::W_WGT);
     float* s_rinv = reinterpret_cast<float*>(misc + C::W_RINV);
     float* s_rlse = reinterpret_cast<float*>(misc + C::W_RLSE);
@@ -347,6 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     constexpr uint32_t id1 = KV_I8 ? idesc_f16_f32(64, TT, false, false) : idesc_bf16_f32(64, TT, false, false);
     constexpr uint32_t id2 = KV_I8 ? idesc_f16_f32(128, NQ, true, false) : idesc_bf16_f32(128, NQ, true, false);
 
+    float m_final = -INFINITY, l_final = 0.f;   // softmax threads: this head's running max and sum
+    int eref_final = 0;                          // and the value-scale exponent O was accumulated in
     if (warp >= kSmWarps && warp < kMmaWarp) {
         // ================================================================ gather
         // score factor per unit value scale: softmax scale * log2(e), times 2^qe for the scaled fp16 query
@@ -656,16 +656,34 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             __syncwarp();
             if (lane == 0) mbar_arrive(BAR(B_PFULL));
         }
-        if (own) {
-            s_mfin[h] = (active && ntiles > 0 && !*s_abort) ? m : -INFINITY;
-            s_lfin[h] = (active && ntiles > 0 && !*s_abort) ? l : 0.f;
-        }
-        // ---- this CTA's O partial -> shared memory [NQ][512] (over the K ring, which no one reads any more)
-        float* o_part = reinterpret_cast<float*>(sm + C::OFF_K);
-        if (ntiles > 0) {
+        if (ntiles > 0) {   // the last second product has finished: O is final
             wait_bar(BAR(B_ODONE), (ntiles - 1) & 1, s_abort, p.status);
             tc_fence_after();
-            const float oscale = __int_as_float((127 + eref) << 23);   // undo the value-scale exponent
+        }
+        m_final = m;
+        l_final = l;
+        eref_final = eref;
+    }
+#undef BAR
+    // ---- exchange through L2: every CTA writes its partial (the unnormalised O row, max and sum of
+    //      each head) to its own slot of the cluster's workspace; after the cluster barrier the CTA
+    //      that merges a row reads that row from all CS slots.  (Distributed shared memory moves only
+    //      ~15-30 GB/s per SM on this part, far too little for 128 KB per CTA.)
+    constexpr int SLOT = NQ * HD + 2 * NQ;   // floats: O [NQ][512], then max [NQ], sum [NQ]
+    float* ws_cluster = p.ws + (size_t)blockIdx.y * kMaxCs * SLOT;
+    if (warp < kSmWarps) {
+        float* mine = ws_cluster + (size_t)rank * SLOT;
+        const int h = warp * 16 + lane;
+        const bool own = lane < 16 && h < NQ;
+        const bool have = ntiles > 0 && !*s_abort;
+        if (own) {
+            const bool ok = have && h < nrows;
+            mine[NQ * HD + h] = ok ? m_final : -INFINITY;
+            mine[NQ * HD + NQ + h] = ok ? l_final : 0.f;
+        }
+        if (have) {   // an empty partial writes no O: its weight is 0 and its rows are never read
+            const float oscale = __int_as_float((127 + eref_final) << 23);   // undo the value-scale exponent
+            const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
             for (int mb = 0; mb < 4; ++mb)
 #pragma unroll
                 for (int cb = 0; cb < NQ / 16; ++cb) {
@@ -673,28 +691,23 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                     tmem_ld16(tbase + lane_base + C::O_COL + mb * NQ + cb * 16, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int u = 0; u < 16; ++u)
-                        o_part[(cb * 16 + u) * HD + mb * 128 + warp * 32 + lane] = v[u] * oscale;
+                    for (int u = 0; u < 16; ++u) mine[(cb * 16 + u) * HD + mb * 128 + warp * 32 + lane] = v[u] * oscale;
                 }
-        } else {
-            for (int j = tid; j < NQ * HD; j += 32 * kSmWarps) o_part[j] = 0.f;
         }
     }
-#undef BAR
     tc_fence_before();
     __syncthreads();
-    cluster_sync();
+    cluster_sync();   // release / acquire at cluster scope: every slot of the cluster is visible
 
-    // ---- merge the cluster's partials: this CTA owns rows [r_lo, r_lo + RPC)
-    const float* o_part = reinterpret_cast<const float*>(sm + C::OFF_K);
+    // ---- merge the rows this CTA owns [r_lo, r_lo + RPC)
     const int r_lo = rank * NQ / CS, RPC = (rank + 1) * NQ / CS - r_lo;
     if (tid < RPC) {
         const int h = r_lo + tid;
-        float M = -INFINITY;
         float mc[kMaxCs];
+        float M = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kMaxCs; ++c) {
-            mc[c] = c < CS ? dsmem_ld_f32(dsmem_addr(smem_u32(s_mfin + h), c)) : -INFINITY;
+            mc[c] = c < CS ? __ldcg(ws_cluster + (size_t)c * SLOT + NQ * HD + h) : -INFINITY;
             M = fmaxf(M, mc[c]);
         }
         float L = 0.f;
@@ -702,57 +715,43 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
         for (int c = 0; c < kMaxCs; ++c) {
             const float w = (mc[c] == -INFINITY) ? 0.f : ex2(mc[c] - M);
             s_wgt[tid * 8 + c] = w;
-            if (w != 0.f) L += w * dsmem_ld_f32(dsmem_addr(smem_u32(s_lfin + h), c));
+            if (w != 0.f) L += w * __ldcg(ws_cluster + (size_t)c * SLOT + NQ * HD + NQ + h);
         }
         const bool empty = !(L > 0.f);
         s_rinv[tid] = empty ? 0.f : 1.f / L;
         s_rlse[tid] = empty ? -INFINITY : M * kLn2 + logf(L);
     }
     __syncthreads();
-    // two float4 of every peer in flight per thread
-    for (int j0 = tid; j0 < RPC * (HD / 4); j0 += 2 * kThreads) {
-        float4 v[2][kMaxCs];
+    for (int j = tid; j < RPC * (HD / 4); j += kThreads) {
+        const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
+        const int h = r_lo + hl;
+        if (h >= nrows) continue;
+        float4 v[kMaxCs];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int j = j0 + u * kThreads;
-            if (j >= RPC * (HD / 4)) continue;
-            const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
-            const uint32_t src = smem_u32(o_part + (r_lo + hl) * HD + d4 * 4);
+        for (int c = 0; c < kMaxCs; ++c)   // every slot's load in flight together
+            if (c < CS && s_wgt[hl * 8 + c] != 0.f)
+                v[c] = __ldcg(reinterpret_cast<const float4*>(ws_cluster + (size_t)c * SLOT + h * HD + d4 * 4));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < kMaxCs; ++c)
-                if (c < CS && s_wgt[hl * 8 + c] != 0.f) v[u][c] = dsmem_ld_f32x4(dsmem_addr(src, c));
+        for (int c = 0; c < kMaxCs; ++c) {
+            const float w = c < CS ? s_wgt[hl * 8 + c] : 0.f;
+            if (w == 0.f) continue;
+            acc.x = fmaf(w, v[c].x, acc.x); acc.y = fmaf(w, v[c].y, acc.y);
+            acc.z = fmaf(w, v[c].z, acc.z); acc.w = fmaf(w, v[c].w, acc.w);
         }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int j = j0 + u * kThreads;
-            if (j >= RPC * (HD / 4)) continue;
-            const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
-            const int h = r_lo + hl;
-            if (h >= nrows) continue;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int c = 0; c < kMaxCs; ++c) {
-                const float w = c < CS ? s_wgt[hl * 8 + c] : 0.f;
-                if (w == 0.f) continue;
-                acc.x = fmaf(w, v[u][c].x, acc.x); acc.y = fmaf(w, v[u][c].y, acc.y);
-                acc.z = fmaf(w, v[u][c].z, acc.z); acc.w = fmaf(w, v[u][c].w, acc.w);
-            }
-            const float inv = s_rinv[hl];
-            const int64_t oi = ((int64_t)seq * p.nq + row0 + h) * HD + d4 * 4;
-            if (p.out_f32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
-                    make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-            } else {
-                __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
-                *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-                *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-            }
+        const float inv = s_rinv[hl];
+        const int64_t oi = ((int64_t)seq * p.nq + row0 + h) * HD + d4 * 4;
+        if (p.out_f32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        } else {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
+            *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+            *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
         }
     }
     if (tid < RPC && r_lo + tid < nrows && p.out_lse)
         p.out_lse[(int64_t)seq * p.nq + row0 + r_lo + tid] = s_rlse[tid];
-    // peers keep their shared memory until every CTA of the cluster has read it
-    cluster_sync();
     tc_fence_after();
     if (warp == kMmaWarp) tmem_dealloc(tbase, C::TMEM_COLS);
 }
@@ -837,8 +836,19 @@ static int launch(const Params& p, int bs, int64_t entries_per_seq, cudaStream_t
 
 }  // namespace csa
 
+size_t csa_workspace_bytes(int bs, int nq, int q_f32) {
+    using namespace csa;
+    const int NQ = q_f32 ? Cfg<true>::NQ : Cfg<false>::NQ;
+    const int64_t clusters = (int64_t)bs * ((nq + NQ - 1) / NQ);
+    return (size_t)std::max<int64_t>(clusters, 1) * kMaxCs * (NQ * HD + 2 * NQ) * sizeof(float);
+}
+
 int csa_launch(const CsaLaunch& a) {
     using namespace csa;
+    if (!a.workspace || a.workspace_bytes < csa_workspace_bytes(a.bs, a.nq, a.q_f32))
+        return set_error(WS_ERR_WORKSPACE, "csa_decode: workspace missing or smaller than ws_csa_decode_workspace_size");
+    if (reinterpret_cast<uintptr_t>(a.workspace) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode: workspace must be 16-byte aligned");
     Params p;
     memset(&p, 0, sizeof(p));
     p.q = a.q;
@@ -862,6 +872,7 @@ int csa_launch(const CsaLaunch& a) {
     p.out = a.out;
     p.out_f32 = a.out_f32;
     p.out_lse = a.out_lse;
+    p.ws = static_cast<float*>(a.workspace);
     p.status = device_status_word();
     // entries one sequence selects (a sharded sorted list selects about k * nc_local / nc; k bounds it)
     const int64_t per_seq = a.idx ? (int64_t)a.k : p.dense_end - p.dense_begin;

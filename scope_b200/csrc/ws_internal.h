@@ -87,10 +87,13 @@ struct CsaLaunch {
     void* out;
     int out_f32;
     float* out_lse;
+    void* workspace;
+    size_t workspace_bytes;
     void* stream;
 };
 
 int csa_launch(const CsaLaunch& a);
+size_t csa_workspace_bytes(int bs, int nq, int q_f32);
 int csa_cluster_size(int64_t entries_per_seq);
 int csa_kv_quantize_launch(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
                            cudaStream_t st);
