@@ -240,10 +240,9 @@ class GqaDense(Workload):
             self.out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(B, H, dtype=torch.float32, device=dev)
         else:
-            self.part_o = torch.empty(B * H, D, dtype=torch.float32, device=dev)
-            self.part_l = torch.empty(B * H, dtype=torch.float32, device=dev)
-            self.all_o = torch.empty(world, B * H, D, dtype=torch.float32, device=dev)
-            self.all_l = torch.empty(world, B * H, dtype=torch.float32, device=dev)
+            from scope_b200.shard import PartialExchange
+            self.ex = PartialExchange(B * H, D, world, dev)
+            self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
             self.out = torch.empty(B * H, D, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(B * H, dtype=torch.float32, device=dev)
         nbytes = self.lib.ws_gqa_decode_workspace_size(rows, self.G, D, self.Lloc)
@@ -283,11 +282,7 @@ class GqaDense(Workload):
     def step(self, i):
         self.kernel(i)
         if self.world > 1:
-            import torch.distributed as dist
-            from scope_b200 import lse_merge
-            dist.all_gather_into_tensor(self.all_o.view(-1), self.part_o.view(-1))
-            dist.all_gather_into_tensor(self.all_l.view(-1), self.part_l.view(-1))
-            lse_merge(self.all_o, self.all_l, torch.bfloat16, out=self.out, out_lse=self.lse)
+            self.ex.step(torch.bfloat16, out=self.out, out_lse=self.lse)
 
     def e2e_step(self, i):
         c = i % self.copies
@@ -478,7 +473,8 @@ class Csa(Workload):
         self.scale = 512 ** -0.5
         self.workload = f"csa_ds4_b{bs}_h{nH}_nc{nc}_top{k}_int8"
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.lo, self.hi = nc * rank // world, nc * (rank + 1) // world
+        from scope_b200.shard import shard_bounds
+        self.lo, self.hi = shard_bounds(nc, world, rank)
         ncl = self.hi - self.lo
         shard_bytes = bs * ncl * (512 + 4)
         self.n_kv = max(1, -(-3 * L2_BYTES // shard_bytes))
@@ -503,10 +499,9 @@ class Csa(Workload):
             self.out = torch.empty(bs, nH, 512, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(bs, nH, dtype=torch.float32, device=dev)
         else:
-            self.part_o = torch.empty(bs * nH, 512, dtype=torch.float32, device=dev)
-            self.part_l = torch.empty(bs * nH, dtype=torch.float32, device=dev)
-            self.all_o = torch.empty(world, bs * nH, 512, dtype=torch.float32, device=dev)
-            self.all_l = torch.empty(world, bs * nH, dtype=torch.float32, device=dev)
+            from scope_b200.shard import PartialExchange
+            self.ex = PartialExchange(bs * nH, 512, world, dev)
+            self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
             self.out = torch.empty(bs * nH, 512, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(bs * nH, dtype=torch.float32, device=dev)
         self.ws = torch.zeros(self.lib.ws_csa_decode_workspace_size(bs, nH, self._lib.WS_DTYPE_BF16),
@@ -550,16 +545,12 @@ class Csa(Workload):
     def step(self, i):
         self.kernel(i)
         if self.world > 1:
-            import torch.distributed as dist
-            from scope_b200 import lse_merge
-            dist.all_gather_into_tensor(self.all_o.view(-1), self.part_o.view(-1))
-            dist.all_gather_into_tensor(self.all_l.view(-1), self.part_l.view(-1))
-            lse_merge(self.all_o, self.all_l, torch.bfloat16, out=self.out, out_lse=self.lse)
+            self.ex.step(torch.bfloat16, out=self.out, out_lse=self.lse)
 
     def e2e_step(self, i):
         """Through the public API: q and the step's top-k ids come from host
         memory, out and lse go back to it."""
-        from scope_b200 import csa_attn, lse_merge
+        from scope_b200 import csa_attn
         c, kvc = i % self.n_sets, i % self.n_kv
         q, idx = self.q[c], self.idx[c]
         q.copy_(self.q_host, non_blocking=True)
@@ -567,12 +558,11 @@ class Csa(Workload):
         if self.world == 1:
             out, lse = csa_attn.csa_sparse_decode(q, self.kv[kvc], idx, self.scale, self.kv_scales[kvc])
         else:
-            import torch.distributed as dist
             po, pl = csa_attn.csa_sparse_decode(q, self.kv[kvc], idx, self.scale, self.kv_scales[kvc],
                                                 shard_lo=self.lo, idx_mode="sorted_shard", out_dtype=torch.float32)
-            dist.all_gather_into_tensor(self.all_o.view(-1), po.view(-1))
-            dist.all_gather_into_tensor(self.all_l.view(-1), pl.view(-1))
-            out, lse = lse_merge(self.all_o, self.all_l, torch.bfloat16)
+            self.ex.part_o.copy_(po.view(-1, 512))
+            self.ex.part_l.copy_(pl.view(-1))
+            out, lse = self.ex.step(torch.bfloat16)
         if self.rank == 0:
             self.out_host.copy_(out.view(-1), non_blocking=True)
             self.lse_host.copy_(lse.view(-1), non_blocking=True)
