@@ -172,8 +172,9 @@ size_t ws_mla_decode_workspace_size(int B, int nH, int S);
  *   (WS_DTYPE_F32 or WS_DTYPE_BF16), out_lse [bs, nq] fp32 (may be NULL).
  * A row with no entry gives out = 0, lse = -inf (the partial of an empty
  * shard).  One launch; the workspace (ws_csa_decode_workspace_size bytes,
- * 16-byte aligned, no zeroing needed) carries the partials the CTAs of a
- * sequence exchange.
+ * 16-byte aligned) carries the partials the CTAs of a sequence exchange,
+ * after the counter header, which this entry never touches (so one zeroed
+ * workspace can serve it and the GQA / MLA entries in turn).
  */
 int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void* kv, int kv_dtype,
                   const float* kv_scales, int64_t nc, int64_t shard_lo, const int32_t* idx, int k, int idx_mode,
@@ -204,6 +205,12 @@ int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float*
  */
 int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D,
                  void* out, int out_dtype, float* out_lse, void* stream);
+/* The same with partial p's o rows at o_parts + p * o_part_stride and its lse
+ * values at lse_parts + p * lse_part_stride (elements): the layout of one
+ * all_gather over per-rank blocks [o (R*D), lse (R)], merged in place. */
+int ws_lse_merge_strided(const float* o_parts, int64_t o_part_stride, const float* lse_parts,
+                         int64_t lse_part_stride, int P, int64_t R, int D, void* out, int out_dtype,
+                         float* out_lse, void* stream);
 
 #ifdef __cplusplus
 }

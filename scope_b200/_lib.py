@@ -59,6 +59,7 @@ SIGNATURES = {
     "ws_gqa_decode_shares": (_i, [_V, _i, _i, _i, _i, _i, _f, ctypes.POINTER(KvShare), _i, _V, _V, _V, _sz, _V]),
     "ws_gqa_decode_shares_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "ws_lse_merge": (_i, [_V, _V, _i, _i64, _i, _V, _i, _V, _V]),
+    "ws_lse_merge_strided": (_i, [_V, _i64, _V, _i64, _i, _i64, _i, _V, _i, _V, _V]),
     "ws_gqa_decode_noalloc": (_i, [_V, _V, _V, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _i, _f, _i,
                                    _V, _V, _V, _V, _V]),
     "ws_gqa_decode_noalloc_max_scratch": (_sz, []),

@@ -313,7 +313,20 @@ int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R,
     if (R == 0) return WS_OK;
     if (!o_parts || !lse_parts || !out) return set_error(WS_ERR_INVALID_ARG, "null pointer");
     if (out_dtype != WS_DTYPE_BF16 && out_dtype != WS_DTYPE_F32) return set_error(WS_ERR_INVALID_ARG, "bad out dtype");
-    return lse_merge_launch(o_parts, lse_parts, P, R, D, out, out_dtype, out_lse, static_cast<cudaStream_t>(stream));
+    return lse_merge_launch(o_parts, R * D, lse_parts, R, P, R, D, out, out_dtype, out_lse,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int ws_lse_merge_strided(const float* o_parts, int64_t o_part_stride, const float* lse_parts,
+                         int64_t lse_part_stride, int P, int64_t R, int D, void* out, int out_dtype, float* out_lse,
+                         void* stream) {
+    if (P < 1 || R < 0 || D < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");
+    if (o_part_stride < R * D || lse_part_stride < R) return set_error(WS_ERR_INVALID_ARG, "part strides too small");
+    if (R == 0) return WS_OK;
+    if (!o_parts || !lse_parts || !out) return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    if (out_dtype != WS_DTYPE_BF16 && out_dtype != WS_DTYPE_F32) return set_error(WS_ERR_INVALID_ARG, "bad out dtype");
+    return lse_merge_launch(o_parts, o_part_stride, lse_parts, lse_part_stride, P, R, D, out, out_dtype, out_lse,
+                            static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -840,7 +840,9 @@ size_t csa_workspace_bytes(int bs, int nq, int q_f32) {
     using namespace csa;
     const int NQ = q_f32 ? Cfg<true>::NQ : Cfg<false>::NQ;
     const int64_t clusters = (int64_t)bs * ((nq + NQ - 1) / NQ);
-    return (size_t)std::max<int64_t>(clusters, 1) * kMaxCs * (NQ * HD + 2 * NQ) * sizeof(float);
+    // the partials follow the fixed counter header every workspace starts with (left untouched here),
+    // so one workspace can serve this kernel and the kernels whose merge tickets live in that header
+    return kCounterHeaderBytes + (size_t)std::max<int64_t>(clusters, 1) * kMaxCs * (NQ * HD + 2 * NQ) * sizeof(float);
 }
 
 int csa_launch(const CsaLaunch& a) {
@@ -872,7 +874,7 @@ int csa_launch(const CsaLaunch& a) {
     p.out = a.out;
     p.out_f32 = a.out_f32;
     p.out_lse = a.out_lse;
-    p.ws = static_cast<float*>(a.workspace);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
     p.status = device_status_word();
     // entries one sequence selects (a sharded sorted list selects about k * nc_local / nc; k bounds it)
     const int64_t per_seq = a.idx ? (int64_t)a.k : p.dense_end - p.dense_begin;

@@ -9,7 +9,8 @@ and lse fp32; a rank whose range holds nothing of a row gives o = 0 and
 lse = -inf.  The ranks then exchange the partials with one all_gather and merge
 them by log-sum-exp -- the merge the reference's runtimes do on the host
 (system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464) -- here on
-the device with ws_lse_merge.  There is no other collective on the path.
+the device with ws_lse_merge_strided, straight from the gathered blocks.
+There is no other collective on the path.
 """
 from __future__ import annotations
 
@@ -37,28 +38,42 @@ def local_ids(ids: torch.Tensor, lo: int, hi: int) -> torch.Tensor:
 class PartialExchange:
     """Buffers and the exchange step for R query rows of width D over `world` ranks.
 
-    part_o [R, D] / part_l [R] are where this rank's kernel writes its partial;
-    ``gather()`` all-gathers them into all_o [world, R, D] / all_l [world, R];
-    ``merge()`` reduces those by log-sum-exp (ws_lse_merge by default).
+    This rank's kernel writes its partial into part_o [R, D] and part_l [R],
+    which are views of one block [o (R*D), lse (R)], so ``gather()`` is a single
+    all_gather into [world, R*D + R]; ``merge()`` reduces that in place by
+    log-sum-exp (ws_lse_merge_strided by default).
     """
 
     def __init__(self, rows: int, dim: int, world: int, device, group=None):
-        self.world, self.group = world, group
-        self.part_o = torch.empty(rows, dim, dtype=torch.float32, device=device)
-        self.part_l = torch.empty(rows, dtype=torch.float32, device=device)
-        self.all_o = torch.empty(world, rows, dim, dtype=torch.float32, device=device)
-        self.all_l = torch.empty(world, rows, dtype=torch.float32, device=device)
+        self.world, self.group, self.rows, self.dim = world, group, rows, dim
+        self.block = rows * dim + rows
+        self.part = torch.empty(self.block, dtype=torch.float32, device=device)
+        self.part_o = self.part[:rows * dim].view(rows, dim)
+        self.part_l = self.part[rows * dim:]
+        self.all = torch.empty(world, self.block, dtype=torch.float32, device=device)
+        self.all_o = self.all[:, :rows * dim].view(world, rows, dim)   # strided views of the gathered blocks
+        self.all_l = self.all[:, rows * dim:]
 
     def gather(self) -> None:
-        dist.all_gather_into_tensor(self.all_o.view(-1), self.part_o.view(-1), group=self.group)
-        dist.all_gather_into_tensor(self.all_l.view(-1), self.part_l.view(-1), group=self.group)
+        dist.all_gather_into_tensor(self.all.view(-1), self.part, group=self.group)
 
-    def merge(self, out_dtype=torch.bfloat16, out=None, out_lse=None,
-              merge_fn: Callable | None = None):
-        if merge_fn is None:
-            from .ops import lse_merge
-            merge_fn = lse_merge
-        return merge_fn(self.all_o, self.all_l, out_dtype, out=out, out_lse=out_lse)
+    def merge(self, out_dtype=torch.bfloat16, out=None, out_lse=None, merge_fn: Callable | None = None):
+        if merge_fn is not None:
+            return merge_fn(self.all_o.contiguous(), self.all_l.contiguous(), out_dtype, out=out, out_lse=out_lse)
+        from . import _lib
+        from ._lib import check, lib, ptr, stream_ptr
+        dev = self.all.device
+        if out is None:
+            out = torch.empty(self.rows, self.dim, dtype=out_dtype, device=dev)
+        if out_lse is None:
+            out_lse = torch.empty(self.rows, dtype=torch.float32, device=dev)
+        code = _lib.WS_DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.WS_DTYPE_F32
+        with torch.cuda.device(dev):
+            rc = lib().ws_lse_merge_strided(ptr(self.all), self.block, ptr(self.all) + 4 * self.rows * self.dim,
+                                            self.block, self.world, self.rows, self.dim, ptr(out), code,
+                                            ptr(out_lse), stream_ptr(dev))
+        check(rc, "ws_lse_merge_strided")
+        return out, out_lse
 
     def step(self, out_dtype=torch.bfloat16, out=None, out_lse=None, merge_fn: Callable | None = None):
         self.gather()

@@ -305,3 +305,21 @@ def test_cfg5_size():
                                   torch.stack([p[1].reshape(-1) for p in parts]), torch.float32)
     assert (mo - o.float().reshape(-1, 512)).abs().max().item() < 2e-2
     assert (ml - lse.reshape(-1)).abs().max().item() < 1e-4
+
+
+def test_workspace_pool_shared_with_gqa():
+    """The CSA kernel's partials live past the counter header of the pooled
+    workspace, so a GQA decode (whose merge tickets use that header) that
+    follows a CSA call on the same stream stays exact."""
+    ext = scope_b200.build()
+    q, kv, sc, idx = rand_case(2, 64, 3000, 900, seed=91, int8=True, q_bf16=True)
+    scope_b200.csa_attn.csa_sparse_decode(q.to(DEV), kv.to(DEV), idx.to(DEV), 0.05, sc.to(DEV))
+    g = torch.Generator().manual_seed(92)
+    qg = torch.randn(8, 4, 128, generator=g).bfloat16()
+    k = torch.randn(8, 3000, 128, generator=g).bfloat16()
+    v = torch.randn(8, 3000, 128, generator=g).bfloat16()
+    for _ in range(2):
+        o, m, s = ext.fused_cpu_attn_mla(qg.to(DEV), k.to(DEV), v.to(DEV), 128 ** -0.5)
+        ro, rm, rs = oracle.gqa_decode(oracle.bf16_bits(qg), oracle.bf16_bits(k), oracle.bf16_bits(v), 128 ** -0.5)
+        assert np.abs((o / s).cpu().numpy() - ro).max() < TOL_OUT
+        scope_b200.csa_attn.csa_sparse_decode(q.to(DEV), kv.to(DEV), idx.to(DEV), 0.05, sc.to(DEV))
