@@ -462,7 +462,7 @@ class Csa(Workload):
     so the rows one step reads were last read many steps (and > L2 bytes) ago."""
 
     name = "cfg5"
-    kernel_name = "csa_decode_kernel<int8,bf16 q> (tcgen05, cluster/DSMEM merge)"
+    kernel_name = "csa_decode_kernel<int8,bf16 q> (tcgen05, clusters, L2 exchange)"
     profile_name = "csa_decode_cfg5"
     graph = True
 
