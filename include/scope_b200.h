@@ -195,6 +195,24 @@ int ws_csa_kv_quantize_s8(const void* kv, int64_t rows, int hd, void* out, float
                           void* stream);
 int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float* scales, void* stream);
 
+/* ---- indexer top-k orders */
+#define WS_TOPK_BY_SCORE 0   /* descending score, ties: lower id first (the reference's partial_sort order) */
+#define WS_TOPK_BY_ID 1      /* ascending id: the layout WS_CSA_IDX_SORTED_SHARD wants */
+
+/*
+ * Indexer top-k of the CSA path.  Replaces indexer_topk_cpu / indexer_topk_cpu_par
+ * (kernel/cpu_attn_ds4_ext/csa_attn.cpp:1658-1817).
+ *   q [bs, nH, hd], kv [bs, nc, hd] in dtype (WS_DTYPE_F32 or WS_DTYPE_BF16), w [bs, nH] fp32
+ *   score[b, j] = sum_h w[b, h] * relu(q[b, h] . kv[b, j])   (fp32)
+ *   out_ids [bs, min(k, nc)] int32 in `order`; out_scores [bs, nc] fp32 (optional: NULL keeps them in the
+ *   workspace of ws_indexer_topk_workspace_size bytes, which is then required).
+ * nH <= 64, hd % 16 == 0 and <= 256, k <= 4096.  Two launches.
+ */
+int ws_indexer_topk(const void* q, const void* kv, int dtype, const float* w, int bs, int nH, int hd, int64_t nc,
+                    int k, int order, int32_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                    void* stream);
+size_t ws_indexer_topk_workspace_size(int bs, int64_t nc);
+
 /*
  * Log-sum-exp merge of P partial attention results (the cross-GPU combine of
  * a sequence-sharded KV cache, and the runtime merges it replaces:

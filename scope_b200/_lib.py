@@ -34,6 +34,9 @@ WS_CSA_IDX_ALL = 0
 WS_CSA_IDX_SORTED_SHARD = 1
 WS_CSA_IDX_SHARD = 2
 
+WS_TOPK_BY_SCORE = 0
+WS_TOPK_BY_ID = 1
+
 _V = ctypes.c_void_p
 _i = ctypes.c_int
 _i64 = ctypes.c_int64
@@ -70,6 +73,8 @@ SIGNATURES = {
     "ws_csa_decode": (_i, [_V, _i, _i, _i, _i, _V, _i, _V, _i64, _i64, _V, _i, _i, _i64, _i64, _f, _V, _i, _V,
                            _V, _sz, _V]),
     "ws_csa_decode_workspace_size": (_sz, [_i, _i, _i]),
+    "ws_indexer_topk": (_i, [_V, _V, _i, _V, _i, _i, _i, _i64, _i, _i, _V, _V, _V, _sz, _V]),
+    "ws_indexer_topk_workspace_size": (_sz, [_i, _i64]),
 }
 
 _lib = None

@@ -290,3 +290,58 @@ def csa_sparse_decode(q, kv, topk_idxs, scale, kv_scales=None, *, shard_lo: int 
         raise ValueError(f"idx_mode must be one of {sorted(_IDX_MODES)}")
     _launch(q, kv, scale, out, lse, idx=topk_idxs, kv_scales=kv_scales, shard_lo=shard_lo, idx_mode=idx_mode)
     return out, lse
+
+
+# ------------------------------------------------------------ indexer top-k
+def indexer_topk(q_idx, kv_idx, weights, k: int, order: str = "score", return_scores: bool = False):
+    """Indexer top-k (csa_attn.cpp:1658-1817) on the device.
+
+    q_idx [bs, nH, hd] and kv_idx [bs, nc, hd] fp32 or bf16 (alike), weights
+    [bs, nH] fp32; score = sum_h w_h * relu(q_h . kv_j) in fp32.  Returns ids
+    int32 [bs, min(k, nc)] in descending score order (ties: lower id first) or,
+    with ``order="id"``, ascending (the layout the sharded CSA decode wants);
+    with ``return_scores`` also the scores fp32 [bs, nc].
+    """
+    _require_cuda("indexer_topk", q_idx, kv_idx, weights)
+    if q_idx.dim() != 3 or kv_idx.dim() != 3:
+        raise RuntimeError("q_idx/kv_idx must be 3D")
+    if q_idx.dtype != kv_idx.dtype or q_idx.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("q_idx and kv_idx must both be fp32 or both bf16")
+    if not (q_idx.is_contiguous() and kv_idx.is_contiguous() and weights.is_contiguous()):
+        raise RuntimeError("must be contiguous")
+    bs, nH, hd = q_idx.shape
+    nc = kv_idx.shape[1]
+    if kv_idx.shape[0] != bs or kv_idx.shape[2] != hd or tuple(weights.shape) != (bs, nH):
+        raise RuntimeError("shape mismatch")
+    if weights.dtype != torch.float32:
+        raise RuntimeError("weights must be fp32")
+    if hd % 16:
+        raise RuntimeError("hd must be multiple of 16")
+    if order not in ("score", "id"):
+        raise ValueError("order must be 'score' or 'id'")
+    k = min(int(k), nc)
+    dev = q_idx.device
+    ids = torch.empty(bs, k, dtype=torch.int32, device=dev)
+    scores = torch.empty(bs, nc, dtype=torch.float32, device=dev) if return_scores else None
+    code = _lib.WS_DTYPE_F32 if q_idx.dtype == torch.float32 else _lib.WS_DTYPE_BF16
+    with torch.cuda.device(dev):
+        L_ = lib()
+        ws = workspaces.get(L_.ws_indexer_topk_workspace_size(bs, nc), dev)
+        rc = L_.ws_indexer_topk(ptr(q_idx), ptr(kv_idx), code, ptr(weights), bs, nH, hd, nc, k,
+                                _lib.WS_TOPK_BY_ID if order == "id" else _lib.WS_TOPK_BY_SCORE,
+                                ptr(ids), ptr(scores), ptr(ws), ws.numel(), stream_ptr(dev))
+    check(rc, "ws_indexer_topk")
+    return (ids, scores) if return_scores else ids
+
+
+def indexer_topk_cpu(q_idx, kv_idx, weights, k: int, n_threads: int = 0):
+    """Drop-in for indexer_topk_cpu (csa_attn.cpp:1658-1736): fp32 inputs,
+    ids int32 [bs, min(k, nc)] by descending score."""
+    if q_idx.dtype != torch.float32 or kv_idx.dtype != torch.float32:
+        raise RuntimeError("must be fp32")
+    return indexer_topk(q_idx, kv_idx, weights, k)
+
+
+def indexer_topk_cpu_par(q_idx, kv_idx, weights, k: int, n_threads: int = 0):
+    """Drop-in for indexer_topk_cpu_par (csa_attn.cpp:1738-1817); same result."""
+    return indexer_topk(q_idx, kv_idx, weights, k)

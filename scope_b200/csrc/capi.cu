@@ -307,6 +307,24 @@ int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float*
     return csa_q_quantize_launch(q, rows, hd, out, scales, static_cast<cudaStream_t>(stream));
 }
 
+size_t ws_indexer_topk_workspace_size(int bs, int64_t nc) { return indexer_workspace_bytes(bs, nc); }
+
+int ws_indexer_topk(const void* q, const void* kv, int dtype, const float* w, int bs, int nH, int hd, int64_t nc,
+                    int k, int order, int32_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+    if (bs < 0 || nH < 1 || hd < 1 || nc < 0 || k < 0) return set_error(WS_ERR_INVALID_ARG, "indexer_topk: bad shape");
+    if (bs > 65535) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: bs > 65535");
+    if (dtype != WS_DTYPE_F32 && dtype != WS_DTYPE_BF16) return set_error(WS_ERR_INVALID_ARG, "indexer_topk: dtype");
+    if (order != WS_TOPK_BY_SCORE && order != WS_TOPK_BY_ID) return set_error(WS_ERR_INVALID_ARG, "indexer_topk: order");
+    k = (int)std::min<int64_t>(k, nc);   // as the reference: k = min(k, nc)
+    if (bs == 0 || nc == 0) return WS_OK;
+    if (!q || !kv || !w || (k > 0 && !out_ids)) return set_error(WS_ERR_INVALID_ARG, "indexer_topk: null pointer");
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv)) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "indexer_topk: q and kv must be 16-byte aligned");
+    return indexer_topk_launch(q, kv, dtype == WS_DTYPE_BF16, w, bs, nH, hd, nc, k, order == WS_TOPK_BY_ID, out_ids,
+                               out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out, int out_dtype,
                  float* out_lse, void* stream) {
     if (P < 1 || R < 0 || D < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");

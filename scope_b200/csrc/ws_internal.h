@@ -99,6 +99,11 @@ int csa_kv_quantize_launch(const void* kv, int64_t rows, int hd, void* out, floa
                            cudaStream_t st);
 int csa_q_quantize_launch(const float* q, int64_t rows, int hd, void* out, float* scales, cudaStream_t st);
 
+size_t indexer_workspace_bytes(int bs, int64_t nc);
+int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w, int bs, int nH, int hd, int64_t nc,
+                        int k, int by_id, int32_t* out_ids, float* out_scores, void* workspace,
+                        size_t workspace_bytes, cudaStream_t st);
+
 int lse_merge_launch(const float* o_parts, int64_t o_part_stride, const float* lse_parts, int64_t lse_part_stride,
                      int P, int64_t R, int D, void* out, int out_dtype, float* out_lse, cudaStream_t st);
 

@@ -1,0 +1,111 @@
+"""GPU parity of the indexer top-k (ws_indexer_topk) against the reference's
+golden output (indexer_topk_cpu, kernel/cpu_attn_ds4_ext/csa_attn.cpp:1658-1736)
+and the float64 oracle.
+
+Scores are fp32 sums in a different order than the reference's AVX-512 sums,
+so the selected set is checked up to near-ties at the k-th score: every
+selected entry scores at least s_k - eps and every other entry at most
+s_k + eps (eps = 1e-5 of the score scale); exact ties are ordered by id.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import scope_b200
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def csa():
+    return scope_b200.build_csa_attn()
+
+
+def check_selection(ids, scores_ref, k, order="score", our_scores=None):
+    bs = scores_ref.shape[0]
+    for b in range(bs):
+        s = scores_ref[b]
+        sel = ids[b]
+        assert len(set(sel.tolist())) == len(sel) == min(k, s.shape[0])
+        eps = 1e-5 * (np.abs(s).max() + 1.0)
+        t = np.sort(s)[::-1][len(sel) - 1]
+        mask = np.zeros(s.shape[0], bool)
+        mask[sel] = True
+        assert s[mask].min() >= t - eps
+        if (~mask).any():
+            assert s[~mask].max() <= t + eps
+        if order == "id":
+            assert np.all(np.diff(sel) > 0)
+        elif our_scores is not None:
+            o = our_scores[b][sel]
+            assert np.all(np.diff(o) <= 0)
+            ties = np.diff(o) == 0
+            assert np.all(np.diff(sel)[ties] > 0)
+
+
+def rand_case(bs, nH, hd, nc, seed, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(bs, nH, hd, generator=g)
+    kv = torch.randn(bs, nc, hd, generator=g)
+    w = torch.rand(bs, nH, generator=g) - 0.3     # some negative weights, as a learned projection gives
+    if dtype == torch.bfloat16:
+        q, kv = q.bfloat16(), kv.bfloat16()
+    return q, kv, w
+
+
+def oracle_scores(q, kv, w, k):
+    ids, sc = oracle.indexer_topk(q.float().numpy(), kv.float().numpy(), w.numpy(), k)
+    return ids, sc
+
+
+def test_golden(csa, golden):
+    g = golden("indexer_topk")
+    k = int(g["k"])
+    ids = csa.indexer_topk_cpu(torch.from_numpy(g["q_idx"]).to(DEV), torch.from_numpy(g["kv_idx"]).to(DEV),
+                               torch.from_numpy(g["weights"]).to(DEV), k)
+    assert ids.dtype == torch.int32 and tuple(ids.shape) == (g["ids"].shape[0], k)
+    _, sc = oracle.indexer_topk(g["q_idx"], g["kv_idx"], g["weights"], k)
+    check_selection(ids.cpu().numpy(), sc, k)
+    for b in range(ids.shape[0]):     # the reference's own set
+        assert set(ids[b].tolist()) == set(g["ids"][b].tolist())
+
+
+@pytest.mark.parametrize("bs,nH,hd,nc,k", [(1, 1, 16, 10, 3), (2, 4, 64, 200, 16), (3, 8, 128, 5000, 100),
+                                           (2, 64, 128, 20000, 2048), (1, 16, 256, 4096, 4096),
+                                           (2, 5, 48, 777, 777), (1, 3, 32, 100, 500)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_random(csa, bs, nH, hd, nc, k, dtype):
+    q, kv, w = rand_case(bs, nH, hd, nc, seed=bs * 7919 + nc + k, dtype=dtype)
+    ids, our = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), k, return_scores=True)
+    _, sc = oracle_scores(q, kv, w, k)
+    our = our.cpu().numpy()
+    assert np.abs(our - sc).max() <= 1e-5 * (np.abs(sc).max() + 1.0)
+    check_selection(ids.cpu().numpy(), sc, k, our_scores=our)
+    ids_id = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), k, order="id")
+    check_selection(ids_id.cpu().numpy(), sc, k, order="id")
+    assert all(set(a.tolist()) == set(b.tolist()) for a, b in zip(ids.cpu(), ids_id.cpu()))
+
+
+def test_exact_ties_take_lower_ids_first():
+    g = torch.Generator().manual_seed(3)
+    nc, hd = 1000, 32
+    base = torch.randn(10, hd, generator=g)
+    kv = base[torch.randint(0, 10, (nc,), generator=g)][None]       # only 10 distinct rows: many exact ties
+    q = torch.randn(1, 2, hd, generator=g)
+    w = torch.ones(1, 2)
+    ids, our = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.contiguous().to(DEV), w.to(DEV), 150,
+                                                return_scores=True)
+    ids, our = ids.cpu().numpy()[0], our.cpu().numpy()[0]
+    order = sorted(range(nc), key=lambda j: (-our[j], j))[:150]     # descending score, then ascending id
+    assert ids.tolist() == order
+
+
+def test_ds4_size():
+    """A DeepSeek-V4-like indexer shape: 64 index heads x 128 dims over 65536
+    compressed entries, top-2048, two sequences against the oracle."""
+    q, kv, w = rand_case(2, 64, 128, 65536, seed=11)
+    ids = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), 2048)
+    _, sc = oracle_scores(q, kv, w, 2048)
+    check_selection(ids.cpu().numpy(), sc, 2048)
