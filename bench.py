@@ -21,6 +21,7 @@ Workloads (the default is the one the metric's
   cfg4  GQA Qwen3, B=32, L=131072 sequence-sharded over N GPUs (default)
   cfg5  CSA sparse decode, DeepSeek-V4 style: bs=16, 64 heads, 65536 int8
         entries, top-2048 gather, entry-sharded over N GPUs
+  idx   the CSA indexer top-k that produces cfg5's ids (one GPU)
 """
 from __future__ import annotations
 
@@ -586,6 +587,72 @@ class Csa(Workload):
         return cpu_ref_csa(self.bs, self.nH, self.nc, self.k, budget_s, max_calls, warm)
 
 
+class Indexer(Workload):
+    """idx: the CSA indexer top-k that produces cfg5's ids (SURVEY "next" row):
+    bs=16 sequences, 64 index heads x 128 dims over nc=65536 compressed entries,
+    bf16 q/kv (the dtype the DeepSeek-V4 runtime passes, system/ds4offload.py:95-125),
+    fp32 weights, top-2048 by descending score (ws_indexer_topk: scoring kernel +
+    select kernel).  Inputs larger than L2 (256 MiB of kv)."""
+
+    name = "idx"
+    kernel_name = "indexer_score_kernel<bf16> (fp32 FMA) + indexer_select_kernel"
+    profile_name = "indexer_topk_idx"
+    graph = True
+
+    def __init__(self, world, rank, bs=16, nH=64, hd=128, nc=65536, k=2048, seed=6):
+        from scope_b200 import _lib
+        self.world, self.rank = world, rank
+        self.bs, self.nH, self.hd, self.nc, self.k = bs, nH, hd, nc, k
+        self.workload = f"indexer_ds4_b{bs}_h{nH}_d{hd}_nc{nc}_top{k}_bf16"
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.copies = max(1, -(-3 * L2_BYTES // (bs * nc * hd * 2)))
+        self.kv = [bf16_randn((bs, nc, hd), g, dev) for _ in range(self.copies)]
+        self.q = bf16_randn((bs, nH, hd), g, dev)
+        self.w = torch.rand(bs, nH, generator=g, device=dev)
+        self.ids = torch.empty(bs, k, dtype=torch.int32, device=dev)
+        self.lib, self._lib = _lib.lib(), _lib
+        self.ws = torch.zeros(self.lib.ws_indexer_topk_workspace_size(bs, nc), dtype=torch.uint8, device=dev)
+        self.q_host = torch.randn(bs, nH, hd).bfloat16().pin_memory()
+        self.ids_host = torch.empty(bs, k, dtype=torch.int32).pin_memory()
+        self.kernels_per_step = 2
+
+    def kernel_bytes(self):
+        return self.bs * self.nc * self.hd * 2 + self.bs * self.nH * (self.hd * 2 + 4) + self.bs * self.k * 4
+
+    def kernel_flops(self):
+        return 2 * self.bs * self.nc * self.nH * self.hd
+
+    def kernel(self, i):
+        kv = self.kv[i % self.copies]
+        rc = self.lib.ws_indexer_topk(self.q.data_ptr(), kv.data_ptr(), self._lib.WS_DTYPE_BF16, self.w.data_ptr(),
+                                      self.bs, self.nH, self.hd, self.nc, self.k, self._lib.WS_TOPK_BY_SCORE,
+                                      self.ids.data_ptr(), None, self.ws.data_ptr(), self.ws.numel(),
+                                      torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(self.lib.ws_last_error().decode())
+
+    step = kernel
+
+    def e2e_step(self, i):
+        from scope_b200 import csa_attn
+        self.q.copy_(self.q_host, non_blocking=True)
+        ids = csa_attn.indexer_topk(self.q, self.kv[i % self.copies], self.w, self.k)
+        self.ids_host.copy_(ids, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.q_host.numel() * 2, self.ids_host.numel() * 4
+
+    def config(self):
+        return {"workload": self.workload, "batch": self.bs, "index_heads": self.nH, "head_dim": self.hd,
+                "n_compressed": self.nc, "topk": self.k, "dtype_in": "bf16 q/kv, fp32 weights, fp32 math",
+                "parallelism": "single-gpu", "l2": f"{self.copies} rotating kv copies > 3x L2",
+                "timing": "cuda-graph replay"}
+
+    def cpu_reference(self, budget_s, max_calls, warm=1):
+        return cpu_ref_indexer(self.bs, self.nH, self.hd, self.nc, self.k, budget_s, max_calls, warm)
+
+
 # ------------------------------------------------- reference CPU measurements
 def cfg2_geometry(B=16, seed=2):
     """Seeded ragged lengths ~ U[1024, 32768] and share ratios in {.25, .5, .75}."""
@@ -709,6 +776,28 @@ def cpu_ref_csa(bs, nH, nc, k, budget_s, max_calls, warm=1):
                                   f"entries (full cfg5 step, {nbytes / 1e6:.1f} MB algorithmic)"}
 
 
+def cpu_ref_indexer(bs, nH, hd, nc, k, budget_s, max_calls, warm=1):
+    """The reference's indexer_topk_cpu (csa_attn.cpp:1658-1736) on all cores,
+    fp32 copies of the same shapes (the reference op takes fp32)."""
+    import oracle
+    torch.manual_seed(16)
+    q = torch.randn(bs, nH, hd)
+    kv = torch.randn(bs, nc, hd)
+    w = torch.rand(bs, nH)
+    nbytes = bs * nc * hd * 2 + bs * nH * (hd * 2 + 4) + bs * k * 4
+    ref = load_cpu_ref("csa_attn_kernel")
+    n = os.cpu_count() or 1
+    if ref is not None:
+        kind, fn = "reference", (lambda: ref.indexer_topk_cpu(q, kv, w, k, n))
+    else:
+        qn, kvn, wn = q.numpy(), kv.numpy(), w.numpy()
+        kind, fn = "port", (lambda: oracle.indexer_topk(qn, kvn, wn, k))
+    t, calls = median_time(fn, budget_s, max_calls, warm)
+    return nbytes / t, {"kind": kind, "cores": n, "calls": calls, "sec_per_call": t,
+                        "sample": f"indexer_topk_cpu fp32, bs={bs}, nH={nH}, hd={hd}, nc={nc}, k={k} (full step; "
+                                  f"bytes counted as the bf16 GPU workload's)"}
+
+
 def cpu_reference_for(name, args, budget_s, max_calls, warm):
     if name == "cfg4":
         return cpu_ref_dense(32, 4, 8, 128, args.kv_len or 131072, budget_s, max_calls, warm), \
@@ -722,6 +811,9 @@ def cpu_reference_for(name, args, budget_s, max_calls, warm):
         return cpu_ref_mla(8, 16, 16384, budget_s, max_calls, warm), "mla_absorbed_ds2lite_b8_h16_s16384"
     if name == "cfg5":
         return cpu_ref_csa(16, 64, 65536, 2048, budget_s, max_calls, warm), "csa_ds4_b16_h64_nc65536_top2048_int8"
+    if name == "idx":
+        return cpu_ref_indexer(16, 64, 128, 65536, 2048, budget_s, max_calls, warm), \
+            "indexer_ds4_b16_h64_d128_nc65536_top2048_bf16"
     raise ValueError(name)
 
 
@@ -736,10 +828,12 @@ def make_workload(name, world, rank, args):
         return Mla(world, rank, S=args.kv_len or 16384)
     if name == "cfg5":
         return Csa(world, rank, nc=args.kv_len or 65536)
+    if name == "idx":
+        return Indexer(world, rank, nc=args.kv_len or 65536)
     raise ValueError(name)
 
 
-WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5")
+WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "idx")
 
 
 # -------------------------------------------------------------------- main

@@ -127,16 +127,44 @@ __device__ __forceinline__ int block_scan(int v, int* s_warp, int* total) {
     return before;
 }
 
+constexpr int kBatch = 16;     // scores per thread per step: four independent 16-byte loads in flight
+constexpr int kEqCap = 2048;   // ties at the threshold gathered in one pass (more: ordered scan)
+
+// The kBatch scores of step j0 this thread owns: ids j0 + 4 * (u * kSelThreads + tid) + e for u < 4, e < 4
+// (16-byte loads when the row is 16-byte aligned); keys past nc are returned as 0 with valid = false.
+__device__ __forceinline__ void load_keys(const float* sc, int64_t nc, int64_t j0, bool vec, uint32_t (&key)[kBatch],
+                                          int64_t (&id)[kBatch]) {
+#pragma unroll
+    for (int u = 0; u < kBatch / 4; ++u) {
+        const int64_t j = j0 + 4 * ((int64_t)u * kSelThreads + threadIdx.x);
+        float v[4];
+        if (vec && j + 3 < nc) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(sc + j));
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = j + e < nc ? __ldcg(sc + j + e) : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            id[4 * u + e] = j + e < nc ? j + e : -1;
+            key[4 * u + e] = ordered_key(v[e]);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float* __restrict__ scores, int64_t nc,
                                                                      int k, int by_id, int32_t* __restrict__ out) {
     __shared__ int s_hist[256];
     __shared__ int s_warp[32];
     __shared__ uint32_t s_prefix, s_mask;
-    __shared__ int s_remaining, s_ngt;
+    __shared__ int s_remaining, s_ngt, s_neq;
     __shared__ uint32_t s_key[kMaxK];
     __shared__ int32_t s_id[kMaxK];
+    __shared__ int32_t s_eq[kEqCap];
     const int b = blockIdx.x, tid = threadIdx.x;
     const float* sc = scores + (int64_t)b * nc;
+    const bool vec = (reinterpret_cast<uintptr_t>(sc) & 15) == 0;
     if (tid == 0) {
         s_prefix = 0;
         s_mask = 0;
@@ -148,14 +176,18 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
         for (int i = tid; i < 256; i += kSelThreads) s_hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix, mask = s_mask;
-        for (int64_t j0 = 0; j0 < nc; j0 += kSelThreads) {   // warp-uniform trip count (for __match_any_sync)
-            const int64_t j = j0 + tid;
-            const uint32_t key = j < nc ? ordered_key(__ldcg(sc + j)) : 0u;
-            const bool hit = j < nc && (key & mask) == prefix;
-            const int bin = hit ? (int)((key >> shift) & 255) : 256;
-            // one atomic per distinct bin in the warp: scores of similar magnitude share a few bins
-            const uint32_t same = __match_any_sync(0xffffffffu, bin);
-            if (hit && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&s_hist[bin], __popc(same));
+        for (int64_t j0 = 0; j0 < nc; j0 += (int64_t)kSelThreads * kBatch) {   // warp-uniform trip count
+            uint32_t key[kBatch];
+            int64_t id[kBatch];
+            load_keys(sc, nc, j0, vec, key, id);
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                const bool hit = id[u] >= 0 && (key[u] & mask) == prefix;
+                const int bin = hit ? (int)((key[u] >> shift) & 255) : 256;
+                // one atomic per distinct bin in the warp: scores of similar magnitude share a few bins
+                const uint32_t same = __match_any_sync(0xffffffffu, bin);
+                if (hit && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&s_hist[bin], __popc(same));
+            }
         }
         __syncthreads();
         if (tid == 0) {
@@ -175,32 +207,72 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
     }
     const uint32_t thr = s_prefix;       // the k-th largest key
     const int need_eq = s_remaining;     // keys equal to it that belong to the top k
-    if (tid == 0) s_ngt = 0;
+    if (tid == 0) {
+        s_ngt = 0;
+        s_neq = 0;
+    }
     __syncthreads();
-    // ---- collect: every key above the threshold, then the first need_eq keys equal to it, in id order
-    for (int64_t j = tid; j < nc; j += kSelThreads) {
-        const uint32_t key = ordered_key(__ldcg(sc + j));
-        if (key > thr) {
-            const int slot = atomicAdd(&s_ngt, 1);
-            if (slot < kMaxK) {
-                s_key[slot] = key;
-                s_id[slot] = (int32_t)j;
+    // ---- collect every key above the threshold, and (up to kEqCap) the ids of keys equal to it
+    for (int64_t j0 = 0; j0 < nc; j0 += (int64_t)kSelThreads * kBatch) {
+        uint32_t key[kBatch];
+        int64_t id[kBatch];
+        load_keys(sc, nc, j0, vec, key, id);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int64_t j = id[u];
+            if (j < 0) continue;
+            if (key[u] > thr) {
+                const int slot = atomicAdd(&s_ngt, 1);
+                if (slot < kMaxK) {
+                    s_key[slot] = key[u];
+                    s_id[slot] = (int32_t)j;
+                }
+            } else if (key[u] == thr) {
+                const int slot = atomicAdd(&s_neq, 1);
+                if (slot < kEqCap) s_eq[slot] = (int32_t)j;
             }
         }
     }
     __syncthreads();
     const int ngt = min(s_ngt, k);
-    int taken = 0;
-    for (int64_t j0 = 0; j0 < nc && taken < need_eq; j0 += kSelThreads) {
-        const int64_t j = j0 + tid;
-        const int eq = (j < nc && ordered_key(__ldcg(sc + j)) == thr) ? 1 : 0;
-        int total = 0;
-        const int before = block_scan(eq, s_warp, &total);
-        if (eq && taken + before < need_eq) {
-            s_key[ngt + taken + before] = thr;
-            s_id[ngt + taken + before] = (int32_t)j;
+    const int neq = s_neq;
+    if (neq <= kEqCap) {
+        // the ties, lowest ids first: sort the gathered ids ascending and take need_eq of them
+        int m2 = 1;
+        while (m2 < neq) m2 <<= 1;
+        for (int i = neq + tid; i < m2; i += kSelThreads) s_eq[i] = 0x7fffffff;
+        __syncthreads();
+        for (int size = 2; size <= m2; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = tid; i < m2 / 2; i += kSelThreads) {
+                    const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+                    const bool up = (lo & size) == 0;
+                    const int32_t a = s_eq[lo], c = s_eq[hi];
+                    if ((a < c) != up && a != c) {
+                        s_eq[lo] = c;
+                        s_eq[hi] = a;
+                    }
+                }
+                __syncthreads();
+            }
+        for (int i = tid; i < need_eq; i += kSelThreads) {
+            s_key[ngt + i] = thr;
+            s_id[ngt + i] = s_eq[i];
         }
-        taken += total;   // uniform across the block
+    } else {
+        // very many ties: take them in id order with a block-wide scan
+        int taken = 0;
+        for (int64_t j0 = 0; j0 < nc && taken < need_eq; j0 += kSelThreads) {
+            const int64_t j = j0 + tid;
+            const int eq = (j < nc && ordered_key(__ldcg(sc + j)) == thr) ? 1 : 0;
+            int total = 0;
+            const int before = block_scan(eq, s_warp, &total);
+            if (eq && taken + before < need_eq) {
+                s_key[ngt + taken + before] = thr;
+                s_id[ngt + taken + before] = (int32_t)j;
+            }
+            taken += total;   // uniform across the block
+        }
     }
     __syncthreads();
     // ---- bitonic sort of the k winners (padded to a power of two): descending key, then ascending id;
@@ -233,6 +305,162 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
     for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = s_id[i];
 }
 
+// ---------------------------------------------------------------- bf16 scoring on tcgen05
+// D[128 entries x 64 heads] = KV_tile . Q^T (M=128, N=64, K=hd) in TMEM, two D buffers; the
+// sequence's q (zero rows past nH) sits in shared memory, KV tiles stream through a TMA ring.
+// Warp 0: TMA producer; warp 1: MMA issuer (and TMEM owner); warps 2-5: epilogue
+// (thread = entry: score = sum_h w_h * relu(D[entry, h])).  One sequence per CTA, CTAs of a
+// sequence split its tiles evenly.
+namespace tc {
+constexpr int TT = 128, NHP = 64;                // entries per tile, heads padded
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int BOX = TT * 128;                    // 64 dims x 128 entries bf16 = 16 KB
+constexpr int QBOX = NHP * 128;                  // 64 dims x 64 heads = 8 KB
+enum { B_FULL = 0, B_EMPTY = kMaxStages, B_DFULL = 2 * kMaxStages, B_DEMPTY = 2 * kMaxStages + 2,
+       NBARS = 2 * kMaxStages + 4 };
+
+struct TcParams {
+    int nH, kb, stages, ctas_per_seq, kv_tok_in_dim2;
+    int64_t nc;
+    float* scores;
+    int* status;
+};
+
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* status) {
+    if (*abort) return false;
+    if (mbar_wait_bounded(bar, parity)) return true;
+    *abort = 1;
+    atomicExch(status, kDevTimeout);
+    return false;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __grid_constant__ CUtensorMap map_kv,
+                                                                       const __nv_bfloat16* __restrict__ q,
+                                                                       const float* __restrict__ w,
+                                                                       const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int KB = p.kb, ST = p.stages;
+    const int stage_bytes = KB * BOX;
+    uint8_t* s_q = sm;                                   // KB boxes of 8 KB
+    uint8_t* s_ring = sm + KB * QBOX;                    // ST stages
+    float* s_w = reinterpret_cast<float*>(s_ring + ST * stage_bytes);   // [64]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_w + NHP);
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NBARS);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+    const uint32_t bar0 = smem_u32(bars);
+#define TB(i) (bar0 + 8u * (uint32_t)(i))
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.x / p.ctas_per_seq, part = blockIdx.x - b * p.ctas_per_seq;
+    const int64_t ntl = (p.nc + TT - 1) / TT;
+    const int64_t t_begin = ntl * part / p.ctas_per_seq, t_end = ntl * (part + 1) / p.ctas_per_seq;
+    const int n = (int)(t_end - t_begin);
+
+    if (tid == 0) {
+        for (int i = 0; i < kMaxStages; ++i) {
+            mbar_init(TB(B_FULL + i), 1);
+            mbar_init(TB(B_EMPTY + i), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(TB(B_DFULL + i), 1);
+            mbar_init(TB(B_DEMPTY + i), 4);
+        }
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    // q of this sequence -> K-major swizzled bf16 [64 rows x hd] (zero rows past nH); weights (0 past nH)
+    const int hd = KB * 64;
+    for (int j = tid; j < NHP * (hd / 8); j += kThreads) {
+        const int r = j / (hd / 8), c = j - r * (hd / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < p.nH) v = __ldg(reinterpret_cast<const uint4*>(q + ((int64_t)b * p.nH + r) * hd + c * 8));
+        *reinterpret_cast<uint4*>(s_q + (c >> 3) * QBOX + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+    }
+    if (tid < NHP) s_w[tid] = tid < p.nH ? w[(int64_t)b * p.nH + tid] : 0.f;
+    if (warp == 1) tmem_alloc(smem_u32(s_tmem), 128);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *s_tmem;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        int i = 0;
+        if (lane == 0) {
+            tma_prefetch_desc(&map_kv);
+            for (; i < n; ++i) {
+                const int s = i % ST;
+                if (i >= ST && !tc_wait(TB(B_EMPTY + s), ((i / ST) - 1) & 1, s_abort, p.status)) break;
+                mbar_arrive_expect_tx(TB(B_FULL + s), stage_bytes);
+                const int tok = (int)((t_begin + i) * TT);
+                for (int kb = 0; kb < KB; ++kb)
+                    tma_load_3d(smem_u32(s_ring + s * stage_bytes + kb * BOX), &map_kv, TB(B_FULL + s), kb * 64,
+                                p.kv_tok_in_dim2 ? b : tok, p.kv_tok_in_dim2 ? tok : b);
+            }
+            if (*s_abort) {   // leave no bulk copy in flight: wait (bounded) for the last load of every slot
+                for (int s = 0; s < ST; ++s) {
+                    const int last = i - 1 - ((i - 1 - s) % ST + ST) % ST;
+                    if (last >= 0) mbar_wait_bounded(TB(B_FULL + s), (uint32_t)(last / ST) & 1, 200000000ull);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        const uint32_t id = idesc_bf16_f32(TT, NHP, false, false);
+        for (int i = 0; i < n; ++i) {
+            const int s = i % ST, d = i & 1;
+            bool ok = tc_wait(TB(B_FULL + s), (i / ST) & 1, s_abort, p.status);
+            if (ok && i >= 2) ok = tc_wait(TB(B_DEMPTY + d), ((i >> 1) - 1) & 1, s_abort, p.status);
+            if (!ok) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a0 = smem_u32(s_ring + s * stage_bytes), b0 = smem_u32(s_q);
+                for (int kb = 0; kb < KB; ++kb)
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16(tbase + d * NHP, sdesc_sw128(a0 + kb * BOX + kk * 32, 16, 1024),
+                                  sdesc_sw128(b0 + kb * QBOX + kk * 32, 16, 1024), id, (kb | kk) != 0);
+                umma_commit(TB(B_EMPTY + s));
+                umma_commit(TB(B_DFULL + d));
+            }
+            __syncwarp();
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue (thread = entry)
+        const int quad = warp & 3;                        // TMEM lane quadrant this warp may read
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        for (int i = 0; i < n; ++i) {
+            const int d = i & 1;
+            if (!tc_wait(TB(B_DFULL + d), (i >> 1) & 1, s_abort, p.status)) break;
+            tc_fence_after();
+            float x[NHP];
+#pragma unroll
+            for (int c = 0; c < NHP / 16; ++c) tmem_ld16(tbase + lane_base + d * NHP + c * 16, x + c * 16);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(TB(B_DEMPTY + d));
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int h = 0; h < NHP; h += 2) {
+                s0 = fmaf(fmaxf(x[h], 0.f), s_w[h], s0);
+                s1 = fmaf(fmaxf(x[h + 1], 0.f), s_w[h + 1], s1);
+            }
+            const int64_t j = (t_begin + i) * TT + quad * 32 + lane;
+            if (j < p.nc) p.scores[(int64_t)b * p.nc + j] = s0 + s1;
+        }
+    }
+#undef TB
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tbase, 128);
+}
+}  // namespace tc
+
 }  // namespace idx
 
 size_t indexer_workspace_bytes(int bs, int64_t nc) {
@@ -252,6 +480,48 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
         if (!workspace || workspace_bytes < indexer_workspace_bytes(bs, nc))
             return set_error(WS_ERR_WORKSPACE, "indexer_topk: workspace missing or too small");
         scores = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterHeaderBytes);
+    }
+    if (bf16 && hd % 64 == 0 && hd <= 256) {
+        // tensor-core scoring: one sequence per CTA group, the CTAs of a sequence split its tiles
+        using namespace tc;
+        TcParams tp;
+        tp.nH = nH;
+        tp.kb = hd / 64;
+        const size_t fixed = 1024 + (size_t)tp.kb * QBOX + NHP * 4 + NBARS * 8 + 16;
+        tp.stages = (int)std::min<size_t>(kMaxStages, (200 * 1024 - fixed) / ((size_t)tp.kb * BOX));
+        tp.nc = nc;
+        tp.scores = scores;
+        tp.status = device_status_word();
+        const int sms = device_sm_count();
+        const int64_t tiles = (nc + TT - 1) / TT;
+        tp.ctas_per_seq = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms / std::max(bs, 1)));
+        CUtensorMap map;
+        int tok_in_dim2 = 0;
+        int rc = make_kv_map(&map, kv, hd, nc * hd, hd, nc, bs, TT, &tok_in_dim2);
+        if (rc != WS_OK) return rc;
+        tp.kv_tok_in_dim2 = tok_in_dim2;
+        const size_t smem = fixed + (size_t)tp.stages * tp.kb * BOX;
+        static int configured_dev = -1;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (configured_dev != dev) {
+            if (cudaFuncSetAttribute(indexer_score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024 + 1024) != cudaSuccess)
+                return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for indexer_score_tc_kernel");
+            configured_dev = dev;
+        }
+        const int64_t grid = (int64_t)bs * tp.ctas_per_seq;
+        if (grid > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: too many sequences");
+        indexer_score_tc_kernel<<<(unsigned)grid, kThreads, smem, st>>>(
+            map, static_cast<const __nv_bfloat16*>(q), w, tp);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+        if (k > 0) {
+            indexer_select_kernel<<<bs, kSelThreads, 0, st>>>(scores, nc, k, by_id, out_ids);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+        }
+        return WS_OK;
     }
     const size_t smem = ((size_t)nH * hd + nH) * sizeof(float);
     auto kfn = bf16 ? indexer_score_kernel<true> : indexer_score_kernel<false>;
