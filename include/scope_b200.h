@@ -214,6 +214,19 @@ int ws_indexer_topk(const void* q, const void* kv, int dtype, const float* w, in
 size_t ws_indexer_topk_workspace_size(int bs, int64_t nc);
 
 /*
+ * Append n_new tokens to a device-resident KV cache (the write side of the
+ * partitioned cache; replaces the host copies of InplaceKVCache.append_4d,
+ * system/qwenoffload.py:97-122, and InplaceKVCacheCompressed.append,
+ * system/deepseek.py:171-194).  Strides in elements:
+ *   dst (row, t0 + i, d) at dst + row*dst_stride_row + (t0+i)*dst_stride_tok + d, t0 + n_new <= capacity
+ *   src (row, i, d)      at src + row*src_stride_row + i*src_stride_tok + d
+ * for row < rows, i < n_new, d < D; dtype WS_DTYPE_BF16 / F32 / I8.  One launch.
+ */
+int ws_kv_append(void* dst, int64_t dst_stride_row, int64_t dst_stride_tok, int64_t capacity, const void* src,
+                 int64_t src_stride_row, int64_t src_stride_tok, int64_t rows, int64_t n_new, int D, int dtype,
+                 int64_t t0, void* stream);
+
+/*
  * Log-sum-exp merge of P partial attention results (the cross-GPU combine of
  * a sequence-sharded KV cache, and the runtime merges it replaces:
  * system/qwenoffload.py:1606-1617 lse form).

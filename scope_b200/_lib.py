@@ -75,6 +75,7 @@ SIGNATURES = {
     "ws_csa_decode_workspace_size": (_sz, [_i, _i, _i]),
     "ws_indexer_topk": (_i, [_V, _V, _i, _V, _i, _i, _i, _i64, _i, _i, _V, _V, _V, _sz, _V]),
     "ws_indexer_topk_workspace_size": (_sz, [_i, _i64]),
+    "ws_kv_append": (_i, [_V, _i64, _i64, _i64, _V, _i64, _i64, _i64, _i64, _i, _i, _i64, _V]),
 }
 
 _lib = None

@@ -179,18 +179,23 @@ def mla_decode(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_p
     return out, lse
 
 
-def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float):
-    """GQA decode returning (out bf16 [B_kv, G, Dv] normalised, lse fp32 [B_kv, G]).
+def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, out_dtype=torch.bfloat16):
+    """GQA decode returning (out [B_kv, G, Dv] normalised in out_dtype (bf16 or fp32),
+    lse fp32 [B_kv, G]).
 
     The fp32 log-sum-exp (max + log sum) is what the LSE merges consume; the
     reference's bf16 fused_cpu_attn rounds max and sum to bf16 (~1e-2 LSE error).
+    An fp32 out is the partial a sharded cache exchanges.
     """
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise RuntimeError("gqa_decode requires bf16 inputs")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("gqa_decode: out_dtype must be bf16 or fp32")
     dev, B, G, Dk, L, Dv = _gqa_common("gqa_decode", q, k, v)
-    out = torch.empty(B, G, Dv, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B, G, Dv, dtype=out_dtype, device=dev)
     lse = torch.empty(B, G, dtype=torch.float32, device=dev)
-    _run_gqa(q, k, v, scale, _lib.WS_DTYPE_BF16, _lib.WS_OUT_NORM_BF16, out, None, None, lse)
+    mode = _lib.WS_OUT_NORM_BF16 if out_dtype == torch.bfloat16 else _lib.WS_OUT_NORM_F32
+    _run_gqa(q, k, v, scale, _lib.WS_DTYPE_BF16, mode, out, None, None, lse)
     return out, lse
 
 

@@ -325,6 +325,21 @@ int ws_indexer_topk(const void* q, const void* kv, int dtype, const float* w, in
                                out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int ws_kv_append(void* dst, int64_t dst_stride_row, int64_t dst_stride_tok, int64_t capacity, const void* src,
+                 int64_t src_stride_row, int64_t src_stride_tok, int64_t rows, int64_t n_new, int D, int dtype,
+                 int64_t t0, void* stream) {
+    if (rows < 0 || n_new < 0 || D < 1 || t0 < 0 || capacity < 0) return set_error(WS_ERR_INVALID_ARG, "kv_append: bad shape");
+    if (t0 + n_new > capacity) return set_error(WS_ERR_INVALID_ARG, "kv_append: the cache is full");
+    const int eb = dtype == WS_DTYPE_BF16 ? 2 : dtype == WS_DTYPE_F32 ? 4 : dtype == WS_DTYPE_I8 ? 1 : 0;
+    if (!eb) return set_error(WS_ERR_INVALID_ARG, "kv_append: dtype");
+    if (rows == 0 || n_new == 0) return WS_OK;
+    if (!dst || !src) return set_error(WS_ERR_INVALID_ARG, "kv_append: null pointer");
+    if (dst_stride_row < 0 || dst_stride_tok < D || src_stride_row < 0 || src_stride_tok < 0)
+        return set_error(WS_ERR_INVALID_ARG, "kv_append: bad strides");
+    return kv_append_launch(dst, dst_stride_row, dst_stride_tok, src, src_stride_row, src_stride_tok, rows, n_new, D,
+                            eb, t0, static_cast<cudaStream_t>(stream));
+}
+
 int ws_lse_merge(const float* o_parts, const float* lse_parts, int P, int64_t R, int D, void* out, int out_dtype,
                  float* out_lse, void* stream) {
     if (P < 1 || R < 0 || D < 1) return set_error(WS_ERR_INVALID_ARG, "bad shape");

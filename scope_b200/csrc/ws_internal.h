@@ -104,6 +104,9 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
                         int k, int by_id, int32_t* out_ids, float* out_scores, void* workspace,
                         size_t workspace_bytes, cudaStream_t st);
 
+int kv_append_launch(void* dst, int64_t dst_row, int64_t dst_tok, const void* src, int64_t src_row, int64_t src_tok,
+                     int64_t rows, int64_t n_new, int D, int elem_bytes, int64_t t0, cudaStream_t st);
+
 int lse_merge_launch(const float* o_parts, int64_t o_part_stride, const float* lse_parts, int64_t lse_part_stride,
                      int P, int64_t R, int D, void* out, int out_dtype, float* out_lse, cudaStream_t st);
 
