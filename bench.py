@@ -463,7 +463,7 @@ class Csa(Workload):
     so the rows one step reads were last read many steps (and > L2 bytes) ago."""
 
     name = "cfg5"
-    kernel_name = "csa_decode_kernel<int8,bf16 q> (tcgen05, clusters, L2 exchange)"
+    kernel_name = "csa_decode_kernel<int8,bf16 q> (tcgen05, 9 CTAs per sequence) + lse_merge_vec_kernel"
     profile_name = "csa_decode_cfg5"
     graph = True
 
@@ -595,7 +595,7 @@ class Indexer(Workload):
     select kernel).  Inputs larger than L2 (256 MiB of kv)."""
 
     name = "idx"
-    kernel_name = "indexer_score_kernel<bf16> (fp32 FMA) + indexer_select_kernel"
+    kernel_name = "indexer_score_tc_kernel<bf16> (tcgen05) + indexer_select_kernel"
     profile_name = "indexer_topk_idx"
     graph = True
 

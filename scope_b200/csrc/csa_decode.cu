@@ -8,8 +8,9 @@
 // int8-entry storage of the int8 family (values = int8 * scale, :1338-1344)
 // without quantising the query.
 //
-// One thread-block cluster per (sequence, group of query rows); its CS CTAs
-// split the sequence's selected entries evenly.  Inside a CTA, warp roles:
+// One CTA per (sequence, group of query rows, split): the `splits` CTAs of a
+// (sequence, group) divide its selected entries evenly, with splits chosen so
+// that the whole grid is one wave over the SMs.  Inside a CTA, warp roles:
 //   * gather warps (3): resolve entry ids to rows of this buffer (512 at a
 //     time), load each 64-entry tile's rows straight from global memory into
 //     registers (two tiles in flight for int8) and write them as a
@@ -23,10 +24,10 @@
 //     and sum need no cross-thread reduction; the max is updated lazily (O is
 //     rescaled in TMEM only when a head's max grows by more than 2^8, which
 //     keeps P <= 256 and is exact because m, l and O always share one max).
-// Then the cluster merges its CS partials: each CTA writes (m, l, O) of every
-// head to its slot of a workspace (L2), and after one cluster barrier CTA r
-// reduces query rows [r*NQ/CS, (r+1)*NQ/CS) by log-sum-exp over the CS slots
-// and writes the output.  One launch.
+// All eight warps then write the CTA's normalised O rows and log-sum-exp:
+// the output itself when splits == 1, else partial `split` of the workspace
+// (fp32, L2-resident), which the log-sum-exp merge kernel (merge.cu, launched
+// as a programmatic dependent of this grid) combines into the output.
 //
 // Every wait is bounded: a wait that gives up records kDevTimeout in the
 // status word and sets a CTA-wide abort flag, after which the remaining waits
@@ -53,11 +54,15 @@ constexpr int kThreads = 32 * (kMmaWarp + 1);   // 256
 constexpr int kGaRows = (TT + kGaWarps - 1) / kGaWarps;   // tile rows per gather warp (22)
 constexpr int kResolve = (CHUNK + kGaThreads - 1) / kGaThreads;   // entries per gather thread per chunk
 constexpr float kLazy = 8.f;             // rescale O only when a head's max grows by more than 2^8
-constexpr int kMaxCs = 8;
-constexpr int BAR_SOFTMAX = 1, BAR_GATHER = 2;  // named barriers (0 is __syncthreads)
+constexpr int kMaxSplit = 32;          // CTAs one (sequence, group) is split over, at most
+// named barriers (0 is __syncthreads); BAR_Q: the softmax warps arrive once the query tile is in
+// shared memory, the gather and MMA warps wait on it before they first use it
+constexpr int BAR_SOFTMAX = 1, BAR_GATHER = 2, BAR_Q = 3;
 
 // mbarriers
-enum { B_KFULL = 0, B_KEMPTY = 2, B_SFULL = 4, B_SEMPTY = 6, B_PFULL = 8, B_ODONE = 9, NBARS = 10 };
+// two of each: K slot full / empty, S buffer full / empty, P buffer full / empty (P empty: the second
+// product that read the buffer, and every product issued before it, has finished)
+enum { B_KFULL = 0, B_KEMPTY = 2, B_SFULL = 4, B_SEMPTY = 6, B_PFULL = 8, B_PEMPTY = 10, NBARS = 12 };
 
 // QSPLIT: an fp32 query is held as bf16 hi + lo parts (lo = q - hi, rounded
 // again) and the first product runs on both, so the scores keep ~16 mantissa
@@ -73,8 +78,9 @@ struct Cfg {
     // extra rows are the next box (garbage rows of S nobody reads); the last
     // box reads into this pad
     static constexpr int QPAD = QSPLIT ? 4096 : 0;
-    static constexpr int OFF_P = OFF_Q + QBYTES + QPAD;    // P [NQ rows x 64 entries], K-major
-    static constexpr int OFF_MISC = OFF_P + NQ * 128;
+    static constexpr int OFF_P = OFF_Q + QBYTES + QPAD;    // 2 x P [NQ rows x 64 entries], K-major
+    static constexpr int PBYTES = NQ * 128;
+    static constexpr int OFF_MISC = OFF_P + 2 * PBYTES;
     // misc, in 4-byte words
     static constexpr int W_CROW = 0;                       // [CHUNK] local row of each entry, -1 = none
     static constexpr int W_CSC = W_CROW + CHUNK;           // [CHUNK] value scale of each entry
@@ -83,9 +89,8 @@ struct Cfg {
     static constexpr int W_PSC = W_BIAS + 2 * TT;          // [2][TT] value scale folded into P
     static constexpr int W_ALPHA = W_PSC + 2 * TT;         // [2][64] per-head rescale factor, by tile parity
     static constexpr int W_NEED = W_ALPHA + 128;           // [2][4] per-warp "some head rescales"
-    static constexpr int W_WGT = W_NEED + 8;               // [64][8] merge weights of the cluster's partials
-    static constexpr int W_RINV = W_WGT + 64 * 8;          // [64] 1 / L
-    static constexpr int W_RLSE = W_RINV + 64;             // [64]
+    static constexpr int W_RINV = W_NEED + 8;              // [64] 2^eref / l: normalises a head's O row
+    static constexpr int W_RLSE = W_RINV + 64;             // [64] log-sum-exp of a head, -inf when empty
     static constexpr int W_QEXP = W_RLSE + 64;             // [64] per-head query exponent (fp16 products)
     static constexpr int W_TEXP = W_QEXP + 64;             // [2] value-scale exponent of the tile in each slot
     static constexpr int W_WMAX = W_TEXP + 2;              // [4] per-gather-warp max value scale of a chunk
@@ -119,8 +124,10 @@ struct Params {
     float scale_log2;
     void* out;
     int out_f32;
+    int out_aligned;          // out is 16-byte aligned: rows are written with bulk copies
     float* out_lse;
-    float* ws;                // [clusters][8 slots][NQ * 512 + 2 * NQ] partials exchanged through L2
+    float* part_o;            // splits > 1: [splits][bs * nq][512] normalised partial outputs
+    float* part_lse;          //             [splits][bs * nq] their log-sum-exp
     int* status;
 };
 
@@ -166,7 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     float* s_psc = reinterpret_cast<float*>(misc + C::W_PSC);
     float* s_alpha = reinterpret_cast<float*>(misc + C::W_ALPHA);
     int* s_need = reinterpret_cast<int*>(misc + C::W_NEED);
-    float* s_wgt = reinterpret_cast<float*>(misc + C::W_WGT);
     float* s_rinv = reinterpret_cast<float*>(misc + C::W_RINV);
     float* s_rlse = reinterpret_cast<float*>(misc + C::W_RLSE);
     int* s_qexp = reinterpret_cast<int*>(misc + C::W_QEXP);
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rank = (int)cluster_ctarank(), CS = (int)cluster_nctarank();
+    const int split = blockIdx.x, splits = gridDim.x;
     const int seq = blockIdx.y / p.ngroups, grp = blockIdx.y - seq * p.ngroups;
     const int row0 = grp * NQ;                       // first query row of this group
     const int nrows = min(NQ, p.nq - row0);
@@ -202,54 +208,28 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             hi = p.dense_end;
         }
         const int64_t cnt = hi - lo;
-        e_begin = lo + cnt * rank / CS;
-        e_end = lo + cnt * (rank + 1) / CS;
+        e_begin = lo + cnt * split / splits;
+        e_end = lo + cnt * (split + 1) / splits;
     }
     const int ntiles = (int)((e_end - e_begin + TT - 1) / TT);
 
-    const uint32_t kbase = smem_u32(sm + C::OFF_K), qbase = smem_u32(sm + C::OFF_Q), pbase = smem_u32(sm + C::OFF_P);
-    if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(BAR(B_KFULL + i), kGaThreads);
-            mbar_init(BAR(B_KEMPTY + i), 1);
-            mbar_init(BAR(B_SFULL + i), 1);
-            mbar_init(BAR(B_SEMPTY + i), kSmWarps);
-        }
-        mbar_init(BAR(B_PFULL), kSmWarps);
-        mbar_init(BAR(B_ODONE), 1);
-        *s_abort = 0;
-        s_qexp[0] = 0;   // largest |q| of the group (float bits), for the fp16 query scale
-        fence_mbar_init();
-    }
-    if (warp == kMmaWarp) tmem_alloc(smem_u32(s_tmem), C::TMEM_COLS);
-    __syncthreads();
-
-    // ---- queries -> registers (TPR threads per row); converted after the entry ids are resolved, so
-    //      the two sets of loads are in flight together
-    constexpr int TPR = kThreads / NQ, DPT = HD / TPR;   // DPT dims per thread: 128 (bf16 q) or 64 (fp32 q)
-    static_assert(DPT % 8 == 0 && DPT * TPR == HD, "query split");
-    const int r = tid / TPR, part = tid - r * TPR;
-    const bool ok = r < nrows;
-    const int64_t qoff = ((int64_t)seq * p.nq + row0 + (ok ? r : 0)) * HD + part * DPT;
-    constexpr int QL = DPT * (QSPLIT ? 4 : 2) / 16;     // 16-byte loads per thread (16)
-    uint4 qraw[QL];
-    {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.q) +
-                                                          qoff * (QSPLIT ? 4 : 2));
-#pragma unroll
-        for (int j = 0; j < QL; ++j) qraw[j] = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
-    }
     // ---- entry ids -> local rows and value scales, CHUNK entries at a time (gather warps)
     const int gtid = tid - 32 * kSmWarps;   // 0..95 in the gather warps
-    auto resolve_chunk = [&](int64_t cbase) {
-        int64_t id[kResolve];
-        int row[kResolve];
+    // resolve_rows: ids -> local rows (s_crow) and the value-scale loads issued; finish_scales: the
+    // scales and the chunk's largest scale (s_csc, s_wmax).  Between the two, the rows are known and
+    // the first tile's row loads can be in flight with the scale loads.
+    int64_t id[kResolve];   // issue_ids -> resolve_rows: the chunk's ids in flight
+    float sc_pend[kResolve];
+    auto issue_ids = [&](int64_t cbase) {
 #pragma unroll
         for (int u = 0; u < kResolve; ++u) {
             const int j = gtid + u * kGaThreads;
             const int64_t e = cbase + j;
             id[u] = (j < CHUNK && e < e_end) ? (ids ? (int64_t)__ldg(ids + e) : e) : INT64_MIN;
         }
+    };
+    auto resolve_rows = [&]() {
+        int row[kResolve];
 #pragma unroll
         for (int u = 0; u < kResolve; ++u) {
             row[u] = -1;
@@ -258,88 +238,87 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                 else if (p.window == WS_CSA_IDX_ALL) atomicExch(p.status, kDevBadIndex);   // skipped, and reported
             }
         }
-        float sc[kResolve];
 #pragma unroll
-        for (int u = 0; u < kResolve; ++u)
-            sc[u] = row[u] >= 0 ? (KV_I8 ? __ldg(p.kv_scales + kv_seq + row[u]) : 1.f) : 0.f;
+        for (int u = 0; u < kResolve; ++u) {
+            sc_pend[u] = row[u] >= 0 ? (KV_I8 ? __ldg(p.kv_scales + kv_seq + row[u]) : 1.f) : 0.f;
+            const int j = gtid + u * kGaThreads;
+            if (j < CHUNK) s_crow[j] = row[u];
+        }
+    };
+    auto finish_scales = [&]() {
         float mx = 0.f;
 #pragma unroll
         for (int u = 0; u < kResolve; ++u) {
             const int j = gtid + u * kGaThreads;
             if (j < CHUNK) {
-                s_crow[j] = row[u];
-                s_csc[j] = sc[u];
-                mx = fmaxf(mx, sc[u]);
+                s_csc[j] = sc_pend[u];
+                mx = fmaxf(mx, sc_pend[u]);
             }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         if (lane == 0) s_wmax[warp - kSmWarps] = mx;
     };
-    if (warp >= kSmWarps && warp < kMmaWarp && ntiles > 0) resolve_chunk(e_begin);
+    auto resolve_chunk = [&](int64_t cbase) {
+        issue_ids(cbase);
+        resolve_rows();
+        finish_scales();
+    };
+    // the first chunk's ids are requested before anything else: every later step of the gather waits on them
+    if (warp >= kSmWarps && warp < kMmaWarp && ntiles > 0) issue_ids(e_begin);
 
-    // ---- queries -> K-major swizzled fp16 / bf16 tile (rows past nrows are zero)
-    float v[DPT];
+    // ---- the query rows (softmax warps, QTPR threads per row, QDPT dims each): every 16-byte load is
+    //      issued at once and lands, unconverted, in the 16-byte slot its converted form takes (an fp32
+    //      chunk of 8 dims: its two halves in the hi and the lo slot); rows past nrows are zero
+    constexpr int QTPR = 32 * kSmWarps / NQ, QDPT = HD / QTPR;   // 2 x 256 dims (bf16 q), 4 x 128 (fp32 q)
+    constexpr int QL = QDPT * (QSPLIT ? 4 : 2) / 16;             // 16-byte loads per thread (32)
+    static_assert(QDPT % 32 == 0 && QDPT * QTPR == HD, "query split");
+    const int qr = tid / QTPR, qpart = tid - qr * QTPR;          // meaningful for the softmax warps
+    auto qslot = [&](int c, int half) {   // 8-dim chunk c of this thread's share; half: lo part (fp32 q)
+        const int c8 = qpart * (QDPT / 8) + c;
+        return sm + C::OFF_Q + (half * 8 + (c8 >> 3)) * C::QBOX + swz(qr, c8 & 7);
+    };
+    uint4 qraw[QL];
+    if (warp < kSmWarps) {   // requested now; stored once the CTA-wide setup below is done
+        const bool ok = qr < nrows;
+        const int64_t qoff = ((int64_t)seq * p.nq + row0 + (ok ? qr : 0)) * HD + qpart * QDPT;
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.q) + qoff * (QSPLIT ? 4 : 2));
 #pragma unroll
-    for (int j = 0; j < QL; ++j) {
-        const uint32_t w[4] = {qraw[j].x, qraw[j].y, qraw[j].z, qraw[j].w};
-        if (QSPLIT) {
+        for (int j = 0; j < QL; ++j) qraw[j] = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+    }
+    uint32_t qmax_bits = 0;   // largest |q| of this thread's share, as float bits (fp16 products only)
+    auto store_q = [&]() {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) v[4 * j + u] = __uint_as_float(w[u]);
-        } else {
+        for (int j = 0; j < QL; ++j) {
+            if (KV_I8) {   // magnitudes by integer max: non-negative floats order as their bits
+                const uint32_t w[4] = {qraw[j].x, qraw[j].y, qraw[j].z, qraw[j].w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                v[8 * j + 2 * u] = __uint_as_float(w[u] << 16);
-                v[8 * j + 2 * u + 1] = __uint_as_float(w[u] & 0xffff0000u);
+                for (int u = 0; u < 4; ++u)
+                    qmax_bits = QSPLIT ? max(qmax_bits, w[u] & 0x7fffffffu) : __vmaxu2(qmax_bits, w[u] & 0x7fff7fffu);
             }
+            *reinterpret_cast<uint4*>(QSPLIT ? qslot(j >> 1, j & 1) : qslot(j, 0)) = qraw[j];
         }
-    }
-    if (KV_I8) {   // fp16 products: the group's q * 2^-qe has its largest magnitude in [2^14, 2^15)
-        float mx = 0.f;
-#pragma unroll
-        for (int j = 0; j < DPT; ++j) mx = fmaxf(mx, fabsf(v[j]));
-#pragma unroll
-        for (int o = 1; o < TPR; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (part == 0 && mx > 0.f) atomicMax(&s_qexp[0], __float_as_int(mx));   // non-negative: int order
-        __syncthreads();
-        const int mb = s_qexp[0];
-        const int qe = mb > 0 ? min(max(((mb >> 23) & 0xff) - 127 - 14, -126), 113) : 0;
-        const float sq = __int_as_float((127 - qe) << 23);
-#pragma unroll
-        for (int j = 0; j < DPT; ++j) v[j] *= sq;   // exact: a power of two
-        if (tid == 0) s_qexp[1] = qe;
-    }
-#pragma unroll
-    for (int j = 0; j < DPT / 8; ++j) {
-        const int c8 = part * (DPT / 8) + j;   // 8-dim chunk index 0..63
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const float a = v[8 * j + 2 * u], b = v[8 * j + 2 * u + 1];
-            if (KV_I8) {
-                const __half2 h = __floats2half2_rn(a, b);
-                hi[u] = *reinterpret_cast<const uint32_t*>(&h);
-                const float2 hf = __half22float2(h);
-                const __half2 l2 = __floats2half2_rn(a - hf.x, b - hf.y);
-                lo[u] = *reinterpret_cast<const uint32_t*>(&l2);
-            } else {
-                hi[u] = pack_bf16(a, b);
-                lo[u] = pack_bf16(a - __uint_as_float(hi[u] << 16), b - __uint_as_float(hi[u] & 0xffff0000u));
-            }
+        if (!QSPLIT) qmax_bits = max(qmax_bits & 0xffffu, qmax_bits >> 16) << 16;   // bf16 -> float bits
+    };
+
+    const uint32_t kbase = smem_u32(sm + C::OFF_K), qbase = smem_u32(sm + C::OFF_Q), pbase = smem_u32(sm + C::OFF_P);
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(BAR(B_KFULL + i), kGaThreads);
+            mbar_init(BAR(B_KEMPTY + i), 1);
+            mbar_init(BAR(B_SFULL + i), 1);
+            mbar_init(BAR(B_SEMPTY + i), kSmWarps);
+            mbar_init(BAR(B_PFULL + i), kSmWarps);
+            mbar_init(BAR(B_PEMPTY + i), 1);
         }
-        *reinterpret_cast<uint4*>(sm + C::OFF_Q + (c8 >> 3) * C::QBOX + swz(r, c8 & 7)) =
-            make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        if (QSPLIT)
-            *reinterpret_cast<uint4*>(sm + C::OFF_Q + (8 + (c8 >> 3)) * C::QBOX + swz(r, c8 & 7)) =
-                make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *s_abort = 0;
+        s_qexp[0] = 0;   // largest |q| of the group (float bits), for the fp16 query scale
+        fence_mbar_init();
     }
-
-
-    cp_async_wait_all();
-    fence_proxy_async_smem();
-    tc_fence_before();
+    if (warp == kMmaWarp) tmem_alloc(smem_u32(s_tmem), C::TMEM_COLS);
     __syncthreads();
-    tc_fence_after();
+    pdl_launch_dependents();   // the merge grid may be scheduled now; it waits for this grid's completion
+
     const uint32_t tbase = *s_tmem;
     // S = Q . K^T and O^T += K^T . P^T
     constexpr uint32_t id1 = KV_I8 ? idesc_f16_f32(64, TT, false, false) : idesc_bf16_f32(64, TT, false, false);
@@ -349,10 +328,25 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     int eref_final = 0;                          // and the value-scale exponent O was accumulated in
     if (warp >= kSmWarps && warp < kMmaWarp) {
         // ================================================================ gather
-        // score factor per unit value scale: softmax scale * log2(e), times 2^qe for the scaled fp16 query
-        const float fscale = KV_I8 ? p.scale_log2 * __int_as_float((127 + s_qexp[1]) << 23) : p.scale_log2;
+        // the first chunk's rows are resolved (and its first tile's loads issued) while the softmax
+        // warps convert the query tile
+        if (ntiles > 0) {
+            resolve_rows();
+            named_bar_sync(BAR_GATHER, kGaThreads);   // the first chunk's rows
+        }
+        // score factor per unit value scale: softmax scale * log2(e), times 2^qe for the scaled fp16
+        // query; known once the query tile is ready
+        float fscale = 0.f;
+        bool q_ready = false;
+        auto wait_q = [&]() {
+            if (q_ready) return;
+            named_bar_sync(BAR_Q, kThreads);
+            q_ready = true;
+            fscale = KV_I8 ? p.scale_log2 * __int_as_float((127 + s_qexp[1]) << 23) : p.scale_log2;
+        };
         // publish tile t's per-entry factors (thread gtid < TT owns entry gtid) and signal the MMA warp
         auto publish = [&](int t, float sc, int ex) {   // ex: the chunk's value-scale exponent
+            wait_q();
             const int slot = t & 1;
             if (gtid < TT) {
                 const bool ok = sc >= 0.f;
@@ -426,11 +420,16 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             float sca = 0.f, scb = 0.f;
             int exa = 0, exb = 0;
             if (ntiles > 0) {
+                load(ra, 0);   // needs only the rows; the scales arrive meanwhile
+                finish_scales();
+                named_bar_sync(BAR_GATHER, kGaThreads);
                 sca = entry_scale(0);
                 exa = chunk_exp();
-                load(ra, 0);
             }
-            for (int t = 0; t < ntiles; t += 2) {
+            // one call site each for load and store (the code of this loop stays small): the buffers
+            // trade places after every tile instead
+#pragma unroll 1
+            for (int t = 0; t < ntiles; ++t) {
                 if (t + 1 < ntiles) {
                     if (((t + 1) * TT) % CHUNK == 0) next_chunk(t + 1);
                     scb = entry_scale(t + 1);
@@ -438,18 +437,18 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                     load(rb2, t + 1);
                 }
                 store(ra, t, sca, exa);
-                if (t + 1 >= ntiles) break;
-                if (t + 2 < ntiles) {
-                    if (((t + 2) * TT) % CHUNK == 0) next_chunk(t + 2);
-                    sca = entry_scale(t + 2);
-                    exa = chunk_exp();
-                    load(ra, t + 2);
-                }
-                store(rb2, t + 1, scb, exb);
+#pragma unroll
+                for (int i = 0; i < kGaRows; ++i) ra[i] = rb2[i];
+                sca = scb;
+                exa = exb;
             }
         } else {
             const __nv_bfloat16* kv = static_cast<const __nv_bfloat16*>(p.kv);
             const int rb = warp - kSmWarps;   // 64 chunks of 8 bf16 per row: lane and lane + 32; rows rb + 3i
+            if (ntiles > 0) {
+                finish_scales();
+                named_bar_sync(BAR_GATHER, kGaThreads);
+            }
             for (int t = 0; t < ntiles; ++t) {
                 if (t > 0 && (t * TT) % CHUNK == 0) next_chunk(t);
                 const float sc = entry_scale(t);
@@ -476,19 +475,22 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                 publish(t, sc, 0);
             }
         }
+        wait_q();   // every gather thread takes part in the query barrier once, with or without tiles
     } else if (warp == kMmaWarp) {
         // ================================================================ MMA issue (lane 0)
         // Issue whichever product is ready: the second product of the oldest
         // tile first (it frees a K slot and lets the next P be written), else
         // the first product of the next tile.
         int g1 = 0, g2 = 0;   // next tile for the first / second product
+        named_bar_sync(BAR_Q, kThreads);   // the query tile is in shared memory
+        tc_fence_after();
         uint64_t t_last = globaltimer_ns();
         while (g2 < ntiles) {
             int choice = 0;
             if (lane == 0) {
                 if (*s_abort) {
                     choice = 3;
-                } else if (g2 < g1 && mbar_try_wait(BAR(B_PFULL), g2 & 1)) {
+                } else if (g2 < g1 && mbar_try_wait(BAR(B_PFULL + (g2 & 1)), (g2 >> 1) & 1)) {
                     choice = 2;
                 } else if (g1 < ntiles && mbar_try_wait(BAR(B_KFULL + (g1 & 1)), (g1 >> 1) & 1) &&
                            (g1 < 2 || mbar_try_wait(BAR(B_SEMPTY + (g1 & 1)), ((g1 >> 1) + 1) & 1))) {
@@ -505,32 +507,107 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             tc_fence_after();
             if (lane == 0) {
                 t_last = globaltimer_ns();
+                // Descriptors are formed once per product; the operand steps are added to the start-address
+                // field (address >> 4, 14 bits: every shared address here is below 256 KB, so no carry),
+                // which keeps the issue loop at a few instructions per MMA.
                 if (choice == 1) {
                     const int slot = g1 & 1;
-                    const uint32_t kb_base = kbase + slot * KSLOT;
+                    const uint64_t dq = sdesc_sw128(qbase, 16, 1024), dk = sdesc_sw128(kbase + slot * KSLOT, 16, 1024);
+                    const uint32_t td = tbase + C::S_COL + slot * TT;
+#pragma unroll
                     for (int part = 0; part < (QSPLIT ? 2 : 1); ++part)
+#pragma unroll
                         for (int kb = 0; kb < 8; ++kb)
+#pragma unroll
                             for (int kk = 0; kk < 4; ++kk)
-                                umma_bf16(tbase + C::S_COL + slot * TT,
-                                          sdesc_sw128(qbase + (part * 8 + kb) * C::QBOX + kk * 32, 16, 1024),
-                                          sdesc_sw128(kb_base + kb * KBOX + kk * 32, 16, 1024), id1,
-                                          (part | kb | kk) != 0);
+                                umma_bf16(td, dq + (uint64_t)(((part * 8 + kb) * C::QBOX + kk * 32) >> 4),
+                                          dk + (uint64_t)((kb * KBOX + kk * 32) >> 4), id1, (part | kb | kk) != 0);
                     umma_commit(BAR(B_SFULL + slot));
                 } else {
-                    const uint32_t ks_base = kbase + (g2 & 1) * KSLOT;
+                    const uint64_t dv = sdesc_sw128(kbase + (g2 & 1) * KSLOT, KBOX, 1024);
+                    const uint64_t dp = sdesc_sw128(pbase + (g2 & 1) * C::PBYTES, 16, 1024);
+                    const uint32_t acc0 = g2 > 0 ? 1u : 0u;
+#pragma unroll
                     for (int mb = 0; mb < 4; ++mb)
+#pragma unroll
                         for (int ks = 0; ks < TT / 16; ++ks)
-                            umma_bf16(tbase + C::O_COL + mb * NQ,
-                                      sdesc_sw128(ks_base + (2 * mb) * KBOX + ks * 2048, KBOX, 1024),
-                                      sdesc_sw128(pbase + ks * 32, 16, 1024), id2, (g2 > 0 || ks > 0) ? 1u : 0u);
+                            umma_bf16(tbase + C::O_COL + mb * NQ, dv + (uint64_t)((2 * mb * KBOX + ks * 2048) >> 4),
+                                      dp + (uint64_t)((ks * 32) >> 4), id2, ks > 0 ? 1u : acc0);
                     umma_commit(BAR(B_KEMPTY + (g2 & 1)));
-                    umma_commit(BAR(B_ODONE));
+                    umma_commit(BAR(B_PEMPTY + (g2 & 1)));
                 }
             }
             if (choice == 1) ++g1; else ++g2;
             __syncwarp();
         }
     } else {
+        // ================================================================ query tile (softmax warps)
+        store_q();
+        {   // the query tile, continued: the group's exponent (fp16 products), then the conversion in place,
+            // four chunks at a time (a compact loop: this once-per-CTA code is bound by instruction fetch,
+            // and four independent chunks keep a single warp per scheduler busy)
+            auto chunk8 = [&](int c, float (&v)[8]) {   // dims [8c, 8c + 8) of this thread's share, unconverted
+                const uint4 a = *reinterpret_cast<const uint4*>(qslot(c, 0));
+                if (QSPLIT) {
+                    const uint4 b = *reinterpret_cast<const uint4*>(qslot(c, 1));
+                    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y);
+                    v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+                    v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y);
+                    v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
+                } else {
+                    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        v[2 * u] = __uint_as_float(w[u] << 16);
+                        v[2 * u + 1] = __uint_as_float(w[u] & 0xffff0000u);
+                    }
+                }
+            };
+            float sq = 1.f;
+            if (KV_I8) {   // fp16 products: the group's q * 2^-qe has its largest magnitude in [2^14, 2^15)
+                uint32_t mx = qmax_bits;
+#pragma unroll
+                for (int o = 1; o < QTPR; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (qpart == 0 && mx > 0u) atomicMax(&s_qexp[0], (int)mx);   // non-negative float bits: int order
+                named_bar_sync(BAR_SOFTMAX, 32 * kSmWarps);
+                const int mb = s_qexp[0];
+                const int qe = mb > 0 ? min(max(((mb >> 23) & 0xff) - 127 - 14, -126), 113) : 0;
+                sq = __int_as_float((127 - qe) << 23);
+                if (tid == 0) s_qexp[1] = qe;
+            }
+            if (KV_I8 || QSPLIT) {   // a bf16 query for bf16 products is already in its final form
+#pragma unroll 1
+                for (int c0 = 0; c0 < QDPT / 8; c0 += 4) {
+                    float vv[4][8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) chunk8(c0 + k, vv[k]);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                    const int c = c0 + k;
+                    const float (&v)[8] = vv[k];
+                    uint32_t hi[4], lo[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float a = v[2 * u] * sq, b = v[2 * u + 1] * sq;   // exact: a power of two
+                        if (KV_I8) {
+                            const __half2 hh = __floats2half2_rn(a, b);
+                            hi[u] = *reinterpret_cast<const uint32_t*>(&hh);
+                            const float2 hf = __half22float2(hh);
+                            const __half2 l2 = __floats2half2_rn(a - hf.x, b - hf.y);
+                            lo[u] = *reinterpret_cast<const uint32_t*>(&l2);
+                        } else {
+                            hi[u] = pack_bf16(a, b);
+                            lo[u] = pack_bf16(a - __uint_as_float(hi[u] << 16), b - __uint_as_float(hi[u] & 0xffff0000u));
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(qslot(c, 0)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    if (QSPLIT) *reinterpret_cast<uint4*>(qslot(c, 1)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    }
+                }
+            }
+            fence_proxy_async_smem();   // the tile -> the async proxy (tensor-core operand)
+            named_bar_arrive(BAR_Q, kThreads);
+        }
         // ================================================================ softmax (thread = head)
         const int h = warp * 16 + lane;
         const bool own = lane < 16 && h < NQ;
@@ -612,27 +689,39 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             if (lane == 0) s_need[sb * 4 + warp] = need;
             named_bar_sync(BAR_SOFTMAX, 32 * kSmWarps);
             const int any = s_need[sb * 4] | s_need[sb * 4 + 1] | s_need[sb * 4 + 2] | s_need[sb * 4 + 3];
-            if (t > 0) {
-                // the previous second product has finished: O is stable and P may be rewritten
-                wait_bar(BAR(B_ODONE), (t - 1) & 1, s_abort, p.status);
+            // Second product j is the (j >> 1)-th completion of P-empty barrier j & 1.  Each wait below
+            // is for a product no older than one this thread already waited for two tiles ago and
+            // no newer than the last P it wrote, so the barrier is never two phases from the parity.
+            if (t >= 2) {   // second product t - 2 has read P buffer t & 1
+                wait_bar(BAR(B_PEMPTY + sb), ((t >> 1) + 1) & 1, s_abort, p.status);
                 tc_fence_after();
-                if (any) {   // O *= alpha per head (column); this warp's 32 dims of each 128-dim block
-                    for (int mb = 0; mb < 4; ++mb)
+            }
+            if (t > 0 && any) {
+                // second product t - 1 has finished: O is stable
+                wait_bar(BAR(B_PEMPTY + (sb ^ 1)), ((t - 1) >> 1) & 1, s_abort, p.status);
+                tc_fence_after();
+                // O *= alpha per head (column); this warp's 32 dims of each 128-dim block.  Rare (lazy
+                // rescale), so kept as a compact loop; the 16 factors are read before the TMEM store.
+#pragma unroll 1
+                for (int it = 0; it < 4 * (NQ / 16); ++it) {
+                    const int mb = it / (NQ / 16), cb = it % (NQ / 16);
+                    const uint32_t ta = tbase + lane_base + C::O_COL + mb * NQ + cb * 16;
+                    float v[16], a[16];
+                    tmem_ld16(ta, v);
 #pragma unroll
-                        for (int cb = 0; cb < NQ / 16; ++cb) {
-                            float v[16];
-                            const uint32_t ta = tbase + lane_base + C::O_COL + mb * NQ + cb * 16;
-                            tmem_ld16(ta, v);
-                            tmem_wait_ld();
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 x = reinterpret_cast<const float4*>(s_alpha + sb * 64 + cb * 16)[q];
+                        a[4 * q] = x.x; a[4 * q + 1] = x.y; a[4 * q + 2] = x.z; a[4 * q + 3] = x.w;
+                    }
+                    tmem_wait_ld();
 #pragma unroll
-                            for (int u = 0; u < 16; ++u) v[u] *= s_alpha[sb * 64 + cb * 16 + u];
-                            tmem_st16(ta, v);
-                        }
-                    tmem_wait_st();
+                    for (int u = 0; u < 16; ++u) v[u] *= a[u];
+                    tmem_st16(ta, v);
                 }
+                tmem_wait_st();
             }
             if (own) {   // this head's P row: 64 entries, 8 swizzled 16-byte chunks (zeros when inactive)
-                uint8_t* prow = sm + C::OFF_P + h * 128;
+                uint8_t* prow = sm + C::OFF_P + sb * C::PBYTES + h * 128;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     uint32_t w4[4] = {0u, 0u, 0u, 0u};
@@ -654,10 +743,10 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(BAR(B_PFULL));
+            if (lane == 0) mbar_arrive(BAR(B_PFULL + sb));
         }
         if (ntiles > 0) {   // the last second product has finished: O is final
-            wait_bar(BAR(B_ODONE), (ntiles - 1) & 1, s_abort, p.status);
+            wait_bar(BAR(B_PEMPTY + ((ntiles - 1) & 1)), ((ntiles - 1) >> 1) & 1, s_abort, p.status);
             tc_fence_after();
         }
         m_final = m;
@@ -665,133 +754,142 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
         eref_final = eref;
     }
 #undef BAR
-    // ---- exchange through L2: every CTA writes its partial (the unnormalised O row, max and sum of
-    //      each head) to its own slot of the cluster's workspace; after the cluster barrier the CTA
-    //      that merges a row reads that row from all CS slots.  (Distributed shared memory moves only
-    //      ~15-30 GB/s per SM on this part, far too little for 128 KB per CTA.)
-    constexpr int SLOT = NQ * HD + 2 * NQ;   // floats: O [NQ][512], then max [NQ], sum [NQ]
-    float* ws_cluster = p.ws + (size_t)blockIdx.y * kMaxCs * SLOT;
-    if (warp < kSmWarps) {
-        float* mine = ws_cluster + (size_t)rank * SLOT;
+    // ---- epilogue: each head's normaliser and log-sum-exp (softmax threads), then all eight warps
+    //      move O^T out of TMEM (warp w reads TMEM lanes 32*(w%4).., dims of blocks 2*(w/4), 2*(w/4)+1)
+    const bool have = ntiles > 0 && !*s_abort;
+    if (warp < kSmWarps && lane < 16 && warp * 16 + lane < NQ) {
         const int h = warp * 16 + lane;
-        const bool own = lane < 16 && h < NQ;
-        const bool have = ntiles > 0 && !*s_abort;
-        if (own) {
-            const bool ok = have && h < nrows;
-            mine[NQ * HD + h] = ok ? m_final : -INFINITY;
-            mine[NQ * HD + NQ + h] = ok ? l_final : 0.f;
-        }
-        if (have) {   // an empty partial writes no O: its weight is 0 and its rows are never read
-            const float oscale = __int_as_float((127 + eref_final) << 23);   // undo the value-scale exponent
-            const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-            for (int mb = 0; mb < 4; ++mb)
-#pragma unroll
-                for (int cb = 0; cb < NQ / 16; ++cb) {
-                    float v[16];
-                    tmem_ld16(tbase + lane_base + C::O_COL + mb * NQ + cb * 16, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int u = 0; u < 16; ++u) mine[(cb * 16 + u) * HD + mb * 128 + warp * 32 + lane] = v[u] * oscale;
-                }
-        }
+        const bool ok = have && h < nrows && l_final > 0.f;
+        // O^T was accumulated with the value scales times 2^-eref: 2^eref / l normalises it
+        s_rinv[h] = ok ? __int_as_float((127 + eref_final) << 23) / l_final : 0.f;
+        s_rlse[h] = ok ? m_final * kLn2 + logf(l_final) : -INFINITY;
     }
     tc_fence_before();
     __syncthreads();
-    cluster_sync();   // release / acquire at cluster scope: every slot of the cluster is visible
-
-    // ---- merge the rows this CTA owns [r_lo, r_lo + RPC)
-    const int r_lo = rank * NQ / CS, RPC = (rank + 1) * NQ / CS - r_lo;
-    if (tid < RPC) {
-        const int h = r_lo + tid;
-        float mc[kMaxCs];
-        float M = -INFINITY;
+    tc_fence_after();
+    const int64_t orow0 = (int64_t)seq * p.nq + row0;   // output row of this group's first query row
+    const int64_t nrows_all = (int64_t)gridDim.y / p.ngroups * p.nq;   // bs * nq
+    const bool partial = splits > 1;
+    const bool bf16_out = !partial && !p.out_f32;
+    // this group's nrows output rows are contiguous: staged row-major in the (now idle) K ring and
+    // written with one bulk copy, or, when the output is not 16-byte aligned, stored directly
+    const bool bulk = partial || p.out_aligned;
+    uint8_t* dst = partial ? reinterpret_cast<uint8_t*>(p.part_o + ((size_t)split * nrows_all + orow0) * HD)
+                           : static_cast<uint8_t*>(p.out) + orow0 * HD * (bf16_out ? 2 : 4);
+    // Warp w: TMEM lanes 32*(w%4).. = dims d, 16 heads (columns) at a time.  The 16 factors are read
+    // into registers before the stores (shared-memory stores would otherwise order every later factor
+    // load behind them); s_rinv is 0 for rows past nrows and for empty heads, where O is 0 too (P was 0),
+    // except with no tiles at all, when O was never written: zeros then.  The loops are kept compact and
+    // free of branches: this once-per-CTA code is bound by instruction fetch, not arithmetic.
+    const int q4 = warp & 3;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const uint32_t stage = smem_u32(sm + C::OFF_K);
+    auto o_block = [&](int mb, int cb, float (&v)[16]) {   // v = O[head cb*16 + u][dim] * factor
+        float f[16];
+        if (have) tmem_ld16(tbase + lane_base + C::O_COL + mb * NQ + cb * 16, v);
 #pragma unroll
-        for (int c = 0; c < kMaxCs; ++c) {
-            mc[c] = c < CS ? __ldcg(ws_cluster + (size_t)c * SLOT + NQ * HD + h) : -INFINITY;
-            M = fmaxf(M, mc[c]);
+        for (int q = 0; q < 4; ++q) {
+            const float4 x = reinterpret_cast<const float4*>(s_rinv + cb * 16)[q];
+            f[4 * q] = x.x; f[4 * q + 1] = x.y; f[4 * q + 2] = x.z; f[4 * q + 3] = x.w;
         }
-        float L = 0.f;
-#pragma unroll
-        for (int c = 0; c < kMaxCs; ++c) {
-            const float w = (mc[c] == -INFINITY) ? 0.f : ex2(mc[c] - M);
-            s_wgt[tid * 8 + c] = w;
-            if (w != 0.f) L += w * __ldcg(ws_cluster + (size_t)c * SLOT + NQ * HD + NQ + h);
-        }
-        const bool empty = !(L > 0.f);
-        s_rinv[tid] = empty ? 0.f : 1.f / L;
-        s_rlse[tid] = empty ? -INFINITY : M * kLn2 + logf(L);
-    }
-    __syncthreads();
-    for (int j = tid; j < RPC * (HD / 4); j += kThreads) {
-        const int hl = j / (HD / 4), d4 = j - hl * (HD / 4);
-        const int h = r_lo + hl;
-        if (h >= nrows) continue;
-        float4 v[kMaxCs];
-#pragma unroll
-        for (int c = 0; c < kMaxCs; ++c)   // every slot's load in flight together
-            if (c < CS && s_wgt[hl * 8 + c] != 0.f)
-                v[c] = __ldcg(reinterpret_cast<const float4*>(ws_cluster + (size_t)c * SLOT + h * HD + d4 * 4));
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < kMaxCs; ++c) {
-            const float w = c < CS ? s_wgt[hl * 8 + c] : 0.f;
-            if (w == 0.f) continue;
-            acc.x = fmaf(w, v[c].x, acc.x); acc.y = fmaf(w, v[c].y, acc.y);
-            acc.z = fmaf(w, v[c].z, acc.z); acc.w = fmaf(w, v[c].w, acc.w);
-        }
-        const float inv = s_rinv[hl];
-        const int64_t oi = ((int64_t)seq * p.nq + row0 + h) * HD + d4 * 4;
-        if (p.out_f32) {
-            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
-                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        if (have) {
+            tmem_wait_ld();
         } else {
-            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
-            *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-            *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] *= f[u];
+    };
+    if (partial) {
+        if (have) {   // an empty partial writes only its -inf log-sum-exp
+            // 16 rows at a time: staged (fp32, row-major), then one bulk copy, which overlaps the staging
+            // of the next 16 rows
+            float* po = p.part_o + ((size_t)split * nrows_all + orow0) * HD;
+#pragma unroll 1
+            for (int cb = 0; cb < NQ / 16 && cb * 16 < nrows; ++cb) {
+#pragma unroll 1
+                for (int mi = 0; mi < 2; ++mi) {
+                    const int mb = (warp >> 2) * 2 + mi, d = mb * 128 + q4 * 32 + lane;
+                    float v[16];
+                    o_block(mb, cb, v);
+#pragma unroll
+                    for (int u = 0; u < 16; ++u)
+                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(stage + (uint32_t)(((cb * 16 + u) * HD + d) * 4)),
+                                     "f"(v[u]) : "memory");
+                }
+                fence_proxy_async_smem();   // the staged rows -> the async proxy
+                __syncthreads();
+                if (tid == 0) {
+                    bulk_store(po + cb * 16 * HD, stage + (uint32_t)(cb * 16 * HD * 4),
+                               (uint32_t)(min(16, nrows - cb * 16) * HD * 4));
+                    bulk_commit();
+                }
+            }
+            if (tid == 0) bulk_wait_all();   // complete before the CTA exits (the merge grid reads it)
+        }
+    } else {
+        // the output itself (bf16 or fp32): staged and written with one bulk copy when 16-byte aligned
+        const int esz = bf16_out ? 2 : 4;
+#pragma unroll 1
+        for (int it = 0; it < 2 * (NQ / 16); ++it) {
+            const int mb = (warp >> 2) * 2 + it / (NQ / 16), cb = it % (NQ / 16);
+            if (cb * 16 >= nrows) continue;   // uniform across the warp
+            const int d = mb * 128 + q4 * 32 + lane;
+            float v[16];
+            o_block(mb, cb, v);
+            if (bulk) {
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const uint32_t a = stage + (uint32_t)(((cb * 16 + u) * HD + d) * esz);
+                    if (bf16_out) {
+                        const __nv_bfloat16 b = __float2bfloat16_rn(v[u]);
+                        asm volatile("st.shared.b16 [%0], %1;" ::"r"(a), "h"(*reinterpret_cast<const uint16_t*>(&b))
+                                     : "memory");
+                    } else {
+                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v[u]) : "memory");
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int h = cb * 16 + u;
+                    if (h >= nrows) break;
+                    if (bf16_out) reinterpret_cast<__nv_bfloat16*>(dst)[h * HD + d] = __float2bfloat16_rn(v[u]);
+                    else reinterpret_cast<float*>(dst)[h * HD + d] = v[u];
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (bulk && tid == 0) {
+            bulk_store(dst, stage, (uint32_t)(nrows * HD * esz));
+            bulk_commit();
+            bulk_wait_all();
         }
     }
-    if (tid < RPC && r_lo + tid < nrows && p.out_lse)
-        p.out_lse[(int64_t)seq * p.nq + row0 + r_lo + tid] = s_rlse[tid];
+    tc_fence_before();   // every TMEM read is done before the dealloc below
+    __syncthreads();
+    if (tid < nrows) {
+        if (partial) p.part_lse[(size_t)split * nrows_all + orow0 + tid] = s_rlse[tid];
+        else if (p.out_lse) p.out_lse[orow0 + tid] = s_rlse[tid];
+    }
     tc_fence_after();
     if (warp == kMmaWarp) tmem_dealloc(tbase, C::TMEM_COLS);
 }
 
-// Clusters of `cs` CTAs of this kernel that the device runs at once.
-template <bool KV_I8, bool QSPLIT>
-static int max_active_clusters(int cs) {
-    static int cached[kMaxCs + 1] = {};   // for the device last asked about
-    static int cached_dev = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cached_dev != dev) {
-        for (int& v : cached) v = 0;
-        cached_dev = dev;
-    }
-    int& slot = cached[cs];
-    if (slot == 0) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(cs, 1, 1);
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = Cfg<QSPLIT>::SMEM;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = cs;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, csa_decode_kernel<KV_I8, QSPLIT>, &cfg) != cudaSuccess || n < 1) {
-            cudaGetLastError();
-            return 1;   // not cached: asked again next time
-        }
-        slot = n;
-    }
-    return slot;
+// CTAs each (sequence, group) is split over: the most that keep the whole
+// grid within one wave of one CTA per SM, at most kMaxSplit, and no more than
+// give every CTA one full tile.  `per_seq` bounds the entries of one sequence.
+static int split_count(int64_t groups, int64_t per_seq, int nsm) {
+    if (groups >= nsm) return 1;
+    int64_t s = std::min<int64_t>(nsm / groups, kMaxSplit);
+    s = std::min<int64_t>(s, per_seq / TT);
+    return (int)std::max<int64_t>(s, 1);
 }
 
 template <bool KV_I8, bool QSPLIT>
-static int launch(const Params& p, int bs, int64_t entries_per_seq, cudaStream_t st) {
+static int launch(const Params& p, int groups, int splits, cudaStream_t st) {
     auto kfn = csa_decode_kernel<KV_I8, QSPLIT>;
     static int configured_dev = -1;
     int dev = 0;
@@ -802,35 +900,8 @@ static int launch(const Params& p, int bs, int64_t entries_per_seq, cudaStream_t
             return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for csa_decode_kernel");
         configured_dev = dev;
     }
-    // CTAs per cluster: the fewest tile-times, counting waves of clusters the
-    // device cannot run at once and one tile-time per wave for the merge.
-    const int64_t clusters = (int64_t)bs * p.ngroups;
-    int cs = 1;
-    int64_t best = INT64_MAX;
-    for (int c = 1; c <= kMaxCs; ++c) {
-        if (c > 1 && entries_per_seq <= (int64_t)(c - 1) * TT) break;   // some CTA would get no full tile
-        const int64_t active = max_active_clusters<KV_I8, QSPLIT>(c);
-        const int64_t waves = (clusters + active - 1) / active;
-        const int64_t tiles = (entries_per_seq + (int64_t)c * TT - 1) / ((int64_t)c * TT);
-        const int64_t cost = waves * (tiles + 1);
-        if (cost < best) {
-            best = cost;
-            cs = c;
-        }
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(cs, (unsigned)clusters, 1);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg<QSPLIT>::SMEM;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cs;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, p);
+    kfn<<<dim3((unsigned)splits, (unsigned)groups, 1), kThreads, Cfg<QSPLIT>::SMEM, st>>>(p);
+    const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -839,10 +910,12 @@ static int launch(const Params& p, int bs, int64_t entries_per_seq, cudaStream_t
 size_t csa_workspace_bytes(int bs, int nq, int q_f32) {
     using namespace csa;
     const int NQ = q_f32 ? Cfg<true>::NQ : Cfg<false>::NQ;
-    const int64_t clusters = (int64_t)bs * ((nq + NQ - 1) / NQ);
+    const int64_t groups = (int64_t)bs * ((nq + NQ - 1) / NQ);
+    const int splits = split_count(groups, INT64_MAX, device_sm_count());   // the most any k can use
     // the partials follow the fixed counter header every workspace starts with (left untouched here),
     // so one workspace can serve this kernel and the kernels whose merge tickets live in that header
-    return kCounterHeaderBytes + (size_t)std::max<int64_t>(clusters, 1) * kMaxCs * (NQ * HD + 2 * NQ) * sizeof(float);
+    const size_t parts = splits > 1 ? (size_t)splits * bs * nq * (HD + 1) * sizeof(float) : 0;
+    return kCounterHeaderBytes + parts;
 }
 
 int csa_launch(const CsaLaunch& a) {
@@ -873,15 +946,28 @@ int csa_launch(const CsaLaunch& a) {
     p.scale_log2 = a.scale * kLog2e;
     p.out = a.out;
     p.out_f32 = a.out_f32;
+    p.out_aligned = reinterpret_cast<uintptr_t>(a.out) % 16 == 0;
     p.out_lse = a.out_lse;
-    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
     p.status = device_status_word();
+    if (a.bs == 0 || a.nq == 0) return WS_OK;
     // entries one sequence selects (a sharded sorted list selects about k * nc_local / nc; k bounds it)
     const int64_t per_seq = a.idx ? (int64_t)a.k : p.dense_end - p.dense_begin;
+    const int groups = a.bs * p.ngroups;
+    const int splits = split_count(groups, per_seq, device_sm_count());
+    const int64_t rows = (int64_t)a.bs * a.nq;
+    if (splits > 1) {
+        p.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
+        p.part_lse = p.part_o + (size_t)splits * rows * HD;
+    }
     cudaStream_t st = static_cast<cudaStream_t>(a.stream);
+    int rc;
     if (a.kv_i8)
-        return a.q_f32 ? launch<true, true>(p, a.bs, per_seq, st) : launch<true, false>(p, a.bs, per_seq, st);
-    return a.q_f32 ? launch<false, true>(p, a.bs, per_seq, st) : launch<false, false>(p, a.bs, per_seq, st);
+        rc = a.q_f32 ? launch<true, true>(p, groups, splits, st) : launch<true, false>(p, groups, splits, st);
+    else
+        rc = a.q_f32 ? launch<false, true>(p, groups, splits, st) : launch<false, false>(p, groups, splits, st);
+    if (rc != WS_OK || splits == 1) return rc;
+    return lse_merge_launch(p.part_o, rows * HD, p.part_lse, rows, splits, rows, HD, a.out,
+                            a.out_f32 ? WS_DTYPE_F32 : WS_DTYPE_BF16, a.out_lse, st, /*after_primary=*/true);
 }
 
 }  // namespace ws

@@ -1,21 +1,77 @@
 // Log-sum-exp merge of P partial attention results.
 //
-// The cross-GPU combine of a sequence-sharded KV cache, and the GPU form of
-// the runtime merges of the reference (system/qwenoffload.py:1606-1617,
-// system/mixoffload.py:1456-1464, system/deepseek.py:397-404):
+// The cross-GPU combine of a sequence-sharded KV cache, the combine of a CSA
+// decode split over several CTAs, and the GPU form of the runtime merges of
+// the reference (system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464,
+// system/deepseek.py:397-404):
 //   M = max_p lse_p ;  L = M + log(sum_p exp(lse_p - M)) ;
 //   o = sum_p exp(lse_p - L) * o_p
-// One warp per output row; o_p rows are read with 16-byte loads when D % 4 == 0.
+// A partial whose lse is -inf has weight 0 and its o row is never read.
 #include "common.cuh"
 #include "ws_internal.h"
 
 namespace ws {
+namespace {
 
-// Partial p's o rows start at o_parts + p * os, its lse values at lse_parts + p * ls.
-template <bool VEC>
+// P <= 32, D % 4 == 0: one warp per (row, 128-column chunk).  Lane p holds
+// partial p's weight; every partial's 16-byte load of the chunk is issued
+// before the first is used, so a warp keeps up to P loads in flight.
+template <bool PDL>
+__global__ void __launch_bounds__(128) lse_merge_vec_kernel(const float* __restrict__ o_parts, int64_t os, const float* __restrict__ lse_parts,
+                                     int64_t ls, int P, int64_t R, int D, void* __restrict__ out, int out_dtype,
+                                     float* __restrict__ out_lse) {
+    if (PDL) pdl_wait_primary();   // the partials are written by the previous grid
+    const int nchunk = (D + 127) / 128;
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (item >= R * nchunk) return;
+    const int64_t row = item / nchunk;
+    const int chunk = (int)(item - row * nchunk);
+    const float lp = lane < P ? __ldg(lse_parts + (int64_t)lane * ls + row) : -INFINITY;
+    float M = lp;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float e = (M == -INFINITY || lp == -INFINITY) ? 0.f : ex2((lp - M) * kLog2e);
+    float S = e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    const float w = S > 0.f ? e / S : 0.f;   // exp(lse_p - L)
+    const int d = chunk * 128 + lane * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (d < D) {
+        for (int p0 = 0; p0 < P; p0 += 8) {
+            float4 v[8];
+            float wp[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                wp[u] = __shfl_sync(0xffffffffu, w, (p0 + u) & 31);
+                v[u] = (p0 + u < P && wp[u] != 0.f)
+                           ? __ldg(reinterpret_cast<const float4*>(o_parts + (int64_t)(p0 + u) * os + row * D + d))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                acc.x = fmaf(wp[u], v[u].x, acc.x); acc.y = fmaf(wp[u], v[u].y, acc.y);
+                acc.z = fmaf(wp[u], v[u].z, acc.z); acc.w = fmaf(wp[u], v[u].w, acc.w);
+            }
+        }
+        if (out_dtype == WS_DTYPE_F32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(out) + row * D + d) = acc;
+        } else {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + row * D + d;
+            *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x, acc.y);
+            *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z, acc.w);
+        }
+    }
+    if (lane == 0 && chunk == 0 && out_lse) out_lse[row] = (S > 0.f) ? M + logf(S) : -INFINITY;
+}
+
+// Any P and D: one warp per row, partials in sequence.
+template <bool PDL>
 __global__ void lse_merge_kernel(const float* __restrict__ o_parts, int64_t os, const float* __restrict__ lse_parts,
                                  int64_t ls, int P, int64_t R, int D, void* __restrict__ out, int out_dtype,
                                  float* __restrict__ out_lse) {
+    if (PDL) pdl_wait_primary();
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= R) return;
@@ -25,55 +81,53 @@ __global__ void lse_merge_kernel(const float* __restrict__ o_parts, int64_t os, 
     if (M != -INFINITY)
         for (int p = 0; p < P; ++p) S += ex2((__ldg(lse_parts + (int64_t)p * ls + row) - M) * kLog2e);
     const float L = (M == -INFINITY) ? -INFINITY : M + logf(S);
-    if (VEC) {
-        for (int d = lane * 4; d < D; d += 128) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (M != -INFINITY)
-                for (int p = 0; p < P; ++p) {
-                    const float w = ex2((__ldg(lse_parts + (int64_t)p * ls + row) - L) * kLog2e);
-                    if (w == 0.f) continue;
-                    const float4 v = __ldg(reinterpret_cast<const float4*>(o_parts + (int64_t)p * os + row * D + d));
-                    acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
-                }
-            if (out_dtype == WS_DTYPE_F32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(out) + row * D + d) = acc;
-            } else {
-                __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-                __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + row * D + d;
-                *reinterpret_cast<__nv_bfloat162*>(o) = lo;
-                *reinterpret_cast<__nv_bfloat162*>(o + 2) = hi;
+    for (int d = lane; d < D; d += 32) {
+        float acc = 0.f;
+        if (M != -INFINITY)
+            for (int p = 0; p < P; ++p) {
+                const float w = ex2((__ldg(lse_parts + (int64_t)p * ls + row) - L) * kLog2e);
+                if (w == 0.f) continue;
+                acc += w * __ldg(o_parts + (int64_t)p * os + row * D + d);
             }
-        }
-    } else {
-        for (int d = lane; d < D; d += 32) {
-            float acc = 0.f;
-            if (M != -INFINITY)
-                for (int p = 0; p < P; ++p) {
-                    const float w = ex2((__ldg(lse_parts + (int64_t)p * ls + row) - L) * kLog2e);
-                    if (w == 0.f) continue;
-                    acc += w * __ldg(o_parts + (int64_t)p * os + row * D + d);
-                }
-            if (out_dtype == WS_DTYPE_F32) static_cast<float*>(out)[row * D + d] = acc;
-            else static_cast<__nv_bfloat16*>(out)[row * D + d] = __float2bfloat16_rn(acc);
-        }
+        if (out_dtype == WS_DTYPE_F32) static_cast<float*>(out)[row * D + d] = acc;
+        else static_cast<__nv_bfloat16*>(out)[row * D + d] = __float2bfloat16_rn(acc);
     }
     if (lane == 0 && out_lse) out_lse[row] = L;
 }
 
+}  // namespace
+
+// Partial p's o rows start at o_parts + p * os, its lse values at lse_parts + p * ls.
 int lse_merge_launch(const float* o_parts, int64_t os, const float* lse_parts, int64_t ls, int P, int64_t R, int D,
-                     void* out, int out_dtype, float* out_lse, cudaStream_t st) {
-    const int warps = 8;
-    const int64_t blocks = (R + warps - 1) / warps;
-    if (blocks > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "lse_merge: too many rows");
-    const bool vec = (D % 4 == 0) && (os % 4 == 0) && (reinterpret_cast<uintptr_t>(o_parts) % 16 == 0) &&
+                     void* out, int out_dtype, float* out_lse, cudaStream_t st, bool after_primary) {
+    if (R == 0) return WS_OK;
+    const int warps = 4;   // small blocks: the whole grid of a decode-sized merge is resident at once
+    const bool vec = P <= 32 && (D % 4 == 0) && (os % 4 == 0) && (reinterpret_cast<uintptr_t>(o_parts) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(out) % (out_dtype == WS_DTYPE_F32 ? 16 : 8) == 0);
+    const int64_t items = vec ? R * ((D + 127) / 128) : R;
+    const int64_t blocks = (items + warps - 1) / warps;
+    if (blocks > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "lse_merge: too many rows");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(warps * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = after_primary ? 1 : 0;
+    cudaError_t e;
     if (vec)
-        lse_merge_kernel<true><<<(unsigned)blocks, warps * 32, 0, st>>>(o_parts, os, lse_parts, ls, P, R, D, out,
-                                                                          out_dtype, out_lse);
+        e = after_primary ? cudaLaunchKernelEx(&cfg, lse_merge_vec_kernel<true>, o_parts, os, lse_parts, ls, P, R, D,
+                                               out, out_dtype, out_lse)
+                          : cudaLaunchKernelEx(&cfg, lse_merge_vec_kernel<false>, o_parts, os, lse_parts, ls, P, R, D,
+                                               out, out_dtype, out_lse);
     else
-        lse_merge_kernel<false><<<(unsigned)blocks, warps * 32, 0, st>>>(o_parts, os, lse_parts, ls, P, R, D, out,
-                                                                           out_dtype, out_lse);
-    const cudaError_t e = cudaGetLastError();
+        e = after_primary ? cudaLaunchKernelEx(&cfg, lse_merge_kernel<true>, o_parts, os, lse_parts, ls, P, R, D, out,
+                                               out_dtype, out_lse)
+                          : cudaLaunchKernelEx(&cfg, lse_merge_kernel<false>, o_parts, os, lse_parts, ls, P, R, D, out,
+                                               out_dtype, out_lse);
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 

@@ -94,7 +94,6 @@ struct CsaLaunch {
 
 int csa_launch(const CsaLaunch& a);
 size_t csa_workspace_bytes(int bs, int nq, int q_f32);
-int csa_cluster_size(int64_t entries_per_seq);
 int csa_kv_quantize_launch(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
                            cudaStream_t st);
 int csa_q_quantize_launch(const float* q, int64_t rows, int hd, void* out, float* scales, cudaStream_t st);
@@ -108,6 +107,7 @@ int kv_append_launch(void* dst, int64_t dst_row, int64_t dst_tok, const void* sr
                      int64_t rows, int64_t n_new, int D, int elem_bytes, int64_t t0, cudaStream_t st);
 
 int lse_merge_launch(const float* o_parts, int64_t o_part_stride, const float* lse_parts, int64_t lse_part_stride,
-                     int P, int64_t R, int D, void* out, int out_dtype, float* out_lse, cudaStream_t st);
+                     int P, int64_t R, int D, void* out, int out_dtype, float* out_lse, cudaStream_t st,
+                     bool after_primary = false);   // true: a programmatic dependent launch of the previous grid
 
 }  // namespace ws

@@ -160,7 +160,7 @@ def test_quantisers_bit_exact_random(csa, rows, hd):
 # ------------------------------------------------------------ seeded shapes
 @pytest.mark.parametrize("bs,nq,nc,k", [(1, 1, 64, 1), (2, 8, 300, 100), (3, 16, 1000, 128), (2, 17, 1000, 129),
                                         (1, 64, 4096, 2048), (2, 65, 3000, 700), (1, 33, 5000, 4097),
-                                        (4, 128, 2000, 256)])
+                                        (4, 128, 2000, 256), (160, 2, 300, 100), (20, 8, 600, 400)])
 @pytest.mark.parametrize("int8", [False, True])
 @pytest.mark.parametrize("q_bf16", [False, True])
 def test_gather_random(bs, nq, nc, k, int8, q_bf16):

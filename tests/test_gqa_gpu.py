@@ -199,13 +199,16 @@ def test_shares_one_empty_share(ext):
     assert torch.all(out[1] == 0) and torch.all(torch.isneginf(lse[1]))
 
 
-def test_lse_merge_kernel():
-    rng = np.random.default_rng(3)
-    P, R, D = 3, 100, 128
+@pytest.mark.parametrize("P,R,D", [(3, 100, 128), (1, 7, 512), (9, 1024, 512), (32, 50, 512), (2, 10, 36),
+                                   (33, 20, 64), (5, 9, 130)])
+def test_lse_merge_kernel(P, R, D):
+    """Both merge kernels: P <= 32 with D % 4 == 0 (lane-per-partial weights,
+    all loads in flight) and the general one (P > 32 or D % 4 != 0)."""
+    rng = np.random.default_rng(3 + P)
     o = rng.standard_normal((P, R, D))
     lse = rng.standard_normal((P, R)) * 3
-    lse[1, :10] = -np.inf
-    lse[:, 50] = -np.inf
+    lse[P // 2, :5] = -np.inf
+    lse[:, R // 2] = -np.inf
     ro, rl = oracle.lse_merge(o, lse)
     out, ol = scope_b200.lse_merge(torch.tensor(o, dtype=torch.float32, device=DEV),
                                    torch.tensor(lse, dtype=torch.float32, device=DEV), torch.float32)
