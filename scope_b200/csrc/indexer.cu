@@ -10,11 +10,15 @@
 // Two launches:
 //   indexer_score_kernel  -- thread = entry, the sequence's q in shared memory,
 //                            fp32 FMA on the CUDA cores (exact fp32 products);
-//   indexer_select_kernel -- one CTA per sequence: radix select of the k-th
-//                            largest score (four 8-bit passes over the scores,
-//                            which stay in L2), collection of the k winners
-//                            (ties at the threshold taken in id order), and a
-//                            bitonic sort in shared memory.
+//   indexer_select_kernel -- one CTA per sequence: a threshold placed from a
+//                            sample of the scores keeps ~1.5 k candidates in
+//                            shared memory (one pass over the scores, which
+//                            stay in L2); radix select of the k-th largest
+//                            among them (four 8-bit passes; over all scores
+//                            when the sample misjudges), collection of the k
+//                            winners (ties at the threshold taken in id
+//                            order), and a bitonic sort in shared memory.
+// (The tcgen05 scoring kernel below replaces indexer_score_kernel for bf16.)
 #include "common.cuh"
 #include "ws_internal.h"
 
@@ -127,8 +131,10 @@ __device__ __forceinline__ int block_scan(int v, int* s_warp, int* total) {
     return before;
 }
 
-constexpr int kBatch = 16;     // scores per thread per step: four independent 16-byte loads in flight
+constexpr int kBatch = 16;     // global scores per thread per step: four independent 16-byte loads in flight
 constexpr int kEqCap = 2048;   // ties at the threshold gathered in one pass (more: ordered scan)
+constexpr int kCand = 8192;    // candidates kept in shared memory
+constexpr int kSample = 1024;  // sampled scores that place the candidate threshold
 
 // The kBatch scores of step j0 this thread owns: ids j0 + 4 * (u * kSelThreads + tid) + e for u < 4, e < 4
 // (16-byte loads when the row is 16-byte aligned); keys past nc are returned as 0 with valid = false.
@@ -153,89 +159,313 @@ __device__ __forceinline__ void load_keys(const float* sc, int64_t nc, int64_t j
     }
 }
 
-__global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float* __restrict__ scores, int64_t nc,
-                                                                     int k, int by_id, int32_t* __restrict__ out) {
-    __shared__ int s_hist[256];
-    __shared__ int s_warp[32];
-    __shared__ uint32_t s_prefix, s_mask;
-    __shared__ int s_remaining, s_ngt, s_neq;
-    __shared__ uint32_t s_key[kMaxK];
-    __shared__ int32_t s_id[kMaxK];
-    __shared__ int32_t s_eq[kEqCap];
-    const int b = blockIdx.x, tid = threadIdx.x;
-    const float* sc = scores + (int64_t)b * nc;
-    const bool vec = (reinterpret_cast<uintptr_t>(sc) & 15) == 0;
+// The keys of load_keys without the ids (0 past nc; callers test the position).
+__device__ __forceinline__ void load_keys_only(const float* sc, int64_t nc, int64_t j0, bool vec,
+                                               uint32_t (&key)[kBatch]) {
+#pragma unroll
+    for (int u = 0; u < kBatch / 4; ++u) {
+        const int64_t j = j0 + 4 * ((int64_t)u * kSelThreads + threadIdx.x);
+        float v[4];
+        if (vec && j + 3 < nc) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(sc + j));
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = j + e < nc ? __ldcg(sc + j + e) : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) key[4 * u + e] = j + e < nc ? ordered_key(v[e]) : 0u;
+    }
+}
+
+// Sources of keys for the select passes: each thread takes KB keys per step of kSelThreads * KB
+// positions (ids past the end come back as -1).
+struct GlobalKeys {   // a sequence's scores in global memory (L2: just written by the scoring kernel)
+    static constexpr int KB = kBatch;
+    const float* sc;
+    int64_t n;
+    bool vec;
+    __device__ __forceinline__ void load(int64_t j0, uint32_t (&key)[KB], int64_t (&id)[KB]) const {
+        load_keys(sc, n, j0, vec, key, id);
+    }
+};
+template <int KB_>
+struct SharedKeys {   // keys in shared memory with their ids alongside, or (id == nullptr) the position
+    static constexpr int KB = KB_;
+    const uint32_t* key;
+    const int32_t* id;
+    int n;
+    __device__ __forceinline__ void load(int64_t j0, uint32_t (&k)[KB], int64_t (&i)[KB]) const {
+#pragma unroll
+        for (int u = 0; u < KB; ++u) {
+            const int64_t j = j0 + (int64_t)u * kSelThreads + threadIdx.x;
+            const bool ok = j < n;
+            k[u] = ok ? key[j] : 0u;
+            i[u] = ok ? (id ? (int64_t)id[j] : j) : -1;
+        }
+    }
+};
+
+
+struct SelectSmem {   // the select kernel's dynamic shared memory
+    uint32_t ckey[kCand];   // candidates (before them: the samples; after them: the sort's scratch)
+    int32_t cid[kCand];
+    uint32_t key[kMaxK];    // the k winners
+    int32_t id[kMaxK];
+    int32_t eq[kEqCap];     // ids of keys equal to the threshold
+    int whist[32][256];     // warp-private histograms of a radix pass
+    int hist[256];
+    int warp[32];
+    uint32_t prefix, mask;
+    int remaining, ngt, neq, ncand;
+};
+
+// Radix select, 8 bits per pass from the top: the r-th largest key (1 <= r <= n) of the source is left in
+// s.prefix, and s.remaining = how many keys equal to it belong to the r largest.
+template <class Src>
+__device__ void radix_select(const Src& src, int64_t n, int r, SelectSmem& s) {
+    const int tid = threadIdx.x, lane = tid & 31;
     if (tid == 0) {
-        s_prefix = 0;
-        s_mask = 0;
-        s_remaining = k;
+        s.prefix = 0;
+        s.mask = 0;
+        s.remaining = r;
     }
     __syncthreads();
-    // ---- radix select: the k-th largest key, 8 bits per pass from the top
+    const int warp = tid >> 5;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = tid; i < 256; i += kSelThreads) s_hist[i] = 0;
+        for (int i = tid; i < 32 * 256; i += kSelThreads) (&s.whist[0][0])[i] = 0;
         __syncthreads();
-        const uint32_t prefix = s_prefix, mask = s_mask;
-        for (int64_t j0 = 0; j0 < nc; j0 += (int64_t)kSelThreads * kBatch) {   // warp-uniform trip count
-            uint32_t key[kBatch];
-            int64_t id[kBatch];
-            load_keys(sc, nc, j0, vec, key, id);
+        const uint32_t prefix = s.prefix, mask = s.mask;
+        for (int64_t j0 = 0; j0 < n; j0 += (int64_t)kSelThreads * Src::KB) {   // warp-uniform trip count
+            uint32_t key[Src::KB];
+            int64_t id[Src::KB];
+            src.load(j0, key, id);
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
+            for (int u = 0; u < Src::KB; ++u) {
                 const bool hit = id[u] >= 0 && (key[u] & mask) == prefix;
+                if (!__any_sync(0xffffffffu, hit)) continue;   // later passes: most warps hold no key of the prefix
                 const int bin = hit ? (int)((key[u] >> shift) & 255) : 256;
-                // one atomic per distinct bin in the warp: scores of similar magnitude share a few bins
+                // the lowest lane of each distinct bin adds the count to this warp's own histogram
+                // (keys of similar magnitude share a few bins: a block-wide histogram would serialise)
                 const uint32_t same = __match_any_sync(0xffffffffu, bin);
-                if (hit && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&s_hist[bin], __popc(same));
+                if (hit && lane == __ffs(same) - 1) s.whist[warp][bin] += __popc(same);
             }
         }
         __syncthreads();
-        if (tid == 0) {
-            int rem = s_remaining, bin = 0;
-            for (int d = 255; d >= 0; --d) {
-                if (s_hist[d] >= rem) {
-                    bin = d;
-                    break;
-                }
-                rem -= s_hist[d];
+        for (int i = tid; i < 256; i += kSelThreads) {
+            int t = 0;
+#pragma unroll 8
+            for (int w = 0; w < 32; ++w) t += s.whist[w][i];
+            s.hist[i] = t;
+        }
+        __syncthreads();
+        if (tid < 32) {   // the bin of the remaining-th largest: lane l sums bins 255-8l .. 248-8l
+            const int rem = s.remaining;
+            int c[8], tot = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                c[e] = s.hist[255 - 8 * lane - e];
+                tot += c[e];
             }
-            s_remaining = rem;   // keys of this bin (among those with the prefix) still to take
-            s_prefix = prefix | ((uint32_t)bin << shift);
-            s_mask = mask | (255u << shift);
+            int incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const int excl = incl - tot;
+            const uint32_t hitm = __ballot_sync(0xffffffffu, excl < rem && incl >= rem);
+            if (lane == (hitm ? __ffs(hitm) - 1 : 31)) {
+                int r2 = rem - excl, bin = 255 - 8 * lane - 7;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    if (c[e] >= r2) {
+                        bin = 255 - 8 * lane - e;
+                        break;
+                    }
+                    r2 -= c[e];
+                }
+                s.remaining = r2;   // keys of this bin (among those with the prefix) still to take
+                s.prefix = prefix | ((uint32_t)bin << shift);
+                s.mask = mask | (255u << shift);
+            }
         }
         __syncthreads();
     }
-    const uint32_t thr = s_prefix;       // the k-th largest key
-    const int need_eq = s_remaining;     // keys equal to it that belong to the top k
-    if (tid == 0) {
-        s_ngt = 0;
-        s_neq = 0;
+}
+
+// Every key above thr into s.key / s.id (s.ngt of them, at most kMaxK kept), and the ids of keys equal
+// to it into s.eq (s.neq of them, at most kEqCap kept).
+template <class Src>
+__device__ void collect_above(const Src& src, int64_t n, uint32_t thr, SelectSmem& s) {
+    if (threadIdx.x == 0) {
+        s.ngt = 0;
+        s.neq = 0;
     }
     __syncthreads();
-    // ---- collect every key above the threshold, and (up to kEqCap) the ids of keys equal to it
-    for (int64_t j0 = 0; j0 < nc; j0 += (int64_t)kSelThreads * kBatch) {
-        uint32_t key[kBatch];
-        int64_t id[kBatch];
-        load_keys(sc, nc, j0, vec, key, id);
+    for (int64_t j0 = 0; j0 < n; j0 += (int64_t)kSelThreads * Src::KB) {
+        uint32_t key[Src::KB];
+        int64_t id[Src::KB];
+        src.load(j0, key, id);
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
+        for (int u = 0; u < Src::KB; ++u) {
             const int64_t j = id[u];
             if (j < 0) continue;
             if (key[u] > thr) {
-                const int slot = atomicAdd(&s_ngt, 1);
+                const int slot = atomicAdd(&s.ngt, 1);
                 if (slot < kMaxK) {
-                    s_key[slot] = key[u];
-                    s_id[slot] = (int32_t)j;
+                    s.key[slot] = key[u];
+                    s.id[slot] = (int32_t)j;
                 }
             } else if (key[u] == thr) {
-                const int slot = atomicAdd(&s_neq, 1);
-                if (slot < kEqCap) s_eq[slot] = (int32_t)j;
+                const int slot = atomicAdd(&s.neq, 1);
+                if (slot < kEqCap) s.eq[slot] = (int32_t)j;
             }
         }
     }
     __syncthreads();
-    const int ngt = min(s_ngt, k);
-    const int neq = s_neq;
+}
+
+// Sorts the k winners into descending order of v, where v = key << 32 | ~id (descending key, then
+// ascending id) or v = ~id (ascending id); v is unique per winner.  Padded to N = 1024 E with values
+// below every winner's.  Each warp sorts a run of 32 E in registers (bitonic network: a pair at
+// stride s < E within a thread, else across lanes by shuffles), then the runs are merged pairwise in
+// shared memory, log2(32) levels: thread t finds where its E outputs start with one merge-path search
+// and takes them in order.  The winners' ids, in order, go to ids_out[0, k).
+template <int E>
+__device__ void merge_sort_desc(const uint32_t* key, const int32_t* id, int k, int by_id, uint64_t* A, uint64_t* B,
+                                int32_t* ids_out) {
+    constexpr int N = kSelThreads * E, R0 = 32 * E;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int j = warp * R0 + E * lane + e;
+        const uint64_t nid = (uint64_t)(uint32_t)~(j < k ? id[j] : 0x7fffffff);
+        v[e] = (j < k && !by_id) ? ((uint64_t)key[j] << 32 | nid) : nid;   // padding: ~0x7fffffff, below all
+    }
+    for (int size = 2; size <= R0; size <<= 1) {
+        for (int s = size >> 1; s > 0; s >>= 1) {
+            if (s < E) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    if (e & s) continue;
+                    const bool up = ((E * lane + e) & size) == 0;   // up: the larger first
+                    if ((v[e] > v[e + s]) != up) {
+                        const uint64_t t = v[e]; v[e] = v[e + s]; v[e + s] = t;
+                    }
+                }
+            } else {
+                const int ls = s / E;
+                const bool lower = (lane & ls) == 0;
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v[e], ls);
+                    const bool up = ((E * lane + e) & size) == 0;
+                    const bool lower_first = lower ? v[e] > o : o > v[e];
+                    if (lower_first != up) v[e] = o;   // keep own exactly when lower_first == up
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) A[warp * R0 + E * lane + e] = v[e];
+    __syncthreads();
+    for (int L = R0; L < N; L <<= 1) {
+        const int o0 = E * tid, base = o0 / (2 * L) * (2 * L), op = o0 - base;
+        const uint64_t* a = A + base;
+        const uint64_t* b = A + base + L;
+        int lo = max(0, op - L), hi = min(op, L);
+        while (lo < hi) {   // A elements among the first op outputs (ties, padding only: to B first)
+            const int mid = (lo + hi) >> 1;
+            if (a[mid] > b[op - mid - 1]) lo = mid + 1; else hi = mid;
+        }
+        int i = lo, j = op - lo;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const bool take_a = i < L && (j >= L || a[i] > b[j]);
+            B[base + op + e] = take_a ? a[i] : b[j];
+            if (take_a) ++i; else ++j;
+        }
+        __syncthreads();
+        uint64_t* t = A; A = B; B = t;
+    }
+    for (int j = tid; j < k; j += kSelThreads) ids_out[j] = (int32_t)~(uint32_t)A[j];   // A: the merged run
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float* __restrict__ scores, int64_t nc,
+                                                                     int k, int by_id, int32_t* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t sel_smem[];
+    SelectSmem& s = *reinterpret_cast<SelectSmem*>(sel_smem);
+    uint32_t* s_key = s.key;
+    int32_t* s_id = s.id;
+    int32_t* s_eq = s.eq;
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+    const float* sc = scores + (int64_t)b * nc;
+    const GlobalKeys all{sc, nc, (reinterpret_cast<uintptr_t>(sc) & 15) == 0};
+    // ---- candidates: every key at or above a threshold placed from a sample of the scores (the r-th
+    //      largest of kSample evenly spaced ones, r a few standard deviations above k's share), so that
+    //      at least k and at most kCand of them pass; the exact select then reads only the candidates,
+    //      in shared memory.  When the sample misjudges (heavy ties, adversarial orders), it reads all.
+    uint32_t t_lo = 0;   // every key passes
+    if (nc > kCand) {
+        for (int i = tid; i < kSample; i += kSelThreads) s.ckey[i] = ordered_key(__ldcg(sc + (int64_t)i * nc / kSample));
+        __syncthreads();
+        const double base = (double)k * kSample / (double)nc;
+        const int r = min(kSample, (int)ceil(base + 6.0 * sqrt(base) + 16.0));
+        radix_select(SharedKeys<kSample / kSelThreads>{s.ckey, nullptr, kSample}, kSample, r, s);
+        t_lo = s.prefix;
+    }
+    if (tid == 0) s.ncand = 0;
+    __syncthreads();
+    constexpr int G = 2;   // steps whose loads are all in flight together (128 bytes per thread)
+    for (int64_t g0 = 0; g0 < nc; g0 += (int64_t)G * kSelThreads * kBatch) {
+        uint32_t key[G][kBatch];
+#pragma unroll
+        for (int g = 0; g < G; ++g) load_keys_only(sc, nc, g0 + (int64_t)g * kSelThreads * kBatch, all.vec, key[g]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int64_t j0 = g0 + (int64_t)g * kSelThreads * kBatch;
+            auto pos = [&](int u) { return j0 + 4 * ((int64_t)(u >> 2) * kSelThreads + tid) + (u & 3); };
+            int cnt = 0;   // this thread's candidates of the step, then one shared atomic per warp
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) cnt += (pos(u) < nc && key[g][u] >= t_lo) ? 1 : 0;
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            int base = 0;
+            if (lane == 31 && incl > 0) base = atomicAdd(&s.ncand, incl);
+            int slot = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (pos(u) < nc && key[g][u] >= t_lo) {
+                    if (slot < kCand) {
+                        s.ckey[slot] = key[g][u];
+                        s.cid[slot] = (int32_t)pos(u);
+                    }
+                    ++slot;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int ncand = s.ncand;
+    if (ncand >= k && ncand <= kCand) {
+        const SharedKeys<4> cand{s.ckey, s.cid, ncand};
+        radix_select(cand, ncand, k, s);
+        collect_above(cand, ncand, s.prefix, s);
+    } else {
+        radix_select(all, nc, k, s);
+        collect_above(all, nc, s.prefix, s);
+    }
+    const uint32_t thr = s.prefix;       // the k-th largest key
+    const int need_eq = s.remaining;     // keys equal to it that belong to the top k
+    const int ngt = min(s.ngt, k);
+    const int neq = s.neq;
     if (neq <= kEqCap) {
         // the ties, lowest ids first: sort the gathered ids ascending and take need_eq of them
         int m2 = 1;
@@ -260,13 +490,13 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
             s_id[ngt + i] = s_eq[i];
         }
     } else {
-        // very many ties: take them in id order with a block-wide scan
+        // very many ties: take them in id order with a block-wide scan over all scores
         int taken = 0;
         for (int64_t j0 = 0; j0 < nc && taken < need_eq; j0 += kSelThreads) {
             const int64_t j = j0 + tid;
             const int eq = (j < nc && ordered_key(__ldcg(sc + j)) == thr) ? 1 : 0;
             int total = 0;
-            const int before = block_scan(eq, s_warp, &total);
+            const int before = block_scan(eq, s.warp, &total);
             if (eq && taken + before < need_eq) {
                 s_key[ngt + taken + before] = thr;
                 s_id[ngt + taken + before] = (int32_t)j;
@@ -275,33 +505,11 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
         }
     }
     __syncthreads();
-    // ---- bitonic sort of the k winners (padded to a power of two): descending key, then ascending id;
-    //      or ascending id
-    int n2 = 1;
-    while (n2 < k) n2 <<= 1;
-    for (int i = k + tid; i < n2; i += kSelThreads) {
-        s_key[i] = 0u;           // below every real key
-        s_id[i] = 0x7fffffff;
-    }
-    __syncthreads();
-    for (int size = 2; size <= n2; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < n2 / 2; i += kSelThreads) {
-                const int lo = 2 * i - (i & (stride - 1));
-                const int hi = lo + stride;
-                const bool up = (lo & size) == 0;   // this run sorts into the final order
-                const uint32_t ka = s_key[lo], kb = s_key[hi];
-                const int32_t ia = s_id[lo], ib = s_id[hi];
-                // "a before b" in the final order
-                const bool a_first = by_id ? (ia < ib) : (ka > kb || (ka == kb && ia < ib));
-                if (a_first != up) {
-                    s_key[lo] = kb; s_key[hi] = ka;
-                    s_id[lo] = ib;  s_id[hi] = ia;
-                }
-            }
-            __syncthreads();
-        }
-    }
+    // ---- order the k winners: descending key, then ascending id; or ascending id (the candidate
+    //      buffers, free now, hold the merge buffers)
+    uint64_t* mA = reinterpret_cast<uint64_t*>(s.ckey);   // ckey + cid: 64 KB = 2 x 4096 values
+    if (k <= 2048) merge_sort_desc<2>(s_key, s_id, k, by_id, mA, mA + 4096, s_id);
+    else merge_sort_desc<4>(s_key, s_id, k, by_id, mA, mA + 4096, s_id);
     for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = s_id[i];
 }
 
@@ -463,6 +671,23 @@ __global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __g
 
 }  // namespace idx
 
+static int select_launch(const float* scores, int64_t nc, int k, int by_id, int32_t* out, int bs, cudaStream_t st) {
+    using namespace idx;
+    const int smem = (int)sizeof(SelectSmem);
+    static int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        if (cudaFuncSetAttribute(indexer_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for indexer_select_kernel");
+        configured_dev = dev;
+    }
+    indexer_select_kernel<<<bs, kSelThreads, smem, st>>>(scores, nc, k, by_id, out);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
 size_t indexer_workspace_bytes(int bs, int64_t nc) {
     return kCounterHeaderBytes + align_up((size_t)std::max(bs, 1) * (size_t)std::max<int64_t>(nc, 1) * 4, 256);
 }
@@ -516,12 +741,7 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
             map, static_cast<const __nv_bfloat16*>(q), w, tp);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-        if (k > 0) {
-            indexer_select_kernel<<<bs, kSelThreads, 0, st>>>(scores, nc, k, by_id, out_ids);
-            e = cudaGetLastError();
-            if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-        }
-        return WS_OK;
+        return k > 0 ? select_launch(scores, nc, k, by_id, out_ids, bs, st) : WS_OK;
     }
     const size_t smem = ((size_t)nH * hd + nH) * sizeof(float);
     auto kfn = bf16 ? indexer_score_kernel<true> : indexer_score_kernel<false>;
@@ -532,12 +752,7 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
     kfn<<<grid, kScoreThreads, smem, st>>>(q, kv, w, nH, hd, nc, scores);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-    if (k > 0) {
-        indexer_select_kernel<<<bs, kSelThreads, 0, st>>>(scores, nc, k, by_id, out_ids);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-    }
-    return WS_OK;
+    return k > 0 ? select_launch(scores, nc, k, by_id, out_ids, bs, st) : WS_OK;
 }
 
 }  // namespace ws

@@ -102,6 +102,24 @@ def test_exact_ties_take_lower_ids_first():
     assert ids.tolist() == order
 
 
+@pytest.mark.parametrize("nc,distinct,k", [(30000, 10, 150), (20000, 3000, 2048), (50000, 1, 7)])
+def test_ties_beyond_the_candidate_buffer(nc, distinct, k):
+    """More scores than the shared-memory candidate buffer holds, with heavy ties: the sampled
+    threshold then passes too many keys (or exactly-equal ones straddle it) and the select runs over
+    all scores; ties still go to the lowest ids first."""
+    g = torch.Generator().manual_seed(nc + distinct)
+    base = torch.randn(distinct, 32, generator=g)
+    kv = base[torch.randint(0, distinct, (nc,), generator=g)][None].contiguous()
+    q = torch.randn(1, 2, 32, generator=g)
+    w = torch.ones(1, 2)
+    ids, our = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), k, return_scores=True)
+    ids, our = ids.cpu().numpy()[0], our.cpu().numpy()[0]
+    order = np.lexsort((np.arange(nc), -our))[:k]     # descending score, then ascending id
+    assert ids.tolist() == order.tolist()
+    ids_id = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), k, order="id").cpu().numpy()[0]
+    assert ids_id.tolist() == sorted(order.tolist())
+
+
 def test_ds4_size():
     """A DeepSeek-V4-like indexer shape: 64 index heads x 128 dims over 65536
     compressed entries, top-2048, two sequences against the oracle."""
