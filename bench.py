@@ -22,6 +22,7 @@ Workloads (the default is the one the metric's
   cfg5  CSA sparse decode, DeepSeek-V4 style: bs=16, 64 heads, 65536 int8
         entries, top-2048 gather, entry-sharded over N GPUs
   idx   the CSA indexer top-k that produces cfg5's ids (one GPU)
+  mla_abs  cfg3 with the absorb and up-projection GEMMs either side (one GPU)
 """
 from __future__ import annotations
 
@@ -449,6 +450,62 @@ class Mla(Workload):
         return cpu_ref_mla(self.B, self.nH, self.S, budget_s, max_calls, warm)
 
 
+class MlaAbsorbed(Mla):
+    """mla_abs: cfg3's absorbed-MLA step with the projections either side
+    (ws_mla_decode_absorbed: q_nope . W_UK, the tcgen05 decode, and the merge
+    fused with the up-projection o . W_UV^T), DeepSeek-V2-Lite shapes: nop = 128,
+    vhd = 128, random-init kv_b_proj weight; output [8, 16, 128] bf16.  The
+    reference runs this step as torch.bmm + fused_cpu_attn_mla_compressed + bmm
+    (system/deepseek.py:257-265, :355-407)."""
+
+    name = "mla_abs"
+    kernel_name = "mla_absorb_kernel + mla_decode_kernel (tcgen05) + mla_merge_up_kernel"
+    profile_name = "mla_decode_cfg3"
+
+    def __init__(self, world, rank, B=8, nH=16, S=16384, seed=3):
+        super().__init__(world, rank, B=B, nH=nH, S=S, seed=seed)
+        from scope_b200 import cpu_attn
+        self.workload = f"mla_absorbed_step_ds2lite_b{B}_h{nH}_s{S}_nop128_vhd128"
+        dev = self.qp.device
+        g = torch.Generator(device=dev).manual_seed(seed + 100)
+        self.nop = self.vhd = 128
+        self.q_nope = bf16_randn((B, nH, self.nop), g, dev)
+        self.w = (torch.randn(nH * (self.nop + self.vhd), 512, generator=g, device=dev) * 0.05).bfloat16()
+        self._absorbed = cpu_attn.mla_decode_absorbed
+        self.qn_host = torch.randn(B, nH, self.nop).bfloat16().pin_memory()
+        self.outv_host = torch.empty(B, nH, self.vhd, dtype=torch.bfloat16).pin_memory()
+        self.kernels_per_step = 3
+
+    def kernel_bytes(self):
+        return (self.B * self.S * (512 + 64) * 2 + self.B * self.nH * (self.nop + 64 + self.vhd) * 2
+                + 2 * self.nH * 128 * 512 * 2 + self.B * self.nH * 4)
+
+    def kernel(self, i):
+        c = i % self.copies
+        self.out = self._absorbed(self.q_nope, self.qpe, self.c[c], self.p[c], self.w, self.scale)
+
+    step = kernel
+
+    def e2e_step(self, i):
+        c = i % self.copies
+        self.q_nope.copy_(self.qn_host, non_blocking=True)
+        self.qpe.copy_(self.qpe_host, non_blocking=True)
+        self.c[c][:, self.S - 1].copy_(self.cnew_host, non_blocking=True)
+        self.p[c][:, self.S - 1].copy_(self.pnew_host, non_blocking=True)
+        out = self._absorbed(self.q_nope, self.qpe, self.c[c], self.p[c], self.w, self.scale)
+        self.outv_host.copy_(out, non_blocking=True)
+
+    def e2e_bytes(self):
+        return ((self.qn_host.numel() + self.qpe_host.numel() + self.cnew_host.numel() + self.pnew_host.numel()) * 2,
+                self.outv_host.numel() * 2)
+
+    def config(self):
+        d = super().config()
+        d.update({"workload": self.workload, "qk_nope_head_dim": self.nop, "v_head_dim": self.vhd,
+                  "weights": "random-init kv_b_proj (N(0,1) x 0.05)"})
+        return d
+
+
 class Csa(Workload):
     """cfg5: CSA sparse decode (DeepSeek-V4 style), bs=16, 64 heads over a
     512-wide latent, nc=65536 int8 entries with one fp32 scale each, top-2048
@@ -807,7 +864,7 @@ def cpu_reference_for(name, args, budget_s, max_calls, warm):
     if name == "cfg2":
         return cpu_ref_shares(16, 32, 8, 128, budget_s, max_calls, warm), \
             "gqa_mixtral_b16_ragged_1024_32768_two_shares"
-    if name == "cfg3":
+    if name in ("cfg3", "mla_abs"):   # the reference's CPU part of the step (its bmm's run on the GPU)
         return cpu_ref_mla(8, 16, 16384, budget_s, max_calls, warm), "mla_absorbed_ds2lite_b8_h16_s16384"
     if name == "cfg5":
         return cpu_ref_csa(16, 64, 65536, 2048, budget_s, max_calls, warm), "csa_ds4_b16_h64_nc65536_top2048_int8"
@@ -826,6 +883,8 @@ def make_workload(name, world, rank, args):
         return GqaShares(world, rank)
     if name == "cfg3":
         return Mla(world, rank, S=args.kv_len or 16384)
+    if name == "mla_abs":
+        return MlaAbsorbed(world, rank, S=args.kv_len or 16384)
     if name == "cfg5":
         return Csa(world, rank, nc=args.kv_len or 65536)
     if name == "idx":
@@ -833,7 +892,7 @@ def make_workload(name, world, rank, args):
     raise ValueError(name)
 
 
-WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "idx")
+WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "idx", "mla_abs")
 
 
 # -------------------------------------------------------------------- main

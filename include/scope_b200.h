@@ -147,6 +147,31 @@ int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const 
                   void* workspace, size_t workspace_bytes, void* stream);
 size_t ws_mla_decode_workspace_size(int B, int nH, int S);
 
+/* Absorbed-MLA decode step with the projections either side of the attention:
+ * the decode branch of _mla_compressed_forward (system/deepseek.py:257-265 the
+ * absorb, :355-404 the attention over the cache and the merge, :405-407 the
+ * up-projection), which the reference runs as torch.bmm + the CPU kernel + bmm:
+ *   q_proj = q_nope . W_UK ;  o = softmax(scale (q_proj . c + q_pe . p)) . c ;
+ *   out = bf16(o / l) . W_UV^T
+ *   q_nope [B, nH, nop] bf16 (nop % 4 == 0, <= 256); q_pe [B*nH, 64], c_kv [B, S, 512],
+ *   k_pe [B, S, 64] bf16;
+ *   w_uk: head h's [nop, 512] block at w_uk + h * w_uk_head_stride, w_uv: head
+ *   h's [vhd, 512] block at w_uv + h * w_uv_head_stride (elements; bf16, 16-byte
+ *   aligned).  The reference's kv_b_proj.weight viewed [nH, nop + vhd, 512] is
+ *   passed as is: w_uk = weight, w_uv = weight + nop * 512, both head strides
+ *   (nop + vhd) * 512;
+ *   out [B, nH, vhd] bf16; out_lse [B*nH] fp32 optional (NULL).
+ * Four launches: the absorb GEMM (fp32 accumulation, bf16 q_proj kept in the
+ * workspace), the split-KV decode and its merge (bf16 o_n in the workspace), and
+ * the up-projection GEMM (programmatic dependent launches after the decode).
+ * This build supports nH == 16.
+ */
+int ws_mla_decode_absorbed(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
+                           const void* c_kv, const void* k_pe, const void* w_uv, int64_t w_uv_head_stride, int B,
+                           int nH, int S, int nop, int vhd, float scale, void* out, float* out_lse, void* workspace,
+                           size_t workspace_bytes, void* stream);
+size_t ws_mla_decode_absorbed_workspace_size(int B, int nH, int S);
+
 /* ---- CSA index modes (ws_csa_decode with an id list) */
 #define WS_CSA_IDX_ALL 0            /* every id must lie in this buffer's range; others are skipped and
                                        reported as WS_ERR_DEVICE by ws_status_take */

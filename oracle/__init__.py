@@ -157,6 +157,35 @@ def mla_compressed(q_proj, q_pe, c_kv, k_pe, scale):
     return o, m, s
 
 
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """x rounded to bf16 (round-half-even) and returned as float64."""
+    return bits_to_f32(f32_to_bf16_bits(np.asarray(x, np.float32))).astype(np.float64)
+
+
+def mla_absorbed(q_nope, q_pe, c_kv, k_pe, w_uk, w_uv, scale):
+    """The absorbed-MLA decode step with its projections (system/deepseek.py:257-265
+    q_proj = bmm(q_nope, W_UK) in bf16; :355-404 attention over the cache and merge;
+    :405-407 o_n = (o / s).to(bf16), out = bmm(o_n, W_UV^T)).  uint16 bf16 inputs:
+    q_nope [B, nH, nop], q_pe [B*nH, 64], c_kv [B, S, 512], k_pe [B, S, 64],
+    w_uk [nH, nop, 512], w_uv [nH, vhd, 512].
+
+    Returns float64 (out [B, nH, vhd], lse [B*nH]); the bf16 roundings the reference
+    makes (q_proj, o_n) are made here too.
+    """
+    qn = bits_to_f32(np.ascontiguousarray(q_nope)).astype(np.float64)
+    wk = bits_to_f32(np.ascontiguousarray(w_uk)).astype(np.float64)
+    wv = bits_to_f32(np.ascontiguousarray(w_uv)).astype(np.float64)
+    B, nH, nop = qn.shape
+    q_proj = bf16_round(np.einsum("bhk,hkc->bhc", qn, wk)).reshape(B * nH, -1)
+    o, m, s = mla_compressed(f32_to_bf16_bits(q_proj.astype(np.float32)), q_pe, c_kv, k_pe, scale)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        on = np.where(s[:, None] > 0, o / s[:, None], 0.0)
+        lse = np.where(s > 0, m + np.log(s), -np.inf)
+    on = bf16_round(on).reshape(B, nH, -1)
+    out = np.einsum("bhc,hvc->bhv", on, wv)
+    return out, lse
+
+
 def csa_attend(q, kv, scale, idx=None, kv_range=None, kv_scale=None):
     """CSA attention over a shared latent (csa_attn.cpp:200-281, :1587-1656, :1819-1883).
 

@@ -179,6 +179,47 @@ def mla_decode(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_p
     return out, lse
 
 
+def mla_decode_absorbed(q_nope: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_pe: torch.Tensor,
+                        kv_b_proj_weight: torch.Tensor, scale: float, return_lse: bool = False):
+    """The decode branch of the reference's absorbed MLA forward with the projections
+    either side of the attention (system/deepseek.py:257-265 absorb, :355-404 attention
+    and merge, :405-407 up-projection), on the GPU:
+
+        q_proj = q_nope . W_UK ;  o = attention over (c_kv, k_pe) ;  out = bf16(o) . W_UV^T
+
+    q_nope [B, nH, nop] (or [B, nH, 1, nop]), q_pe [B, nH, 64] (or [B*nH, 64] / [B, nH, 1, 64]),
+    c_kv [B, S, 512], k_pe [B, S, 64], kv_b_proj_weight [nH * (nop + vhd), 512], all bf16.
+    Returns out [B, nH, vhd] bf16 (and lse [B, nH] fp32 with return_lse)."""
+    dev = _require_cuda("mla_decode_absorbed", q_nope, q_pe, c_kv, k_pe, kv_b_proj_weight)
+    for t in (q_nope, q_pe, c_kv, k_pe, kv_b_proj_weight):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError("mla_decode_absorbed requires bf16 inputs")
+    B, S, CLR = c_kv.shape
+    if CLR != 512 or k_pe.shape != (B, S, 64):
+        raise RuntimeError("expected c_kv [B, S, 512] and k_pe [B, S, 64]")
+    nH = q_nope.shape[1]
+    nop = q_nope.shape[-1]
+    qn = q_nope.reshape(B, nH, nop).contiguous()
+    qpe = q_pe.reshape(B * nH, 64).contiguous()
+    w = kv_b_proj_weight if kv_b_proj_weight.is_contiguous() else kv_b_proj_weight.contiguous()
+    w = w.reshape(nH, -1, 512)
+    vhd = w.shape[1] - nop
+    if vhd < 1:
+        raise RuntimeError("kv_b_proj_weight must hold nH x (nop + vhd) rows of 512")
+    hs = (nop + vhd) * 512   # W_UK and W_UV are read in place: head blocks at this stride
+    c_kv, k_pe = c_kv.contiguous(), k_pe.contiguous()
+    out = torch.empty(B, nH, vhd, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, nH, dtype=torch.float32, device=dev) if return_lse else None
+    L_ = lib()
+    with torch.cuda.device(dev):
+        ws = workspaces.get(L_.ws_mla_decode_absorbed_workspace_size(B, nH, S), dev)
+        rc = L_.ws_mla_decode_absorbed(ptr(qn), w.data_ptr(), hs, ptr(qpe), ptr(c_kv), ptr(k_pe),
+                                       w.data_ptr() + nop * 512 * 2, hs, B, nH, S, nop, vhd, float(scale), ptr(out),
+                                       ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
+    check(rc, "ws_mla_decode_absorbed")
+    return (out, lse) if return_lse else out
+
+
 def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, out_dtype=torch.bfloat16):
     """GQA decode returning (out [B_kv, G, Dv] normalised in out_dtype (bf16 or fp32),
     lse fp32 [B_kv, G]).

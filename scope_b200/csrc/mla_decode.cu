@@ -204,15 +204,7 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
             int b = (int)(t_begin / p.tpb);
             int tl = (int)(t_begin - (int64_t)b * p.tpb);
             for (int64_t t = t_begin; t < t_end; ++t, ++i) {
-                if (b != seg) {
-                    if (qn > 0 && !wait_bar(s, bar(s, B_Q_EMPTY), (qn - 1) & 1, p.status)) break;
-                    mbar_arrive_expect_tx(bar(s, B_Q_FULL), 9 * QBOX_BYTES);
-                    for (int kb = 0; kb < 8; ++kb)
-                        tma_load_3d(qs + kb * QBOX_BYTES, &maps.q, bar(s, B_Q_FULL), kb * 64, b * NH, 0);
-                    tma_load_3d(qs + 8 * QBOX_BYTES, &maps.qpe, bar(s, B_Q_FULL), 0, b * NH, 0);
-                    ++qn;
-                    seg = b;
-                }
+                const bool new_seg = b != seg;   // this tile starts a sequence: its q follows the tile's latent
                 bool ok = true;
                 for (int pr = 0; pr < 4 && ok; ++pr) {
                     const int64_t n = 4 * i + pr;
@@ -227,6 +219,18 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
                                 c1, c2);
                 }
                 if (!ok) break;
+                if (new_seg) {
+                    if (qn > 0 && !wait_bar(s, bar(s, B_Q_EMPTY), (qn - 1) & 1, p.status)) break;
+                    // q may come from the previous grid on the stream (the absorb GEMM, launched as its
+                    // programmatic dependent); without one this returns at once
+                    if (qn == 0) pdl_wait_primary();
+                    mbar_arrive_expect_tx(bar(s, B_Q_FULL), 9 * QBOX_BYTES);
+                    for (int kb = 0; kb < 8; ++kb)
+                        tma_load_3d(qs + kb * QBOX_BYTES, &maps.q, bar(s, B_Q_FULL), kb * 64, b * NH, 0);
+                    tma_load_3d(qs + 8 * QBOX_BYTES, &maps.qpe, bar(s, B_Q_FULL), 0, b * NH, 0);
+                    ++qn;
+                    seg = b;
+                }
                 const int e = (int)(i % NE);
                 const uint32_t ue = (uint32_t)(i / NE);
                 if (ue > 0 && !wait_bar(s, bar(s, B_PE_EMPTY + e), (ue - 1) & 1, p.status)) break;
@@ -514,16 +518,15 @@ struct MergeParams {
     float* out_lse;
 };
 
-// Log-sum-exp merge of a batch's pieces.  One warp per (batch, head, quarter
-// of the 512 latent dims); lane k first fetches piece k's (m, l), the warp
-// reduces them, then every lane accumulates one float4 of the quarter over
-// all pieces with eight loads in flight.
-__global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
-    pdl_wait_primary();
-    const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (wid >= p.B * NH * 4) return;
-    const int row = wid >> 2, quarter = wid & 3;
+// Log-sum-exp merge of one row's pieces over one quarter of the 512 latent dims, by one warp: lane k
+// first fetches piece k's (m, l), the warp reduces them, then every lane accumulates one float4 of the
+// quarter over all pieces with eight loads in flight.  Returns the un-normalised quarter (lane's
+// float4), the row's sum L and max M (log2 units; -inf when empty).
+struct MergedQuarter {
+    float4 acc;
+    float L, M;
+};
+__device__ __forceinline__ MergedQuarter merge_quarter(const MergeParams& p, int row, int quarter, int lane) {
     const int b = row / NH, h = row - b * NH;
     int c0 = 0, npc = 0;
     if (p.tpb > 0) {
@@ -572,13 +575,32 @@ __global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    return {acc, L, M};
+}
+
+__device__ __forceinline__ void write_row_stats(const MergeParams& p, int row, float L, float M) {
     const bool empty = !(L > 0.f);
     const float mnat = empty ? -INFINITY : M * kLn2;
+    if (p.out_max) p.out_max[row] = mnat;
+    if (p.out_sum) p.out_sum[row] = empty ? 0.f : L;
+    if (p.out_lse) p.out_lse[row] = empty ? -INFINITY : mnat + logf(L);
+}
+
+// The merge: one warp per (batch, head, quarter of the latent).
+__global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
+    pdl_wait_primary();
+    const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wid >= p.B * NH * 4) return;
+    const int row = wid >> 2, quarter = wid & 3;
+    const MergedQuarter m = merge_quarter(p, row, quarter, lane);
+    const float4 acc = m.acc;
+    const bool empty = !(m.L > 0.f);
     const int64_t oi = (int64_t)row * CLR + quarter * 128 + lane * 4;
     if (p.out_mode == WS_OUT_UNNORM_F32) {
         *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc;
     } else {
-        const float inv = empty ? 0.f : 1.f / L;
+        const float inv = empty ? 0.f : 1.f / m.L;
         if (p.out_mode == WS_OUT_NORM_F32) {
             *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
                 make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
@@ -588,10 +610,107 @@ __global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
             *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
         }
     }
-    if (lane == 0 && quarter == 0) {
-        if (p.out_max) p.out_max[row] = mnat;
-        if (p.out_sum) p.out_sum[row] = empty ? 0.f : L;
-        if (p.out_lse) p.out_lse[row] = empty ? -INFINITY : mnat + logf(L);
+    if (lane == 0 && quarter == 0) write_row_stats(p, row, m.L, m.M);
+}
+
+// The up-projection of the absorbed form (system/deepseek.py:405-407): out[b, h, v] = sum_c o_n[b, h, c] *
+// w_uv[h][v][c], o_n the merged output rounded to bf16 (as the reference rounds it before its bmm).
+// CTA (h, 32 outputs v): the 32 weight rows (32 KB, contiguous) and the B rows o_n[:, h, :] are staged in
+// shared memory with every 16-byte load issued at once; thread (b, v) then accumulates in fp32.
+// A programmatic dependent launch of the merge.
+constexpr int kUpV = 32;
+__global__ void __launch_bounds__(256) mla_up_kernel(const __nv_bfloat16* __restrict__ o_n, int B,
+                                                     const __nv_bfloat16* __restrict__ w_uv, int64_t w_head_stride,
+                                                     int vhd, __nv_bfloat16* __restrict__ out) {
+    __shared__ __align__(16) __nv_bfloat16 s_w[kUpV * CLR];   // 32 KB
+    __shared__ __align__(16) __nv_bfloat16 s_o[8 * CLR];      // 8 KB: eight batches at a time
+    const int h = blockIdx.x, v0 = blockIdx.y * kUpV, tid = threadIdx.x;
+    const int nv = min(kUpV, vhd - v0);
+    const __nv_bfloat16* wh = w_uv + (size_t)h * w_head_stride + (size_t)v0 * CLR;
+    // the weights do not depend on the merge: requested first (asynchronous copies, all in flight)
+    for (int i = tid; i < nv * CLR / 8; i += 256) cp_async16(smem_u32(s_w + 8 * i), wh + 8 * i, true);
+    pdl_wait_primary();   // o_n is written by the merge
+    for (int b0 = 0; b0 < B; b0 += 8) {
+        const int nb = min(8, B - b0);
+        __syncthreads();
+        for (int i = tid; i < nb * CLR / 8; i += 256) {
+            const int bb = i / (CLR / 8), q = i - bb * (CLR / 8);
+            cp_async16(smem_u32(s_o + bb * CLR + 8 * q), o_n + ((size_t)(b0 + bb) * NH + h) * CLR + 8 * q, true);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        const int bb = tid / kUpV, v = tid - bb * kUpV;   // 8 batches x 32 outputs
+        if (bb < nb && v < nv) {
+            const __nv_bfloat16* wr = s_w + v * CLR;
+            const __nv_bfloat16* orow = s_o + bb * CLR;
+            float acc = 0.f;
+#pragma unroll 4
+            for (int c = 0; c < CLR; c += 8) {
+                // rotate the start by v so the 32 threads of a warp read different banks of s_w
+                const int cc = (c + v * 8) & (CLR - 1);
+                const uint4 w8 = *reinterpret_cast<const uint4*>(wr + cc);
+                const uint4 o8 = *reinterpret_cast<const uint4*>(orow + cc);
+                const uint32_t ww[4] = {w8.x, w8.y, w8.z, w8.w}, oo[4] = {o8.x, o8.y, o8.z, o8.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    acc = fmaf(__uint_as_float(oo[u] << 16), __uint_as_float(ww[u] << 16), acc);
+                    acc = fmaf(__uint_as_float(oo[u] & 0xffff0000u), __uint_as_float(ww[u] & 0xffff0000u), acc);
+                }
+            }
+            out[((size_t)(b0 + bb) * NH + h) * vhd + v0 + v] = __float2bfloat16_rn(acc);
+        }
+    }
+}
+
+// The absorb step of the absorbed form (system/deepseek.py:257-265): q_proj[b, h, :] = q_nope[b, h, :] . w_uk[h]
+// (q_nope [B, NH, nop], w_uk[h] [nop, 512] at head stride w_head_stride, both bf16; fp32 accumulation, bf16
+// q_proj [B * NH, 512]).  CTA (h, 128 latent columns): the weight block (nop x 128, 16-byte loads all
+// issued at once) and eight batches' q rows at a time in shared memory; thread = latent column.
+__global__ void __launch_bounds__(128) mla_absorb_kernel(const __nv_bfloat16* __restrict__ q_nope,
+                                                         const __nv_bfloat16* __restrict__ w_uk, int64_t w_head_stride,
+                                                         int B, int nop, __nv_bfloat16* __restrict__ q_proj) {
+    extern __shared__ __align__(16) __nv_bfloat16 s_w[];   // nop rows of 128 columns (<= 64 KB, dynamic)
+    __shared__ __align__(16) float s_q[8][256];
+    pdl_launch_dependents();   // the decode grid may start streaming the latent cache now
+    const int h = blockIdx.x, c0 = blockIdx.y * 128, tid = threadIdx.x;
+    const __nv_bfloat16* wb = w_uk + (size_t)h * w_head_stride + c0;
+    for (int i = tid; i < nop * 16; i += 128) {   // row k: 16 copies of 8 columns, all in flight
+        const int k = i >> 4, q = i & 15;
+        cp_async16(smem_u32(s_w + k * 128 + 8 * q), wb + (size_t)k * CLR + 8 * q, true);
+    }
+    cp_async_wait_all();
+    for (int b0 = 0; b0 < B; b0 += 8) {
+        const int nb = min(8, B - b0);
+        __syncthreads();
+        float qv[16];   // every load issued before the first store (nb * nop <= 2048)
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int i = tid + r * 128, bb = i / nop, k = i - bb * nop;
+            qv[r] = i < nb * nop ? __bfloat162float(q_nope[((size_t)(b0 + bb) * NH + h) * nop + k]) : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int i = tid + r * 128, bb = i / nop, k = i - bb * nop;
+            if (i < nb * nop) s_q[bb][k] = qv[r];
+        }
+        __syncthreads();
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+        for (int k = 0; k < nop; k += 4) {   // four k per step: the loads of a step are independent
+            float w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) w[u] = __bfloat162float(s_w[(k + u) * 128 + tid]);
+#pragma unroll
+            for (int bb = 0; bb < 8; ++bb) {
+                const float4 q4 = *reinterpret_cast<const float4*>(&s_q[bb][k]);
+                acc[bb] = fmaf(q4.x, w[0], acc[bb]);
+                acc[bb] = fmaf(q4.y, w[1], acc[bb]);
+                acc[bb] = fmaf(q4.z, w[2], acc[bb]);
+                acc[bb] = fmaf(q4.w, w[3], acc[bb]);
+            }
+        }
+        for (int bb = 0; bb < nb; ++bb)
+            q_proj[((size_t)(b0 + bb) * NH + h) * CLR + c0 + tid] = __float2bfloat16_rn(acc[bb]);
     }
 }
 
@@ -605,7 +724,7 @@ size_t mla_workspace_bytes(int B, int nH, int S) {
 
 int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
                float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
-               size_t workspace_bytes, cudaStream_t st) {
+               size_t workspace_bytes, cudaStream_t st, bool after_primary) {
     using namespace mla;
     if (nH != NH) return set_error(WS_ERR_UNSUPPORTED, "mla_decode: this build supports 16 heads per sequence");
     if (B < 0 || S < 0) return set_error(WS_ERR_INVALID_ARG, "mla_decode: bad shape");
@@ -648,8 +767,17 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
                 return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for mla_decode_kernel");
             configured_dev = dev;
         }
-        mla_decode_kernel<<<nctas, kThreads, SMEM_BYTES, st>>>(maps, prm);
-        cudaError_t e = cudaGetLastError();
+        cudaLaunchConfig_t dcfg = {};
+        dcfg.gridDim = dim3((unsigned)nctas);
+        dcfg.blockDim = dim3(kThreads);
+        dcfg.dynamicSmemBytes = SMEM_BYTES;
+        dcfg.stream = st;
+        cudaLaunchAttribute dattr[1];
+        dattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        dattr[0].val.programmaticStreamSerializationAllowed = 1;
+        dcfg.attrs = dattr;
+        dcfg.numAttrs = after_primary ? 1 : 0;
+        cudaError_t e = cudaLaunchKernelEx(&dcfg, mla_decode_kernel, maps, prm);
         if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
     }
     MergeParams mp;
@@ -676,6 +804,63 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
     cudaError_t e = cudaLaunchKernelEx(&cfg, mla_merge_kernel, mp);
     if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
     return WS_OK;
+}
+
+size_t mla_absorbed_workspace_bytes(int B, int nH, int S) {
+    // the decode's own part, then q_proj and o_n (bf16 [B * 16, 512] each)
+    return align_up(mla_workspace_bytes(B, nH, S), 256) + 2 * align_up((size_t)std::max(B, 1) * mla::NH * mla::CLR * 2, 256);
+}
+
+int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
+                        const void* c_kv, const void* k_pe, const void* w_uv, int64_t w_uv_head_stride, int B, int nH,
+                        int S, int nop, int vhd, float scale, void* out, float* out_lse, void* workspace,
+                        size_t workspace_bytes, cudaStream_t st) {
+    using namespace mla;
+    if (nH != NH) return set_error(WS_ERR_UNSUPPORTED, "mla_decode_absorbed: this build supports 16 heads per sequence");
+    if (B < 0 || S < 0 || nop < 4 || nop > 256 || nop % 4 || vhd < 1 || w_uk_head_stride < (int64_t)nop * CLR ||
+        w_uv_head_stride < (int64_t)vhd * CLR)
+        return set_error(WS_ERR_INVALID_ARG, "mla_decode_absorbed: bad shape or head stride");
+    if (B == 0) return WS_OK;
+    if (!workspace || workspace_bytes < mla_absorbed_workspace_bytes(B, nH, S))
+        return set_error(WS_ERR_WORKSPACE, "mla_decode_absorbed: workspace too small (see ws_mla_decode_absorbed_workspace_size)");
+    if (reinterpret_cast<uintptr_t>(w_uk) % 16 || reinterpret_cast<uintptr_t>(w_uv) % 16 || w_uk_head_stride % 8 ||
+        w_uv_head_stride % 8)
+        return set_error(WS_ERR_INVALID_ARG, "mla_decode_absorbed: weights and head strides must be 16-byte aligned");
+    const size_t dec = align_up(mla_workspace_bytes(B, nH, S), 256);
+    const size_t rowbuf = align_up((size_t)B * NH * CLR * 2, 256);
+    __nv_bfloat16* q_proj = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + dec);
+    __nv_bfloat16* o_n = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + dec + rowbuf);
+    const int smem = nop * 128 * 2;
+    static int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        if (cudaFuncSetAttribute(mla_absorb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 256 * 128 * 2) !=
+            cudaSuccess)
+            return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for mla_absorb_kernel");
+        configured_dev = dev;
+    }
+    mla_absorb_kernel<<<dim3(NH, CLR / 128), 128, smem, st>>>(static_cast<const __nv_bfloat16*>(q_nope),
+                                                              static_cast<const __nv_bfloat16*>(w_uk), w_uk_head_stride,
+                                                              B, nop, q_proj);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+    int rc = mla_launch(q_proj, q_pe, c_kv, k_pe, B, nH, S, scale, WS_OUT_NORM_BF16, o_n, nullptr, nullptr, out_lse,
+                        workspace, dec, st, /*after_primary=*/true);
+    if (rc != WS_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(NH, (unsigned)((vhd + kUpV - 1) / kUpV));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, mla_up_kernel, static_cast<const __nv_bfloat16*>(o_n), B,
+                           static_cast<const __nv_bfloat16*>(w_uv), w_uv_head_stride, vhd,
+                           static_cast<__nv_bfloat16*>(out));
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
 }  // namespace ws

@@ -68,9 +68,16 @@ int gqa_f32_launch(const void* q, const void* k, const void* v, int64_t k_sb, in
                    void* out_sum, float* out_lse, void* workspace, size_t workspace_bytes, cudaStream_t st);
 
 size_t mla_workspace_bytes(int B, int nH, int S);
+// after_primary: the decode grid is a programmatic dependent of the previous launch on the stream, which
+// writes q_proj (its producer waits for that grid before loading q)
 int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
                float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
-               size_t workspace_bytes, cudaStream_t st);
+               size_t workspace_bytes, cudaStream_t st, bool after_primary = false);
+size_t mla_absorbed_workspace_bytes(int B, int nH, int S);
+int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
+                        const void* c_kv, const void* k_pe, const void* w_uv, int64_t w_uv_head_stride, int B, int nH,
+                        int S, int nop, int vhd, float scale, void* out, float* out_lse, void* workspace,
+                        size_t workspace_bytes, cudaStream_t st);
 
 struct CsaLaunch {
     const void* q;

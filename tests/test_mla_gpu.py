@@ -96,3 +96,53 @@ def test_cfg3_size(ext):
     mo, ml = scope_b200.lse_merge(parts_o, parts_l, torch.float32)
     assert (mo - o / s[:, None]).abs().max().item() < 1e-3
     assert (ml - (m + s.log())).abs().max().item() < 1e-3
+
+
+# ------------------------------------------------ absorbed step with its projections
+def absorbed_inputs(B, S, nop, vhd, nH=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q_nope = torch.randn(B, nH, nop, generator=g).bfloat16()
+    qpe = torch.randn(B * nH, 64, generator=g).bfloat16()
+    c = torch.randn(B, S, 512, generator=g).bfloat16()
+    p = torch.randn(B, S, 64, generator=g).bfloat16()
+    w = (torch.randn(nH * (nop + vhd), 512, generator=g) * 0.05).bfloat16()   # kv_b_proj.weight
+    return q_nope, qpe, c, p, w
+
+
+@pytest.mark.parametrize("B,S,nop,vhd", [(1, 1, 128, 128), (2, 300, 128, 128), (8, 4096, 128, 128),
+                                         (3, 129, 64, 96), (11, 257, 128, 128), (2, 0, 128, 128)])
+def test_absorbed_step_matches_oracle(B, S, nop, vhd):
+    """ws_mla_decode_absorbed (absorb GEMM, tcgen05 decode, merge fused with the up-projection) against
+    the oracle of system/deepseek.py's absorbed decode branch, bf16 roundings included."""
+    q_nope, qpe, c, p, w = absorbed_inputs(B, S, nop, vhd, seed=B * 131 + S)
+    scale = 192 ** -0.5
+    out, lse = scope_b200.cpu_attn.mla_decode_absorbed(q_nope.to(DEV), qpe.to(DEV), c.to(DEV), p.to(DEV),
+                                                        w.to(DEV), scale, return_lse=True)
+    assert out.dtype == torch.bfloat16 and tuple(out.shape) == (B, 16, vhd)
+    w3 = w.view(16, nop + vhd, 512)
+    ro, rl = oracle.mla_absorbed(oracle.bf16_bits(q_nope), oracle.bf16_bits(qpe), oracle.bf16_bits(c),
+                                 oracle.bf16_bits(p), oracle.bf16_bits(w3[:, :nop].contiguous()),
+                                 oracle.bf16_bits(w3[:, nop:].contiguous()), scale)
+    o = out.float().cpu().numpy()
+    assert np.abs(o - ro).max() < TOL_OUT
+    lse = lse.cpu().numpy().reshape(-1)
+    if S == 0:
+        assert np.all(o == 0) and np.all(np.isneginf(lse))
+    else:
+        assert np.abs(lse - rl).max() < TOL_LSE
+
+
+def test_absorbed_step_equals_unfused_composition():
+    """The fused step against the reference's own order of operations on the GPU: bmm absorb (torch),
+    the MLA decode, bf16 cast, bmm up-projection (torch)."""
+    B, S, nop, vhd = 8, 16384, 128, 128
+    q_nope, qpe, c, p, w = (t.to(DEV) for t in absorbed_inputs(B, S, nop, vhd, seed=7))
+    scale = 192 ** -0.5
+    out = scope_b200.cpu_attn.mla_decode_absorbed(q_nope, qpe, c, p, w, scale)
+    w3 = w.view(16, nop + vhd, 512)
+    w_uk, w_uv = w3[:, :nop], w3[:, nop:]
+    qp = torch.bmm(q_nope.reshape(B * 16, 1, nop), w_uk.expand(B, 16, nop, 512).reshape(B * 16, nop, 512))
+    o, _ = scope_b200.cpu_attn.mla_decode(qp.reshape(B * 16, 512).contiguous(), qpe, c, p, scale)
+    ref = torch.bmm(o.view(B * 16, 1, 512),
+                    w_uv.transpose(1, 2).expand(B, 16, 512, vhd).reshape(B * 16, 512, vhd)).view(B, 16, vhd)
+    assert (out.float() - ref.float()).abs().max().item() < TOL_OUT
