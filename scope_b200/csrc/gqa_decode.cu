@@ -64,6 +64,7 @@ struct GqaParams {
     float* ws_part;
     int* ws_cnt;
     int* status;
+    int defer_merge;           // dense rows split over many CTAs: pieces are merged by gqa_merge_kernel
 };
 
 struct Seg {
@@ -262,6 +263,7 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
         flags[0] = 0;   // abort
     }
     __syncthreads();
+    pdl_launch_dependents();   // a deferred merge may be scheduled now; it waits for this grid's completion
 
     const int64_t total = tab.total();
     // Tiles are split over min(grid, total) CTAs so that every working CTA
@@ -425,7 +427,7 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                 }
             }
         }
-        if (np > 1) {
+        if (np > 1 && !p.defer_merge) {
             __threadfence();
             named_bar_sync(1, kConsumerWarps * 32);
             if (ctid == 0) flags[1] = (atomicAdd(p.ws_cnt + sg.group, 1) == np - 1);
@@ -476,7 +478,7 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                 {
                     constexpr int NCH = NG * DVP / 4;
                     constexpr int CPT = (NCH + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
-                    constexpr int KB = CPT >= 4 ? 4 : 16 / (2 * CPT);
+                    constexpr int KB = CPT >= 4 ? 8 : 32 / CPT;   // 16 or 32 pieces' loads in flight per chunk
                     float4 acc[CPT];
 #pragma unroll
                     for (int c = 0; c < CPT; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -624,6 +626,107 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
     if (cur.j >= 0) flush(cur);
 }
 
+// --------------------------------------------------------------- deferred merge
+// Dense rows whose tiles span many CTAs: each CTA has filed its piece (un-normalised o of the group's
+// heads, their max and sum), and the group's pieces are combined here by log-sum-exp.  One single-warp
+// CTA per (group, head, 32 value dims), so the reads spread over as many SMs as there are such items:
+// lane k takes piece k's (m, l) and lane d accumulates value dim d over the pieces; up to 64 pieces
+// are read in one round trip.  A programmatic dependent launch of the decode grid.
+constexpr int kMergeBatch = 64;   // pieces merged in one round trip (two lanes' worth of (m, l))
+template <int DVP, int NG>
+__global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tpr, int64_t total, int nctas) {
+    constexpr int SLOT_FLOATS = NG * DVP + 2 * NG;
+    __shared__ float s_w[kMaxPieces];
+    pdl_wait_primary();
+    const int lane = threadIdx.x;
+    const int nchunk = (p.Dv + 31) / 32;
+    const int64_t item = blockIdx.x;
+    const int chunk = (int)(item % nchunk);
+    const int64_t gg = item / nchunk;
+    const int group = (int)(gg / p.G), grp = (int)(gg - (int64_t)group * p.G);
+    const int64_t t0 = (int64_t)group * tpr;
+    const int c0 = (int)split_owner(t0, total, nctas);
+    const int npc = (int)split_owner(t0 + tpr - 1, total, nctas) - c0 + 1;
+    if (npc <= 1) return;   // a group inside one CTA: the decode kernel wrote its output itself
+    const float* base = p.ws_part + (int64_t)(c0 + group) * SLOT_FLOATS;   // piece k: slot c0 + k + group
+    const int d = chunk * 32 + lane;
+    const bool dv = d < p.Dv;
+    const float* col = base + grp * DVP + (dv ? d : 0);
+    float M, L, acc = 0.f;
+    if (npc <= kMergeBatch) {
+        // one round trip: lane k's (m, l) of pieces k and k + 32 and lane d's value column, all issued together
+        float v[kMergeBatch], mk[2], lk[2];
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) v[u] = u < npc ? __ldcg(col + (int64_t)u * SLOT_FLOATS) : 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int k = lane + 32 * r;
+            const float* pp = base + (int64_t)k * SLOT_FLOATS + NG * DVP;
+            mk[r] = k < npc ? __ldcg(pp + grp) : -INFINITY;
+            lk[r] = k < npc ? __ldcg(pp + NG + grp) : 0.f;
+        }
+        M = fmaxf(mk[0], mk[1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        float w[2];
+        L = 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            w[r] = mk[r] == -INFINITY ? 0.f : ex2(mk[r] - Mu);
+            L += w[r] * lk[r];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) acc = fmaf(__shfl_sync(0xffffffffu, w[u >> 5], u & 31), v[u], acc);
+    } else {
+        M = -INFINITY;
+        for (int k = lane; k < npc; k += 32) M = fmaxf(M, __ldcg(base + (int64_t)k * SLOT_FLOATS + NG * DVP + grp));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        L = 0.f;
+        for (int k = lane; k < npc; k += 32) {
+            const float* pp = base + (int64_t)k * SLOT_FLOATS + NG * DVP;
+            const float w = ex2(__ldcg(pp + grp) - Mu);
+            s_w[k] = w;
+            L += w * __ldcg(pp + NG + grp);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        __syncwarp();
+        for (int k0 = 0; k0 < npc; k0 += kMergeBatch) {
+            float v[kMergeBatch];
+#pragma unroll
+            for (int u = 0; u < kMergeBatch; ++u)
+                v[u] = k0 + u < npc ? __ldcg(col + (int64_t)(k0 + u) * SLOT_FLOATS) : 0.f;
+#pragma unroll
+            for (int u = 0; u < kMergeBatch; ++u)
+                if (k0 + u < npc) acc = fmaf(s_w[k0 + u], v[u], acc);
+        }
+    }
+    if (!dv) return;
+    store_final(p, group, grp, d, acc, M, L);
+}
+
+template <int DVP, int NG>
+static int launch_merge(const GqaParams& p, int tpr, int64_t total, int nctas, cudaStream_t st) {
+    const int64_t items = (int64_t)p.n_rows * p.G * ((p.Dv + 31) / 32);
+    if (items > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: too many rows for the deferred merge");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)items);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_merge_kernel<DVP, NG>, p, tpr, total, nctas);
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
 // -------------------------------------------------------------------- host
 template <int DKP, int DVP, int NT, int STAGES>
 static int launch_cfg(const GqaMaps& maps, const GqaParams& p, int nctas, size_t extra_smem, cudaStream_t st) {
@@ -726,8 +829,22 @@ int gqa_launch(const GqaLaunch& a) {
     p.ws_cnt = static_cast<int*>(a.workspace);
     p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
     const size_t extra_smem = a.varlen ? size_t(a.B + 1) * 4 : 0;
-    (void)total_tiles;
-    return dispatch(maps, p, a.Dk, a.Dv, nctas, extra_smem, static_cast<cudaStream_t>(a.stream));
+    // Dense rows spanning more than 8 CTAs each: the last CTA of a row would read every piece of it alone,
+    // so the pieces are merged by gqa_merge_kernel over many SMs instead.
+    const int tpr = (a.L + kTile - 1) / kTile;
+    if (!a.varlen && a.L > 0 && total_tiles > 0) {
+        const int64_t per_cta = (total_tiles + nctas - 1) / nctas;
+        p.defer_merge = (tpr + per_cta - 1) / per_cta + 1 > 8;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(a.stream);
+    int rc = dispatch(maps, p, a.Dk, a.Dv, nctas, extra_smem, st);
+    if (rc != WS_OK || !p.defer_merge) return rc;
+    const int DVP = (a.Dv + 63) / 64 * 64, NG = (a.G <= 8 ? 1 : 2) * 8;
+    if (DVP == 64 && NG == 8) return launch_merge<64, 8>(p, tpr, total_tiles, nctas, st);
+    if (DVP == 64 && NG == 16) return launch_merge<64, 16>(p, tpr, total_tiles, nctas, st);
+    if (DVP == 128 && NG == 8) return launch_merge<128, 8>(p, tpr, total_tiles, nctas, st);
+    if (DVP == 128 && NG == 16) return launch_merge<128, 16>(p, tpr, total_tiles, nctas, st);
+    return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: unsupported value width for the deferred merge");
 }
 
 size_t gqa_workspace_bytes(int G, int Dv, int nseg, int n_groups, int nctas) {
