@@ -13,11 +13,11 @@
 namespace ws {
 namespace {
 
-// P <= 32, D % 4 == 0: one warp per (row, 128-column chunk).  Lane p holds
-// partial p's weight; every partial's 16-byte load of the chunk is issued
-// before the first is used, so a warp keeps up to P loads in flight.
-template <bool PDL>
-__global__ void __launch_bounds__(128) lse_merge_vec_kernel(const float* __restrict__ o_parts, int64_t os, const float* __restrict__ lse_parts,
+// P <= PB (8, 16 or 32), D % 4 == 0: one warp per (row, 128-column chunk).  Lane p holds partial p's
+// log-sum-exp; every partial's 16-byte load of the lane's four columns is issued together with them,
+// so the merge costs one round trip to memory.
+template <bool PDL, int PB>
+__global__ void lse_merge_vec_kernel(const float* __restrict__ o_parts, int64_t os, const float* __restrict__ lse_parts,
                                      int64_t ls, int P, int64_t R, int D, void* __restrict__ out, int out_dtype,
                                      float* __restrict__ out_lse) {
     if (PDL) pdl_wait_primary();   // the partials are written by the previous grid
@@ -27,6 +27,13 @@ __global__ void __launch_bounds__(128) lse_merge_vec_kernel(const float* __restr
     if (item >= R * nchunk) return;
     const int64_t row = item / nchunk;
     const int chunk = (int)(item - row * nchunk);
+    const int d = chunk * 128 + lane * 4;
+    const bool dv = d < D;
+    float4 v[PB];
+#pragma unroll
+    for (int u = 0; u < PB; ++u)
+        v[u] = (u < P && dv) ? __ldg(reinterpret_cast<const float4*>(o_parts + (int64_t)u * os + row * D + d))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
     const float lp = lane < P ? __ldg(lse_parts + (int64_t)lane * ls + row) : -INFINITY;
     float M = lp;
 #pragma unroll
@@ -35,26 +42,17 @@ __global__ void __launch_bounds__(128) lse_merge_vec_kernel(const float* __restr
     float S = e;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-    const float w = S > 0.f ? e / S : 0.f;   // exp(lse_p - L)
-    const int d = chunk * 128 + lane * 4;
+    const float w = S > 0.f ? e / S : 0.f;   // exp(lse_p - L); 0 for an empty partial, whose o is never used
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (d < D) {
-        for (int p0 = 0; p0 < P; p0 += 8) {
-            float4 v[8];
-            float wp[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                wp[u] = __shfl_sync(0xffffffffu, w, (p0 + u) & 31);
-                v[u] = (p0 + u < P && wp[u] != 0.f)
-                           ? __ldg(reinterpret_cast<const float4*>(o_parts + (int64_t)(p0 + u) * os + row * D + d))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                acc.x = fmaf(wp[u], v[u].x, acc.x); acc.y = fmaf(wp[u], v[u].y, acc.y);
-                acc.z = fmaf(wp[u], v[u].z, acc.z); acc.w = fmaf(wp[u], v[u].w, acc.w);
-            }
+    for (int u = 0; u < PB; ++u) {
+        const float wu = __shfl_sync(0xffffffffu, w, u & 31);
+        if (wu != 0.f) {   // an empty partial may hold anything (even NaN): skip it
+            acc.x = fmaf(wu, v[u].x, acc.x); acc.y = fmaf(wu, v[u].y, acc.y);
+            acc.z = fmaf(wu, v[u].z, acc.z); acc.w = fmaf(wu, v[u].w, acc.w);
         }
+    }
+    if (dv) {
         if (out_dtype == WS_DTYPE_F32) {
             *reinterpret_cast<float4*>(static_cast<float*>(out) + row * D + d) = acc;
         } else {
@@ -118,12 +116,13 @@ int lse_merge_launch(const float* o_parts, int64_t os, const float* lse_parts, i
     cfg.attrs = attr;
     cfg.numAttrs = after_primary ? 1 : 0;
     cudaError_t e;
-    if (vec)
-        e = after_primary ? cudaLaunchKernelEx(&cfg, lse_merge_vec_kernel<true>, o_parts, os, lse_parts, ls, P, R, D,
-                                               out, out_dtype, out_lse)
-                          : cudaLaunchKernelEx(&cfg, lse_merge_vec_kernel<false>, o_parts, os, lse_parts, ls, P, R, D,
-                                               out, out_dtype, out_lse);
-    else
+    if (vec) {
+        auto kv = after_primary ? (P <= 8 ? lse_merge_vec_kernel<true, 8>
+                                          : P <= 16 ? lse_merge_vec_kernel<true, 16> : lse_merge_vec_kernel<true, 32>)
+                                : (P <= 8 ? lse_merge_vec_kernel<false, 8>
+                                          : P <= 16 ? lse_merge_vec_kernel<false, 16> : lse_merge_vec_kernel<false, 32>);
+        e = cudaLaunchKernelEx(&cfg, kv, o_parts, os, lse_parts, ls, P, R, D, out, out_dtype, out_lse);
+    } else
         e = after_primary ? cudaLaunchKernelEx(&cfg, lse_merge_kernel<true>, o_parts, os, lse_parts, ls, P, R, D, out,
                                                out_dtype, out_lse)
                           : cudaLaunchKernelEx(&cfg, lse_merge_kernel<false>, o_parts, os, lse_parts, ls, P, R, D, out,
