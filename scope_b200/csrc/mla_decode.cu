@@ -518,66 +518,6 @@ struct MergeParams {
     float* out_lse;
 };
 
-// Log-sum-exp merge of one row's pieces over one quarter of the 512 latent dims, by one warp: lane k
-// first fetches piece k's (m, l), the warp reduces them, then every lane accumulates one float4 of the
-// quarter over all pieces with eight loads in flight.  Returns the un-normalised quarter (lane's
-// float4), the row's sum L and max M (log2 units; -inf when empty).
-struct MergedQuarter {
-    float4 acc;
-    float L, M;
-};
-__device__ __forceinline__ MergedQuarter merge_quarter(const MergeParams& p, int row, int quarter, int lane) {
-    const int b = row / NH, h = row - b * NH;
-    int c0 = 0, npc = 0;
-    if (p.tpb > 0) {
-        const int64_t total = (int64_t)p.B * p.tpb;
-        const int64_t t0 = (int64_t)b * p.tpb;
-        c0 = (int)split_owner(t0, total, p.nctas);
-        npc = (int)split_owner(t0 + p.tpb - 1, total, p.nctas) - c0 + 1;
-    }
-    const float* base = p.ws_part + (int64_t)(c0 + b) * SLOT_FLOATS;
-    // pass 1: global max and sum over the pieces (32 pieces per round)
-    float M = -INFINITY;
-    for (int k0 = 0; k0 < npc; k0 += 32) {
-        const int k = k0 + lane;
-        const float m = k < npc ? __ldg(base + (int64_t)k * SLOT_FLOATS + NH * CLR + h) : -INFINITY;
-        M = fmaxf(M, m);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int off = h * CLR + quarter * 128 + lane * 4;
-    for (int k0 = 0; k0 < npc; k0 += 32) {
-        const int kl = k0 + lane;
-        float wl = 0.f;
-        if (kl < npc) {
-            const float* pp = base + (int64_t)kl * SLOT_FLOATS;
-            wl = ex2(__ldg(pp + NH * CLR + h) - Mu);
-            L += wl * __ldg(pp + NH * CLR + NH + h);
-        }
-        const int n = min(32, npc - k0);
-        for (int u0 = 0; u0 < n; u0 += 8) {
-            float4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                v[u] = (u0 + u < n) ? __ldg(reinterpret_cast<const float4*>(base + (int64_t)(k0 + u0 + u) * SLOT_FLOATS + off))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float w = __shfl_sync(0xffffffffu, wl, (u0 + u) & 31);
-                if (u0 + u < n) {
-                    acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    return {acc, L, M};
-}
-
 __device__ __forceinline__ void write_row_stats(const MergeParams& p, int row, float L, float M) {
     const bool empty = !(L > 0.f);
     const float mnat = empty ? -INFINITY : M * kLn2;
@@ -586,31 +526,73 @@ __device__ __forceinline__ void write_row_stats(const MergeParams& p, int row, f
     if (p.out_lse) p.out_lse[row] = empty ? -INFINITY : mnat + logf(L);
 }
 
-// The merge: one warp per (batch, head, quarter of the latent).
+// Log-sum-exp merge of a row's pieces.  One warp per (batch, head, 32 latent dims), so the reads spread
+// over many SMs: lane k takes piece k's (m, l) and lane d accumulates latent dim d over the pieces.
+// Up to 64 pieces are read in one round trip (the common case: a sequence spans ~20 CTAs); more take
+// batches of 64.
+constexpr int kMlaMergeBatch = 64;
 __global__ void __launch_bounds__(256) mla_merge_kernel(const MergeParams p) {
     pdl_wait_primary();
-    const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (wid >= p.B * NH * 4) return;
-    const int row = wid >> 2, quarter = wid & 3;
-    const MergedQuarter m = merge_quarter(p, row, quarter, lane);
-    const float4 acc = m.acc;
-    const bool empty = !(m.L > 0.f);
-    const int64_t oi = (int64_t)row * CLR + quarter * 128 + lane * 4;
-    if (p.out_mode == WS_OUT_UNNORM_F32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc;
-    } else {
-        const float inv = empty ? 0.f : 1.f / m.L;
-        if (p.out_mode == WS_OUT_NORM_F32) {
-            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oi) =
-                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        } else {
-            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + oi;
-            *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-            *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-        }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wid = blockIdx.x * 8 + warp;
+    if (wid >= p.B * NH * (CLR / 32)) return;
+    const int row = wid / (CLR / 32), chunk = wid - row * (CLR / 32);
+    const int b = row / NH, h = row - b * NH;
+    int c0 = 0, npc = 0;
+    if (p.tpb > 0) {
+        const int64_t total = (int64_t)p.B * p.tpb;
+        const int64_t t0 = (int64_t)b * p.tpb;
+        c0 = (int)split_owner(t0, total, p.nctas);
+        npc = (int)split_owner(t0 + p.tpb - 1, total, p.nctas) - c0 + 1;
     }
-    if (lane == 0 && quarter == 0) write_row_stats(p, row, m.L, m.M);
+    const float* base = p.ws_part + (int64_t)(c0 + b) * SLOT_FLOATS;   // piece k at base + k * SLOT_FLOATS
+    const int d = chunk * 32 + lane;
+    const float* col = base + h * CLR + d;
+    // a batch's (m, l) loads are issued together with its values: one round trip per 64 pieces
+    float M = -INFINITY, L = 0.f, acc = 0.f;
+    for (int k0 = 0; k0 < npc; k0 += kMlaMergeBatch) {
+        float v[kMlaMergeBatch], mk[2], lk[2];
+#pragma unroll
+        for (int u = 0; u < kMlaMergeBatch; ++u)
+            v[u] = k0 + u < npc ? __ldg(col + (int64_t)(k0 + u) * SLOT_FLOATS) : 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int k = k0 + lane + 32 * r;
+            const float* pp = base + (int64_t)k * SLOT_FLOATS + NH * CLR;
+            mk[r] = k < npc ? __ldg(pp + h) : -INFINITY;
+            lk[r] = k < npc ? __ldg(pp + NH + h) : 0.f;
+        }
+        float Mb = fmaxf(mk[0], mk[1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Mb = fmaxf(Mb, __shfl_xor_sync(0xffffffffu, Mb, o));
+        const float Mn = fmaxf(M, Mb);
+        const float Mu = (Mn == -INFINITY) ? 0.f : Mn;
+        const float a = (M == -INFINITY) ? 0.f : ex2(M - Mu);   // rescale of the earlier batches
+        float w[2], Lb = 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            w[r] = mk[r] == -INFINITY ? 0.f : ex2(mk[r] - Mu);
+            Lb += w[r] * lk[r];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Lb += __shfl_xor_sync(0xffffffffu, Lb, o);
+        float ab = 0.f;
+#pragma unroll
+        for (int u = 0; u < kMlaMergeBatch; ++u) ab = fmaf(__shfl_sync(0xffffffffu, w[u >> 5], u & 31), v[u], ab);
+        acc = acc * a + ab;
+        L = L * a + Lb;
+        M = Mn;
+    }
+    const bool empty = !(L > 0.f);
+    const int64_t oi = (int64_t)row * CLR + d;
+    if (p.out_mode == WS_OUT_UNNORM_F32) {
+        static_cast<float*>(p.out)[oi] = empty ? 0.f : acc;
+    } else {
+        const float o = empty ? 0.f : acc / L;
+        if (p.out_mode == WS_OUT_NORM_F32) static_cast<float*>(p.out)[oi] = o;
+        else static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
+    }
+    if (lane == 0 && chunk == 0) write_row_stats(p, row, L, M);
 }
 
 // The up-projection of the absorbed form (system/deepseek.py:405-407): out[b, h, v] = sum_c o_n[b, h, c] *
@@ -792,7 +774,7 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
     mp.out_sum = out_sum;
     mp.out_lse = out_lse;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((B * NH * 4 + 7) / 8));
+    cfg.gridDim = dim3((unsigned)((B * NH * (CLR / 32) + 7) / 8));
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
