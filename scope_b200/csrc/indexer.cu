@@ -207,17 +207,25 @@ struct SharedKeys {   // keys in shared memory with their ids alongside, or (id 
 };
 
 
-struct SelectSmem {   // the select kernel's dynamic shared memory
+constexpr int kBuckets = 4096;   // linear buckets of the bucket select (four per thread)
+constexpr int kBucketCap = 64;   // largest bucket among the winners the bucket select ranks (more: radix select)
+static_assert(kBuckets == 4 * kSelThreads, "bucket_count gives each thread four buckets");
+static_assert(kSample == kSelThreads, "sample_threshold gives each thread one sample");
+
+struct SelectSmem {   // the select kernels' dynamic shared memory
     uint32_t ckey[kCand];   // candidates (before them: the samples; after them: the sort's scratch)
     int32_t cid[kCand];
-    uint32_t key[kMaxK];    // the k winners
-    int32_t id[kMaxK];
+    uint32_t key[kMaxK + kBucketCap];   // the k winners (bucket select: bucket order, up to a bucket past k)
+    int32_t id[kMaxK + kBucketCap];
     int32_t eq[kEqCap];     // ids of keys equal to the threshold
     int whist[32][256];     // warp-private histograms of a radix pass
+    int bstart[kBuckets + 1];   // bucket select: keys in the buckets above each bucket, then the count
+    int bcur[kBuckets];         // bucket counts, then the scatter cursors
     int hist[256];
     int warp[32];
-    uint32_t prefix, mask;
-    int remaining, ngt, neq, ncand;
+    uint32_t wlo[32], whi[32];
+    uint32_t prefix, mask, kmin, kmax;
+    int remaining, ngt, neq, ncand, flag, dstar, gbase, last;
 };
 
 // Radix select, 8 bits per pass from the top: the r-th largest key (1 <= r <= n) of the source is left in
@@ -394,74 +402,159 @@ __device__ void merge_sort_desc(const uint32_t* key, const int32_t* id, int k, i
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float* __restrict__ scores, int64_t nc,
-                                                                     int k, int by_id, int32_t* __restrict__ out) {
-    extern __shared__ __align__(16) uint8_t sel_smem[];
-    SelectSmem& s = *reinterpret_cast<SelectSmem*>(sel_smem);
-    uint32_t* s_key = s.key;
-    int32_t* s_id = s.id;
-    int32_t* s_eq = s.eq;
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
-    const float* sc = scores + (int64_t)b * nc;
-    const GlobalKeys all{sc, nc, (reinterpret_cast<uintptr_t>(sc) & 15) == 0};
-    // ---- candidates: every key at or above a threshold placed from a sample of the scores (the r-th
-    //      largest of kSample evenly spaced ones, r a few standard deviations above k's share), so that
-    //      at least k and at most kCand of them pass; the exact select then reads only the candidates,
-    //      in shared memory.  When the sample misjudges (heavy ties, adversarial orders), it reads all.
-    uint32_t t_lo = 0;   // every key passes
-    if (nc > kCand) {
-        for (int i = tid; i < kSample; i += kSelThreads) s.ckey[i] = ordered_key(__ldcg(sc + (int64_t)i * nc / kSample));
-        __syncthreads();
-        const double base = (double)k * kSample / (double)nc;
-        const int r = min(kSample, (int)ceil(base + 6.0 * sqrt(base) + 16.0));
-        radix_select(SharedKeys<kSample / kSelThreads>{s.ckey, nullptr, kSample}, kSample, r, s);
-        t_lo = s.prefix;
+// Block-wide min and max (of one key pair per thread) into s.kmin / s.kmax.
+__device__ __forceinline__ void block_minmax(uint32_t lo, uint32_t hi, SelectSmem& s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
     }
-    if (tid == 0) s.ncand = 0;
+    if (lane == 0) {
+        s.wlo[warp] = lo;
+        s.whi[warp] = hi;
+    }
     __syncthreads();
-    constexpr int G = 2;   // steps whose loads are all in flight together (128 bytes per thread)
-    for (int64_t g0 = 0; g0 < nc; g0 += (int64_t)G * kSelThreads * kBatch) {
-        uint32_t key[G][kBatch];
+    if (warp == 0) {
+        lo = s.wlo[lane];
+        hi = s.whi[lane];
 #pragma unroll
-        for (int g = 0; g < G; ++g) load_keys_only(sc, nc, g0 + (int64_t)g * kSelThreads * kBatch, all.vec, key[g]);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const int64_t j0 = g0 + (int64_t)g * kSelThreads * kBatch;
-            auto pos = [&](int u) { return j0 + 4 * ((int64_t)(u >> 2) * kSelThreads + tid) + (u & 3); };
-            int cnt = 0;   // this thread's candidates of the step, then one shared atomic per warp
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) cnt += (pos(u) < nc && key[g][u] >= t_lo) ? 1 : 0;
-            int incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            int base = 0;
-            if (lane == 31 && incl > 0) base = atomicAdd(&s.ncand, incl);
-            int slot = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                if (pos(u) < nc && key[g][u] >= t_lo) {
-                    if (slot < kCand) {
-                        s.ckey[slot] = key[g][u];
-                        s.cid[slot] = (int32_t)pos(u);
-                    }
-                    ++slot;
-                }
-            }
+        for (int o = 16; o > 0; o >>= 1) {
+            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        }
+        if (lane == 0) {
+            s.kmin = lo;
+            s.kmax = hi;
         }
     }
     __syncthreads();
-    const int ncand = s.ncand;
-    if (ncand >= k && ncand <= kCand) {
-        const SharedKeys<4> cand{s.ckey, s.cid, ncand};
-        radix_select(cand, ncand, k, s);
-        collect_above(cand, ncand, s.prefix, s);
-    } else {
-        radix_select(all, nc, k, s);
-        collect_above(all, nc, s.prefix, s);
+}
+
+// kBuckets equal-width buckets over the keys [lo, hi], numbered from the top (bucket 0 holds the
+// largest keys): a key's bucket is its offset above lo shifted right until the range fits 12 bits.
+struct Buckets {
+    uint32_t lo;
+    int shift;
+    __device__ __forceinline__ Buckets(uint32_t lo_, uint32_t hi_) : lo(lo_) {
+        const int bits = 32 - __clz(hi_ - lo_);   // 0 when lo == hi
+        shift = max(0, bits - 12);
     }
+    __device__ __forceinline__ int of(uint32_t key) const { return kBuckets - 1 - (int)((key - lo) >> shift); }
+    __device__ __forceinline__ uint32_t lower_edge(int d) const { return lo + ((uint32_t)(kBuckets - 1 - d) << shift); }
+};
+
+// Counts the n keys (shared memory) per bucket: s.bstart[d] = keys in the buckets above d,
+// s.bstart[kBuckets] = n, s.bcur = s.bstart; s.dstar = the bucket of the r-th largest key (1 <= r <= n);
+// s.flag = 1 when a bucket that starts before r holds more than cap keys.
+__device__ void bucket_count(const uint32_t* key, int n, const Buckets& bk, int r, int cap, SelectSmem& s) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < kBuckets; i += kSelThreads) s.bcur[i] = 0;
+    if (tid == 0) s.flag = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += kSelThreads) atomicAdd(&s.bcur[bk.of(key[i])], 1);
+    __syncthreads();
+    int c[4], tot = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        c[e] = s.bcur[4 * tid + e];
+        tot += c[e];
+    }
+    int total = 0;
+    int st = block_scan(tot, s.warp, &total);
+    bool over = false;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        s.bstart[4 * tid + e] = st;
+        s.bcur[4 * tid + e] = st;
+        if (st < r && st + c[e] >= r) s.dstar = 4 * tid + e;
+        over |= st < r && c[e] > cap;
+        st += c[e];
+    }
+    if (over) s.flag = 1;
+    if (tid == 0) s.bstart[kBuckets] = total;
+    __syncthreads();
+}
+
+// The candidate threshold of a sequence with nc > kCand scores: the lower edge of the bucket that holds
+// the r-th largest of kSample evenly spaced scores (r = k's share plus six standard deviations plus 16),
+// so at least r samples lie at or above it.  Uses s.ckey [0, kSample).
+__device__ uint32_t sample_threshold(const float* sc, int64_t nc, int k, SelectSmem& s) {
+    const int tid = threadIdx.x;
+    const uint32_t key = ordered_key(__ldcg(sc + (int64_t)tid * nc / kSample));
+    s.ckey[tid] = key;
+    block_minmax(key, key, s);
+    const double base = (double)k * kSample / (double)nc;
+    const int r = min(kSample, (int)ceil(base + 6.0 * sqrt(base) + 16.0));
+    const Buckets bk(s.kmin, s.kmax);
+    bucket_count(s.ckey, kSample, bk, r, kSample, s);
+    return bk.lower_edge(s.dstar);
+}
+
+// The k largest of the n candidates in s.ckey / s.cid (k <= n <= kCand), in descending key order and
+// ascending id among equal keys, into s.ckey / s.cid [0, k): count the candidates per bucket, place the
+// keys of every bucket that starts before k in bucket order, and rank each inside its bucket.  Returns
+// false, with the candidates untouched, when one of those buckets holds more than kBucketCap keys
+// (heavy ties, or a few keys far above the rest).
+__device__ bool bucket_select(int n, int k, SelectSmem& s) {
+    const int tid = threadIdx.x;
+    uint32_t lo = 0xffffffffu, hi = 0;
+    for (int i = tid; i < n; i += kSelThreads) {
+        lo = min(lo, s.ckey[i]);
+        hi = max(hi, s.ckey[i]);
+    }
+    block_minmax(lo, hi, s);
+    const Buckets bk(s.kmin, s.kmax);
+    bucket_count(s.ckey, n, bk, k, kBucketCap, s);
+    if (s.flag) return false;
+    for (int i = tid; i < n; i += kSelThreads) {
+        const uint32_t key = s.ckey[i];
+        const int d = bk.of(key);
+        if (s.bstart[d] < k) {   // positions stay below k - 1 + kBucketCap
+            const int pos = atomicAdd(&s.bcur[d], 1);
+            s.key[pos] = key;
+            s.id[pos] = s.cid[i];
+        }
+    }
+    __syncthreads();
+    const int filled = s.bstart[s.dstar + 1];
+    for (int p = tid; p < filled; p += kSelThreads) {
+        const uint32_t key = s.key[p];
+        const int32_t id = s.id[p];
+        const int d = bk.of(key);
+        const int b0 = s.bstart[d], b1 = s.bstart[d + 1];
+        int rank = 0;
+        for (int q = b0; q < b1; ++q) {
+            const uint32_t kq = s.key[q];
+            rank += (kq > key || (kq == key && s.id[q] < id)) ? 1 : 0;
+        }
+        const int f = b0 + rank;
+        if (f < k) {
+            s.ckey[f] = key;
+            s.cid[f] = id;
+        }
+    }
+    __syncthreads();
+    return true;
+}
+
+// Orders the k winners in s.key / s.id (descending key then ascending id, or ascending id) into s.id;
+// the candidate buffers, free by now, hold the merge buffers (ckey + cid: 64 KB = 2 x 4096 values).
+__device__ __forceinline__ void sort_winners(int k, int by_id, SelectSmem& s) {
+    uint64_t* mA = reinterpret_cast<uint64_t*>(s.ckey);
+    if (k <= 2048) merge_sort_desc<2>(s.key, s.id, k, by_id, mA, mA + 4096, s.id);
+    else merge_sort_desc<4>(s.key, s.id, k, by_id, mA, mA + 4096, s.id);
+}
+
+// The k winners among the n keys of src by radix select, the ties at the threshold in id order, then
+// ordered: their ids into s.id [0, k).  sc / nc: the sequence's scores, for the ordered scan that takes
+// very many ties.
+template <class Src>
+__device__ void radix_path(const Src& src, int64_t n, int k, int by_id, const float* sc, int64_t nc,
+                           SelectSmem& s) {
+    const int tid = threadIdx.x;
+    radix_select(src, n, k, s);
+    collect_above(src, n, s.prefix, s);
     const uint32_t thr = s.prefix;       // the k-th largest key
     const int need_eq = s.remaining;     // keys equal to it that belong to the top k
     const int ngt = min(s.ngt, k);
@@ -470,24 +563,24 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
         // the ties, lowest ids first: sort the gathered ids ascending and take need_eq of them
         int m2 = 1;
         while (m2 < neq) m2 <<= 1;
-        for (int i = neq + tid; i < m2; i += kSelThreads) s_eq[i] = 0x7fffffff;
+        for (int i = neq + tid; i < m2; i += kSelThreads) s.eq[i] = 0x7fffffff;
         __syncthreads();
         for (int size = 2; size <= m2; size <<= 1)
             for (int stride = size >> 1; stride > 0; stride >>= 1) {
                 for (int i = tid; i < m2 / 2; i += kSelThreads) {
                     const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
                     const bool up = (lo & size) == 0;
-                    const int32_t a = s_eq[lo], c = s_eq[hi];
+                    const int32_t a = s.eq[lo], c = s.eq[hi];
                     if ((a < c) != up && a != c) {
-                        s_eq[lo] = c;
-                        s_eq[hi] = a;
+                        s.eq[lo] = c;
+                        s.eq[hi] = a;
                     }
                 }
                 __syncthreads();
             }
         for (int i = tid; i < need_eq; i += kSelThreads) {
-            s_key[ngt + i] = thr;
-            s_id[ngt + i] = s_eq[i];
+            s.key[ngt + i] = thr;
+            s.id[ngt + i] = s.eq[i];
         }
     } else {
         // very many ties: take them in id order with a block-wide scan over all scores
@@ -498,19 +591,158 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
             int total = 0;
             const int before = block_scan(eq, s.warp, &total);
             if (eq && taken + before < need_eq) {
-                s_key[ngt + taken + before] = thr;
-                s_id[ngt + taken + before] = (int32_t)j;
+                s.key[ngt + taken + before] = thr;
+                s.id[ngt + taken + before] = (int32_t)j;
             }
             taken += total;   // uniform across the block
         }
     }
     __syncthreads();
-    // ---- order the k winners: descending key, then ascending id; or ascending id (the candidate
-    //      buffers, free now, hold the merge buffers)
-    uint64_t* mA = reinterpret_cast<uint64_t*>(s.ckey);   // ckey + cid: 64 KB = 2 x 4096 values
-    if (k <= 2048) merge_sort_desc<2>(s_key, s_id, k, by_id, mA, mA + 4096, s_id);
-    else merge_sort_desc<4>(s_key, s_id, k, by_id, mA, mA + 4096, s_id);
-    for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = s_id[i];
+    sort_winners(k, by_id, s);
+}
+
+// The selection of a sequence once its candidates (ncand of them, all keys >= the threshold) sit in
+// s.ckey / s.cid: the bucket select when k <= ncand <= kCand, else (or when a bucket overflows) the
+// radix path over the candidates or over all scores.  Returns the array holding the k ids in order.
+__device__ const int32_t* select_candidates(int ncand, int k, int by_id, const GlobalKeys& all, SelectSmem& s) {
+    const int tid = threadIdx.x;
+    if (ncand >= k && ncand <= kCand) {
+        if (bucket_select(ncand, k, s)) {
+            if (!by_id) return s.cid;
+            for (int i = tid; i < k; i += kSelThreads) {
+                s.key[i] = s.ckey[i];
+                s.id[i] = s.cid[i];
+            }
+            __syncthreads();
+            sort_winners(k, by_id, s);
+            return s.id;
+        }
+        radix_path(SharedKeys<4>{s.ckey, s.cid, ncand}, ncand, k, by_id, all.sc, all.n, s);
+    } else {
+        radix_path(all, all.n, k, by_id, all.sc, all.n, s);
+    }
+    return s.id;
+}
+
+// Candidate pass over the scores [lo, hi) of one sequence: every key >= t_lo goes, with its id, to
+// emit(slot, key, id) at a slot from take(count) (block-uniform; called once per step with the step's
+// total).  Sixteen keys per thread per step, all loads in flight together.
+template <class Take, class Emit>
+__device__ __forceinline__ void candidate_pass(const float* sc, int64_t lo, int64_t hi, bool vec, uint32_t t_lo,
+                                               SelectSmem& s, Take take, Emit emit) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid == 0) s.ncand = 0;
+    __syncthreads();
+    for (int64_t j0 = lo; j0 < hi; j0 += (int64_t)kSelThreads * kBatch) {
+        uint32_t key[kBatch];
+        load_keys_only(sc, hi, j0, vec, key);
+        auto pos = [&](int u) { return j0 + 4 * ((int64_t)(u >> 2) * kSelThreads + tid) + (u & 3); };
+        int cnt = 0;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) cnt += (pos(u) < hi && key[u] >= t_lo) ? 1 : 0;
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int wbase = 0;
+        if (lane == 31 && incl > 0) wbase = atomicAdd(&s.ncand, incl);
+        __syncthreads();
+        if (tid == 0) {
+            s.gbase = take(s.ncand);
+            s.ncand = 0;
+        }
+        __syncthreads();
+        int slot = s.gbase + __shfl_sync(0xffffffffu, wbase, 31) + incl - cnt;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            if (pos(u) < hi && key[u] >= t_lo) {
+                emit(slot, key[u], (int32_t)pos(u));
+                ++slot;
+            }
+        }
+    }
+}
+
+// One CTA per sequence: candidates against the sampled threshold into shared memory, then the select.
+__global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float* __restrict__ scores, int64_t nc,
+                                                                     int k, int by_id, int32_t* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t sel_smem[];
+    SelectSmem& s = *reinterpret_cast<SelectSmem*>(sel_smem);
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const float* sc = scores + (int64_t)b * nc;
+    const GlobalKeys all{sc, nc, (reinterpret_cast<uintptr_t>(sc) & 15) == 0};
+    // every key passes when all scores fit the buffer; else a sampled threshold keeps (for any but
+    // adversarial orders) between k and kCand of them
+    const uint32_t t_lo = nc > kCand ? sample_threshold(sc, nc, k, s) : 0u;
+    int total = 0;
+    candidate_pass(
+        sc, 0, nc, all.vec, t_lo, s,
+        [&](int n) {
+            const int base = total;
+            total += n;
+            return base;
+        },
+        [&](int slot, uint32_t key, int32_t id) {
+            if (slot < kCand) {
+                s.ckey[slot] = key;
+                s.cid[slot] = id;
+            }
+        });
+    if (tid == 0) s.ncand = total;
+    __syncthreads();
+    const int32_t* ids = select_candidates(s.ncand, k, by_id, all, s);
+    for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = ids[i];
+}
+
+// `parts` CTAs per sequence (blockIdx.x; blockIdx.y = sequence), each over `chunk` of its scores: the
+// same sampled threshold in every CTA, candidates appended to the sequence's global buffer (cand,
+// kCand per sequence; counters[2 b] counts them), then a ticket (counters[2 b + 1]): the last CTA of
+// the sequence to finish reads the candidates back, returns both counters to zero and selects.
+__global__ void __launch_bounds__(kSelThreads) indexer_select_split_kernel(const float* __restrict__ scores,
+                                                                           int64_t nc, int k, int by_id,
+                                                                           int64_t chunk, int parts, uint2* cand,
+                                                                           int* counters,
+                                                                           int32_t* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t sel_smem[];
+    SelectSmem& s = *reinterpret_cast<SelectSmem*>(sel_smem);
+    const int part = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const float* sc = scores + (int64_t)b * nc;
+    const GlobalKeys all{sc, nc, (reinterpret_cast<uintptr_t>(sc) & 15) == 0};
+    int* count = counters + 2 * b;
+    int* ticket = count + 1;
+    uint2* gc = cand + (int64_t)b * kCand;
+    const uint32_t t_lo = sample_threshold(sc, nc, k, s);
+    const int64_t lo = (int64_t)part * chunk, hi = min(nc, lo + chunk);
+    candidate_pass(
+        sc, lo, hi, all.vec, t_lo, s, [&](int n) { return n > 0 ? atomicAdd(count, n) : 0; },
+        [&](int slot, uint32_t key, int32_t id) {
+            if (slot < kCand) gc[slot] = make_uint2(key, (uint32_t)id);
+        });
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s.last = atomicAdd(ticket, 1) == parts - 1;
+    __syncthreads();
+    if (!s.last) return;
+    __threadfence();
+    if (tid == 0) {
+        s.ncand = *reinterpret_cast<volatile int*>(count);
+        *reinterpret_cast<volatile int*>(count) = 0;
+        *reinterpret_cast<volatile int*>(ticket) = 0;
+    }
+    __syncthreads();
+    const int ncand = s.ncand;
+    if (ncand >= k && ncand <= kCand) {
+        for (int i = tid; i < ncand; i += kSelThreads) {
+            const uint2 c = __ldcg(gc + i);
+            s.ckey[i] = c.x;
+            s.cid[i] = (int32_t)c.y;
+        }
+        __syncthreads();
+    }
+    const int32_t* ids = select_candidates(ncand, k, by_id, all, s);
+    for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = ids[i];
 }
 
 // ---------------------------------------------------------------- bf16 scoring on tcgen05
@@ -671,7 +903,19 @@ __global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __g
 
 }  // namespace idx
 
-static int select_launch(const float* scores, int64_t nc, int k, int by_id, int32_t* out, int bs, cudaStream_t st) {
+// Candidate buffer of the split select: after the counter header and the scores.
+static size_t cand_offset(int bs, int64_t nc) {
+    return kCounterHeaderBytes + align_up((size_t)std::max(bs, 1) * (size_t)std::max<int64_t>(nc, 1) * 4, 256);
+}
+
+size_t indexer_workspace_bytes(int bs, int64_t nc) {
+    return cand_offset(bs, nc) + align_up((size_t)std::max(bs, 1) * idx::kCand * sizeof(uint2), 256);
+}
+
+// The select: `parts` CTAs per sequence when a workspace holds the candidate buffer and fewer than
+// half the SMs would otherwise work (the split kernel), else one CTA per sequence.
+static int select_launch(const float* scores, int64_t nc, int k, int by_id, int32_t* out, int bs, void* workspace,
+                         size_t workspace_bytes, cudaStream_t st) {
     using namespace idx;
     const int smem = (int)sizeof(SelectSmem);
     static int configured_dev = -1;
@@ -679,17 +923,35 @@ static int select_launch(const float* scores, int64_t nc, int k, int by_id, int3
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
         if (cudaFuncSetAttribute(indexer_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-            return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for indexer_select_kernel");
+                cudaSuccess ||
+            cudaFuncSetAttribute(indexer_select_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+                cudaSuccess)
+            return set_error(WS_ERR_CUDA, "cudaFuncSetAttribute failed for the indexer select kernels");
         configured_dev = dev;
     }
-    indexer_select_kernel<<<bs, kSelThreads, smem, st>>>(scores, nc, k, by_id, out);
+    int parts = 1;
+    int64_t chunk = nc;
+    const bool have_ws = workspace && workspace_bytes >= indexer_workspace_bytes(bs, nc) &&
+                         (size_t)bs * 2 * sizeof(int) <= kCounterHeaderBytes;
+    if (have_ws && nc > kCand) {
+        const int target = std::min(16, device_sm_count() / std::max(bs, 1));
+        if (target >= 2) {
+            const int64_t grain = 4 * kSelThreads;   // one 16-byte load per thread (keeps chunks 16-byte aligned)
+            chunk = (nc + target - 1) / target;
+            chunk = (chunk + grain - 1) / grain * grain;
+            parts = (int)((nc + chunk - 1) / chunk);
+        }
+    }
+    if (parts >= 2) {
+        uint8_t* base = static_cast<uint8_t*>(workspace);
+        indexer_select_split_kernel<<<dim3((unsigned)parts, (unsigned)bs), kSelThreads, smem, st>>>(
+            scores, nc, k, by_id, chunk, parts, reinterpret_cast<uint2*>(base + cand_offset(bs, nc)),
+            reinterpret_cast<int*>(base), out);
+    } else {
+        indexer_select_kernel<<<bs, kSelThreads, smem, st>>>(scores, nc, k, by_id, out);
+    }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-}
-
-size_t indexer_workspace_bytes(int bs, int64_t nc) {
-    return kCounterHeaderBytes + align_up((size_t)std::max(bs, 1) * (size_t)std::max<int64_t>(nc, 1) * 4, 256);
 }
 
 int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w, int bs, int nH, int hd, int64_t nc,
@@ -741,7 +1003,7 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
             map, static_cast<const __nv_bfloat16*>(q), w, tp);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-        return k > 0 ? select_launch(scores, nc, k, by_id, out_ids, bs, st) : WS_OK;
+        return k > 0 ? select_launch(scores, nc, k, by_id, out_ids, bs, workspace, workspace_bytes, st) : WS_OK;
     }
     const size_t smem = ((size_t)nH * hd + nH) * sizeof(float);
     auto kfn = bf16 ? indexer_score_kernel<true> : indexer_score_kernel<false>;
@@ -752,7 +1014,7 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
     kfn<<<grid, kScoreThreads, smem, st>>>(q, kv, w, nH, hd, nc, scores);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-    return k > 0 ? select_launch(scores, nc, k, by_id, out_ids, bs, st) : WS_OK;
+    return k > 0 ? select_launch(scores, nc, k, by_id, out_ids, bs, workspace, workspace_bytes, st) : WS_OK;
 }
 
 }  // namespace ws

@@ -120,6 +120,59 @@ def test_ties_beyond_the_candidate_buffer(nc, distinct, k):
     assert ids_id.tolist() == sorted(order.tolist())
 
 
+def _exact_order(scores, k):
+    return np.lexsort((np.arange(scores.shape[0]), -scores))[:k]     # descending score, then ascending id
+
+
+@pytest.mark.parametrize("k", [500, 2048])
+def test_one_cta_per_sequence_without_workspace(k):
+    """Scores returned to the caller and no workspace: the select runs one CTA per sequence (sampled
+    threshold, candidates in shared memory) instead of spreading the candidate pass."""
+    from scope_b200 import _lib
+    bs, nH, hd, nc = 3, 8, 64, 30000
+    q, kv, w = rand_case(bs, nH, hd, nc, seed=k)
+    q, kv, w = q.to(DEV), kv.to(DEV), w.to(DEV)
+    L = _lib.lib()
+    for order in (_lib.WS_TOPK_BY_SCORE, _lib.WS_TOPK_BY_ID):
+        ids = torch.empty(bs, k, dtype=torch.int32, device=DEV)
+        sc = torch.empty(bs, nc, dtype=torch.float32, device=DEV)
+        rc = L.ws_indexer_topk(_lib.ptr(q), _lib.ptr(kv), _lib.WS_DTYPE_F32, _lib.ptr(w), bs, nH, hd, nc, k, order,
+                               _lib.ptr(ids), _lib.ptr(sc), None, 0, _lib.stream_ptr(torch.device(DEV)))
+        _lib.check(rc, "ws_indexer_topk")
+        ids, sc = ids.cpu().numpy(), sc.cpu().numpy()
+        for b in range(bs):
+            want = _exact_order(sc[b], k)
+            assert ids[b].tolist() == (want.tolist() if order == _lib.WS_TOPK_BY_SCORE else sorted(want.tolist()))
+
+
+def test_many_sequences_one_cta_each():
+    """More sequences than half the SMs: one select CTA per sequence even with a workspace."""
+    bs, nH, hd, nc, k = 80, 2, 16, 9000, 300
+    q, kv, w = rand_case(bs, nH, hd, nc, seed=80)
+    ids, our = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), k, return_scores=True)
+    ids, our = ids.cpu().numpy(), our.cpu().numpy()
+    for b in range(bs):
+        assert ids[b].tolist() == _exact_order(our[b], k).tolist()
+    _, sc = oracle_scores(q, kv, w, k)
+    assert np.abs(our - sc).max() <= 1e-5 * (np.abs(sc).max() + 1.0)
+
+
+@pytest.mark.parametrize("order", ["score", "id"])
+def test_outlier_score(order):
+    """One entry scores ~10^4 times the rest: the equal-width buckets over the candidates' range then
+    put almost every candidate into a few buckets and the select falls back to radix passes."""
+    bs, nH, hd, nc, k = 2, 4, 32, 20000, 2048
+    q, kv, w = rand_case(bs, nH, hd, nc, seed=5)
+    w = w.abs() + 0.1
+    kv[:, 77] = 1e4 * q[:, 0]     # head 0 scores 1e4 |q_0|^2 there
+    ids, our = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), k, order=order,
+                                                return_scores=True)
+    ids, our = ids.cpu().numpy(), our.cpu().numpy()
+    for b in range(bs):
+        want = _exact_order(our[b], k).tolist()
+        assert ids[b].tolist() == (want if order == "score" else sorted(want))
+
+
 def test_ds4_size():
     """A DeepSeek-V4-like indexer shape: 64 index heads x 128 dims over 65536
     compressed entries, top-2048, two sequences against the oracle."""
