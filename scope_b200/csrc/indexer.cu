@@ -224,7 +224,7 @@ struct SelectSmem {   // the select kernels' dynamic shared memory
     int hist[256];
     int warp[32];
     uint32_t wlo[32], whi[32];
-    uint32_t prefix, mask, kmin, kmax;
+    uint32_t prefix, mask;
     int remaining, ngt, neq, ncand, flag, dstar, gbase, last;
 };
 
@@ -402,8 +402,8 @@ __device__ void merge_sort_desc(const uint32_t* key, const int32_t* id, int k, i
     __syncthreads();
 }
 
-// Block-wide min and max (of one key pair per thread) into s.kmin / s.kmax.
-__device__ __forceinline__ void block_minmax(uint32_t lo, uint32_t hi, SelectSmem& s) {
+// Block-wide min and max of per-thread partials, one barrier; every thread gets the result.
+__device__ __forceinline__ void block_range(uint32_t& lo, uint32_t& hi, SelectSmem& s) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -415,20 +415,13 @@ __device__ __forceinline__ void block_minmax(uint32_t lo, uint32_t hi, SelectSme
         s.whi[warp] = hi;
     }
     __syncthreads();
-    if (warp == 0) {
-        lo = s.wlo[lane];
-        hi = s.whi[lane];
+    lo = s.wlo[lane];
+    hi = s.whi[lane];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-        }
-        if (lane == 0) {
-            s.kmin = lo;
-            s.kmax = hi;
-        }
+    for (int o = 16; o > 0; o >>= 1) {
+        lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
     }
-    __syncthreads();
 }
 
 // kBuckets equal-width buckets over the keys [lo, hi], numbered from the top (bucket 0 holds the
@@ -444,14 +437,18 @@ struct Buckets {
     __device__ __forceinline__ uint32_t lower_edge(int d) const { return lo + ((uint32_t)(kBuckets - 1 - d) << shift); }
 };
 
+// Zeroes the bucket counts and the overflow flag (a barrier must follow before bucket_count).
+__device__ __forceinline__ void bucket_clear(SelectSmem& s) {
+    for (int i = threadIdx.x; i < kBuckets; i += kSelThreads) s.bcur[i] = 0;
+    if (threadIdx.x == 0) s.flag = 0;
+}
+
 // Counts the n keys (shared memory) per bucket: s.bstart[d] = keys in the buckets above d,
 // s.bstart[kBuckets] = n, s.bcur = s.bstart; s.dstar = the bucket of the r-th largest key (1 <= r <= n);
-// s.flag = 1 when a bucket that starts before r holds more than cap keys.
+// s.flag = 1 when a bucket that starts before r holds more than cap keys.  Expects bucket_clear and a
+// barrier since; three barriers.
 __device__ void bucket_count(const uint32_t* key, int n, const Buckets& bk, int r, int cap, SelectSmem& s) {
-    const int tid = threadIdx.x;
-    for (int i = tid; i < kBuckets; i += kSelThreads) s.bcur[i] = 0;
-    if (tid == 0) s.flag = 0;
-    __syncthreads();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int i = tid; i < n; i += kSelThreads) atomicAdd(&s.bcur[bk.of(key[i])], 1);
     __syncthreads();
     int c[4], tot = 0;
@@ -460,8 +457,23 @@ __device__ void bucket_count(const uint32_t* key, int n, const Buckets& bk, int 
         c[e] = s.bcur[4 * tid + e];
         tot += c[e];
     }
-    int total = 0;
-    int st = block_scan(tot, s.warp, &total);
+    int x = tot;   // inclusive scan over the warp's threads
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s.warp[warp] = x;
+    __syncthreads();
+    int wx = s.warp[lane];   // every warp scans the 32 warp totals itself
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, wx, o);
+        if (lane >= o) wx += y;
+    }
+    const int wbefore = __shfl_sync(0xffffffffu, wx, (warp + 31) & 31);
+    const int total = __shfl_sync(0xffffffffu, wx, 31);
+    int st = (warp > 0 ? wbefore : 0) + x - tot;
     bool over = false;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -483,28 +495,25 @@ __device__ uint32_t sample_threshold(const float* sc, int64_t nc, int k, SelectS
     const int tid = threadIdx.x;
     const uint32_t key = ordered_key(__ldcg(sc + (int64_t)tid * nc / kSample));
     s.ckey[tid] = key;
-    block_minmax(key, key, s);
+    bucket_clear(s);
+    uint32_t lo = key, hi = key;
+    block_range(lo, hi, s);
     const double base = (double)k * kSample / (double)nc;
     const int r = min(kSample, (int)ceil(base + 6.0 * sqrt(base) + 16.0));
-    const Buckets bk(s.kmin, s.kmax);
+    const Buckets bk(lo, hi);
     bucket_count(s.ckey, kSample, bk, r, kSample, s);
     return bk.lower_edge(s.dstar);
 }
 
-// The k largest of the n candidates in s.ckey / s.cid (k <= n <= kCand), in descending key order and
-// ascending id among equal keys, into s.ckey / s.cid [0, k): count the candidates per bucket, place the
-// keys of every bucket that starts before k in bucket order, and rank each inside its bucket.  Returns
-// false, with the candidates untouched, when one of those buckets holds more than kBucketCap keys
-// (heavy ties, or a few keys far above the rest).
-__device__ bool bucket_select(int n, int k, SelectSmem& s) {
+// The k largest of the n candidates in s.ckey / s.cid (k <= n <= kCand; keys within [lo, hi]), in
+// descending key order and ascending id among equal keys, into s.ckey / s.cid [0, k): count the
+// candidates per bucket, place the keys of every bucket that starts before k in bucket order, and rank
+// each inside its bucket.  Returns false, with the candidates untouched, when one of those buckets holds
+// more than kBucketCap keys (heavy ties, or a few keys far above the rest).  Expects bucket_clear and a
+// barrier since.
+__device__ bool bucket_select(int n, int k, uint32_t lo, uint32_t hi, SelectSmem& s) {
     const int tid = threadIdx.x;
-    uint32_t lo = 0xffffffffu, hi = 0;
-    for (int i = tid; i < n; i += kSelThreads) {
-        lo = min(lo, s.ckey[i]);
-        hi = max(hi, s.ckey[i]);
-    }
-    block_minmax(lo, hi, s);
-    const Buckets bk(s.kmin, s.kmax);
+    const Buckets bk(lo, hi);
     bucket_count(s.ckey, n, bk, k, kBucketCap, s);
     if (s.flag) return false;
     for (int i = tid; i < n; i += kSelThreads) {
@@ -601,13 +610,14 @@ __device__ void radix_path(const Src& src, int64_t n, int k, int by_id, const fl
     sort_winners(k, by_id, s);
 }
 
-// The selection of a sequence once its candidates (ncand of them, all keys >= the threshold) sit in
+// The selection of a sequence once its candidates (ncand of them, keys within [lo, hi]) sit in
 // s.ckey / s.cid: the bucket select when k <= ncand <= kCand, else (or when a bucket overflows) the
 // radix path over the candidates or over all scores.  Returns the array holding the k ids in order.
-__device__ const int32_t* select_candidates(int ncand, int k, int by_id, const GlobalKeys& all, SelectSmem& s) {
+__device__ const int32_t* select_candidates(int ncand, int k, int by_id, uint32_t lo, uint32_t hi,
+                                           const GlobalKeys& all, SelectSmem& s) {
     const int tid = threadIdx.x;
     if (ncand >= k && ncand <= kCand) {
-        if (bucket_select(ncand, k, s)) {
+        if (bucket_select(ncand, k, lo, hi, s)) {
             if (!by_id) return s.cid;
             for (int i = tid; i < k; i += kSelThreads) {
                 s.key[i] = s.ckey[i];
@@ -624,18 +634,22 @@ __device__ const int32_t* select_candidates(int ncand, int k, int by_id, const G
     return s.id;
 }
 
-// Candidate pass over the scores [lo, hi) of one sequence: every key >= t_lo goes, with its id, to
-// emit(slot, key, id) at a slot from take(count) (block-uniform; called once per step with the step's
-// total).  Sixteen keys per thread per step, all loads in flight together.
-template <class Take, class Emit>
-__device__ __forceinline__ void candidate_pass(const float* sc, int64_t lo, int64_t hi, bool vec, uint32_t t_lo,
+// Candidate pass over the scores [lo, hi) of one sequence: every key >= the threshold (from thr(),
+// called while the first step's loads are in flight) goes, with its id, to emit(slot, key, id) at a slot
+// from take(count) (block-uniform; called by one thread per step with the step's total).  Sixteen keys
+// per thread per step, all loads in flight together.  Clears the buckets for the final select.
+template <class Thr, class Take, class Emit>
+__device__ __forceinline__ void candidate_pass(const float* sc, int64_t lo, int64_t hi, bool vec, Thr thr,
                                                SelectSmem& s, Take take, Emit emit) {
     const int tid = threadIdx.x, lane = tid & 31;
+    uint32_t key[kBatch];
+    load_keys_only(sc, hi, lo, vec, key);
+    const uint32_t t_lo = thr();
+    bucket_clear(s);   // for the final select
     if (tid == 0) s.ncand = 0;
     __syncthreads();
     for (int64_t j0 = lo; j0 < hi; j0 += (int64_t)kSelThreads * kBatch) {
-        uint32_t key[kBatch];
-        load_keys_only(sc, hi, j0, vec, key);
+        if (j0 != lo) load_keys_only(sc, hi, j0, vec, key);
         auto pos = [&](int u) { return j0 + 4 * ((int64_t)(u >> 2) * kSelThreads + tid) + (u & 3); };
         int cnt = 0;
 #pragma unroll
@@ -673,12 +687,13 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
     const int b = blockIdx.x, tid = threadIdx.x;
     const float* sc = scores + (int64_t)b * nc;
     const GlobalKeys all{sc, nc, (reinterpret_cast<uintptr_t>(sc) & 15) == 0};
+    pdl_wait_primary();   // the scores come from the previous grid
     // every key passes when all scores fit the buffer; else a sampled threshold keeps (for any but
     // adversarial orders) between k and kCand of them
-    const uint32_t t_lo = nc > kCand ? sample_threshold(sc, nc, k, s) : 0u;
     int total = 0;
+    uint32_t klo = 0xffffffffu, khi = 0;   // range of the stored candidates
     candidate_pass(
-        sc, 0, nc, all.vec, t_lo, s,
+        sc, 0, nc, all.vec, [&] { return nc > kCand ? sample_threshold(sc, nc, k, s) : 0u; }, s,
         [&](int n) {
             const int base = total;
             total += n;
@@ -688,60 +703,65 @@ __global__ void __launch_bounds__(kSelThreads) indexer_select_kernel(const float
             if (slot < kCand) {
                 s.ckey[slot] = key;
                 s.cid[slot] = id;
+                klo = min(klo, key);
+                khi = max(khi, key);
             }
         });
     if (tid == 0) s.ncand = total;
-    __syncthreads();
-    const int32_t* ids = select_candidates(s.ncand, k, by_id, all, s);
+    block_range(klo, khi, s);
+    const int32_t* ids = select_candidates(s.ncand, k, by_id, klo, khi, all, s);
     for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = ids[i];
 }
 
 // `parts` CTAs per sequence (blockIdx.x; blockIdx.y = sequence), each over `chunk` of its scores: the
-// same sampled threshold in every CTA, candidates appended to the sequence's global buffer (cand,
-// kCand per sequence; counters[2 b] counts them), then a ticket (counters[2 b + 1]): the last CTA of
-// the sequence to finish reads the candidates back, returns both counters to zero and selects.
+// same sampled threshold in every CTA, candidates appended to the sequence's global buffer (cand, kCand
+// per sequence).  counters[b] packs the candidate count (low 32 bits, slots taken by atomic adds) and a
+// ticket (high 32 bits): the CTA that takes the last ticket learns the total from it, reads the
+// candidates back, returns the counter to zero and selects.
 __global__ void __launch_bounds__(kSelThreads) indexer_select_split_kernel(const float* __restrict__ scores,
                                                                            int64_t nc, int k, int by_id,
                                                                            int64_t chunk, int parts, uint2* cand,
-                                                                           int* counters,
+                                                                           unsigned long long* counters,
                                                                            int32_t* __restrict__ out) {
     extern __shared__ __align__(16) uint8_t sel_smem[];
     SelectSmem& s = *reinterpret_cast<SelectSmem*>(sel_smem);
     const int part = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const float* sc = scores + (int64_t)b * nc;
     const GlobalKeys all{sc, nc, (reinterpret_cast<uintptr_t>(sc) & 15) == 0};
-    int* count = counters + 2 * b;
-    int* ticket = count + 1;
+    unsigned long long* counter = counters + b;
     uint2* gc = cand + (int64_t)b * kCand;
-    const uint32_t t_lo = sample_threshold(sc, nc, k, s);
     const int64_t lo = (int64_t)part * chunk, hi = min(nc, lo + chunk);
+    pdl_wait_primary();   // the scores come from the previous grid
     candidate_pass(
-        sc, lo, hi, all.vec, t_lo, s, [&](int n) { return n > 0 ? atomicAdd(count, n) : 0; },
+        sc, lo, hi, all.vec, [&] { return sample_threshold(sc, nc, k, s); }, s,
+        [&](int n) { return n > 0 ? (int)(uint32_t)atomicAdd(counter, (unsigned long long)n) : 0; },
         [&](int slot, uint32_t key, int32_t id) {
             if (slot < kCand) gc[slot] = make_uint2(key, (uint32_t)id);
         });
     __threadfence();
     __syncthreads();
-    if (tid == 0) s.last = atomicAdd(ticket, 1) == parts - 1;
+    if (tid == 0) {
+        const unsigned long long old = atomicAdd(counter, 1ull << 32);
+        s.last = (int)(old >> 32) == parts - 1;
+        s.ncand = (int)(uint32_t)old;   // every CTA's slots were taken before its ticket
+        if (s.last) *reinterpret_cast<volatile unsigned long long*>(counter) = 0ull;
+    }
     __syncthreads();
     if (!s.last) return;
     __threadfence();
-    if (tid == 0) {
-        s.ncand = *reinterpret_cast<volatile int*>(count);
-        *reinterpret_cast<volatile int*>(count) = 0;
-        *reinterpret_cast<volatile int*>(ticket) = 0;
-    }
-    __syncthreads();
     const int ncand = s.ncand;
+    uint32_t klo = 0xffffffffu, khi = 0;
     if (ncand >= k && ncand <= kCand) {
         for (int i = tid; i < ncand; i += kSelThreads) {
             const uint2 c = __ldcg(gc + i);
             s.ckey[i] = c.x;
             s.cid[i] = (int32_t)c.y;
+            klo = min(klo, c.x);
+            khi = max(khi, c.x);
         }
-        __syncthreads();
     }
-    const int32_t* ids = select_candidates(ncand, k, by_id, all, s);
+    block_range(klo, khi, s);
+    const int32_t* ids = select_candidates(ncand, k, by_id, klo, khi, all, s);
     for (int i = tid; i < k; i += kSelThreads) out[(int64_t)b * k + i] = ids[i];
 }
 
@@ -824,6 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __g
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_launch_dependents();   // the select's CTAs may take SMs as this grid's CTAs finish
     const uint32_t tbase = *s_tmem;
 
     if (warp == 0) {
@@ -932,7 +953,7 @@ static int select_launch(const float* scores, int64_t nc, int k, int by_id, int3
     int parts = 1;
     int64_t chunk = nc;
     const bool have_ws = workspace && workspace_bytes >= indexer_workspace_bytes(bs, nc) &&
-                         (size_t)bs * 2 * sizeof(int) <= kCounterHeaderBytes;
+                         (size_t)bs * sizeof(unsigned long long) <= kCounterHeaderBytes;
     if (have_ws && nc > kCand) {
         const int target = std::min(16, device_sm_count() / std::max(bs, 1));
         if (target >= 2) {
@@ -942,15 +963,28 @@ static int select_launch(const float* scores, int64_t nc, int k, int by_id, int3
             parts = (int)((nc + chunk - 1) / chunk);
         }
     }
+    // a programmatic dependent of the scoring kernel: launched while it drains, waits for its scores
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kSelThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     if (parts >= 2) {
         uint8_t* base = static_cast<uint8_t*>(workspace);
-        indexer_select_split_kernel<<<dim3((unsigned)parts, (unsigned)bs), kSelThreads, smem, st>>>(
-            scores, nc, k, by_id, chunk, parts, reinterpret_cast<uint2*>(base + cand_offset(bs, nc)),
-            reinterpret_cast<int*>(base), out);
+        cfg.gridDim = dim3((unsigned)parts, (unsigned)bs);
+        e = cudaLaunchKernelEx(&cfg, indexer_select_split_kernel, scores, nc, k, by_id, chunk, parts,
+                               reinterpret_cast<uint2*>(base + cand_offset(bs, nc)),
+                               reinterpret_cast<unsigned long long*>(base), out);
     } else {
-        indexer_select_kernel<<<bs, kSelThreads, smem, st>>>(scores, nc, k, by_id, out);
+        cfg.gridDim = dim3((unsigned)bs);
+        e = cudaLaunchKernelEx(&cfg, indexer_select_kernel, scores, nc, k, by_id, out);
     }
-    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
