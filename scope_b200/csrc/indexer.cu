@@ -830,6 +830,21 @@ __global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __g
         *s_abort = 0;
         fence_mbar_init();
     }
+    // the producer (thread 0) issues the loads of the first ring-full of tiles at once: they wait on no
+    // barrier and are in flight while q is staged and TMEM allocated
+    const int first = n < ST ? n : ST;
+    auto issue = [&](int i) {
+        const int s = i % ST;
+        mbar_arrive_expect_tx(TB(B_FULL + s), stage_bytes);
+        const int tok = (int)((t_begin + i) * TT);
+        for (int kb = 0; kb < KB; ++kb)
+            tma_load_3d(smem_u32(s_ring + s * stage_bytes + kb * BOX), &map_kv, TB(B_FULL + s), kb * 64,
+                        p.kv_tok_in_dim2 ? b : tok, p.kv_tok_in_dim2 ? tok : b);
+    };
+    if (tid == 0) {
+        tma_prefetch_desc(&map_kv);
+        for (int i = 0; i < first; ++i) issue(i);
+    }
     // q of this sequence -> K-major swizzled bf16 [64 rows x hd] (zero rows past nH); weights (0 past nH)
     const int hd = KB * 64;
     for (int j = tid; j < NHP * (hd / 8); j += kThreads) {
@@ -849,17 +864,12 @@ __global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __g
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
-        int i = 0;
+        int i = first;
         if (lane == 0) {
-            tma_prefetch_desc(&map_kv);
             for (; i < n; ++i) {
                 const int s = i % ST;
-                if (i >= ST && !tc_wait(TB(B_EMPTY + s), ((i / ST) - 1) & 1, s_abort, p.status)) break;
-                mbar_arrive_expect_tx(TB(B_FULL + s), stage_bytes);
-                const int tok = (int)((t_begin + i) * TT);
-                for (int kb = 0; kb < KB; ++kb)
-                    tma_load_3d(smem_u32(s_ring + s * stage_bytes + kb * BOX), &map_kv, TB(B_FULL + s), kb * 64,
-                                p.kv_tok_in_dim2 ? b : tok, p.kv_tok_in_dim2 ? tok : b);
+                if (!tc_wait(TB(B_EMPTY + s), ((i / ST) - 1) & 1, s_abort, p.status)) break;
+                issue(i);
             }
             if (*s_abort) {   // leave no bulk copy in flight: wait (bounded) for the last load of every slot
                 for (int s = 0; s < ST; ++s) {

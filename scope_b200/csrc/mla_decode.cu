@@ -152,7 +152,57 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
     const int64_t t_begin = cta < nctas ? split_start(cta, total, nctas) : total;
     const int64_t t_end = cta < nctas ? split_start(cta + 1, total, nctas) : total;
 
-    if (tid == 0) {
+    const uint32_t pairs = smem_u32(s.base + OFF_PAIRS), pes = smem_u32(s.base + OFF_PE);
+    const uint32_t qs = smem_u32(s.base + OFF_Q), ps = smem_u32(s.base + OFF_P);
+
+    // Producer state (lane 0 of warp 8 issues every TMA load).  It initialises the barriers and issues
+    // the first tile's loads before the setup barrier, so they are in flight during the TMEM allocation.
+    int seg = -1, qn = 0;
+    int64_t pi = 0;   // tiles whose loads were issued (on a failed wait: the tile being issued)
+    int pb = (int)(t_begin / p.tpb);
+    int ptl = (int)(t_begin - (int64_t)pb * p.tpb);
+    auto issue_tile = [&]() -> bool {
+        const int64_t i = pi;
+        const bool new_seg = pb != seg;   // this tile starts a sequence: its q follows the tile's latent
+        for (int pr = 0; pr < 4; ++pr) {
+            const int64_t n = 4 * i + pr;
+            const int sl = (int)(n % NP);
+            const uint32_t u = (uint32_t)(n / NP);
+            if (u > 0 && !wait_bar(s, bar(s, B_PAIR_EMPTY + sl), (u - 1) & 1, p.status)) return false;
+            mbar_arrive_expect_tx(bar(s, B_PAIR_FULL + sl), PAIR_BYTES);
+            const int c1 = p.c_tok_in_dim2 ? pb : ptl * TT, c2 = p.c_tok_in_dim2 ? ptl * TT : pb;
+            tma_load_3d(pairs + sl * PAIR_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr, c1, c2);
+            tma_load_3d(pairs + sl * PAIR_BYTES + BOX_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr + 64,
+                        c1, c2);
+        }
+        if (new_seg) {
+            if (qn > 0 && !wait_bar(s, bar(s, B_Q_EMPTY), (qn - 1) & 1, p.status)) return false;
+            // q may come from the previous grid on the stream (the absorb GEMM, launched as its
+            // programmatic dependent); without one this returns at once
+            if (qn == 0) pdl_wait_primary();
+            mbar_arrive_expect_tx(bar(s, B_Q_FULL), 9 * QBOX_BYTES);
+            for (int kb = 0; kb < 8; ++kb)
+                tma_load_3d(qs + kb * QBOX_BYTES, &maps.q, bar(s, B_Q_FULL), kb * 64, pb * NH, 0);
+            tma_load_3d(qs + 8 * QBOX_BYTES, &maps.qpe, bar(s, B_Q_FULL), 0, pb * NH, 0);
+            ++qn;
+            seg = pb;
+        }
+        const int e = (int)(i % NE);
+        const uint32_t ue = (uint32_t)(i / NE);
+        if (ue > 0 && !wait_bar(s, bar(s, B_PE_EMPTY + e), (ue - 1) & 1, p.status)) return false;
+        mbar_arrive_expect_tx(bar(s, B_PE_FULL + e), BOX_BYTES);
+        tma_load_3d(pes + e * BOX_BYTES, &maps.pe, bar(s, B_PE_FULL + e), 0, p.pe_tok_in_dim2 ? pb : ptl * TT,
+                    p.pe_tok_in_dim2 ? ptl * TT : pb);
+        if (++ptl == p.tpb) {
+            ptl = 0;
+            ++pb;
+        }
+        ++pi;
+        return true;
+    };
+
+    bool pok = true;
+    if (warp == 8 && lane == 0) {
         for (int i = 0; i < NP; ++i) {
             mbar_init(bar(s, B_PAIR_FULL + i), 1);
             mbar_init(bar(s, B_PAIR_EMPTY + i), 1);
@@ -181,6 +231,13 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
         mbar_init(bar(s, B_DONE2), 1);
         *s.abort_flag = 0;
         fence_mbar_init();
+        if (t_begin < t_end) {
+            tma_prefetch_desc(&maps.c);
+            tma_prefetch_desc(&maps.pe);
+            tma_prefetch_desc(&maps.q);
+            tma_prefetch_desc(&maps.qpe);
+            pok = issue_tile();   // the first tile waits on no barrier
+        }
     }
     if (warp == 9) tmem_alloc(smem_u32(s.tmem_holder), TMEM_COLS);
     tc_fence_before();
@@ -189,63 +246,14 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
     const uint32_t tbase = *s.tmem_holder;
     pdl_launch_dependents();
 
-    const uint32_t pairs = smem_u32(s.base + OFF_PAIRS), pes = smem_u32(s.base + OFF_PE);
-    const uint32_t qs = smem_u32(s.base + OFF_Q), ps = smem_u32(s.base + OFF_P);
-
     if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0 && t_begin < t_end) {
-            tma_prefetch_desc(&maps.c);
-            tma_prefetch_desc(&maps.pe);
-            tma_prefetch_desc(&maps.q);
-            tma_prefetch_desc(&maps.qpe);
-            int seg = -1, qn = 0;
-            int64_t i = 0;
-            int b = (int)(t_begin / p.tpb);
-            int tl = (int)(t_begin - (int64_t)b * p.tpb);
-            for (int64_t t = t_begin; t < t_end; ++t, ++i) {
-                const bool new_seg = b != seg;   // this tile starts a sequence: its q follows the tile's latent
-                bool ok = true;
-                for (int pr = 0; pr < 4 && ok; ++pr) {
-                    const int64_t n = 4 * i + pr;
-                    const int sl = (int)(n % NP);
-                    const uint32_t u = (uint32_t)(n / NP);
-                    if (u > 0 && !wait_bar(s, bar(s, B_PAIR_EMPTY + sl), (u - 1) & 1, p.status)) ok = false;
-                    if (!ok) break;
-                    mbar_arrive_expect_tx(bar(s, B_PAIR_FULL + sl), PAIR_BYTES);
-                    const int c1 = p.c_tok_in_dim2 ? b : tl * TT, c2 = p.c_tok_in_dim2 ? tl * TT : b;
-                    tma_load_3d(pairs + sl * PAIR_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr, c1, c2);
-                    tma_load_3d(pairs + sl * PAIR_BYTES + BOX_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr + 64,
-                                c1, c2);
-                }
-                if (!ok) break;
-                if (new_seg) {
-                    if (qn > 0 && !wait_bar(s, bar(s, B_Q_EMPTY), (qn - 1) & 1, p.status)) break;
-                    // q may come from the previous grid on the stream (the absorb GEMM, launched as its
-                    // programmatic dependent); without one this returns at once
-                    if (qn == 0) pdl_wait_primary();
-                    mbar_arrive_expect_tx(bar(s, B_Q_FULL), 9 * QBOX_BYTES);
-                    for (int kb = 0; kb < 8; ++kb)
-                        tma_load_3d(qs + kb * QBOX_BYTES, &maps.q, bar(s, B_Q_FULL), kb * 64, b * NH, 0);
-                    tma_load_3d(qs + 8 * QBOX_BYTES, &maps.qpe, bar(s, B_Q_FULL), 0, b * NH, 0);
-                    ++qn;
-                    seg = b;
-                }
-                const int e = (int)(i % NE);
-                const uint32_t ue = (uint32_t)(i / NE);
-                if (ue > 0 && !wait_bar(s, bar(s, B_PE_EMPTY + e), (ue - 1) & 1, p.status)) break;
-                mbar_arrive_expect_tx(bar(s, B_PE_FULL + e), BOX_BYTES);
-                tma_load_3d(pes + e * BOX_BYTES, &maps.pe, bar(s, B_PE_FULL + e), 0,
-                            p.pe_tok_in_dim2 ? b : tl * TT, p.pe_tok_in_dim2 ? tl * TT : b);
-                if (++tl == p.tpb) {
-                    tl = 0;
-                    ++b;
-                }
-            }
+            while (pok && t_begin + pi < t_end) pok = issue_tile();
             if (*s.abort_flag) {
                 // leave no bulk copy in flight into this CTA's shared memory:
                 // wait (bounded) for the last load issued into every slot
-                const int64_t np_issued = 4 * i + 4, ne_issued = i + 1;
+                const int64_t np_issued = 4 * pi + 4, ne_issued = pi + 1;
                 for (int sl = 0; sl < NP; ++sl) {
                     int64_t n = np_issued - 1 - ((np_issued - 1 - sl) % NP + NP) % NP;
                     if (n >= 0) mbar_wait_bounded(bar(s, B_PAIR_FULL + sl), (uint32_t)(n / NP) & 1, 200000000ull);
