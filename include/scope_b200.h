@@ -230,7 +230,9 @@ int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float*
  *   q [bs, nH, hd], kv [bs, nc, hd] in dtype (WS_DTYPE_F32 or WS_DTYPE_BF16), w [bs, nH] fp32
  *   score[b, j] = sum_h w[b, h] * relu(q[b, h] . kv[b, j])   (fp32)
  *   out_ids [bs, min(k, nc)] int32 in `order`; out_scores [bs, nc] fp32 (optional: NULL keeps them in the
- *   workspace of ws_indexer_topk_workspace_size bytes, which is then required).
+ *   workspace of ws_indexer_topk_workspace_size bytes, which is then required).  With a workspace of that
+ *   size the select also spreads its pass over the scores across several CTAs per sequence; without one
+ *   (out_scores given, workspace NULL) it runs one CTA per sequence.
  * nH <= 64, hd % 16 == 0 and <= 256, k <= 4096.  Two launches.
  */
 int ws_indexer_topk(const void* q, const void* kv, int dtype, const float* w, int bs, int nH, int hd, int64_t nc,

@@ -10,15 +10,17 @@
 // Two launches:
 //   indexer_score_kernel  -- thread = entry, the sequence's q in shared memory,
 //                            fp32 FMA on the CUDA cores (exact fp32 products);
-//   indexer_select_kernel -- one CTA per sequence: a threshold placed from a
-//                            sample of the scores keeps ~1.5 k candidates in
-//                            shared memory (one pass over the scores, which
-//                            stay in L2); radix select of the k-th largest
-//                            among them (four 8-bit passes; over all scores
-//                            when the sample misjudges), collection of the k
-//                            winners (ties at the threshold taken in id
-//                            order), and a bitonic sort in shared memory.
-// (The tcgen05 scoring kernel below replaces indexer_score_kernel for bf16.)
+//                            (bf16 inputs: indexer_score_tc_kernel, tcgen05);
+//   indexer_select_split_kernel -- several CTAs per sequence: a threshold placed
+//                            from a sample of the scores, candidates appended to
+//                            a workspace buffer, and the last CTA of the sequence
+//                            (a ticket) selects: a bucket select over the
+//                            candidates that leaves the k winners ordered, with a
+//                            radix select (four 8-bit passes) plus merge sort
+//                            when buckets overflow or the sample misjudges;
+//   indexer_select_kernel -- the same with one CTA per sequence and the
+//                            candidates in shared memory (no workspace, or
+//                            many sequences).
 #include "common.cuh"
 #include "ws_internal.h"
 
