@@ -186,7 +186,7 @@ int ws_gqa_decode(const void* q, const void* k, const void* v, int64_t k_stride_
 }
 
 size_t ws_gqa_decode_shares_workspace_size(int B, int Hkv, int G, int Dv, int n_shares) {
-    return gqa_workspace_bytes(G, Dv, B * Hkv * n_shares, B * Hkv, device_sm_count());
+    return gqa_workspace_bytes(G, Dv, B * Hkv * n_shares, B * Hkv, device_sm_count()) + gqa_varlen_extra_bytes(B);
 }
 
 int ws_gqa_decode_shares(const void* q, int B, int Hkv, int G, int Dk, int Dv, float scale, const ws_kv_share* shares,

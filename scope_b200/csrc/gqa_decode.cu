@@ -64,7 +64,8 @@ struct GqaParams {
     float* ws_part;
     int* ws_cnt;
     int* status;
-    int defer_merge;           // dense rows split over many CTAs: pieces are merged by gqa_merge_kernel
+    int defer_merge;           // pieces are merged by gqa_merge_kernel (dense rows over many CTAs; shares)
+    int* ws_pre;               // deferred varlen merge: the tile prefix over sequences [B+1], from CTA 0
 };
 
 struct Seg {
@@ -252,6 +253,8 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                 acc += th * p.Hkv;
             }
             pre[p.B] = acc;
+            if (p.defer_merge && blockIdx.x == 0)
+                for (int b = 0; b <= p.B; ++b) p.ws_pre[b] = pre[b];   // for gqa_merge_kernel's piece lists
         }
     }
     if (tid == 0) {
@@ -633,7 +636,7 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
 // lane k takes piece k's (m, l) and lane d accumulates value dim d over the pieces; up to 64 pieces
 // are read in one round trip.  A programmatic dependent launch of the decode grid.
 constexpr int kMergeBatch = 64;   // pieces merged in one round trip (two lanes' worth of (m, l))
-template <int DVP, int NG>
+template <int DVP, int NG, bool VARLEN>
 __global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tpr, int64_t total, int nctas) {
     constexpr int SLOT_FLOATS = NG * DVP + 2 * NG;
     __shared__ float s_w[kMaxPieces];
@@ -644,24 +647,68 @@ __global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tp
     const int chunk = (int)(item % nchunk);
     const int64_t gg = item / nchunk;
     const int group = (int)(gg / p.G), grp = (int)(gg - (int64_t)group * p.G);
-    const int64_t t0 = (int64_t)group * tpr;
-    const int c0 = (int)split_owner(t0, total, nctas);
-    const int npc = (int)split_owner(t0 + tpr - 1, total, nctas) - c0 + 1;
-    if (npc <= 1) return;   // a group inside one CTA: the decode kernel wrote its output itself
-    const float* base = p.ws_part + (int64_t)(c0 + group) * SLOT_FLOATS;   // piece k: slot c0 + k + group
+    // The group's pieces as runs of consecutive slots, one run per segment: piece k sits in slot
+    // k + off[r] for the run r with k < end[r] (dense rows: one run, slots c0 + group + k).
+    int end[kMaxShares], off[kMaxShares];
+    int npc = 0;
+#pragma unroll
+    for (int r = 0; r < kMaxShares; ++r) {
+        end[r] = INT_MAX;
+        off[r] = 0;
+    }
+    if constexpr (!VARLEN) {
+        const int64_t t0 = (int64_t)group * tpr;
+        const int c0 = (int)split_owner(t0, total, nctas);
+        npc = (int)split_owner(t0 + tpr - 1, total, nctas) - c0 + 1;
+        end[0] = npc;
+        off[0] = c0 + group;
+    } else {
+        // the decode kernel's tile split: pre[] from its CTA 0, over min(grid, total) CTAs
+        const int64_t tot = __ldcg(p.ws_pre + p.B);
+        const int nct = tot < 1 ? 1 : (int)(tot < nctas ? tot : nctas);
+        const int b = group / p.Hkv, h = group - b * p.Hkv;
+        SegTable tab;
+        tab.p = &p;
+        tab.pre = nullptr;
+        tab.tpr = 0;
+        int ts[kMaxShares], th = 0;
+#pragma unroll
+        for (int sh = 0; sh < kMaxShares; ++sh) {
+            ts[sh] = sh < p.nshare ? (tab.seq_len(sh, b) + kTile - 1) / kTile : 0;
+            th += ts[sh];
+        }
+        int64_t t0 = __ldcg(p.ws_pre + b) + (int64_t)h * th;
+        int r = 0;
+#pragma unroll
+        for (int sh = 0; sh < kMaxShares; ++sh) {
+            if (ts[sh] > 0) {
+                const int c0 = (int)split_owner(t0, tot, nct), c1 = (int)split_owner(t0 + ts[sh] - 1, tot, nct);
+                off[r] = c0 + group * p.nshare + sh - npc;
+                npc += c1 - c0 + 1;
+                end[r] = npc;
+                ++r;
+            }
+            t0 += ts[sh];
+        }
+    }
+    if (npc <= 1) return;   // a group in one piece (or none): the decode kernel wrote its output itself
+    auto piece = [&](int k) -> const float* {
+        const int o = VARLEN ? (k < end[0] ? off[0] : k < end[1] ? off[1] : k < end[2] ? off[2] : off[3]) : off[0];
+        return p.ws_part + (int64_t)(k + o) * SLOT_FLOATS;
+    };
     const int d = chunk * 32 + lane;
     const bool dv = d < p.Dv;
-    const float* col = base + grp * DVP + (dv ? d : 0);
+    const int colo = grp * DVP + (dv ? d : 0);
     float M, L, acc = 0.f;
     if (npc <= kMergeBatch) {
         // one round trip: lane k's (m, l) of pieces k and k + 32 and lane d's value column, all issued together
         float v[kMergeBatch], mk[2], lk[2];
 #pragma unroll
-        for (int u = 0; u < kMergeBatch; ++u) v[u] = u < npc ? __ldcg(col + (int64_t)u * SLOT_FLOATS) : 0.f;
+        for (int u = 0; u < kMergeBatch; ++u) v[u] = u < npc ? __ldcg(piece(u) + colo) : 0.f;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int k = lane + 32 * r;
-            const float* pp = base + (int64_t)k * SLOT_FLOATS + NG * DVP;
+            const float* pp = piece(k < npc ? k : 0) + NG * DVP;
             mk[r] = k < npc ? __ldcg(pp + grp) : -INFINITY;
             lk[r] = k < npc ? __ldcg(pp + NG + grp) : 0.f;
         }
@@ -682,13 +729,13 @@ __global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tp
         for (int u = 0; u < kMergeBatch; ++u) acc = fmaf(__shfl_sync(0xffffffffu, w[u >> 5], u & 31), v[u], acc);
     } else {
         M = -INFINITY;
-        for (int k = lane; k < npc; k += 32) M = fmaxf(M, __ldcg(base + (int64_t)k * SLOT_FLOATS + NG * DVP + grp));
+        for (int k = lane; k < npc; k += 32) M = fmaxf(M, __ldcg(piece(k) + NG * DVP + grp));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         const float Mu = (M == -INFINITY) ? 0.f : M;
         L = 0.f;
         for (int k = lane; k < npc; k += 32) {
-            const float* pp = base + (int64_t)k * SLOT_FLOATS + NG * DVP;
+            const float* pp = piece(k) + NG * DVP;
             const float w = ex2(__ldcg(pp + grp) - Mu);
             s_w[k] = w;
             L += w * __ldcg(pp + NG + grp);
@@ -700,7 +747,7 @@ __global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tp
             float v[kMergeBatch];
 #pragma unroll
             for (int u = 0; u < kMergeBatch; ++u)
-                v[u] = k0 + u < npc ? __ldcg(col + (int64_t)(k0 + u) * SLOT_FLOATS) : 0.f;
+                v[u] = k0 + u < npc ? __ldcg(piece(k0 + u) + colo) : 0.f;
 #pragma unroll
             for (int u = 0; u < kMergeBatch; ++u)
                 if (k0 + u < npc) acc = fmaf(s_w[k0 + u], v[u], acc);
@@ -712,7 +759,7 @@ __global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tp
 
 template <int DVP, int NG>
 static int launch_merge(const GqaParams& p, int tpr, int64_t total, int nctas, cudaStream_t st) {
-    const int64_t items = (int64_t)p.n_rows * p.G * ((p.Dv + 31) / 32);
+    const int64_t items = (int64_t)p.n_groups * p.G * ((p.Dv + 31) / 32);
     if (items > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: too many rows for the deferred merge");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)items);
@@ -723,7 +770,8 @@ static int launch_merge(const GqaParams& p, int tpr, int64_t total, int nctas, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_merge_kernel<DVP, NG>, p, tpr, total, nctas);
+    const cudaError_t e = p.varlen ? cudaLaunchKernelEx(&cfg, gqa_merge_kernel<DVP, NG, true>, p, tpr, total, nctas)
+                                   : cudaLaunchKernelEx(&cfg, gqa_merge_kernel<DVP, NG, false>, p, tpr, total, nctas);
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -823,11 +871,19 @@ int gqa_launch(const GqaLaunch& a) {
     if (p.n_groups > kMaxGroupsPerLaunch)
         return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: more than 65536 output row groups in one launch");
     const int nseg = a.varlen ? a.B * a.Hkv * a.nshare : a.n_rows;
-    const size_t need = gqa_workspace_bytes(a.G, a.Dv, nseg, p.n_groups, nctas);
+    const size_t base_need = gqa_workspace_bytes(a.G, a.Dv, nseg, p.n_groups, nctas);
+    const size_t need = base_need + (a.varlen ? gqa_varlen_extra_bytes(a.B) : 0);
     if (a.workspace_bytes < need || (need && !a.workspace))
         return set_error(WS_ERR_WORKSPACE, "gqa_decode: workspace too small (see ws_gqa_workspace_size)");
     p.ws_cnt = static_cast<int*>(a.workspace);
     p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
+    if (a.varlen) {
+        // Ragged shares: a CTA's range crosses many short segments, and a ticket merge at each segment end
+        // (fence, atomic, the last CTA reading the group's pieces) stalls its tile stream for microseconds
+        // each time; the pieces are filed and merged by gqa_merge_kernel instead.
+        p.defer_merge = 1;
+        p.ws_pre = reinterpret_cast<int*>(static_cast<uint8_t*>(a.workspace) + base_need);
+    }
     const size_t extra_smem = a.varlen ? size_t(a.B + 1) * 4 : 0;
     // Dense rows spanning more than 8 CTAs each: the last CTA of a row would read every piece of it alone,
     // so the pieces are merged by gqa_merge_kernel over many SMs instead.
@@ -851,5 +907,7 @@ size_t gqa_workspace_bytes(int G, int Dv, int nseg, int n_groups, int nctas) {
     (void)n_groups;
     return kCounterHeaderBytes + size_t(nseg + nctas) * gqa_slot_bytes(G, Dv);
 }
+
+size_t gqa_varlen_extra_bytes(int B) { return align_up(size_t(B + 1) * 4, 256); }
 
 }  // namespace ws

@@ -61,6 +61,7 @@ struct GqaLaunch {
 
 int gqa_launch(const GqaLaunch& a);
 size_t gqa_workspace_bytes(int G, int Dv, int nseg, int n_groups, int nctas);
+size_t gqa_varlen_extra_bytes(int B);   // ragged shares: the tile prefix for the deferred merge
 size_t gqa_slot_bytes(int G, int Dv);
 
 int gqa_f32_launch(const void* q, const void* k, const void* v, int64_t k_sb, int64_t k_st, int64_t v_sb,

@@ -183,6 +183,48 @@ def test_shares_ragged_two_way(ext, layout):
         assert np.abs(lse[b].reshape(Hkv, G) - (rm + np.log(rs))).max() < TOL_LSE, b
 
 
+def _torch_ref(q, k, v, scale):
+    """fp32 attention of q [G, D] over k, v [L, D] on the device: (out [G, D], lse [G])."""
+    s = (q.float() @ k.float().T) * scale
+    lse = torch.logsumexp(s, dim=1)
+    return torch.softmax(s, dim=1) @ v.float(), lse
+
+
+@pytest.mark.parametrize("B,nshare,max_len,seed", [(40, 3, 3000, 7), (64, 4, 700, 8), (16, 2, 32768, 2)])
+def test_shares_many_segments(ext, B, nshare, max_len, seed):
+    """Many short ragged segments per CTA (up to four shares per sequence, some empty), so a group's
+    pieces come from several CTAs and shares and are merged by the deferred merge kernel; the last
+    case is the cfg2 size.  Checked against an fp32 PyTorch reference on the device."""
+    gen = torch.Generator().manual_seed(seed)
+    Hkv, G, D = 8, 4, 128
+    lens = torch.randint(1, max_len + 1, (B,), generator=gen)
+    cuts = torch.sort(torch.randint(0, max_len + 1, (B, nshare - 1), generator=gen), dim=1).values
+    bounds = torch.cat([torch.zeros(B, 1, dtype=torch.long), torch.minimum(cuts, lens[:, None]), lens[:, None]], 1)
+    q = rand_bf16(B, Hkv * G, D, gen=gen).to(DEV)
+    shares, full_k, full_v = [], [], []
+    g2 = torch.Generator(device=DEV).manual_seed(seed)
+    for b in range(B):
+        full_k.append(torch.randn(Hkv, int(lens[b]), D, generator=g2, device=DEV).bfloat16())
+        full_v.append(torch.randn(Hkv, int(lens[b]), D, generator=g2, device=DEV).bfloat16())
+    for sh in range(nshare):
+        n = (bounds[:, sh + 1] - bounds[:, sh]).tolist()
+        cap = max(max(n), 1)
+        k = torch.zeros(B * Hkv, cap, D, dtype=torch.bfloat16, device=DEV)
+        v = torch.zeros(B * Hkv, cap, D, dtype=torch.bfloat16, device=DEV)
+        for b in range(B):
+            a0, a1 = int(bounds[b, sh]), int(bounds[b, sh + 1])
+            k[b * Hkv:(b + 1) * Hkv, :a1 - a0] = full_k[b][:, a0:a1]
+            v[b * Hkv:(b + 1) * Hkv, :a1 - a0] = full_v[b][:, a0:a1]
+        shares.append(scope_b200.Share(k, v, seqlens=torch.tensor(n, dtype=torch.int32, device=DEV)))
+    for rep in range(2):   # the workspace is reused: nothing may depend on a previous call's contents
+        out, lse = scope_b200.gqa_decode_shares(q, shares, D ** -0.5)
+        for b in range(B):
+            for h in range(Hkv):
+                ro, rl = _torch_ref(q[b, h * G:(h + 1) * G], full_k[b][h], full_v[b][h], D ** -0.5)
+                assert (out[b, h * G:(h + 1) * G].float() - ro).abs().max().item() < TOL_OUT, (rep, b, h)
+                assert (lse[b, h * G:(h + 1) * G] - rl).abs().max().item() < TOL_LSE, (rep, b, h)
+
+
 def test_shares_one_empty_share(ext):
     """A sequence whose second share is empty, and a batch of all-empty rows."""
     gen = torch.Generator().manual_seed(3)

@@ -13,6 +13,7 @@ import torch
 
 import oracle
 import scope_b200
+import scope_b200.csa_attn   # the submodule is imported on first use, not by the package
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"

@@ -6,6 +6,7 @@ import pytest
 import torch
 
 import scope_b200
+import scope_b200.csa_attn   # the submodule is imported on first use, not by the package
 from scope_b200.shard import PartialExchange, shard_bounds
 
 pytestmark = pytest.mark.gpu
