@@ -29,6 +29,11 @@
 namespace ws {
 
 constexpr int kTile = 64;        // tokens per TMA tile
+// Ragged shares: every non-empty segment starts with kSegLead empty tiles in the flattened tile space.
+// They carry no data (nothing is loaded or computed for them) but count in the even split over the
+// CTAs, so a CTA whose range crosses many short segments takes fewer tiles: each segment change costs
+// it a segment lookup, a piece and a query reload, about as long as kSegLead tiles of streaming.
+constexpr int kSegLead = 3;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxShares = 4;
@@ -76,6 +81,7 @@ struct Seg {
     int len;      // tokens
     int group;    // output group-row
     int t0;       // first tile in the flattened tile space
+    int lead;     // empty tiles before the segment's first data tile (ragged shares: kSegLead)
 };
 
 template <int DKP, int DVP, int NT, int STAGES>
@@ -106,6 +112,9 @@ struct SegTable {
         return p->lens[s] ? __ldg(p->lens[s] + b) : __ldg(p->cu[s] + b + 1) - __ldg(p->cu[s] + b);
     }
 
+    // Tiles of a ragged segment of len tokens in the flattened tile space (its lead-in included).
+    __device__ __forceinline__ static int vtiles(int len) { return len > 0 ? (len + kTile - 1) / kTile + kSegLead : 0; }
+
     __device__ __forceinline__ int64_t total() const {
         return p->varlen ? (int64_t)pre[p->B] : (int64_t)p->n_rows * tpr;
     }
@@ -114,7 +123,7 @@ struct SegTable {
         Seg s;
         if (!p->varlen) {
             int j = (int)(t / tpr);
-            s.j = j; s.map = 0; s.y = j; s.x0 = 0; s.len = p->L; s.group = j; s.t0 = j * tpr;
+            s.j = j; s.map = 0; s.y = j; s.x0 = 0; s.len = p->L; s.group = j; s.t0 = j * tpr; s.lead = 0;
             return s;
         }
         // largest b with pre[b] <= t
@@ -125,14 +134,14 @@ struct SegTable {
         }
         const int b = lo;
         int th = 0;
-        for (int sh = 0; sh < p->nshare; ++sh) th += (seq_len(sh, b) + kTile - 1) / kTile;
+        for (int sh = 0; sh < p->nshare; ++sh) th += vtiles(seq_len(sh, b));
         int r = (int)(t - pre[b]);
         const int h = r / th;
         r -= h * th;
         int base = pre[b] + h * th;
         int sh = 0;
         for (; sh < p->nshare; ++sh) {
-            const int ts = (seq_len(sh, b) + kTile - 1) / kTile;
+            const int ts = vtiles(seq_len(sh, b));
             if (r < ts) break;
             r -= ts;
             base += ts;
@@ -147,7 +156,7 @@ struct SegTable {
             s.x0 = __ldg(p->cu[sh] + b);
         }
         s.len = seq_len(sh, b);
-        s.group = b * p->Hkv + h; s.t0 = base;
+        s.group = b * p->Hkv + h; s.t0 = base; s.lead = kSegLead;
         return s;
     }
 
@@ -161,7 +170,7 @@ struct SegTable {
         const int b = group / p->Hkv, h = group - b * p->Hkv;
         int th = 0, before = 0, mine = 0;
         for (int sh = 0; sh < p->nshare; ++sh) {
-            const int ts = (seq_len(sh, b) + kTile - 1) / kTile;
+            const int ts = vtiles(seq_len(sh, b));
             if (sh < js) before += ts;
             if (sh == js) mine = ts;
             th += ts;
@@ -249,7 +258,7 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
             for (int b = 0; b < p.B; ++b) {
                 pre[b] = acc;
                 int th = 0;
-                for (int sh = 0; sh < p.nshare; ++sh) th += (tab.seq_len(sh, b) + kTile - 1) / kTile;
+                for (int sh = 0; sh < p.nshare; ++sh) th += SegTable::vtiles(tab.seq_len(sh, b));
                 acc += th * p.Hkv;
             }
             pre[p.B] = acc;
@@ -291,15 +300,17 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
             int stage = 0;
             uint32_t use = 0;
             for (int64_t t = t_begin; t < t_end; ++t, ++i) {
+                if (t >= seg_end) {
+                    sg = tab.of_tile(t);
+                    seg_end = sg.t0 + sg.lead + (sg.len + kTile - 1) / kTile;
+                }
+                const int r = (int)(t - sg.t0) - sg.lead;
+                if (r < 0) continue;   // a segment's lead-in: no data, no stage
                 if (use > 0 && !mbar_wait_bounded(empty0 + 8 * stage, (use & 1) ^ 1)) {
                     atomicExch(p.status, kDevTimeout);
                     break;
                 }
-                if (t >= seg_end) {
-                    sg = tab.of_tile(t);
-                    seg_end = sg.t0 + (sg.len + kTile - 1) / kTile;
-                }
-                const int x = sg.x0 + (int)(t - sg.t0) * kTile;
+                const int x = sg.x0 + r * kTile;
                 const int c1 = p.tok_in_dim2[sg.map] ? sg.y : x;
                 const int c2 = p.tok_in_dim2[sg.map] ? x : sg.y;
                 const uint32_t fb = full0 + 8 * stage;
@@ -404,7 +415,19 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
                 }
         named_bar_sync(1, kConsumerWarps * 32);
 
-        const int np = tab.pieces(sg.group, total, nctas);
+        // pieces of the group: counted from the segment table, except for ragged shares (always merged by
+        // gqa_merge_kernel), which only need to know whether this segment is the group's only piece: the
+        // group's tiles per head come from the prefix in shared memory, so no global load is waited on
+        int np;
+        if (p.varlen) {
+            const int b = sg.group / p.Hkv;
+            const int64_t th = (pre[b + 1] - pre[b]) / p.Hkv;
+            const int64_t seg_tiles = SegTable::vtiles(sg.len);
+            np = (seg_tiles == th && split_owner(sg.t0, total, nctas) == split_owner(sg.t0 + th - 1, total, nctas))
+                     ? 1 : 2;
+        } else {
+            np = tab.pieces(sg.group, total, nctas);
+        }
         const int slot = cta + sg.j;
         float* part = p.ws_part + (int64_t)slot * C::SLOT_FLOATS;
         for (int e = ctid; e < NG * DVP; e += kConsumerWarps * 32) {
@@ -535,18 +558,20 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
     for (int64_t t = t_begin; t < t_end; ++t) {
         if (t >= seg_end) {
             const Seg sg = tab.of_tile(t);
+            load_q(sg.group);   // its loads land while the previous segment is flushed (qf is free now)
             if (cur.j >= 0) flush(cur);
             cur = sg;
-            seg_end = sg.t0 + (sg.len + kTile - 1) / kTile;
-            load_q(sg.group);
+            seg_end = sg.t0 + sg.lead + (sg.len + kTile - 1) / kTile;
             reset_state();
         }
         const Seg& sg = cur;
+        const int rt = (int)(t - sg.t0) - sg.lead;   // data tile of the segment
+        if (rt < 0) continue;                         // a segment's lead-in: nothing was loaded
         if (!mbar_wait_bounded(full0 + 8 * stage, use & 1)) {
             atomicExch(p.status, kDevTimeout);
             break;
         }
-        const int nv = min(kTile, sg.len - (int)(t - sg.t0) * kTile) - warp * 16;   // valid tokens of this warp
+        const int nv = min(kTile, sg.len - rt * kTile) - warp * 16;   // valid tokens of this warp
         if (nv > 0) {
             const uint32_t kbase = smem_u32(stage_base + size_t(stage) * C::STAGE_BYTES);
             const uint32_t vbase = kbase + C::KBOX * C::BOX_BYTES;
@@ -674,7 +699,7 @@ __global__ void __launch_bounds__(32) gqa_merge_kernel(const GqaParams p, int tp
         int ts[kMaxShares], th = 0;
 #pragma unroll
         for (int sh = 0; sh < kMaxShares; ++sh) {
-            ts[sh] = sh < p.nshare ? (tab.seq_len(sh, b) + kTile - 1) / kTile : 0;
+            ts[sh] = sh < p.nshare ? SegTable::vtiles(tab.seq_len(sh, b)) : 0;
             th += ts[sh];
         }
         int64_t t0 = __ldcg(p.ws_pre + b) + (int64_t)h * th;
