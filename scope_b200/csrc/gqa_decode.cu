@@ -33,7 +33,7 @@ constexpr int kTile = 64;        // tokens per TMA tile
 // They carry no data (nothing is loaded or computed for them) but count in the even split over the
 // CTAs, so a CTA whose range crosses many short segments takes fewer tiles: each segment change costs
 // it a segment lookup, a piece and a query reload, about as long as kSegLead tiles of streaming.
-constexpr int kSegLead = 3;
+constexpr int kSegLead = 6;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxShares = 4;
