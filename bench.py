@@ -550,6 +550,16 @@ class Csa(Workload):
         self.idx = [torch.stack([torch.randperm(nc, generator=gi)[:k].sort().values for _ in range(bs)]).int().to(dev)
                     for _ in range(self.n_sets)]
         self.n_local = [int(((t >= self.lo) & (t < self.hi)).sum()) for t in self.idx]
+        # shard load balance: selected entries per rank (all ranks' shards, from the same id sets), as
+        # max / mean over ranks, averaged over the sets; the per-sequence worst case alongside
+        bounds = [shard_bounds(nc, world, r) for r in range(world)]
+        whole, per_seq = [], []
+        for t in self.idx:
+            cnt = torch.stack([((t >= lo_r) & (t < hi_r)).sum(dim=1) for lo_r, hi_r in bounds]).float()  # [world, bs]
+            tot = cnt.sum(dim=1)
+            whole.append(float(tot.max() / tot.mean()))
+            per_seq.append(float((cnt.max(dim=0).values / cnt.mean(dim=0).clamp(min=1e-9)).max()))
+        self.shard_load = (sum(whole) / len(whole), max(per_seq))
         gq = torch.Generator(device=dev).manual_seed(seed + 1)
         self.q = [torch.randn(bs, nH, 512, generator=gq, device=dev).bfloat16() for _ in range(self.n_sets)]
         self.lib, self._lib = _lib.lib(), _lib
@@ -634,6 +644,8 @@ class Csa(Workload):
                 "n_compressed": self.nc, "topk": self.k, "kv_dtype": "int8 + fp32 scale per entry",
                 "entries_per_gpu": self.hi - self.lo,
                 "selected_entries_this_rank": sum(self.n_local) / len(self.n_local),
+                "shard_load_max_over_mean": round(self.shard_load[0], 4),
+                "shard_load_max_over_mean_worst_sequence": round(self.shard_load[1], 4),
                 "parallelism": f"entry-shard{self.world}",
                 "l2": (f"{self.n_sets} rotating top-k sets and q copies, {self.n_kv} KV shard copies "
                        f"({self.n_kv * self.kv[0].numel() / 2 ** 20:.0f} MiB) > 3x L2"),

@@ -236,8 +236,11 @@ int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const 
     if (B == 0) return WS_OK;
     if (!q_proj || !q_pe || !out || (S > 0 && (!c_kv || !k_pe))) return set_error(WS_ERR_INVALID_ARG, "null pointer");
     if (out_mode < WS_OUT_NORM_BF16 || out_mode > WS_OUT_NORM_F32) return set_error(WS_ERR_INVALID_ARG, "bad out_mode");
+    // a programmatic dependent launch: the decode's setup overlaps the previous grid on the stream, and it
+    // waits for that grid before reading q or the latent cache
     return mla_launch(q_proj, q_pe, c_kv, k_pe, B, nH, S, scale, out_mode, out, out_max, out_sum, out_lse, workspace,
-                      workspace_bytes, static_cast<cudaStream_t>(stream));
+                      workspace_bytes, static_cast<cudaStream_t>(stream), /*after_primary=*/true,
+                      /*kv_after_primary=*/true);
 }
 
 size_t ws_mla_decode_absorbed_workspace_size(int B, int nH, int S) { return mla_absorbed_workspace_bytes(B, nH, S); }
