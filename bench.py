@@ -254,7 +254,14 @@ class GqaDense(Workload):
         self.vnew_host = torch.randn(rows, D).bfloat16().pin_memory()
         self.out_host = torch.empty(B * H * D, dtype=torch.bfloat16).pin_memory()
         self.lse_host = torch.empty(B * H, dtype=torch.float32).pin_memory()
-        self.kernels_per_step = 1 if world == 1 else 2
+        # the decode, its deferred merge when a row's tiles span more than eight CTAs (the rule in
+        # gqa_decode.cu's host code), and with N > 1 the merge of the exchanged partials
+        tpr = -(-self.Lloc // 64)
+        total = rows * tpr
+        nctas = min(torch.cuda.get_device_properties(dev).multi_processor_count, 156, max(total, 1))
+        per_cta = -(-total // nctas)
+        deferred = self.Lloc > 0 and -(-tpr // per_cta) + 1 > 8
+        self.kernels_per_step = 1 + int(deferred) + int(world > 1)
 
     def kernel_bytes(self):
         rows = self.B * self.Hkv
@@ -352,7 +359,7 @@ class GqaShares(Workload):
         self.lse_host = torch.empty(B, H, dtype=torch.float32).pin_memory()
         self.copies = 1
         self.graph = True
-        self.kernels_per_step = 1
+        self.kernels_per_step = 2   # the decode and the deferred merge of the ragged groups' pieces
         self._decode = scope_b200.gqa_decode_shares
 
     def kernel_bytes(self):
@@ -474,7 +481,7 @@ class MlaAbsorbed(Mla):
         self._absorbed = cpu_attn.mla_decode_absorbed
         self.qn_host = torch.randn(B, nH, self.nop).bfloat16().pin_memory()
         self.outv_host = torch.empty(B, nH, self.vhd, dtype=torch.bfloat16).pin_memory()
-        self.kernels_per_step = 3
+        self.kernels_per_step = 4   # absorb, decode, merge, up-projection
 
     def kernel_bytes(self):
         return (self.B * self.S * (512 + 64) * 2 + self.B * self.nH * (self.nop + 64 + self.vhd) * 2
@@ -578,7 +585,9 @@ class Csa(Workload):
         self.idx_host = self.idx[0].cpu().pin_memory()
         self.out_host = torch.empty(bs * nH * 512, dtype=torch.bfloat16).pin_memory()
         self.lse_host = torch.empty(bs * nH, dtype=torch.float32).pin_memory()
-        self.kernels_per_step = 1 if world == 1 else 2
+        # the decode and the merge of its split partials (9 CTAs per sequence here), and with N > 1 the
+        # merge of the exchanged partials
+        self.kernels_per_step = 2 + int(world > 1)
 
     def kernel_bytes(self):
         """Per launch on this rank, averaged over the rotating id sets."""
