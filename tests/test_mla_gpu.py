@@ -146,3 +146,31 @@ def test_absorbed_step_equals_unfused_composition():
     ref = torch.bmm(o.view(B * 16, 1, 512),
                     w_uv.transpose(1, 2).expand(B, 16, 512, vhd).reshape(B * 16, 512, vhd)).view(B, 16, vhd)
     assert (out.float() - ref.float()).abs().max().item() < TOL_OUT
+
+
+def test_decode_steps_after_appends_without_host_sync():
+    """Decode steps on one stream, each right after the append of that step's token and with no host
+    synchronisation in between: the decode is a programmatic dependent launch (its setup overlaps the
+    previous grid), so its first latent load must still see the token the append just wrote."""
+    from scope_b200.kv_cache import _append
+    S0, steps, scale = 300, 6, 192 ** -0.5
+    qp, qpe, c, p = rand_inputs(1, S0 + steps, seed=31)
+    cd = torch.zeros(1, S0 + steps, 512, dtype=torch.bfloat16, device=DEV)
+    pd = torch.zeros(1, S0 + steps, 64, dtype=torch.bfloat16, device=DEV)
+    cd[:, :S0] = c[:, :S0].to(DEV)
+    pd[:, :S0] = p[:, :S0].to(DEV)
+    new_c, new_p = c[:, S0:].to(DEV).contiguous(), p[:, S0:].to(DEV).contiguous()
+    qd, qped = qp.to(DEV), qpe.to(DEV)
+    torch.cuda.synchronize()
+    outs = []
+    for s in range(steps):
+        S = S0 + s + 1
+        _append(cd, new_c[:, s:s + 1], S - 1)
+        _append(pd, new_p[:, s:s + 1], S - 1)
+        outs.append(scope_b200.cpu_attn.mla_decode(qd, qped, cd[:, :S], pd[:, :S], scale))
+    torch.cuda.synchronize()
+    for s, (out, lse) in enumerate(outs):
+        S = S0 + s + 1
+        ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, c[:, :S], p[:, :S])), scale)
+        assert np.abs(out.float().cpu().numpy() - ro / rs[:, None]).max() < TOL_OUT, s
+        assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < TOL_LSE, s
