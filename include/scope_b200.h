@@ -102,8 +102,9 @@ size_t ws_gqa_decode_noalloc_max_scratch(void);
 
 /*
  * Ragged-batch GQA decode over up to 4 physically separate KV shares of every
- * sequence, with the per-share partials merged by log-sum-exp inside the same
- * launch.  Replaces the runtime's per-share fused_cpu_attn calls plus the
+ * sequence, with the per-share partials merged by log-sum-exp.  Two launches:
+ * the decode files one partial per (CTA, share segment) in the workspace, and
+ * a programmatic dependent launch merges each row's partials.  Replaces the runtime's per-share fused_cpu_attn calls plus the
  * Python merge (system/mixoffload.py:1263-1268, :1333-1334, :1456-1464;
  * system/qwenoffload.py:1606-1617).
  *   q        [B, Hkv*G, Dk] bf16 contiguous (head h = kvh*G + g)
