@@ -75,7 +75,8 @@ def test_golden(csa, golden):
 
 @pytest.mark.parametrize("bs,nH,hd,nc,k", [(1, 1, 16, 10, 3), (2, 4, 64, 200, 16), (3, 8, 128, 5000, 100),
                                            (2, 64, 128, 20000, 2048), (1, 16, 256, 4096, 4096),
-                                           (2, 5, 48, 777, 777), (1, 3, 32, 100, 500), (1, 8, 64, 20000, 3000)])
+                                           (2, 5, 48, 777, 777), (1, 3, 32, 100, 500), (1, 8, 64, 20000, 3000),
+                                           (2, 4, 32, 9001, 700), (5, 2, 64, 33333, 2048)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_random(csa, bs, nH, hd, nc, k, dtype):
     q, kv, w = rand_case(bs, nH, hd, nc, seed=bs * 7919 + nc + k, dtype=dtype)
