@@ -14,6 +14,10 @@
  * size the matching *_workspace_size() returns.  A workspace must be zeroed
  * once when it is allocated (its counters reset themselves after every
  * launch) and must not be shared by launches that may overlap in time.
+ * Exception: when ws_status_take() returns WS_ERR_DEVICE, a launch may have
+ * given up between taking and returning a merge counter, so every workspace
+ * used since the previous ws_status_take() must be zeroed again before its
+ * next use.
  *
  * bf16 tensors are passed as their 16-bit storage.  The reference interfaces
  * each entry replaces are cited as path:line of the reference checkout.
@@ -207,6 +211,27 @@ int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void
                   int64_t kv_begin, int64_t kv_end, float scale, void* out, int out_dtype, float* out_lse,
                   void* workspace, size_t workspace_bytes, void* stream);
 size_t ws_csa_decode_workspace_size(int bs, int nq, int q_dtype);
+
+/*
+ * CSA decode in the reference's integer-score form: u8 query codes against
+ * s8 entry codes.  Replaces fused_csa_attn_bsq_int8_preq
+ * (kernel/cpu_attn_ds4_ext/csa_attn.cpp:1235-1357), fused_csa_attn_bsq_int8_full
+ * (:1359-1483) and the attention of fused_csa_attn_bsq_int8 (:766-883, after
+ * its two quantisers, ws_csa_q_quantize_u8 and ws_csa_kv_quantize_s8):
+ *   q_u8 [bs, nq, 512] u8 codes (value + 128), q_scales [bs, nq] fp32
+ *   kv_i8 [bs, nc, 512] s8 codes, kv_scales [bs, nc] fp32, kv_sums [bs, nc] int32
+ *   score = ((sum_d q_u8 * kv_i8) - 128 * kv_sums) * q_scale * kv_scale * scale
+ *   (the integer dot is exact, as the reference's VNNI dot is)
+ *   value = kv_i8 * kv_scale, or, with kv_bf16 [bs, nc, 512] non-NULL, the
+ *   bf16 entry itself (the _full operator).
+ * The id list / dense range, shard arguments, outputs and workspace are those
+ * of ws_csa_decode with q_dtype WS_DTYPE_BF16 (64-row query groups).
+ */
+int ws_csa_decode_qcodes(const uint8_t* q_u8, const float* q_scales, int bs, int nq, int hd, const int8_t* kv_i8,
+                         const float* kv_scales, const int32_t* kv_sums, const void* kv_bf16, int64_t nc,
+                         int64_t shard_lo, const int32_t* idx, int k, int idx_mode, int64_t kv_begin, int64_t kv_end,
+                         float scale, void* out, int out_dtype, float* out_lse, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /*
  * Per-row quantisers of the CSA int8 family, bit-exact with the reference:

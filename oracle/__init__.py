@@ -65,6 +65,11 @@ def lib():
         L.orc_q_quantize_u8.restype = None
         L.orc_csa_int8_preq.argtypes = [_F, _V, _F, _I, _int, _int, _int, _int, ctypes.c_float, _D, _D]
         L.orc_csa_int8_preq.restype = None
+        L.orc_csa_int8_codes.argtypes = [_V, _F, _V, _F, _I, _V, _I, _int, _int, _int, _int, _int,
+                                         ctypes.c_float, _D, _D]
+        L.orc_csa_int8_codes.restype = None
+        L.orc_indexer_scores_f32.argtypes = [_F, _F, _F, _int, _int, _int, _i64, _int, _F]
+        L.orc_indexer_scores_f32.restype = None
         L.orc_lse_merge.argtypes = [_D, _D, _int, _i64, _int, _D, _D]
         L.orc_lse_merge.restype = None
         L.orc_indexer_topk.argtypes = [_F, _F, _F, _int, _int, _int, _int, _int, _I, _D]
@@ -256,6 +261,79 @@ def csa_int8_preq(q, kv_i8, kv_scales, kv_sums, scale):
                             _p(np.ascontiguousarray(kv_sums, dtype=np.int32), _I),
                             bs, nq, hd, nc, float(scale), _p(o, _D), _p(lse, _D))
     return o, lse
+
+
+def csa_int8_codes(q_u8, q_scales, kv_i8, kv_scales, kv_sums, scale, kv_bf16=None, idx=None):
+    """The reference's integer-score CSA (csa_attn.cpp:1235-1483): q_u8 [bs, nq, hd]
+    codes with q_scales [bs, nq]; kv_i8 / kv_scales / kv_sums the entry codes;
+    values int8 * scale, or the bf16 entries ``kv_bf16`` (uint16 bits) when
+    given (the _full operator); ``idx`` [bs, k] selects entries (else all)."""
+    q_u8 = np.ascontiguousarray(q_u8, dtype=np.uint8)
+    bs, nq, hd = q_u8.shape
+    nc = kv_i8.shape[1]
+    o = np.zeros((bs, nq, hd), np.float64)
+    lse = np.zeros((bs, nq), np.float64)
+    kvb = None if kv_bf16 is None else np.ascontiguousarray(kv_bf16, dtype=np.uint16)
+    ids = None if idx is None else np.ascontiguousarray(idx, dtype=np.int32)
+    lib().orc_csa_int8_codes(_p(q_u8), _p(np.ascontiguousarray(q_scales, dtype=np.float32), _F),
+                             _p(np.ascontiguousarray(kv_i8, dtype=np.int8)),
+                             _p(np.ascontiguousarray(kv_scales, dtype=np.float32), _F),
+                             _p(np.ascontiguousarray(kv_sums, dtype=np.int32), _I),
+                             None if kvb is None else _p(kvb), None if ids is None else _p(ids, _I),
+                             0 if ids is None else ids.shape[1], bs, nq, hd, nc, float(scale),
+                             _p(o, _D), _p(lse, _D))
+    return o, lse
+
+
+def indexer_scores_f32(q_idx, kv_idx, w, contract=True):
+    """Indexer scores in the reference's fp32 order (csa_attn.cpp:1706-1724):
+    float32 [bs, nc], bit for bit what indexer_topk_cpu ranks."""
+    q_idx = np.ascontiguousarray(q_idx, dtype=np.float32)
+    kv_idx = np.ascontiguousarray(kv_idx, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    bs, nH, hd = q_idx.shape
+    nc = kv_idx.shape[1]
+    out = np.zeros((bs, nc), np.float32)
+    lib().orc_indexer_scores_f32(_p(q_idx, _F), _p(kv_idx, _F), _p(w, _F), bs, nH, hd, nc, int(bool(contract)),
+                                 _p(out, _F))
+    return out
+
+
+def topk_from_scores(scores, k):
+    """ids [bs, min(k, nc)] by descending score, ties by the lower id."""
+    scores = np.asarray(scores)
+    k = min(int(k), scores.shape[1])
+    ids = np.argsort(-scores.astype(np.float64), axis=1, kind="stable")[:, :k]
+    return ids.astype(np.int32)
+
+
+def canonical_topk(ids, scores):
+    """Reorder each row of ``ids`` by (descending score, ascending id): the
+    reference's partial_sort leaves the order of exactly equal scores
+    unspecified, so two correct outputs may differ only inside such runs."""
+    ids = np.asarray(ids)
+    out = np.empty_like(ids)
+    for b in range(ids.shape[0]):
+        s = np.asarray(scores[b], dtype=np.float64)[ids[b]]
+        out[b] = ids[b][np.lexsort((ids[b], -s))]
+    return out
+
+
+def topk_agreement(ids, ref_ids, scores):
+    """Compare two top-k id lists under one score array.  Returns a dict:
+    ``set_diff`` ids in one set but not the other (summed over rows),
+    ``boundary_ties`` how many entries score exactly the k-th score (a set
+    may legitimately differ only among those), ``order_diff`` positions that
+    differ after both lists are put in canonical tie order."""
+    set_diff = boundary = order_diff = 0
+    ci, cr = canonical_topk(ids, scores), canonical_topk(ref_ids, scores)
+    for b in range(ids.shape[0]):
+        a, r = set(ids[b].tolist()), set(ref_ids[b].tolist())
+        set_diff += len(a ^ r)
+        kth = np.asarray(scores[b])[ref_ids[b][-1]] if len(ref_ids[b]) else 0.0
+        boundary += int((np.asarray(scores[b]) == kth).sum()) if len(ref_ids[b]) else 0
+        order_diff += int((ci[b] != cr[b]).sum())
+    return {"set_diff": set_diff, "boundary_ties": boundary, "order_diff": order_diff}
 
 
 def lse_merge(o_parts, lse_parts):

@@ -238,19 +238,19 @@ void orc_q_quantize_u8(const float* q, int64_t rows, int hd, uint8_t* out, float
 }
 
 /*
- * int8 CSA with u8-quantised queries (fused_csa_attn_bsq_int8_preq,
- * csa_attn.cpp:1235-1357).  q fp32 [bs, nq, hd] is quantised per row to u8
- * exactly as the reference does; the score is
- *   ((sum u8*s8) - 128*ksum) * q_scale * k_scale * scale       (fp32, :1328-1329)
- * and the value update uses int8 * k_scale (:1338-1344).  The softmax and
- * value accumulation are then carried in float64.
+ * CSA in the reference's integer-score form (csa_attn.cpp:1235-1483, and the
+ * attention of :766-883 after its quantisers).  Query rows arrive as u8 codes
+ * with one scale each, entries as s8 codes with a scale and a code sum:
+ *   dot   = sum_d u8[d] * s8[d] - 128 * ksum                 (int32, exact; :1323-1328)
+ *   score = (float)dot * q_scale * k_scale * scale            (fp32, this order; :1329)
+ * The value is int8 * k_scale (:1338-1344) or, with kv_bf16 non-NULL, the
+ * bf16 entry (:1465-1470).  Entries are all nc (idx NULL) or the ids
+ * idx[b, 0..n_idx).  The softmax and the value sums are carried in float64.
  */
-void orc_csa_int8_preq(const float* q, const int8_t* kv_i8, const float* kv_scales,
-                       const int32_t* kv_sums, int bs, int nq, int hd, int nc,
-                       float scale, double* o, double* lse) {
-    uint8_t* qu = (uint8_t*)malloc((size_t)bs * nq * hd);
-    float* qs = (float*)malloc((size_t)bs * nq * sizeof(float));
-    orc_q_quantize_u8(q, (int64_t)bs * nq, hd, qu, qs);
+void orc_csa_int8_codes(const uint8_t* q_u8, const float* q_scales, const int8_t* kv_i8,
+                        const float* kv_scales, const int32_t* kv_sums, const uint16_t* kv_bf16,
+                        const int32_t* idx, int n_idx, int bs, int nq, int hd, int nc, float scale,
+                        double* o, double* lse) {
     #pragma omp parallel for collapse(2) schedule(static)
     for (int b = 0; b < bs; b++) {
         for (int r = 0; r < nq; r++) {
@@ -258,25 +258,47 @@ void orc_csa_int8_preq(const float* q, const int8_t* kv_i8, const float* kv_scal
             double* orow = o + row * hd;
             double m = -INFINITY, s_acc = 0.0;
             for (int d = 0; d < hd; d++) orow[d] = 0.0;
-            for (int i = 0; i < nc; i++) {
+            int n = idx ? n_idx : nc;
+            for (int j = 0; j < n; j++) {
+                int64_t i = idx ? (int64_t)idx[(int64_t)b * n_idx + j] : (int64_t)j;
+                if (i < 0 || i >= nc) continue;
                 const int8_t* ki = kv_i8 + ((int64_t)b * nc + i) * hd;
                 float ksc = kv_scales[(int64_t)b * nc + i];
                 int32_t dot = 0;
-                for (int d = 0; d < hd; d++) dot += (int32_t)qu[row * hd + d] * (int32_t)ki[d];
+                for (int d = 0; d < hd; d++) dot += (int32_t)q_u8[row * hd + d] * (int32_t)ki[d];
                 dot -= 128 * kv_sums[(int64_t)b * nc + i];
-                float scf = (float)dot * qs[row] * ksc * scale;
+                float scf = (float)dot * q_scales[row] * ksc * scale;
                 double sc = (double)scf;
                 double nm = sc > m ? sc : m;
                 double eo = exp(m - nm), en = exp(sc - nm);
                 s_acc = eo * s_acc + en;
                 m = nm;
-                for (int d = 0; d < hd; d++) orow[d] = eo * orow[d] + en * (double)ksc * (double)ki[d];
+                if (kv_bf16) {
+                    const uint16_t* vb = kv_bf16 + ((int64_t)b * nc + i) * hd;
+                    for (int d = 0; d < hd; d++) orow[d] = eo * orow[d] + en * bf16_to_d(vb[d]);
+                } else {
+                    for (int d = 0; d < hd; d++) orow[d] = eo * orow[d] + en * (double)ksc * (double)ki[d];
+                }
             }
             if (s_acc > 0.0)
                 for (int d = 0; d < hd; d++) orow[d] /= s_acc;
             lse[row] = m + log(s_acc);
         }
     }
+}
+
+/*
+ * fused_csa_attn_bsq_int8_preq (csa_attn.cpp:1235-1357): the fp32 query is
+ * quantised per row to u8 exactly as the reference does, then scored and
+ * summed as orc_csa_int8_codes does with int8 * k_scale values.
+ */
+void orc_csa_int8_preq(const float* q, const int8_t* kv_i8, const float* kv_scales,
+                       const int32_t* kv_sums, int bs, int nq, int hd, int nc,
+                       float scale, double* o, double* lse) {
+    uint8_t* qu = (uint8_t*)malloc((size_t)bs * nq * hd);
+    float* qs = (float*)malloc((size_t)bs * nq * sizeof(float));
+    orc_q_quantize_u8(q, (int64_t)bs * nq, hd, qu, qs);
+    orc_csa_int8_codes(qu, qs, kv_i8, kv_scales, kv_sums, NULL, NULL, 0, bs, nq, hd, nc, scale, o, lse);
     free(qu);
     free(qs);
 }
@@ -349,4 +371,45 @@ void orc_indexer_topk(const float* q_idx, const float* kv_idx, const float* w,
     }
     free(sc);
     free(ids);
+}
+
+/*
+ * The indexer score in the reference's own fp32 arithmetic
+ * (csa_attn.cpp:1706-1724): per head, 16 lane accumulators (lane l takes
+ * dims l, l+16, ... with a fused multiply-add each, :1712-1716), reduced as
+ * _mm512_reduce_add_ps does (the two 8-lane halves, then the two 4-lane
+ * halves, then lanes {0+2, 1+3}, then the last add; :128-130), then
+ * s = fma(relu(dot), w[h], s) over the heads in order (:1720-1721; the
+ * reference's -O3 -ffast-math build contracts the multiply-add).
+ * contract = 0 evaluates the last step as s + relu(dot) * w[h] instead.
+ */
+void orc_indexer_scores_f32(const float* q_idx, const float* kv_idx, const float* w,
+                            int bs, int nH, int hd, int64_t nc, int contract, float* scores) {
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int b = 0; b < bs; b++) {
+        for (int64_t n = 0; n < nc; n++) {
+            const float* kv = kv_idx + ((int64_t)b * nc + n) * hd;
+            float s = 0.0f;
+            for (int h = 0; h < nH; h++) {
+                const float* q = q_idx + ((int64_t)b * nH + h) * hd;
+                float a[16];
+                for (int l = 0; l < 16; l++) a[l] = 0.0f;
+                for (int d = 0; d < hd; d += 16)
+                    for (int l = 0; l < 16; l++) a[l] = fmaf(q[d + l], kv[d + l], a[l]);
+                float t3[8], t6[4];
+                for (int i = 0; i < 8; i++) t3[i] = a[i + 8] + a[i];
+                for (int i = 0; i < 4; i++) t6[i] = t3[i + 4] + t3[i];
+                float t80 = t6[0] + t6[2], t81 = t6[1] + t6[3];
+                float dot = t80 + t81;
+                float r = dot > 0.0f ? dot : 0.0f;
+                if (contract) {
+                    s = fmaf(r, w[(int64_t)b * nH + h], s);
+                } else {
+                    float pr = r * w[(int64_t)b * nH + h];
+                    s = s + pr;
+                }
+            }
+            scores[(int64_t)b * nc + n] = s;
+        }
+    }
 }

@@ -57,8 +57,14 @@ def status_take(device=None) -> int:
     """Read and clear the device status word of ``device`` (synchronises its
     current stream): 0 when no kernel reported a problem since the last call,
     else WS_ERR_DEVICE (5): a bounded wait gave up, or a CSA id outside the
-    KV buffer was skipped."""
+    KV buffer was skipped.  On WS_ERR_DEVICE the device's pooled workspaces
+    are dropped, so the next launch runs on a freshly zeroed one (a launch
+    that gave up may have left a merge counter set)."""
     import torch
+    from ._lib import workspaces
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with torch.cuda.device(dev):
-        return int(lib().ws_status_take(torch.cuda.current_stream(dev).cuda_stream))
+        rc = int(lib().ws_status_take(torch.cuda.current_stream(dev).cuda_stream))
+    if rc != 0:
+        workspaces.drop_device(dev.index if dev.index is not None else torch.cuda.current_device())
+    return rc

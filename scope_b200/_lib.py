@@ -76,6 +76,8 @@ SIGNATURES = {
     "ws_csa_decode": (_i, [_V, _i, _i, _i, _i, _V, _i, _V, _i64, _i64, _V, _i, _i, _i64, _i64, _f, _V, _i, _V,
                            _V, _sz, _V]),
     "ws_csa_decode_workspace_size": (_sz, [_i, _i, _i]),
+    "ws_csa_decode_qcodes": (_i, [_V, _V, _i, _i, _i, _V, _V, _V, _V, _i64, _i64, _V, _i, _i, _i64, _i64, _f, _V, _i,
+                                  _V, _V, _sz, _V]),
     "ws_indexer_topk": (_i, [_V, _V, _i, _V, _i, _i, _i, _i64, _i, _i, _V, _V, _V, _sz, _V]),
     "ws_indexer_topk_workspace_size": (_sz, [_i, _i64]),
     "ws_kv_append": (_i, [_V, _i64, _i64, _i64, _V, _i64, _i64, _i64, _i64, _i, _i, _i64, _V]),
@@ -143,6 +145,14 @@ class _WorkspacePool:
 
     def clear(self) -> None:
         self._bufs.clear()
+
+    def drop_device(self, index: int) -> None:
+        """Forget every workspace of device ``index``; the next launch there
+        allocates a freshly zeroed one.  Called after a kernel reported a
+        device-side failure: a launch that gave up may leave a merge counter
+        of its workspace non-zero."""
+        for key in [k for k in self._bufs if k[0] == index]:
+            del self._bufs[key]
 
 
 workspaces = _WorkspacePool()

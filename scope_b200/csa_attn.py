@@ -9,12 +9,18 @@ libscope_b200.so (``ws_csa_decode``): bf16 or int8+scale entries, gathered by
 top-k ids or over a dense range; its workspace comes from the per-stream pool.
 There is no CPU path: CPU tensors raise.
 
-Arithmetic differences from the reference, all toward the exact result:
-  * the query is rounded to bf16 inside the kernel (fp32 accumulation);
-  * the int8 variants (``_bsq_int8``, ``_int8_preq``, ``_int8_full``) do not
-    quantise the query: the reference's VNNI dot with a u8 query is a lossy
-    approximation of the same score, and the kernel computes the score from
-    the stored entries (``int8 * scale``, or the bf16 entries) directly.
+Arithmetic:
+  * an fp32 query is held as two bf16 parts (hi + lo) inside the kernel, so
+    the scores keep ~16 mantissa bits of it (fp32 accumulation); a bf16 query
+    is used as it is;
+  * the int8 operators (``_bsq_int8``, ``_int8_preq``, ``_int8_full``) compute
+    the reference's own integer score: the query quantised to u8 codes
+    (bit-exact with the reference's quantiser), the exact integer dot with the
+    s8 entry codes less ``128 * kv_sums``, times the query scale, the entry
+    scale and the softmax scale (``ws_csa_decode_qcodes``);
+  * ``fused_csa_attn_int8_exact`` is the one addition: int8 entries attended
+    with an unquantised query (``value = int8 * scale`` in both products), the
+    arithmetic the cfg5 sparse decode uses.
 """
 from __future__ import annotations
 
@@ -46,8 +52,8 @@ def _launch(q, kv, scale, out, lse, *, idx=None, kv_scales=None, kv_range=None, 
     bs, hd = q.shape[0], q.shape[-1]
     nq = q.numel() // max(1, bs * hd) if bs else 0
     nc = kv.shape[1]
-    if hd != HD:
-        raise RuntimeError(f"csa: this build supports head_dim {HD} (got {hd})")
+    if hd > HD or hd % 16 or hd == 0:
+        raise RuntimeError(f"csa: head_dim must be a multiple of 16 and at most {HD} (got {hd})")
     if kv.dim() != 3 or kv.shape[0] != bs or kv.shape[2] != hd:
         raise RuntimeError("kv shape mismatch")
     for name, t in (("q", q), ("kv", kv), ("o_out", out), ("lse_out", lse)):
@@ -55,6 +61,16 @@ def _launch(q, kv, scale, out, lse, *, idx=None, kv_scales=None, kv_range=None, 
             raise RuntimeError(f"{name} must be contiguous")
     if out.numel() != bs * nq * hd or lse.numel() != bs * nq:
         raise RuntimeError("o_out / lse_out shape mismatch")
+    if hd < HD:
+        # the kernel's latent is 512 wide: narrower heads run on zero-padded copies (zero dims add
+        # nothing to a score or to an output row); the result's first hd dims are copied back
+        if bs == 0 or nq == 0:
+            return
+        wide = torch.empty(bs, nq, HD, dtype=out.dtype, device=dev)
+        _launch(_pad_dims(q.reshape(bs, nq, hd), HD), _pad_dims(kv, HD), scale, wide, lse, idx=idx,
+                kv_scales=kv_scales, kv_range=kv_range, shard_lo=shard_lo, idx_mode=idx_mode)
+        out.view(bs, nq, hd).copy_(wide[..., :hd])
+        return
     if lse.dtype != torch.float32:
         raise RuntimeError("lse_out must be float32")
     q_code = {torch.float32: _lib.WS_DTYPE_F32, torch.bfloat16: _lib.WS_DTYPE_BF16}.get(q.dtype)
@@ -190,12 +206,80 @@ def fused_csa_attn_inplace(q, kv, scale, o_out, lse_out, n_threads: int = 0) -> 
     _inplace(q, kv, scale, o_out, lse_out)
 
 
-def fused_csa_attn_bsq_int8(q, kv, scale, o_out, lse_out, n_threads: int = 0) -> None:
-    """csa_attn.cpp:766-883 quantises q and kv inside the call and takes a VNNI
-    dot; here the bf16 entries are attended exactly (no quantisation)."""
-    if q.shape[-1] % 64 or q.shape[-1] > 512:
+def _check_int8_family(hd):
+    if hd % 64 or hd > 512:
         raise RuntimeError("head_dim must be multiple of 64 and <=512")
-    _inplace(q, kv, scale, o_out, lse_out)
+
+
+def _pad_dims(t, hd):
+    """t [..., d] -> [..., hd] with zeros beyond d (a copy; only when d < hd)."""
+    d = t.shape[-1]
+    if d == hd:
+        return t.contiguous()
+    out = torch.zeros(*t.shape[:-1], hd, dtype=t.dtype, device=t.device)
+    out[..., :d] = t
+    return out
+
+
+def _launch_qcodes(q_u8, q_scales, kv_i8, kv_scales, kv_sums, kv_vals, scale, o_out, lse_out):
+    """The integer-score CSA kernel over every entry of each sequence.
+
+    q_u8 [bs, nH, sq, hd] codes, q_scales [bs, nH, sq]; kv_i8 [bs, nc, hd],
+    kv_scales / kv_sums [bs, nc]; kv_vals None (values int8 * scale) or bf16
+    [bs, nc, hd].  hd < 512 (a multiple of 64) runs on zero-padded copies:
+    zero codes add nothing to the dot, zero values nothing to the output.
+    """
+    bs, hd = q_u8.shape[0], q_u8.shape[-1]
+    nc = kv_i8.shape[1]
+    nq = q_u8.numel() // max(1, bs * hd) if bs else 0
+    if bs == 0 or nq == 0:
+        return
+    dev = q_u8.device
+    if o_out.numel() != bs * nq * hd or lse_out.numel() != bs * nq:
+        raise RuntimeError("o_out / lse_out shape mismatch")
+    if lse_out.dtype != torch.float32 or o_out.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("o_out must be fp32 or bf16 and lse_out fp32")
+    if kv_i8.dim() != 3 or kv_i8.shape[0] != bs or kv_i8.shape[2] != hd:
+        raise RuntimeError("kv shape mismatch")
+    if tuple(kv_scales.shape) != (bs, nc) or tuple(kv_sums.shape) != (bs, nc):
+        raise RuntimeError("kv_scales / kv_sums must be [bs, nc]")
+    if kv_scales.dtype != torch.float32 or kv_sums.dtype != torch.int32:
+        raise RuntimeError("kv_scales must be float32 and kv_sums int32")
+    qp = _pad_dims(q_u8.reshape(bs, nq, hd), HD)
+    kp = _pad_dims(kv_i8, HD)
+    vp = None if kv_vals is None else _pad_dims(kv_vals, HD)
+    out = o_out if hd == HD else torch.empty(bs, nq, HD, dtype=o_out.dtype, device=dev)
+    with torch.cuda.device(dev):
+        L_ = lib()
+        ws = workspaces.get(L_.ws_csa_decode_workspace_size(bs, nq, _lib.WS_DTYPE_BF16), dev)
+        rc = L_.ws_csa_decode_qcodes(ptr(qp), ptr(q_scales.contiguous()), bs, nq, HD, ptr(kp),
+                                     ptr(kv_scales.contiguous()), ptr(kv_sums.contiguous()), ptr(vp), nc, 0, None, 0,
+                                     _lib.WS_CSA_IDX_ALL, 0, nc, float(scale), ptr(out),
+                                     _lib.WS_DTYPE_F32 if out.dtype == torch.float32 else _lib.WS_DTYPE_BF16,
+                                     ptr(lse_out), ptr(ws), ws.numel(), stream_ptr(dev))
+    check(rc, "ws_csa_decode_qcodes")
+    if out is not o_out:
+        o_out.view(bs, nq, hd).copy_(out[..., :hd])
+
+
+def fused_csa_attn_bsq_int8(q, kv, scale, o_out, lse_out, n_threads: int = 0) -> None:
+    """csa_attn.cpp:766-883: q fp32 [bs, nH, sq, hd] and kv bf16 [bs, nc, hd]
+    are both quantised inside the call (q to u8 per row, kv to s8 per entry,
+    each bit-exact with the reference's quantisers), the score is the integer
+    dot and the values are ``int8 * scale``; writes o_out / lse_out."""
+    _require_cuda("fused_csa_attn_bsq_int8", q, kv, o_out, lse_out)
+    if not q.is_contiguous() or not kv.is_contiguous():
+        raise RuntimeError("q/kv must be contiguous")
+    if not o_out.is_contiguous() or not lse_out.is_contiguous():
+        raise RuntimeError("o/lse must be contiguous")
+    _check_int8_family(q.shape[-1])
+    if q.dtype != torch.float32:
+        raise RuntimeError("q must be fp32")
+    if kv.dtype != torch.bfloat16:
+        raise RuntimeError("kv must be bf16")
+    kv_i8, kv_scales, kv_sums = kv_quantize_bf16_to_int8(kv)
+    q_u8, q_scales = q_quantize_fp32_to_u8(q)
+    _launch_qcodes(q_u8, q_scales, kv_i8, kv_scales, kv_sums, None, scale, o_out, lse_out)
 
 
 # ------------------------------------------------------------- int8 storage
@@ -233,31 +317,49 @@ def q_quantize_fp32_to_u8(q: torch.Tensor, n_threads: int = 0):
 
 
 def fused_csa_attn_bsq_int8_preq(q, kv_i8, kv_scales, kv_sums, scale, o_out, lse_out, n_threads: int = 0) -> None:
-    """CSA over int8 entries with per-entry scales (csa_attn.cpp:1235-1357):
-    values are ``int8 * scale`` for both the score and the weighted sum; the
-    query is used unquantised.  ``kv_sums`` is accepted for the signature."""
+    """csa_attn.cpp:1235-1357: pre-quantised entries (int8 codes, scales,
+    code sums), the fp32 query quantised to u8 inside the call; score
+    ``((sum u8*s8) - 128*kv_sums) * q_scale * k_scale * scale``, values
+    ``int8 * k_scale``; writes o_out / lse_out."""
     _require_cuda("fused_csa_attn_bsq_int8_preq", q, kv_i8, kv_scales, kv_sums, o_out, lse_out)
     if not (q.is_contiguous() and kv_i8.is_contiguous() and kv_scales.is_contiguous() and kv_sums.is_contiguous()
             and o_out.is_contiguous() and lse_out.is_contiguous()):
         raise RuntimeError("tensors must be contiguous")
-    if q.shape[-1] % 64 or q.shape[-1] > 512:
-        raise RuntimeError("head_dim must be multiple of 64 and <=512")
-    _launch(q, kv_i8, scale, o_out, lse_out, kv_scales=kv_scales)
+    _check_int8_family(q.shape[-1])
+    if q.dtype != torch.float32 or kv_i8.dtype != torch.int8:
+        raise RuntimeError("q must be fp32 and kv_i8 int8")
+    q_u8, q_scales = q_quantize_fp32_to_u8(q)
+    _launch_qcodes(q_u8, q_scales, kv_i8, kv_scales, kv_sums, None, scale, o_out, lse_out)
 
 
 def fused_csa_attn_bsq_int8_full(q_u8, q_scales, kv_i8, kv_scales, kv_sums, kv_bf16, scale, o_out, lse_out,
                                  n_threads: int = 0) -> None:
-    """csa_attn.cpp:1359-1483 scores a u8 query against the int8 entries and
-    sums the bf16 entries.  Here the query is dequantised ((u8 - 128) * scale,
-    the value the u8 form encodes) and attends the bf16 entries exactly."""
+    """csa_attn.cpp:1359-1483: a pre-quantised u8 query (codes + scales)
+    scored against the int8 entry codes as in ``_preq``, the weighted sum
+    taken over the bf16 entries ``kv_bf16``; writes o_out / lse_out."""
     _require_cuda("fused_csa_attn_bsq_int8_full", q_u8, q_scales, kv_i8, kv_scales, kv_sums, kv_bf16, o_out,
                   lse_out)
-    if not (q_u8.is_contiguous() and kv_bf16.is_contiguous() and o_out.is_contiguous() and lse_out.is_contiguous()):
+    if not (q_u8.is_contiguous() and kv_i8.is_contiguous() and kv_bf16.is_contiguous() and q_scales.is_contiguous()
+            and kv_scales.is_contiguous() and kv_sums.is_contiguous() and o_out.is_contiguous()
+            and lse_out.is_contiguous()):
         raise RuntimeError("tensors must be contiguous")
-    if q_u8.shape[-1] % 64 or q_u8.shape[-1] > 512:
-        raise RuntimeError("head_dim must be multiple of 64 and <=512")
-    q = (q_u8.to(torch.float32) - 128.0) * q_scales.unsqueeze(-1)
-    _launch(q, kv_bf16, scale, o_out, lse_out)
+    _check_int8_family(q_u8.shape[-1])
+    if q_u8.dtype != torch.uint8 or kv_i8.dtype != torch.int8 or kv_bf16.dtype != torch.bfloat16:
+        raise RuntimeError("q_u8 must be uint8, kv_i8 int8 and kv_bf16 bf16")
+    if kv_bf16.shape != kv_i8.shape:
+        raise RuntimeError("kv_bf16 shape mismatch")
+    _launch_qcodes(q_u8, q_scales, kv_i8, kv_scales, kv_sums, kv_bf16, scale, o_out, lse_out)
+
+
+def fused_csa_attn_int8_exact(q, kv_i8, kv_scales, scale, o_out, lse_out) -> None:
+    """Addition (no reference counterpart): dense CSA over int8 entries with
+    one fp32 scale each, the query unquantised (fp32 or bf16); the score and
+    the weighted sum both use ``int8 * scale`` exactly."""
+    _require_cuda("fused_csa_attn_int8_exact", q, kv_i8, kv_scales, o_out, lse_out)
+    if not (q.is_contiguous() and kv_i8.is_contiguous() and kv_scales.is_contiguous() and o_out.is_contiguous()
+            and lse_out.is_contiguous()):
+        raise RuntimeError("tensors must be contiguous")
+    _launch(q, kv_i8, scale, o_out, lse_out, kv_scales=kv_scales)
 
 
 # ------------------------------------------------------------------ gather

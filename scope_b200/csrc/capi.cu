@@ -305,6 +305,54 @@ int ws_csa_decode(const void* q, int q_dtype, int bs, int nq, int hd, const void
     return csa_launch(a);
 }
 
+int ws_csa_decode_qcodes(const uint8_t* q_u8, const float* q_scales, int bs, int nq, int hd, const int8_t* kv_i8,
+                         const float* kv_scales, const int32_t* kv_sums, const void* kv_bf16, int64_t nc,
+                         int64_t shard_lo, const int32_t* idx, int k, int idx_mode, int64_t kv_begin, int64_t kv_end,
+                         float scale, void* out, int out_dtype, float* out_lse, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    if (bs < 0 || nq < 1 || nc < 0 || shard_lo < 0) return set_error(WS_ERR_INVALID_ARG, "csa_decode_qcodes: bad shape");
+    if (hd != 512) return set_error(WS_ERR_UNSUPPORTED, "csa_decode_qcodes: this build supports a 512-wide latent");
+    if (out_dtype != WS_DTYPE_F32 && out_dtype != WS_DTYPE_BF16)
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode_qcodes: out dtype");
+    if (idx && (k < 0 || idx_mode < WS_CSA_IDX_ALL || idx_mode > WS_CSA_IDX_SHARD))
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode_qcodes: bad k or idx_mode");
+    if (!idx && kv_end < kv_begin) return set_error(WS_ERR_INVALID_ARG, "csa_decode_qcodes: kv_end < kv_begin");
+    if (nc > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "csa_decode_qcodes: nc > 2^31 - 1");
+    if (bs == 0) return WS_OK;
+    if (!q_u8 || !q_scales || !out || (nc > 0 && (!kv_i8 || !kv_scales || !kv_sums)))
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode_qcodes: null pointer");
+    if ((reinterpret_cast<uintptr_t>(q_u8) | reinterpret_cast<uintptr_t>(kv_i8) | reinterpret_cast<uintptr_t>(kv_bf16) |
+         reinterpret_cast<uintptr_t>(out)) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "csa_decode_qcodes: q_u8, kv_i8, kv_bf16 and out must be 16-byte aligned");
+    CsaLaunch a;
+    memset(&a, 0, sizeof(a));
+    a.q = q_u8;
+    a.q_u8 = 1;
+    a.q_scales = q_scales;
+    a.kv_sums = kv_sums;
+    a.kv_val = kv_bf16;
+    a.bs = bs;
+    a.nq = nq;
+    a.kv = kv_i8;
+    a.kv_i8 = 1;
+    a.kv_scales = kv_scales;
+    a.nc_local = nc;
+    a.shard_lo = shard_lo;
+    a.idx = idx;
+    a.k = idx ? k : 0;
+    a.window = idx_mode;
+    a.dense_begin = kv_begin;
+    a.dense_end = kv_end;
+    a.scale = scale;
+    a.out = out;
+    a.out_f32 = out_dtype == WS_DTYPE_F32;
+    a.out_lse = out_lse;
+    a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes;
+    a.stream = stream;
+    return csa_launch(a);
+}
+
 int ws_csa_kv_quantize_s8(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
                           void* stream) {
     if (rows < 0 || hd < 8 || hd % 8) return set_error(WS_ERR_INVALID_ARG, "csa_kv_quantize: bad shape");

@@ -5,8 +5,21 @@
 //
 // Replaces indexer_attn_cpu (kernel/cpu_attn_ds4_ext/csa_attn.cpp:1819-1883),
 // fused_csa_attn (:200-281) and fused_csa_attn_range (:1587-1656), and runs the
-// int8-entry storage of the int8 family (values = int8 * scale, :1338-1344)
-// without quantising the query.
+// int8-entry storage (values = int8 * scale, :1338-1344) with an unquantised
+// query.
+//
+// Query-code mode (QM > 0) reproduces the reference's int8 operators
+// (fused_csa_attn_bsq_int8 :766-883, _bsq_int8_preq :1235-1357, _bsq_int8_full
+// :1359-1483): the query arrives as u8 codes with one fp32 scale per row, the
+// entries as s8 codes with a scale and a code sum each, and the score is the
+// reference's integer form
+//     ((sum_d u8[d] * s8[d]) - 128 * ksum) * q_scale * k_scale * scale.
+// u8 and s8 codes are exact in fp16 and every partial sum of the first product
+// is an integer below 2^24, so the fp16 tensor-core product gives the same
+// integer dot as the reference's VNNI dpbusd.  Values are int8 * k_scale
+// (QM = 1) or a separate bf16 entry buffer (QM = 2, the _full operator: the
+// codes tile feeds the first product and the bf16 tile the second, so the ring
+// holds one tile of each instead of two tiles).
 //
 // One CTA per (sequence, group of query rows, split): the `splits` CTAs of a
 // (sequence, group) divide its selected entries evenly, with splits chosen so
@@ -87,7 +100,9 @@ struct Cfg {
     static constexpr int W_F = W_CSC + CHUNK;              // [2][TT] score factor: scale * softmax scale * log2(e)
     static constexpr int W_BIAS = W_F + 2 * TT;            // [2][TT] 0, or -inf where there is no entry
     static constexpr int W_PSC = W_BIAS + 2 * TT;          // [2][TT] value scale folded into P
-    static constexpr int W_ALPHA = W_PSC + 2 * TT;         // [2][64] per-head rescale factor, by tile parity
+    static constexpr int W_CKS = W_PSC + 2 * TT;           // [CHUNK] code sum of each entry (query-code mode)
+    static constexpr int W_COR = W_CKS + CHUNK;            // [2][TT] -128 * code sum (query-code mode)
+    static constexpr int W_ALPHA = W_COR + 2 * TT;         // [2][64] per-head rescale factor, by tile parity
     static constexpr int W_NEED = W_ALPHA + 128;           // [2][4] per-warp "some head rescales"
     static constexpr int W_RINV = W_NEED + 8;              // [64] 2^eref / l: normalises a head's O row
     static constexpr int W_RLSE = W_RINV + 64;             // [64] log-sum-exp of a head, -inf when empty
@@ -115,6 +130,9 @@ struct Params {
     const void* kv;
     int kv_i8;
     const float* kv_scales;   // [bs, nc_local] when kv_i8
+    const float* q_scales;    // query-code mode: [bs * nq] u8 query scales
+    const int* kv_sums;       //                  [bs, nc_local] s8 code sums
+    const void* kv_val;       //                  QM = 2: bf16 values [bs, nc_local, 512]
     const int* idx;           // [bs, k] (gather) or null (dense)
     int k;
     int window;               // WS_CSA_IDX_* for the gather
@@ -159,10 +177,14 @@ __device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, volatile
 // [2^14, 2^15) (no fp16 overflow, elements above 2^-28 of it exact), and the
 // value scales folded into P are scaled per 512-entry chunk by a power of two
 // so that P <= 256.  bf16 entries: bf16 products, no scaling.
-template <bool KV_I8, bool QSPLIT>
+// QM: 0 = float query; 1 = u8 query codes, values int8 * scale; 2 = u8 query
+// codes, bf16 values from p.kv_val (both need KV_I8 and a 64-row group).
+template <bool KV_I8, bool QSPLIT, int QM>
 __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p) {
+    static_assert(QM == 0 || (KV_I8 && !QSPLIT), "query codes need int8 entries and 64-row groups");
     using C = Cfg<QSPLIT>;
     constexpr int NQ = C::NQ;
+    constexpr bool P_F16 = KV_I8 && QM != 2;   // P (and the second product's operands) fp16, else bf16
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint32_t* misc = reinterpret_cast<uint32_t*>(sm + C::OFF_MISC);
@@ -171,6 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     float* s_f = reinterpret_cast<float*>(misc + C::W_F);
     float* s_bias = reinterpret_cast<float*>(misc + C::W_BIAS);
     float* s_psc = reinterpret_cast<float*>(misc + C::W_PSC);
+    int* s_cks = reinterpret_cast<int*>(misc + C::W_CKS);
+    float* s_cor = reinterpret_cast<float*>(misc + C::W_COR);
     float* s_alpha = reinterpret_cast<float*>(misc + C::W_ALPHA);
     int* s_need = reinterpret_cast<int*>(misc + C::W_NEED);
     float* s_rinv = reinterpret_cast<float*>(misc + C::W_RINV);
@@ -220,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     // the first tile's row loads can be in flight with the scale loads.
     int64_t id[kResolve];   // issue_ids -> resolve_rows: the chunk's ids in flight
     float sc_pend[kResolve];
+    int ks_pend[kResolve];  // query-code mode: the entries' code sums in flight
     auto issue_ids = [&](int64_t cbase) {
 #pragma unroll
         for (int u = 0; u < kResolve; ++u) {
@@ -241,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
 #pragma unroll
         for (int u = 0; u < kResolve; ++u) {
             sc_pend[u] = row[u] >= 0 ? (KV_I8 ? __ldg(p.kv_scales + kv_seq + row[u]) : 1.f) : 0.f;
+            if (QM) ks_pend[u] = row[u] >= 0 ? __ldg(p.kv_sums + kv_seq + row[u]) : 0;
             const int j = gtid + u * kGaThreads;
             if (j < CHUNK) s_crow[j] = row[u];
         }
@@ -252,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             const int j = gtid + u * kGaThreads;
             if (j < CHUNK) {
                 s_csc[j] = sc_pend[u];
+                if (QM) s_cks[j] = ks_pend[u];
                 mx = fmaxf(mx, sc_pend[u]);
             }
         }
@@ -271,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     //      issued at once and lands, unconverted, in the 16-byte slot its converted form takes (an fp32
     //      chunk of 8 dims: its two halves in the hi and the lo slot); rows past nrows are zero
     constexpr int QTPR = 32 * kSmWarps / NQ, QDPT = HD / QTPR;   // 2 x 256 dims (bf16 q), 4 x 128 (fp32 q)
-    constexpr int QL = QDPT * (QSPLIT ? 4 : 2) / 16;             // 16-byte loads per thread (32)
+    constexpr int QES = QM ? 1 : (QSPLIT ? 4 : 2);               // bytes per query element as loaded
+    constexpr int QL = QDPT * QES / 16;                          // 16-byte loads per thread (32; 16 for codes)
     static_assert(QDPT % 32 == 0 && QDPT * QTPR == HD, "query split");
     const int qr = tid / QTPR, qpart = tid - qr * QTPR;          // meaningful for the softmax warps
     auto qslot = [&](int c, int half) {   // 8-dim chunk c of this thread's share; half: lo part (fp32 q)
@@ -282,12 +310,32 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     if (warp < kSmWarps) {   // requested now; stored once the CTA-wide setup below is done
         const bool ok = qr < nrows;
         const int64_t qoff = ((int64_t)seq * p.nq + row0 + (ok ? qr : 0)) * HD + qpart * QDPT;
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.q) + qoff * (QSPLIT ? 4 : 2));
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.q) + qoff * QES);
 #pragma unroll
         for (int j = 0; j < QL; ++j) qraw[j] = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
     }
     uint32_t qmax_bits = 0;   // largest |q| of this thread's share, as float bits (fp16 products only)
     auto store_q = [&]() {
+        if (QM) {   // 16 u8 codes -> two 8-dim fp16 chunks: byte b -> fp16 bits 0x6400 | b = 1024 + b, minus 1024
+            const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
+#pragma unroll
+            for (int j = 0; j < QL; ++j) {
+                const uint32_t src[4] = {qraw[j].x, qraw[j].y, qraw[j].z, qraw[j].w};
+                uint32_t w[8];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t lo = __byte_perm(src[u], 0x64646464u, 0x4140);
+                    const uint32_t hi = __byte_perm(src[u], 0x64646464u, 0x4342);
+                    const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo), k1024);
+                    const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi), k1024);
+                    w[2 * u] = *reinterpret_cast<const uint32_t*>(&a);
+                    w[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&b);
+                }
+                *reinterpret_cast<uint4*>(qslot(2 * j, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(qslot(2 * j + 1, 0)) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+            return;
+        }
 #pragma unroll
         for (int j = 0; j < QL; ++j) {
             if (KV_I8) {   // magnitudes by integer max: non-negative floats order as their bits
@@ -322,7 +370,11 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
     const uint32_t tbase = *s_tmem;
     // S = Q . K^T and O^T += K^T . P^T
     constexpr uint32_t id1 = KV_I8 ? idesc_f16_f32(64, TT, false, false) : idesc_bf16_f32(64, TT, false, false);
-    constexpr uint32_t id2 = KV_I8 ? idesc_f16_f32(128, NQ, true, false) : idesc_bf16_f32(128, NQ, true, false);
+    constexpr uint32_t id2 = P_F16 ? idesc_f16_f32(128, NQ, true, false) : idesc_bf16_f32(128, NQ, true, false);
+    // QM = 2: the codes tile (first product) always sits in ring slot 0 and the values tile (second product)
+    // in slot 1; otherwise tile t uses slot t & 1 for both
+    auto k_slot = [&](int t) { return QM == 2 ? 0 : (t & 1); };
+    auto v_slot = [&](int t) { return QM == 2 ? 1 : (t & 1); };
 
     float m_final = -INFINITY, l_final = 0.f;   // softmax threads: this head's running max and sum
     int eref_final = 0;                          // and the value-scale exponent O was accumulated in
@@ -345,14 +397,18 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             fscale = KV_I8 ? p.scale_log2 * __int_as_float((127 + s_qexp[1]) << 23) : p.scale_log2;
         };
         // publish tile t's per-entry factors (thread gtid < TT owns entry gtid) and signal the MMA warp
-        auto publish = [&](int t, float sc, int ex) {   // ex: the chunk's value-scale exponent
+        // cor: -128 * the entry's code sum (query-code mode), read with sc before the chunk can change
+        auto publish = [&](int t, float sc, int ex, float cor) {   // ex: the chunk's value-scale exponent
             wait_q();
             const int slot = t & 1;
             if (gtid < TT) {
                 const bool ok = sc >= 0.f;
                 s_f[slot * TT + gtid] = ok ? sc * fscale : 0.f;
                 s_bias[slot * TT + gtid] = ok ? 0.f : -INFINITY;
-                s_psc[slot * TT + gtid] = ok ? sc * __int_as_float((127 - ex) << 23) : 0.f;
+                // bf16 values (QM = 2) are taken as they are: the entry scale is the score's only
+                const float pv = QM == 2 ? 1.f : sc * __int_as_float((127 - ex) << 23);
+                s_psc[slot * TT + gtid] = ok ? pv : 0.f;
+                if (QM) s_cor[slot * TT + gtid] = ok ? cor : 0.f;
             }
             if (gtid == 0) s_texp[slot] = ex;
             fence_proxy_async_smem();
@@ -373,57 +429,71 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
             const int off = (t * TT) % CHUNK + gtid;
             return (gtid < TT && s_crow[off] >= 0) ? s_csc[off] : -1.f;
         };
-        auto wait_slot = [&](int t) {
-            if (t >= 2) wait_bar(BAR(B_KEMPTY + (t & 1)), ((t >> 1) + 1) & 1, s_abort, p.status);
+        auto entry_cor = [&](int t) {    // query-code mode: -128 * the code sum of this thread's entry of tile t
+            const int off = (t * TT) % CHUNK + gtid;
+            return (QM && gtid < TT && s_crow[off] >= 0) ? -128.f * (float)s_cks[off] : 0.f;
         };
-        if (KV_I8) {
-            const int8_t* kv = static_cast<const int8_t*>(p.kv);
-            const int c = lane, rb = warp - kSmWarps;   // 32 chunks of 16 int8 per row; rows rb + 3i
-            auto load = [&](int4 (&r)[kGaRows], int t) {
-                const int off = (t * TT) % CHUNK;
+        auto wait_slot = [&](int t) {
+            if (QM == 2) {   // one tile of each kind: tile t waits for the second product of tile t - 1
+                if (t >= 1) wait_bar(BAR(B_KEMPTY + ((t - 1) & 1)), ((t - 1) >> 1) & 1, s_abort, p.status);
+            } else if (t >= 2) {
+                wait_bar(BAR(B_KEMPTY + (t & 1)), ((t >> 1) + 1) & 1, s_abort, p.status);
+            }
+        };
+        // 16 int8 codes (one lane's 16-byte chunk c of a row) -> 16 fp16 values in the row's 128-byte box
+        auto store_codes16 = [&](uint8_t* box, int rr, int c, const int4& r) {
+            const __half2 bias2 = __floats2half2_rn(1152.f, 1152.f);   // 1024 + 128
+            const uint32_t src[4] = {(uint32_t)r.x, (uint32_t)r.y, (uint32_t)r.z, (uint32_t)r.w};
+            uint32_t w[8];
 #pragma unroll
-                for (int i = 0; i < kGaRows; ++i) {
-                    const int rr = rb + kGaWarps * i;
-                    const int row = rr < TT ? s_crow[off + rr] : -1;
-                    r[i] = row >= 0 ? __ldg(reinterpret_cast<const int4*>(kv + (kv_seq + row) * HD + c * 16))
-                                    : make_int4(0, 0, 0, 0);
-                }
-            };
-            auto store = [&](const int4 (&r)[kGaRows], int t, float sc, int ex) {
+            for (int u = 0; u < 4; ++u) {
+                // byte b -> fp16 bits 0x6400 | (b + 128) = 1024 + b + 128, then subtract 1152: exact b
+                const uint32_t x = src[u] ^ 0x80808080u;
+                const uint32_t lo = __byte_perm(x, 0x64646464u, 0x4140);
+                const uint32_t hi = __byte_perm(x, 0x64646464u, 0x4342);
+                const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias2);
+                const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias2);
+                w[2 * u] = *reinterpret_cast<const uint32_t*>(&a);
+                w[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            *reinterpret_cast<uint4*>(box + swz(rr, (c & 3) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(box + swz(rr, (c & 3) * 2 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+        };
+        const int8_t* kv8 = static_cast<const int8_t*>(p.kv);
+        // the int8 codes of tile t's rows: lane c holds 16-byte chunk c of rows rb + 3i
+        auto load_codes = [&](int4 (&r)[kGaRows], int t) {
+            const int off = (t * TT) % CHUNK, rb = warp - kSmWarps;
+#pragma unroll
+            for (int i = 0; i < kGaRows; ++i) {
+                const int rr = rb + kGaWarps * i;
+                const int row = rr < TT ? s_crow[off + rr] : -1;
+                r[i] = row >= 0 ? __ldg(reinterpret_cast<const int4*>(kv8 + (kv_seq + row) * HD + lane * 16))
+                                : make_int4(0, 0, 0, 0);
+            }
+        };
+        if (KV_I8 && QM != 2) {
+            const int c = lane, rb = warp - kSmWarps;   // 32 chunks of 16 int8 per row; rows rb + 3i
+            auto store = [&](const int4 (&r)[kGaRows], int t, float sc, int ex, float cor) {
                 wait_slot(t);
                 uint8_t* box = sm + C::OFF_K + (t & 1) * KSLOT + (c >> 2) * KBOX;   // 64 dims per box
-                const __half2 bias2 = __floats2half2_rn(1152.f, 1152.f);          // 1024 + 128
 #pragma unroll
                 for (int i = 0; i < kGaRows; ++i) {
                     const int rr = rb + kGaWarps * i;
-                    if (rr >= TT) continue;
-                    const uint32_t src[4] = {(uint32_t)r[i].x, (uint32_t)r[i].y, (uint32_t)r[i].z, (uint32_t)r[i].w};
-                    uint32_t w[8];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        // byte b -> fp16 bits 0x6400 | (b + 128) = 1024 + b + 128, then subtract 1152: exact b
-                        const uint32_t x = src[u] ^ 0x80808080u;
-                        const uint32_t lo = __byte_perm(x, 0x64646464u, 0x4140);
-                        const uint32_t hi = __byte_perm(x, 0x64646464u, 0x4342);
-                        const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias2);
-                        const __half2 b = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias2);
-                        w[2 * u] = *reinterpret_cast<const uint32_t*>(&a);
-                        w[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&b);
-                    }
-                    *reinterpret_cast<uint4*>(box + swz(rr, (c & 3) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4*>(box + swz(rr, (c & 3) * 2 + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                    if (rr < TT) store_codes16(box, rr, c, r[i]);
                 }
-                publish(t, sc, ex);
+                publish(t, sc, ex, cor);
             };
+            auto load = load_codes;
             // two tiles in flight: the next tile's loads are issued before this tile is converted
             int4 ra[kGaRows], rb2[kGaRows];
-            float sca = 0.f, scb = 0.f;
+            float sca = 0.f, scb = 0.f, cora = 0.f, corb = 0.f;
             int exa = 0, exb = 0;
             if (ntiles > 0) {
                 load(ra, 0);   // needs only the rows; the scales arrive meanwhile
                 finish_scales();
                 named_bar_sync(BAR_GATHER, kGaThreads);
                 sca = entry_scale(0);
+                cora = entry_cor(0);
                 exa = chunk_exp();
             }
             // one call site each for load and store (the code of this loop stays small): the buffers
@@ -433,14 +503,70 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                 if (t + 1 < ntiles) {
                     if (((t + 1) * TT) % CHUNK == 0) next_chunk(t + 1);
                     scb = entry_scale(t + 1);
+                    corb = entry_cor(t + 1);
                     exb = chunk_exp();
                     load(rb2, t + 1);
                 }
-                store(ra, t, sca, exa);
+                store(ra, t, sca, exa, cora);
 #pragma unroll
                 for (int i = 0; i < kGaRows; ++i) ra[i] = rb2[i];
                 sca = scb;
+                cora = corb;
                 exa = exb;
+            }
+        } else if (QM == 2) {
+            // the _full operator: codes of tile t -> slot 0 (fp16, first product), its bf16 values -> slot 1
+            // (second product).  One tile of each, so tile t is written after the second product of t - 1;
+            // the codes and the first half of the value rows are loaded before that wait, the second half
+            // after the codes are stored (registers: 22 + 22 sixteen-byte chunks at most).
+            const __nv_bfloat16* vals = static_cast<const __nv_bfloat16*>(p.kv_val);
+            const int rb = warp - kSmWarps;
+            constexpr int kHalf = (kGaRows + 1) / 2;   // value rows per half (11)
+            auto load_vals = [&](uint4 (&v)[2 * kHalf], int t, int i0) {
+                const int off = (t * TT) % CHUNK;
+#pragma unroll
+                for (int i = 0; i < kHalf; ++i) {
+                    const int rr = rb + kGaWarps * (i0 + i);
+                    const int row = (i0 + i < kGaRows && rr < TT) ? s_crow[off + rr] : -1;
+                    const __nv_bfloat16* src = vals + (kv_seq + max(row, 0)) * HD;
+                    v[2 * i] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(src + lane * 8)) : make_uint4(0, 0, 0, 0);
+                    v[2 * i + 1] = row >= 0 ? __ldg(reinterpret_cast<const uint4*>(src + (lane + 32) * 8))
+                                            : make_uint4(0, 0, 0, 0);
+                }
+            };
+            auto store_vals = [&](const uint4 (&v)[2 * kHalf], int i0) {
+                uint8_t* slot = sm + C::OFF_K + KSLOT;
+#pragma unroll
+                for (int i = 0; i < kHalf; ++i) {
+                    const int rr = rb + kGaWarps * (i0 + i);
+                    if (i0 + i >= kGaRows || rr >= TT) continue;
+                    *reinterpret_cast<uint4*>(slot + (lane >> 3) * KBOX + swz(rr, lane & 7)) = v[2 * i];
+                    *reinterpret_cast<uint4*>(slot + (4 + (lane >> 3)) * KBOX + swz(rr, lane & 7)) = v[2 * i + 1];
+                }
+            };
+            if (ntiles > 0) {
+                finish_scales();
+                named_bar_sync(BAR_GATHER, kGaThreads);
+            }
+#pragma unroll 1
+            for (int t = 0; t < ntiles; ++t) {
+                if (t > 0 && (t * TT) % CHUNK == 0) next_chunk(t);
+                const float sc = entry_scale(t);
+                int4 rc[kGaRows];
+                uint4 va[2 * kHalf];
+                load_codes(rc, t);
+                load_vals(va, t, 0);
+                wait_slot(t);
+                uint8_t* box = sm + C::OFF_K + (lane >> 2) * KBOX;   // slot 0
+#pragma unroll
+                for (int i = 0; i < kGaRows; ++i) {
+                    const int rr = rb + kGaWarps * i;
+                    if (rr < TT) store_codes16(box, rr, lane, rc[i]);
+                }
+                store_vals(va, 0);
+                load_vals(va, t, kHalf);
+                store_vals(va, kHalf);
+                publish(t, sc, 0, entry_cor(t));
             }
         } else {
             const __nv_bfloat16* kv = static_cast<const __nv_bfloat16*>(p.kv);
@@ -472,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                     *reinterpret_cast<uint4*>(slot + (lane >> 3) * KBOX + swz(rr, lane & 7)) = v[2 * i];
                     *reinterpret_cast<uint4*>(slot + (4 + (lane >> 3)) * KBOX + swz(rr, lane & 7)) = v[2 * i + 1];
                 }
-                publish(t, sc, 0);
+                publish(t, sc, 0, 0.f);
             }
         }
         wait_q();   // every gather thread takes part in the query barrier once, with or without tiles
@@ -512,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                 // which keeps the issue loop at a few instructions per MMA.
                 if (choice == 1) {
                     const int slot = g1 & 1;
-                    const uint64_t dq = sdesc_sw128(qbase, 16, 1024), dk = sdesc_sw128(kbase + slot * KSLOT, 16, 1024);
+                    const uint64_t dq = sdesc_sw128(qbase, 16, 1024), dk = sdesc_sw128(kbase + k_slot(g1) * KSLOT, 16, 1024);
                     const uint32_t td = tbase + C::S_COL + slot * TT;
 #pragma unroll
                     for (int part = 0; part < (QSPLIT ? 2 : 1); ++part)
@@ -524,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                                           dk + (uint64_t)((kb * KBOX + kk * 32) >> 4), id1, (part | kb | kk) != 0);
                     umma_commit(BAR(B_SFULL + slot));
                 } else {
-                    const uint64_t dv = sdesc_sw128(kbase + (g2 & 1) * KSLOT, KBOX, 1024);
+                    const uint64_t dv = sdesc_sw128(kbase + v_slot(g2) * KSLOT, KBOX, 1024);
                     const uint64_t dp = sdesc_sw128(pbase + (g2 & 1) * C::PBYTES, 16, 1024);
                     const uint32_t acc0 = g2 > 0 ? 1u : 0u;
 #pragma unroll
@@ -564,7 +690,9 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                 }
             };
             float sq = 1.f;
-            if (KV_I8) {   // fp16 products: the group's q * 2^-qe has its largest magnitude in [2^14, 2^15)
+            if (QM) {   // query codes are final as stored (|code| <= 255): no exponent
+                if (tid == 0) s_qexp[1] = 0;
+            } else if (KV_I8) {   // fp16 products: the group's q * 2^-qe has its largest magnitude in [2^14, 2^15)
                 uint32_t mx = qmax_bits;
 #pragma unroll
                 for (int o = 1; o < QTPR; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -575,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                 sq = __int_as_float((127 - qe) << 23);
                 if (tid == 0) s_qexp[1] = qe;
             }
-            if (KV_I8 || QSPLIT) {   // a bf16 query for bf16 products is already in its final form
+            if ((KV_I8 || QSPLIT) && !QM) {   // a bf16 query for bf16 products is already in its final form
 #pragma unroll 1
                 for (int c0 = 0; c0 < QDPT / 8; c0 += 4) {
                     float vv[4][8];
@@ -615,6 +743,8 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
         float m = -INFINITY, l = 0.f;
         int eref = 0;   // value-scale exponent O is accumulated in (the largest chunk exponent so far)
+        // query-code mode: this head's u8 query scale (the score is ((dot - 128 ksum) * q_scale) * factor)
+        const float qsh = (QM && active) ? __ldg(p.q_scales + (int64_t)seq * p.nq + row0 + h) : 1.f;
         for (int t = 0; t < ntiles; ++t) {
             const int sb = t & 1;
             wait_bar(BAR(B_SFULL + sb), (t >> 1) & 1, s_abort, p.status);
@@ -647,6 +777,13 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
 #pragma unroll
                 for (int j = 0; j < TT / 4; ++j) {
                     const float4 f = f4[j], b = b4[j];
+                    if (QM) {   // the integer dot (exact in fp32) less 128 * ksum, times the query scale
+                        const float4 c = reinterpret_cast<const float4*>(s_cor + sb * TT)[j];
+                        x[4 * j] = (x[4 * j] + c.x) * qsh;
+                        x[4 * j + 1] = (x[4 * j + 1] + c.y) * qsh;
+                        x[4 * j + 2] = (x[4 * j + 2] + c.z) * qsh;
+                        x[4 * j + 3] = (x[4 * j + 3] + c.w) * qsh;
+                    }
                     x[4 * j] = fmaf(x[4 * j], f.x, b.x);
                     x[4 * j + 1] = fmaf(x[4 * j + 1], f.y, b.y);
                     x[4 * j + 2] = fmaf(x[4 * j + 2], f.z, b.z);
@@ -728,7 +865,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_decode_kernel(const Params p)
                     if (active) {
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            if (KV_I8) {
+                            if (P_F16) {
                                 const __half2 hp = __floats2half2_rn(x[8 * j + 2 * u], x[8 * j + 2 * u + 1]);
                                 w4[u] = *reinterpret_cast<const uint32_t*>(&hp);
                             } else {
@@ -888,9 +1025,9 @@ static int split_count(int64_t groups, int64_t per_seq, int nsm) {
     return (int)std::max<int64_t>(s, 1);
 }
 
-template <bool KV_I8, bool QSPLIT>
+template <bool KV_I8, bool QSPLIT, int QM = 0>
 static int launch(const Params& p, int groups, int splits, cudaStream_t st) {
-    auto kfn = csa_decode_kernel<KV_I8, QSPLIT>;
+    auto kfn = csa_decode_kernel<KV_I8, QSPLIT, QM>;
     static int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -935,6 +1072,9 @@ int csa_launch(const CsaLaunch& a) {
     p.kv = a.kv;
     p.kv_i8 = a.kv_i8;
     p.kv_scales = a.kv_scales;
+    p.q_scales = a.q_scales;
+    p.kv_sums = a.kv_sums;
+    p.kv_val = a.kv_val;
     p.idx = a.idx;
     p.k = a.k;
     p.window = a.window;
@@ -961,7 +1101,9 @@ int csa_launch(const CsaLaunch& a) {
     }
     cudaStream_t st = static_cast<cudaStream_t>(a.stream);
     int rc;
-    if (a.kv_i8)
+    if (a.q_u8)
+        rc = a.kv_val ? launch<true, false, 2>(p, groups, splits, st) : launch<true, false, 1>(p, groups, splits, st);
+    else if (a.kv_i8)
         rc = a.q_f32 ? launch<true, true>(p, groups, splits, st) : launch<true, false>(p, groups, splits, st);
     else
         rc = a.q_f32 ? launch<false, true>(p, groups, splits, st) : launch<false, false>(p, groups, splits, st);

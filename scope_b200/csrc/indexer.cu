@@ -9,7 +9,8 @@
 //                 here the lower id comes first), or in ascending id order.
 // Two launches:
 //   indexer_score_kernel  -- thread = entry, the sequence's q in shared memory,
-//                            fp32 FMA on the CUDA cores (exact fp32 products);
+//                            fp32 on the CUDA cores in the reference's own
+//                            order of operations (identical scores);
 //                            (bf16 inputs: indexer_score_tc_kernel, tcgen05);
 //   indexer_select_split_kernel -- several CTAs per sequence: a threshold placed
 //                            from a sample of the scores, candidates appended to
@@ -55,10 +56,81 @@ __global__ void __launch_bounds__(kScoreThreads) indexer_score_kernel(const void
     for (int i = threadIdx.x; i < nH; i += kScoreThreads) s_w[i] = w[(int64_t)b * nH + i];
     __syncthreads();
     if (j >= nc) return;
+    const int64_t row = ((int64_t)b * nc + j) * hd;
+    if constexpr (!BF16) {
+        // fp32: the reference's own arithmetic (csa_attn.cpp:1706-1724), so the scores and hence the ranking
+        // equal indexer_topk_cpu's bit for bit: per head 16 lane accumulators (lane l takes dims l, l+16, ...
+        // by fused multiply-add), reduced pairwise as the AVX-512 horizontal add does (8-lane halves, 4-lane
+        // halves, lanes {0+2, 1+3}, last add), then s = s + relu(dot) * w[h], multiply and add each rounded.
+        // Rows of up to kRegDims dims are held in registers; longer rows are re-read per head (L1).
+        constexpr int kRegDims = 128;
+        const float* kvr = static_cast<const float*>(kv) + row;
+        float xr[kRegDims];
+        const bool inreg = hd <= kRegDims;
+        if (inreg) {
+#pragma unroll
+            for (int c = 0; c < kRegDims / 16; ++c) {
+                if (c * 16 < hd) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(kvr + c * 16) + u);
+                        xr[c * 16 + 4 * u] = v.x; xr[c * 16 + 4 * u + 1] = v.y;
+                        xr[c * 16 + 4 * u + 2] = v.z; xr[c * 16 + 4 * u + 3] = v.w;
+                    }
+                }
+            }
+        }
+        float s = 0.f;
+        for (int h = 0; h < nH; ++h) {
+            const float* qh = s_q + h * hd;
+            float a[16];
+#pragma unroll
+            for (int l = 0; l < 16; ++l) a[l] = 0.f;
+            auto lanes = [&](const float (&x)[16], int d0) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 qq = reinterpret_cast<const float4*>(qh + d0)[u];
+                    a[4 * u] = fmaf(qq.x, x[4 * u], a[4 * u]);
+                    a[4 * u + 1] = fmaf(qq.y, x[4 * u + 1], a[4 * u + 1]);
+                    a[4 * u + 2] = fmaf(qq.z, x[4 * u + 2], a[4 * u + 2]);
+                    a[4 * u + 3] = fmaf(qq.w, x[4 * u + 3], a[4 * u + 3]);
+                }
+            };
+            if (inreg) {
+#pragma unroll
+                for (int c = 0; c < kRegDims / 16; ++c) {
+                    if (c * 16 < hd) {
+                        float x[16];
+#pragma unroll
+                        for (int l = 0; l < 16; ++l) x[l] = xr[c * 16 + l];
+                        lanes(x, c * 16);
+                    }
+                }
+            } else {
+                for (int d0 = 0; d0 < hd; d0 += 16) {
+                    float x[16];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(kvr + d0) + u);
+                        x[4 * u] = v.x; x[4 * u + 1] = v.y; x[4 * u + 2] = v.z; x[4 * u + 3] = v.w;
+                    }
+                    lanes(x, d0);
+                }
+            }
+            float t3[8], t6[4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t3[i] = __fadd_rn(a[i + 8], a[i]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t6[i] = __fadd_rn(t3[i + 4], t3[i]);
+            const float dot = __fadd_rn(__fadd_rn(t6[0], t6[2]), __fadd_rn(t6[1], t6[3]));
+            s = __fadd_rn(s, __fmul_rn(dot > 0.f ? dot : 0.f, s_w[h]));
+        }
+        scores[(int64_t)b * nc + j] = s;
+        return;
+    }
     float acc[kMaxHeads];
 #pragma unroll
     for (int h = 0; h < kMaxHeads; ++h) acc[h] = 0.f;
-    const int64_t row = ((int64_t)b * nc + j) * hd;
     for (int d0 = 0; d0 < hd; d0 += kChunk) {
         float x[kChunk];
         if (BF16) {
@@ -1004,8 +1076,14 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
                         int k, int by_id, int32_t* out_ids, float* out_scores, void* workspace,
                         size_t workspace_bytes, cudaStream_t st) {
     using namespace idx;
-    if (nH < 1 || nH > kMaxHeads) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: 1..64 heads");
-    if (hd < kChunk || hd % kChunk || hd > 256) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: hd % 16 == 0, <= 256");
+    if (nH < 1) return set_error(WS_ERR_INVALID_ARG, "indexer_topk: nH >= 1");
+    if (hd < kChunk || hd % kChunk) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: hd % 16 == 0");
+    // bf16 inputs: up to 64 heads and hd <= 256 (tensor-core tiles, per-head accumulators); fp32 inputs: any
+    // shape whose query block fits in shared memory
+    if (bf16 && (nH > kMaxHeads || hd > 256))
+        return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: bf16 inputs take 1..64 heads and hd <= 256");
+    if (((size_t)nH * hd + nH) * sizeof(float) > 220 * 1024)
+        return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: nH * hd * 4 bytes must fit in 220 KB of shared memory");
     if (k > kMaxK) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: k <= 4096");
     if (nc > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "indexer_topk: nc > 2^31 - 1");
     float* scores = out_scores;

@@ -85,6 +85,10 @@ int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_
 struct CsaLaunch {
     const void* q;
     int q_f32;
+    int q_u8;                     // q holds u8 codes with q_scales (query-code mode; kv_i8 set, q_f32 clear)
+    const float* q_scales;        // [bs * nq]
+    const int32_t* kv_sums;       // [bs, nc_local] code sums of the int8 entries
+    const void* kv_val;           // null, or bf16 values [bs, nc_local, 512] (the _full operator)
     int bs, nq;
     const void* kv;
     int kv_i8;

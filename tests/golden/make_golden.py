@@ -5,7 +5,13 @@ sources into oracle/_ref by ``make -C oracle ref REF_DIR=<reference checkout>``)
 on small seeded inputs and stores inputs + outputs as .npz.  The fixtures are
 committed; this script is only re-run when a fixture is added.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py                 # every fixture
+    python tests/golden/make_golden.py csa_int8 ...    # the named sections only
+
+Sections: base (the first seven fixtures), csa_int8, csa_bf16q, indexer_large.
+indexer_large stores the reference's ids for inputs drawn from numpy's
+``default_rng`` (platform-independent streams) rather than the inputs
+themselves; tests regenerate them from the stored seed and check a checksum.
 
 bf16 tensors are stored as their uint16 bit patterns.
 """
@@ -31,7 +37,7 @@ def save(name, **arrs):
     print("wrote", path, sum(os.path.getsize(path) for _ in [0]), "bytes")
 
 
-def main():
+def base():
     ref = oracle.load_ref("cpu_attn_ext")
     tile = oracle.load_ref("cpu_attn_tile_ext")
     csa = oracle.load_ref("csa_attn_kernel")
@@ -129,5 +135,77 @@ def main():
     save("indexer_topk", q_idx=qi, kv_idx=kvi, weights=w, k=k, ids=ids)
 
 
+def csa_int8():
+    """The reference's integer-score operators: _bsq_int8 (both quantisers
+    inside), _bsq_int8_preq and _bsq_int8_full, at hd 512 and hd 256."""
+    csa = oracle.load_ref("csa_attn_kernel")
+    g = torch.Generator().manual_seed(108)
+    arrs = {}
+    for tag, (bs, nH, sq, hd, nc) in (("h512", (2, 4, 2, 512, 96)), ("h256", (2, 3, 1, 256, 70))):
+        q = torch.randn(bs, nH, sq, hd, generator=g)
+        kv = torch.randn(bs, nc, hd, generator=g).bfloat16()
+        sc = hd ** -0.5
+        bo, bl = torch.empty(bs, nH, sq, hd), torch.empty(bs, nH, sq)
+        csa.fused_csa_attn_bsq_int8(q, kv, sc, bo, bl, 2)
+        ki8, ksc, ksm = csa.kv_quantize_bf16_to_int8(kv, 2)
+        qu8, qsc = csa.q_quantize_fp32_to_u8(q, 2)
+        po, pl = torch.empty(bs, nH, sq, hd), torch.empty(bs, nH, sq)
+        csa.fused_csa_attn_bsq_int8_preq(q, ki8, ksc, ksm, sc, po, pl, 2)
+        fo, fl = torch.empty(bs, nH, sq, hd), torch.empty(bs, nH, sq)
+        csa.fused_csa_attn_bsq_int8_full(qu8, qsc, ki8, ksc, ksm, kv, sc, fo, fl, 2)
+        arrs.update({f"{tag}_q": q, f"{tag}_kv": b(kv), f"{tag}_scale": sc, f"{tag}_bsq_o": bo, f"{tag}_bsq_lse": bl,
+                     f"{tag}_preq_o": po, f"{tag}_preq_lse": pl, f"{tag}_full_o": fo, f"{tag}_full_lse": fl})
+    save("csa_int8", **arrs)
+
+
+def csa_bf16q():
+    """The bf16-query dense variants (_pool_bf16, _bsq_bf16, _fast_bf16,
+    _2pass_bf16) on bf16 q, at hd 512 and hd 256."""
+    csa = oracle.load_ref("csa_attn_kernel")
+    g = torch.Generator().manual_seed(109)
+    arrs = {}
+    for tag, (bs, nH, sq, hd, nc) in (("h512", (2, 8, 2, 512, 96)), ("h256", (2, 4, 1, 256, 50))):
+        q = torch.randn(bs, nH, sq, hd, generator=g).bfloat16()
+        kv = torch.randn(bs, nc, hd, generator=g).bfloat16()
+        sc = hd ** -0.5
+        po, pl = csa.fused_csa_attn_pool_bf16(q, kv, sc, 2)
+        arrs.update({f"{tag}_q": b(q), f"{tag}_kv": b(kv), f"{tag}_scale": sc, f"{tag}_pool_o": po,
+                     f"{tag}_pool_lse": pl})
+        for name in ("bsq_bf16", "fast_bf16", "2pass_bf16"):
+            o, l_ = torch.empty(bs, nH, sq, hd), torch.empty(bs, nH, sq)
+            getattr(csa, "fused_csa_attn_" + name)(q, kv, sc, o, l_, 2)
+            arrs[f"{tag}_{name}_o"] = o
+            arrs[f"{tag}_{name}_lse"] = l_
+    save("csa_bf16q", **arrs)
+
+
+INDEXER_LARGE = ((1101, 2, 64, 128, 20000, 2048), (1102, 1, 16, 64, 65536, 2048))
+
+
+def indexer_large_inputs(seed, bs, nH, hd, nc):
+    """Inputs of one indexer_large case, from numpy's platform-independent generator."""
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((bs, nH, hd), dtype=np.float32)
+    kv = rng.standard_normal((bs, nc, hd), dtype=np.float32)
+    w = rng.random((bs, nH), dtype=np.float32)
+    return q, kv, w
+
+
+def indexer_large():
+    """indexer_topk_cpu at nc >= 20000, k = 2048: the reference's ids."""
+    csa = oracle.load_ref("csa_attn_kernel")
+    arrs = {}
+    for i, (seed, bs, nH, hd, nc, k) in enumerate(INDEXER_LARGE):
+        q, kv, w = indexer_large_inputs(seed, bs, nH, hd, nc)
+        ids = csa.indexer_topk_cpu(torch.from_numpy(q), torch.from_numpy(kv), torch.from_numpy(w), k, 4)
+        arrs.update({f"c{i}_shape": np.array([seed, bs, nH, hd, nc, k]), f"c{i}_ids": ids,
+                     f"c{i}_checksum": np.array([float(q.astype(np.float64).sum()), float(kv.astype(np.float64).sum()),
+                                                 float(w.astype(np.float64).sum())])})
+    save("indexer_topk_large", **arrs)
+
+
+SECTIONS = {"base": base, "csa_int8": csa_int8, "csa_bf16q": csa_bf16q, "indexer_large": indexer_large}
+
 if __name__ == "__main__":
-    main()
+    for name in (sys.argv[1:] or list(SECTIONS)):
+        SECTIONS[name]()

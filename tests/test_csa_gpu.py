@@ -1,10 +1,10 @@
 """GPU parity of the CSA kernel (ws_csa_decode) and the int8 quantisers.
 
 Against the reference's golden outputs (fused_csa_attn, fused_csa_attn_range,
-indexer_attn_cpu, kernel/cpu_attn_ds4_ext/csa_attn.cpp) and against the
-float64 oracle on seeded inputs.  Tolerances: normalised output max-abs 2e-2,
-LSE 1e-3 (exact-arithmetic comparisons); the quantisers and the gather are
-checked bit for bit.
+indexer_attn_cpu, the bf16-query variants and the integer-score int8 family,
+kernel/cpu_attn_ds4_ext/csa_attn.cpp) and against the float64 oracle on seeded
+inputs.  Tolerances: normalised output max-abs 2e-2, LSE 1e-3 everywhere; the
+quantisers and the gather are checked bit for bit.
 """
 import numpy as np
 import pytest
@@ -95,26 +95,145 @@ def test_golden_gather(csa, golden):
 
 
 def test_golden_inplace_variants(csa, golden):
+    """fp32-query in-place forms against the reference's fused_csa_attn output."""
     g = golden("csa")
     qf = torch.from_numpy(g["q"]).to(DEV)
     kv = bf16_dev(g["kv"])
     sc = float(g["scale"])
-    for fn, q in ((csa.fused_csa_attn_bsq, qf), (csa.fused_csa_attn_inplace, qf),
-                  (csa.fused_csa_attn_bsq_bf16, qf.bfloat16()), (csa.fused_csa_attn_fast_bf16, qf.bfloat16()),
-                  (csa.fused_csa_attn_2pass_bf16, qf.bfloat16())):
+    for fn in (csa.fused_csa_attn_bsq, csa.fused_csa_attn_inplace):
         o = torch.full(qf.shape, float("nan"), device=DEV)
         lse = torch.full(qf.shape[:-1], float("nan"), device=DEV)
-        fn(q, kv, sc, o, lse)
-        tol = TOL_OUT if q.dtype == torch.float32 else 3e-2
-        assert np.abs(o.cpu().numpy() - g["dense_o"]).max() < tol, fn.__name__
-        assert np.abs(lse.cpu().numpy() - g["dense_lse"]).max() < (TOL_LSE if q.dtype == torch.float32 else 2e-3)
-    o, lse = csa.fused_csa_attn_pool_bf16(qf.bfloat16(), kv, sc)
-    assert o.dtype == torch.float32
+        fn(qf, kv, sc, o, lse)
+        assert np.abs(o.cpu().numpy() - g["dense_o"]).max() < TOL_OUT, fn.__name__
+        assert np.abs(lse.cpu().numpy() - g["dense_lse"]).max() < TOL_LSE, fn.__name__
+
+
+@pytest.mark.parametrize("tag", ["h512", "h256"])
+def test_golden_bf16_query_variants(csa, golden, tag):
+    """_pool_bf16, _bsq_bf16, _fast_bf16 and _2pass_bf16 against the reference's
+    own outputs on a bf16 query (csa_attn.cpp:379-474, :580-764, :885-1048,
+    :1050-1173), at the full bar; hd 256 runs through the zero-padded path."""
+    g = golden("csa_bf16q")
+    q, kv, sc = bf16_dev(g[tag + "_q"]), bf16_dev(g[tag + "_kv"]), float(g[tag + "_scale"])
+    o, lse = csa.fused_csa_attn_pool_bf16(q, kv, sc)
+    assert o.dtype == torch.float32 and o.shape == q.shape
+    assert np.abs(o.cpu().numpy() - g[tag + "_pool_o"]).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy() - g[tag + "_pool_lse"]).max() < TOL_LSE
+    for name in ("bsq_bf16", "fast_bf16", "2pass_bf16"):
+        o = torch.full(q.shape, float("nan"), device=DEV)
+        lse = torch.full(q.shape[:-1], float("nan"), device=DEV)
+        getattr(csa, "fused_csa_attn_" + name)(q, kv, sc, o, lse)
+        assert np.abs(o.cpu().numpy() - g[f"{tag}_{name}_o"]).max() < TOL_OUT, name
+        assert np.abs(lse.cpu().numpy() - g[f"{tag}_{name}_lse"]).max() < TOL_LSE, name
+
+
+@pytest.mark.parametrize("tag", ["h512", "h256"])
+def test_golden_int8_family(csa, golden, tag):
+    """The reference's integer-score operators against its own outputs:
+    _bsq_int8 (q and kv quantised inside the call), _bsq_int8_preq and
+    _bsq_int8_full (csa_attn.cpp:766-883, :1235-1357, :1359-1483)."""
+    g = golden("csa_int8")
+    qn, kvn, sc = g[tag + "_q"], g[tag + "_kv"], float(g[tag + "_scale"])
+    q, kv = torch.from_numpy(qn).to(DEV), bf16_dev(kvn)
+    bs, nH, sq, hd = q.shape
+
+    def fresh():
+        return (torch.full(q.shape, float("nan"), device=DEV), torch.full(q.shape[:-1], float("nan"), device=DEV))
+
+    o, lse = fresh()
+    csa.fused_csa_attn_bsq_int8(q, kv, sc, o, lse)
+    res = {"bsq": (o, lse)}
+    ki8, ksc, ksm = csa.kv_quantize_bf16_to_int8(kv)
+    qu8, qsc = csa.q_quantize_fp32_to_u8(q)
+    o, lse = fresh()
+    csa.fused_csa_attn_bsq_int8_preq(q, ki8, ksc, ksm, sc, o, lse)
+    res["preq"] = (o, lse)
+    o, lse = fresh()
+    csa.fused_csa_attn_bsq_int8_full(qu8, qsc, ki8, ksc, ksm, kv, sc, o, lse)
+    res["full"] = (o, lse)
+    for name, (o, lse) in res.items():
+        assert np.abs(o.cpu().numpy() - g[f"{tag}_{name}_o"]).max() < TOL_OUT, name
+        assert np.abs(lse.cpu().numpy() - g[f"{tag}_{name}_lse"]).max() < TOL_LSE, name
+
+
+@pytest.mark.parametrize("bs,nH,sq,nc,full", [(2, 64, 1, 2000, False), (2, 64, 1, 2000, True), (3, 16, 3, 777, False),
+                                              (1, 128, 1, 4096, True), (2, 64, 1, 1, False),
+                                              (76, 64, 1, 1100, False), (76, 64, 1, 1100, True)])
+def test_int8_codes_random(csa, bs, nH, sq, nc, full):
+    """Integer-score operators on seeded inputs against the oracle's integer
+    restatement (several CTAs per sequence, ragged last tiles, several query
+    groups, one entry; 76 sequences run one CTA each over 1100 entries, so a
+    CTA crosses the 512-entry chunks its ids are resolved in)."""
+    g = torch.Generator().manual_seed(1000 + nc + nH)
+    q = torch.randn(bs, nH, sq, 512, generator=g)
+    kv = torch.randn(bs, nc, 512, generator=g).bfloat16()
+    sc = 512 ** -0.5
+    qd, kvd = q.to(DEV), kv.to(DEV)
+    ki8, ksc, ksm = csa.kv_quantize_bf16_to_int8(kvd)
+    o = torch.empty(q.shape, device=DEV)
+    lse = torch.empty(q.shape[:-1], device=DEV)
+    if full:
+        qu8, qsc = csa.q_quantize_fp32_to_u8(qd)
+        csa.fused_csa_attn_bsq_int8_full(qu8, qsc, ki8, ksc, ksm, kvd, sc, o, lse)
+    else:
+        csa.fused_csa_attn_bsq_int8_preq(qd, ki8, ksc, ksm, sc, o, lse)
+    torch.cuda.synchronize()
+    qu8n, qscn = oracle.q_quantize_u8(q.numpy().reshape(bs, nH * sq, 512))
+    ro, rl = oracle.csa_int8_codes(qu8n, qscn, ki8.cpu().numpy(), ksc.cpu().numpy(), ksm.cpu().numpy(), sc,
+                                   kv_bf16=oracle.bf16_bits(kv) if full else None)
+    assert np.abs(o.cpu().numpy().reshape(bs, -1, 512) - ro).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy().reshape(bs, -1) - rl).max() < TOL_LSE
+
+
+@pytest.mark.parametrize("full", [False, True])
+def test_int8_codes_gather_capi(full):
+    """ws_csa_decode_qcodes with a top-k id list, through the C ABI."""
+    from scope_b200 import _lib
+    bs, nq, nc, k = 2, 64, 3000, 700
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(bs, nq, 512, generator=g)
+    kv = torch.randn(bs, nc, 512, generator=g).bfloat16()
+    idx = torch.stack([torch.randperm(nc, generator=g)[:k].sort().values for _ in range(bs)]).int()
+    csa = scope_b200.build_csa_attn()
+    kvd = kv.to(DEV)
+    ki8, ksc, ksm = csa.kv_quantize_bf16_to_int8(kvd)
+    qu8, qsc = csa.q_quantize_fp32_to_u8(q.to(DEV))
+    o = torch.empty(bs, nq, 512, device=DEV)
+    lse = torch.empty(bs, nq, device=DEV)
+    L = _lib.lib()
+    ws = torch.zeros(L.ws_csa_decode_workspace_size(bs, nq, _lib.WS_DTYPE_BF16), dtype=torch.uint8, device=DEV)
+    idd = idx.to(DEV)
+    rc = L.ws_csa_decode_qcodes(qu8.data_ptr(), qsc.data_ptr(), bs, nq, 512, ki8.data_ptr(), ksc.data_ptr(),
+                                ksm.data_ptr(), kvd.data_ptr() if full else None, nc, 0, idd.data_ptr(), k,
+                                _lib.WS_CSA_IDX_ALL, 0, nc, 512 ** -0.5, o.data_ptr(), _lib.WS_DTYPE_F32,
+                                lse.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, L.ws_last_error()
+    torch.cuda.synchronize()
+    ro, rl = oracle.csa_int8_codes(qu8.cpu().numpy(), qsc.cpu().numpy(), ki8.cpu().numpy(), ksc.cpu().numpy(),
+                                   ksm.cpu().numpy(), 512 ** -0.5, kv_bf16=oracle.bf16_bits(kv) if full else None,
+                                   idx=idx.numpy())
+    assert np.abs(o.cpu().numpy() - ro).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy() - rl).max() < TOL_LSE
+
+
+def test_int8_exact_addition(csa, golden):
+    """fused_csa_attn_int8_exact (no reference counterpart): int8 * scale
+    entries with the query unquantised, against the oracle's exact arithmetic."""
+    g = golden("csa")
+    q = torch.from_numpy(g["q"]).to(DEV)
+    o = torch.empty_like(q)
+    lse = torch.empty(q.shape[:-1], device=DEV)
+    csa.fused_csa_attn_int8_exact(q, torch.from_numpy(g["kv_i8"]).to(DEV), torch.from_numpy(g["kv_scales"]).to(DEV),
+                                  float(g["scale"]), o, lse)
+    bs, nH, sq, hd = q.shape
+    ro, rl, _ = oracle.csa_attend(g["q"].reshape(bs, nH * sq, hd), g["kv_i8"], float(g["scale"]),
+                                  kv_scale=g["kv_scales"])
+    assert np.abs(o.cpu().numpy().reshape(bs, -1, hd) - ro).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy().reshape(bs, -1) - rl).max() < TOL_LSE
 
 
 def test_golden_int8(csa, golden):
-    """int8 entries: exact int8*scale arithmetic against the oracle; against the
-    reference's VNNI path (u8-quantised query) within that path's own error."""
+    """_bsq_int8_preq against the reference's own output (the first CSA fixture)."""
     g = golden("csa")
     q = torch.from_numpy(g["q"]).to(DEV)
     o = torch.empty_like(q)
@@ -122,13 +241,9 @@ def test_golden_int8(csa, golden):
     csa.fused_csa_attn_bsq_int8_preq(q, torch.from_numpy(g["kv_i8"]).to(DEV), torch.from_numpy(g["kv_scales"]).to(DEV),
                                      torch.from_numpy(g["kv_sums"]).to(DEV), float(g["scale"]), o, lse)
     bs, nH, sq, hd = q.shape
-    ro, rl, _ = oracle.csa_attend(g["q"].reshape(bs, nH * sq, hd), g["kv_i8"], float(g["scale"]),
-                                  kv_scale=g["kv_scales"])
     on, ln = o.cpu().numpy().reshape(bs, -1, hd), lse.cpu().numpy().reshape(bs, -1)
-    assert np.abs(on - ro).max() < TOL_OUT
-    assert np.abs(ln - rl).max() < TOL_LSE
     assert np.abs(on - g["int8_o"].reshape(bs, -1, hd)).max() < TOL_OUT
-    assert np.abs(ln - g["int8_lse"].reshape(bs, -1)).max() < 5e-3   # the reference quantises q to u8
+    assert np.abs(ln - g["int8_lse"].reshape(bs, -1)).max() < TOL_LSE
 
 
 def test_quantisers_bit_exact_golden(csa, golden):

@@ -2,10 +2,14 @@
 golden output (indexer_topk_cpu, kernel/cpu_attn_ds4_ext/csa_attn.cpp:1658-1736)
 and the float64 oracle.
 
-Scores are fp32 sums in a different order than the reference's AVX-512 sums,
-so the selected set is checked up to near-ties at the k-th score: every
-selected entry scores at least s_k - eps and every other entry at most
-s_k + eps (eps = 1e-5 of the score scale); exact ties are ordered by id.
+fp32 inputs are scored in the reference's own order of operations, so the
+scores equal the oracle's fp32 restatement bit for bit and the ids equal the
+reference's (test_golden_large: same sets, same order up to runs of exactly
+equal scores, which the reference's partial_sort leaves unordered).  bf16
+inputs (tensor-core scoring, no reference counterpart) are checked up to
+near-ties at the k-th score: every selected entry scores at least s_k - eps
+and every other entry at most s_k + eps (eps = 1e-5 of the score scale);
+exact ties are ordered by id.
 """
 import numpy as np
 import pytest
@@ -182,3 +186,34 @@ def test_ds4_size():
     ids = scope_b200.csa_attn.indexer_topk(q.to(DEV), kv.to(DEV), w.to(DEV), 2048)
     _, sc = oracle_scores(q, kv, w, 2048)
     check_selection(ids.cpu().numpy(), sc, 2048)
+
+
+def _large_inputs(golden, i):
+    g = golden("indexer_topk_large")
+    seed, bs, nH, hd, nc, k = (int(x) for x in g[f"c{i}_shape"])
+    rng = np.random.default_rng(seed)     # the generator tests/golden/make_golden.py drew them from
+    q = rng.standard_normal((bs, nH, hd), dtype=np.float32)
+    kv = rng.standard_normal((bs, nc, hd), dtype=np.float32)
+    w = rng.random((bs, nH), dtype=np.float32)
+    chk = np.array([q.astype(np.float64).sum(), kv.astype(np.float64).sum(), w.astype(np.float64).sum()])
+    assert np.array_equal(chk, g[f"c{i}_checksum"]), "numpy's generator no longer reproduces the fixture inputs"
+    return q, kv, w, k, g[f"c{i}_ids"]
+
+
+@pytest.mark.parametrize("i", [0, 1])
+def test_golden_large(csa, golden, i):
+    """indexer_topk_cpu at nc >= 20000, k = 2048 against the reference's own
+    ids: identical sets and identical order up to runs of exactly equal fp32
+    scores; the scores themselves equal the fp32 restatement bit for bit."""
+    q, kv, w, k, ref = _large_inputs(golden, i)
+    ids, scores = csa.indexer_topk(torch.from_numpy(q).to(DEV), torch.from_numpy(kv).to(DEV),
+                                   torch.from_numpy(w).to(DEV), k, return_scores=True)
+    ids2 = csa.indexer_topk_cpu(torch.from_numpy(q).to(DEV), torch.from_numpy(kv).to(DEV),
+                                torch.from_numpy(w).to(DEV), k)
+    torch.cuda.synchronize()
+    sc = scores.cpu().numpy()
+    want = oracle.indexer_scores_f32(q, kv, w, contract=False)
+    assert np.array_equal(sc.view(np.uint32), want.view(np.uint32)), int((sc != want).sum())
+    agree = oracle.topk_agreement(ids.cpu().numpy(), ref, want)
+    assert agree["set_diff"] == 0 and agree["order_diff"] == 0, agree
+    assert np.array_equal(ids2.cpu().numpy(), ids.cpu().numpy())

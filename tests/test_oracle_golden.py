@@ -121,6 +121,71 @@ def test_indexer_topk(golden):
         assert np.all(np.diff(scores[b][ids[b]]) <= 0)
 
 
+@pytest.mark.parametrize("tag", ["h512", "h256"])
+def test_csa_int8_family(golden, tag):
+    """_bsq_int8 (both quantisers inside the call), _int8_preq and _int8_full
+    (csa_attn.cpp:766-883, :1235-1483) against the integer-score restatement."""
+    g = golden("csa_int8")
+    q, kv, sc = g[tag + "_q"], g[tag + "_kv"], float(g[tag + "_scale"])
+    bs, nH, sq, hd = q.shape
+    ki8, ksc, ksm = oracle.kv_quantize_s8(kv)
+    qu8, qsc = oracle.q_quantize_u8(q.reshape(bs, nH * sq, hd))
+    for name, vals in (("bsq", None), ("preq", None), ("full", kv)):
+        o, lse = oracle.csa_int8_codes(qu8, qsc, ki8, ksc, ksm, sc, kv_bf16=vals)
+        assert np.abs(o - g[f"{tag}_{name}_o"].reshape(bs, -1, hd)).max() < TOL_O, name
+        assert np.abs(lse - g[f"{tag}_{name}_lse"].reshape(bs, -1)).max() < TOL_LSE, name
+
+
+@pytest.mark.parametrize("tag", ["h512", "h256"])
+def test_csa_bf16_query_variants(golden, tag):
+    """_pool_bf16, _bsq_bf16, _fast_bf16 and _2pass_bf16 (csa_attn.cpp:379-474,
+    :580-764, :885-1048, :1050-1173) on a bf16 query."""
+    g = golden("csa_bf16q")
+    q, kv, sc = g[tag + "_q"], g[tag + "_kv"], float(g[tag + "_scale"])
+    bs, nH, sq, hd = q.shape
+    o, lse, bad = oracle.csa_attend(q.reshape(bs, nH * sq, hd), kv, sc)
+    assert bad == 0
+    # _fast_bf16 takes exp from a degree-5 Taylor polynomial on a range-reduced
+    # argument (csa_attn.cpp:85-103): relative error up to (ln 2)^6 / 720 ~ 1.6e-4
+    # per weight, so its log-sum-exp may sit ~1.6e-4 off the exact one
+    tol = {"fast_bf16": (2e-3, 3e-4)}
+    for name in ("pool", "bsq_bf16", "fast_bf16", "2pass_bf16"):
+        to, tl = tol.get(name, (TOL_O, TOL_LSE))
+        assert np.abs(o - g[f"{tag}_{name}_o"].reshape(bs, -1, hd)).max() < to, name
+        assert np.abs(lse - g[f"{tag}_{name}_lse"].reshape(bs, -1)).max() < tl, name
+
+
+def indexer_large_inputs(seed, bs, nH, hd, nc):
+    """The inputs tests/golden/make_golden.py drew for the large indexer fixture."""
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((bs, nH, hd), dtype=np.float32)
+    kv = rng.standard_normal((bs, nc, hd), dtype=np.float32)
+    w = rng.random((bs, nH), dtype=np.float32)
+    return q, kv, w
+
+
+def indexer_large_case(golden, i):
+    """Regenerate case i of the large indexer fixture; returns (q, kv, w, k, ref_ids)."""
+    g = golden("indexer_topk_large")
+    seed, bs, nH, hd, nc, k = (int(x) for x in g[f"c{i}_shape"])
+    q, kv, w = indexer_large_inputs(seed, bs, nH, hd, nc)
+    chk = np.array([q.astype(np.float64).sum(), kv.astype(np.float64).sum(), w.astype(np.float64).sum()])
+    assert np.array_equal(chk, g[f"c{i}_checksum"]), "numpy's generator no longer reproduces the fixture inputs"
+    return q, kv, w, k, g[f"c{i}_ids"]
+
+
+@pytest.mark.parametrize("i", [0, 1])
+def test_indexer_topk_large_fp32_order(golden, i):
+    """The reference's ranking at nc >= 20000, k = 2048 is the one its fp32
+    scores give (16 FMA lanes, the AVX-512 reduction tree, unfused multiply
+    then add): same id sets, same order up to runs of exactly equal scores."""
+    q, kv, w, k, ref = indexer_large_case(golden, i)
+    sc = oracle.indexer_scores_f32(q, kv, w, contract=False)
+    ids = oracle.topk_from_scores(sc, k)
+    agree = oracle.topk_agreement(ids, ref, sc)
+    assert agree["set_diff"] == 0 and agree["order_diff"] == 0, agree
+
+
 def test_lse_merge_matches_unsplit():
     rng = np.random.default_rng(0)
     B, G, D, L = 3, 4, 64, 257
