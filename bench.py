@@ -69,17 +69,28 @@ def tensor_roofline(wl, t_kernel):
             "flops_per_launch": wl.kernel_flops()}
 
 
-def profile_traffic(name):
-    """dram read+write bytes per launch recorded from an ncu capture
-    (profiles/<name>.txt holds a 'traffic_bytes_per_launch: N' line)."""
+def profile_traffic(name, kernel_bytes):
+    """dram read+write bytes per launch from an ncu capture of the N=1
+    workload (profiles/<name>.txt: 'traffic_bytes_per_launch: T' and, when the
+    capture's launch moved other algorithmic bytes than this one, e.g. one
+    rank's 1/N shard, 'traffic_algorithmic_bytes: A'), scaled to this launch
+    by its algorithmic bytes: T * kernel_bytes / A.  Returns (bytes, note)."""
     path = os.path.join(ROOT, "profiles", name + ".txt")
+    t = a = None
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1])
+                t = float(line.split(":", 1)[1])
+            elif line.startswith("traffic_algorithmic_bytes:"):
+                a = float(line.split(":", 1)[1])
     except OSError:
         pass
-    return None
+    if t is None:
+        return None, None
+    if a is None or abs(a - kernel_bytes) <= 1e-6 * a:
+        return t, f"profiles/{name}.txt"
+    return t * kernel_bytes / a, (f"profiles/{name}.txt ({t:.0f} B for {a:.0f} algorithmic B), scaled to this "
+                                  f"launch's {kernel_bytes} algorithmic B")
 
 
 class ClockSampler:
@@ -307,6 +318,56 @@ class GqaDense(Workload):
     def e2e_bytes(self):
         return (self.world * self.q.numel() * 2 + 2 * self.knew_host.numel() * 2,
                 self.out.numel() * 2 + self.lse.numel() * 4)
+
+    def parity_check(self, seed):
+        """N > 1, before timing: one step on input copy 0, then rank 0 rebuilds
+        whole rows from every rank's shard (each shard is drawn from the
+        generator seeded seed + rank, so rank 0 can draw any of them again)
+        and compares the merged output of those rows with a single-GPU
+        ws_gqa_decode over the whole row.  Every rank takes the same
+        collective steps; only rank 0 computes the check."""
+        if self.world == 1:
+            return None
+        self.step(0)
+        torch.cuda.synchronize()
+        res = None
+        if self.rank == 0:
+            dev = self.q.device
+            rows = self.B * self.Hkv
+            sel = torch.tensor([0, rows // 2 + 1, rows - 1], device=dev)
+            ks, vs = [], []
+            for r in range(self.world):
+                g = torch.Generator(device=dev).manual_seed(seed + r)
+                kr = [bf16_randn((rows, self.Lloc, self.D), g, dev) for _ in range(self.copies)][0][sel]
+                vr = [bf16_randn((rows, self.Lloc, self.D), g, dev) for _ in range(self.copies)][0][sel]
+                ks.append(kr)
+                vs.append(vr)
+            kf, vf = torch.cat(ks, dim=1).contiguous(), torch.cat(vs, dim=1).contiguous()
+            del ks, vs
+            n = sel.numel()
+            q = self.qv[sel].contiguous()
+            out = torch.empty(n, self.G, self.D, dtype=torch.bfloat16, device=dev)
+            lse = torch.empty(n, self.G, dtype=torch.float32, device=dev)
+            ws = torch.zeros(self.lib.ws_gqa_decode_workspace_size(n, self.G, self.D, self.L), dtype=torch.uint8,
+                             device=dev)
+            rc = self.lib.ws_gqa_decode(q.data_ptr(), kf.data_ptr(), vf.data_ptr(), kf.stride(0), kf.stride(1),
+                                        vf.stride(0), vf.stride(1), n, self.G, self.D, self.D, self.L, self.scale,
+                                        self._lib.WS_DTYPE_BF16, self._lib.WS_OUT_NORM_BF16, out.data_ptr(), None,
+                                        None, lse.data_ptr(), ws.data_ptr(), ws.numel(),
+                                        torch.cuda.current_stream().cuda_stream)
+            if rc != 0:
+                raise RuntimeError(self.lib.ws_last_error().decode())
+            heads = (sel[:, None] * self.G + torch.arange(self.G, device=dev)[None, :]).reshape(-1)
+            got_o = self.out.view(-1, self.D)[heads].float()
+            got_l = self.lse.view(-1)[heads]
+            res = {"rows_checked": int(heads.numel()),
+                   "max_abs_out": float((got_o - out.view(-1, self.D).float()).abs().max()),
+                   "max_abs_lse": float((got_l - lse.view(-1)).abs().max()),
+                   "against": "one-GPU ws_gqa_decode over the whole row, rebuilt from every rank's shard"}
+            del kf, vf, ws
+            torch.cuda.empty_cache()
+        barrier(self.world)
+        return res
 
     def config(self):
         return {"workload": self.workload, "batch": self.B, "q_heads": self.H, "kv_heads": self.Hkv,
@@ -589,6 +650,51 @@ class Csa(Workload):
         # merge of the exchanged partials
         self.kernels_per_step = 2 + int(world > 1)
 
+    def parity_check(self, seed):
+        """N > 1, before timing: one step on id set 0 and KV copy 0, then rank 0
+        rebuilds the whole entry buffer from every rank's shard (drawn again
+        from the generator seeded seed + 17 * rank) and compares the merged
+        output with a single-GPU ws_csa_decode over it.  Every rank takes the
+        same collective steps; only rank 0 computes the check."""
+        if self.world == 1:
+            return None
+        from scope_b200.shard import shard_bounds
+        self.step(0)
+        torch.cuda.synchronize()
+        res = None
+        if self.rank == 0:
+            dev = self.q[0].device
+            kvs, scs = [], []
+            for r in range(self.world):
+                lo, hi = shard_bounds(self.nc, self.world, r)
+                g = torch.Generator(device=dev).manual_seed(seed + 17 * r)
+                kv = torch.empty(self.bs, hi - lo, 512, dtype=torch.int8, device=dev)
+                for b in range(self.bs):
+                    kv[b] = (torch.randn(hi - lo, 512, generator=g, device=dev) * 32).round_().clamp_(-127, 127)
+                kvs.append(kv)
+                scs.append(torch.rand(self.bs, hi - lo, generator=g, device=dev) * 0.04 + 0.01)
+            kvf, scf = torch.cat(kvs, dim=1).contiguous(), torch.cat(scs, dim=1).contiguous()
+            del kvs, scs
+            out = torch.empty(self.bs * self.nH, 512, dtype=torch.bfloat16, device=dev)
+            lse = torch.empty(self.bs * self.nH, dtype=torch.float32, device=dev)
+            ws = torch.zeros(self.lib.ws_csa_decode_workspace_size(self.bs, self.nH, self._lib.WS_DTYPE_BF16),
+                             dtype=torch.uint8, device=dev)
+            rc = self.lib.ws_csa_decode(self.q[0].data_ptr(), self._lib.WS_DTYPE_BF16, self.bs, self.nH, 512,
+                                        kvf.data_ptr(), self._lib.WS_DTYPE_I8, scf.data_ptr(), self.nc, 0,
+                                        self.idx[0].data_ptr(), self.k, self._lib.WS_CSA_IDX_ALL, 0, 0, self.scale,
+                                        out.data_ptr(), self._lib.WS_DTYPE_BF16, lse.data_ptr(), ws.data_ptr(),
+                                        ws.numel(), torch.cuda.current_stream().cuda_stream)
+            if rc != 0:
+                raise RuntimeError(self.lib.ws_last_error().decode())
+            res = {"rows_checked": self.bs * self.nH,
+                   "max_abs_out": float((self.out.float() - out.float()).abs().max()),
+                   "max_abs_lse": float((self.lse - lse).abs().max()),
+                   "against": "one-GPU ws_csa_decode over the whole entry buffer, rebuilt from every rank's shard"}
+            del kvf, scf, ws
+            torch.cuda.empty_cache()
+        barrier(self.world)
+        return res
+
     def kernel_bytes(self):
         """Per launch on this rank, averaged over the rotating id sets."""
         out_b = 2 * 512 if self.world == 1 else 4 * 512
@@ -741,16 +847,41 @@ def cfg2_geometry(B=16, seed=2):
     return lens, ratio, L0, lens - L0
 
 
+def randn_bf16_host(shape, seed):
+    """A host bf16 tensor of N(0,1) values, filled one leading-dim slice per
+    task on all host cores (each slice from its own seeded generator), so the
+    8.6 GB of cfg4's KV are drawn in seconds."""
+    import concurrent.futures as cf
+    x = torch.empty(*shape, dtype=torch.bfloat16)
+
+    def fill(i):
+        x[i].normal_(generator=torch.Generator().manual_seed(seed * 100003 + i))
+    with cf.ThreadPoolExecutor(max_workers=os.cpu_count() or 1) as ex:
+        list(ex.map(fill, range(shape[0])))
+    return x
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_ref_dense(B, Hkv, G, D, L, budget_s, max_calls, warm=1):
-    """The reference's fused_cpu_attn on all host cores over B*Hkv rows
-    (long rows are sampled at L=4096 tokens).  Returns (bytes/s, info)."""
+    """The reference's fused_cpu_attn on all host cores over the whole
+    workload: B*Hkv rows of L tokens (cfg4: 128 rows x 131072 tokens, 8.6 GB
+    of host KV, one call per step).  Returns (bytes/s, info)."""
     import oracle
     rows = B * Hkv
-    L = min(L, 4096)
     torch.manual_seed(11)
     q = torch.randn(rows, G, D).bfloat16()
-    k = torch.randn(rows, L, D).bfloat16()
-    v = torch.randn(rows, L, D).bfloat16()
+    k = randn_bf16_host((rows, L, D), 12)
+    v = randn_bf16_host((rows, L, D), 13)
     nbytes = 2 * rows * L * D * 2 + rows * G * D * 2 + rows * G * (D * 2 + 4)
     ref = load_cpu_ref()
     if ref is not None:
@@ -760,8 +891,9 @@ def cpu_ref_dense(B, Hkv, G, D, L, budget_s, max_calls, warm=1):
         kind, fn = "port", (lambda: oracle.gqa_decode(qb, kb, vb, D ** -0.5))
     t, n = median_time(fn, budget_s, max_calls, warm)
     return nbytes / t, {"kind": kind, "cores": os.cpu_count() or 1, "calls": n, "sec_per_call": t,
-                        "sample": f"fused_cpu_attn bf16, B_kv={rows}, G={G}, D={D}, L={L} "
-                                  f"({nbytes / 1e6:.1f} MB per call)"}
+                        "cpu_model": cpu_model(),
+                        "sample": f"fused_cpu_attn bf16, B_kv={rows}, G={G}, D={D}, L={L}: the whole workload "
+                                  f"per call ({nbytes / 1e6:.1f} MB)"}
 
 
 def cpu_ref_shares(B, H, Hkv, D, budget_s, max_calls, warm=1):
@@ -897,9 +1029,9 @@ def cpu_reference_for(name, args, budget_s, max_calls, warm):
 
 def make_workload(name, world, rank, args):
     if name == "cfg4":
-        return GqaDense(world, rank, "cfg4", 32, 32, 4, 128, args.kv_len or 131072, 4000)
+        return GqaDense(world, rank, "cfg4", 32, 32, 4, 128, args.kv_len or 131072, SEEDS["cfg4"])
     if name == "cfg1":
-        return GqaDense(world, rank, "cfg1", 1, 32, 4, 128, args.kv_len or 4096, 1000)
+        return GqaDense(world, rank, "cfg1", 1, 32, 4, 128, args.kv_len or 4096, SEEDS["cfg1"])
     if name == "cfg2":
         return GqaShares(world, rank)
     if name == "cfg3":
@@ -907,13 +1039,14 @@ def make_workload(name, world, rank, args):
     if name == "mla_abs":
         return MlaAbsorbed(world, rank, S=args.kv_len or 16384)
     if name == "cfg5":
-        return Csa(world, rank, nc=args.kv_len or 65536)
+        return Csa(world, rank, nc=args.kv_len or 65536, seed=SEEDS["cfg5"])
     if name == "idx":
         return Indexer(world, rank, nc=args.kv_len or 65536)
     raise ValueError(name)
 
 
 WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "idx", "mla_abs")
+SEEDS = {"cfg4": 4000, "cfg1": 1000, "cfg5": 5}
 
 
 # -------------------------------------------------------------------- main
@@ -1018,7 +1151,7 @@ def run_reference_arm(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
             "config": {"workload": workload, "sample": info["sample"]},
             "cpu_baseline": {"value": value, "unit": "TB/s", "cores": info["cores"], "kind": info["kind"],
-                             "sample": info["sample"]},
+                             "cpu_model": info.get("cpu_model", cpu_model()), "sample": info["sample"]},
             "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -1049,6 +1182,7 @@ def main():
     import scope_b200
     scope_b200.build()
     wl = make_workload(args.workload, world, rank, args)
+    parity = wl.parity_check(SEEDS[args.workload]) if hasattr(wl, "parity_check") else None
 
     t_kernel, _ = time_steps(wl, wl.kernel, args.steps, args.warmup, world)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -1060,6 +1194,7 @@ def main():
 
     hbm, peak_src = peaks()
     kb = wl.kernel_bytes()
+    traffic, traffic_src = profile_traffic(getattr(wl, "profile_name", f"gqa_decode_{wl.name}"), kb)
     achieved = kb / t_kernel / 1e9
     value = wl.step_bytes() / t_step / 1e12
     h2d, d2h = wl.e2e_bytes()
@@ -1067,6 +1202,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         bps, info = wl.cpu_reference(budget_s=10.0, max_calls=200)
         cpu = {"value": bps / 1e12, "unit": "TB/s", "cores": info["cores"], "kind": info["kind"],
+               "cpu_model": info.get("cpu_model", cpu_model()),
                "sample": info["sample"] + f"; median of {info['calls']} calls",
                "us_per_call": info["sec_per_call"] * 1e6}
     if rank == 0:
@@ -1079,11 +1215,12 @@ def main():
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "peak_source": peak_src, "kernel": wl.kernel_name,
                              "kernel_us": t_kernel * 1e6, "algorithmic_bytes_per_launch": kb,
-                             "traffic": profile_traffic(wl.profile_name if hasattr(wl, "profile_name")
-                                                        else f"gqa_decode_{wl.name}")},
+                             "traffic": traffic, "traffic_source": traffic_src},
                 "tensor": tensor_roofline(wl, t_kernel),
                 "gpu_launches": wl.kernels_per_step * n_timed,
                 "clocks": clocks, "cpu_baseline": cpu}
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

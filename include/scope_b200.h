@@ -145,12 +145,21 @@ size_t ws_gqa_decode_shares_workspace_size(int B, int Hkv, int G, int Dv, int n_
  *     [B*nH] fp32 (the reference's outputs); WS_OUT_NORM_BF16 / _F32: out normalised.
  *   out_lse [B*nH] fp32 optional (NULL).  out_max/out_sum may be NULL.
  * Two launches on the stream: the tcgen05 split-KV kernel and its merge
- * (a programmatic dependent launch).  This build supports nH == 16.
+ * (a programmatic dependent launch).  nH must be a multiple of 16: each group
+ * of 16 heads is one tensor-core tile (callers with other head counts pad
+ * q_proj / q_pe with zero rows).
  */
 int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
                   float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse,
                   void* workspace, size_t workspace_bytes, void* stream);
 size_t ws_mla_decode_workspace_size(int B, int nH, int S);
+/* The same over latent sequences c_batch_stride / pe_batch_stride elements
+ * apart (a cache [B, cap, 512] / [B, cap, 64] read for its first S tokens;
+ * strides multiples of 8 elements).  Same reference interface as above. */
+int ws_mla_decode_strided(const void* q_proj, const void* q_pe, const void* c_kv, int64_t c_batch_stride,
+                          const void* k_pe, int64_t pe_batch_stride, int B, int nH, int S, float scale, int out_mode,
+                          void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* Absorbed-MLA decode step with the projections either side of the attention:
  * the decode branch of _mla_compressed_forward (system/deepseek.py:257-265 the

@@ -68,6 +68,7 @@ SIGNATURES = {
     "ws_gqa_decode_noalloc_max_scratch": (_sz, []),
     "ws_mla_decode": (_i, [_V, _V, _V, _V, _i, _i, _i, _f, _i, _V, _V, _V, _V, _V, _sz, _V]),
     "ws_mla_decode_workspace_size": (_sz, [_i, _i, _i]),
+    "ws_mla_decode_strided": (_i, [_V, _V, _V, _i64, _V, _i64, _i, _i, _i, _f, _i, _V, _V, _V, _V, _V, _sz, _V]),
     "ws_mla_decode_absorbed": (_i, [_V, _V, _i64, _V, _V, _V, _V, _i64, _i, _i, _i, _i, _i, _f, _V, _V, _V, _sz,
                                     _V]),
     "ws_mla_decode_absorbed_workspace_size": (_sz, [_i, _i, _i]),

@@ -129,12 +129,18 @@ def fused_cpu_attn_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale
 
 
 def _run_mla(q_proj, q_pe, c_kv, k_pe, scale, out_mode, out, mx, sm, lse):
+    """One ws_mla_decode_strided launch.  c_kv / k_pe may be views of a larger
+    cache (unit stride on the feature dim, tokens contiguous, any batch
+    stride).  A head count that is not a multiple of 16 runs on zero-padded
+    query rows; the padded rows' outputs are dropped."""
     dev = _require_cuda("fused_cpu_attn_mla_compressed", q_proj, q_pe, c_kv, k_pe)
     for t in (q_proj, q_pe, c_kv, k_pe):
         if t.dtype != torch.bfloat16:
             raise RuntimeError("fused_cpu_attn_mla_compressed requires bf16 inputs")
-        if not t.is_contiguous():
-            raise RuntimeError("q_proj, q_pe, c_kv and k_pe must be contiguous")
+    if not q_proj.is_contiguous() or not q_pe.is_contiguous():
+        raise RuntimeError("q_proj and q_pe must be contiguous")
+    if c_kv.dim() != 3 or k_pe.dim() != 3:
+        raise RuntimeError("expected c_kv [B, S, 512] and k_pe [B, S, 64]")
     B, S, CLR = c_kv.shape
     if B == 0 or q_proj.shape[0] % B:
         raise RuntimeError("q_proj rows must be a multiple of the batch")
@@ -143,11 +149,36 @@ def _run_mla(q_proj, q_pe, c_kv, k_pe, scale, out_mode, out, mx, sm, lse):
         raise RuntimeError("expected q_proj [B*nH, 512], q_pe [B*nH, 64], c_kv [B, S, 512], k_pe [B, S, 64]")
     if q_pe.shape[0] != B * nH or k_pe.shape[0] != B or k_pe.shape[1] != S:
         raise RuntimeError("shape mismatch between q_proj, q_pe, c_kv, k_pe")
+    for t, w in ((c_kv, 512), (k_pe, 64)):
+        rows_ok = t.stride(2) == 1 and (S <= 1 or t.stride(1) == w)
+        if not rows_ok or (B > 1 and (t.stride(0) % 8 or t.stride(0) < S * w)):
+            raise RuntimeError("c_kv and k_pe must be contiguous per sequence (batch stride a multiple of 8)")
+    c_bs = c_kv.stride(0) if B > 1 else S * 512
+    pe_bs = k_pe.stride(0) if B > 1 else S * 64
+    nHp = -(-nH // 16) * 16
+    if nHp != nH:   # zero query rows up to a multiple of 16 heads; outputs go through padded buffers
+        qp = torch.zeros(B, nHp, 512, dtype=q_proj.dtype, device=dev)
+        qp[:, :nH] = q_proj.view(B, nH, 512)
+        qe = torch.zeros(B, nHp, 64, dtype=q_pe.dtype, device=dev)
+        qe[:, :nH] = q_pe.view(B, nH, 64)
+
+        def wide(t, tail):
+            return None if t is None else torch.empty(B, nHp, *tail, dtype=t.dtype, device=dev)
+        wo, wm, ws_, wl = wide(out, (512,)), wide(mx, ()), wide(sm, ()), wide(lse, ())
+        _run_mla(qp.view(B * nHp, 512), qe.view(B * nHp, 64), c_kv, k_pe, scale, out_mode,
+                 wo.view(B * nHp, 512), None if wm is None else wm.view(-1), None if ws_ is None else ws_.view(-1),
+                 None if wl is None else wl.view(-1))
+        out.view(B, nH, 512).copy_(wo[:, :nH])
+        for dst, src in ((mx, wm), (sm, ws_), (lse, wl)):
+            if dst is not None:
+                dst.view(B, nH).copy_(src[:, :nH])
+        return
     L_ = lib()
     with torch.cuda.device(dev):
         ws = workspaces.get(L_.ws_mla_decode_workspace_size(B, nH, S), dev)
-        rc = L_.ws_mla_decode(ptr(q_proj), ptr(q_pe), ptr(c_kv), ptr(k_pe), B, nH, S, float(scale), out_mode,
-                              ptr(out), ptr(mx), ptr(sm), ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
+        rc = L_.ws_mla_decode_strided(ptr(q_proj), ptr(q_pe), ptr(c_kv), c_bs, ptr(k_pe), pe_bs, B, nH, S,
+                                      float(scale), out_mode, ptr(out), ptr(mx), ptr(sm), ptr(lse), ptr(ws),
+                                      ws.numel(), stream_ptr(dev))
     check(rc, "ws_mla_decode")
 
 
@@ -169,13 +200,23 @@ def fused_cpu_attn_mla_compressed(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv
     return out, mx, sm
 
 
-def mla_decode(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_pe: torch.Tensor, scale: float):
-    """Absorbed MLA decode returning (out bf16 [B*nH, 512] normalised, lse fp32 [B*nH])."""
+def mla_decode(q_proj: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_pe: torch.Tensor, scale: float,
+               out_dtype=torch.bfloat16, out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+    """Absorbed MLA decode returning (out [B*nH, 512] normalised in out_dtype
+    (bf16, or fp32: the partial a sharded cache exchanges), lse fp32 [B*nH]).
+    ``out`` / ``lse`` may be given (contiguous, of those shapes) to be written
+    in place."""
     R = q_proj.shape[0]
     dev = c_kv.device
-    out = torch.empty(R, 512, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(R, dtype=torch.float32, device=dev)
-    _run_mla(q_proj, q_pe, c_kv, k_pe, scale, _lib.WS_OUT_NORM_BF16, out, None, None, lse)
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("mla_decode: out_dtype must be bf16 or fp32")
+    out = torch.empty(R, 512, dtype=out_dtype, device=dev) if out is None else out
+    lse = torch.empty(R, dtype=torch.float32, device=dev) if lse is None else lse
+    if out.dtype != out_dtype or out.numel() != R * 512 or not out.is_contiguous() or lse.numel() != R \
+            or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise RuntimeError("mla_decode: out / lse must be contiguous [B*nH, 512] out_dtype and [B*nH] fp32")
+    mode = _lib.WS_OUT_NORM_BF16 if out_dtype == torch.bfloat16 else _lib.WS_OUT_NORM_F32
+    _run_mla(q_proj, q_pe, c_kv, k_pe, scale, mode, out, None, None, lse)
     return out, lse
 
 
@@ -220,21 +261,26 @@ def mla_decode_absorbed(q_nope: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Te
     return (out, lse) if return_lse else out
 
 
-def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, out_dtype=torch.bfloat16):
+def gqa_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, out_dtype=torch.bfloat16,
+               out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
     """GQA decode returning (out [B_kv, G, Dv] normalised in out_dtype (bf16 or fp32),
     lse fp32 [B_kv, G]).
 
     The fp32 log-sum-exp (max + log sum) is what the LSE merges consume; the
     reference's bf16 fused_cpu_attn rounds max and sum to bf16 (~1e-2 LSE error).
-    An fp32 out is the partial a sharded cache exchanges.
+    An fp32 out is the partial a sharded cache exchanges.  ``out`` / ``lse``
+    may be given (contiguous, of those shapes) to be written in place.
     """
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise RuntimeError("gqa_decode requires bf16 inputs")
     if out_dtype not in (torch.bfloat16, torch.float32):
         raise RuntimeError("gqa_decode: out_dtype must be bf16 or fp32")
     dev, B, G, Dk, L, Dv = _gqa_common("gqa_decode", q, k, v)
-    out = torch.empty(B, G, Dv, dtype=out_dtype, device=dev)
-    lse = torch.empty(B, G, dtype=torch.float32, device=dev)
+    out = torch.empty(B, G, Dv, dtype=out_dtype, device=dev) if out is None else out
+    lse = torch.empty(B, G, dtype=torch.float32, device=dev) if lse is None else lse
+    if out.dtype != out_dtype or out.numel() != B * G * Dv or not out.is_contiguous() or lse.numel() != B * G \
+            or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise RuntimeError("gqa_decode: out / lse must be contiguous [B_kv, G, Dv] out_dtype and [B_kv, G] fp32")
     mode = _lib.WS_OUT_NORM_BF16 if out_dtype == torch.bfloat16 else _lib.WS_OUT_NORM_F32
     _run_gqa(q, k, v, scale, _lib.WS_DTYPE_BF16, mode, out, None, None, lse)
     return out, lse

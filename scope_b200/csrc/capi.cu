@@ -243,6 +243,20 @@ int ws_mla_decode(const void* q_proj, const void* q_pe, const void* c_kv, const 
                       /*kv_after_primary=*/true);
 }
 
+int ws_mla_decode_strided(const void* q_proj, const void* q_pe, const void* c_kv, int64_t c_batch_stride,
+                          const void* k_pe, int64_t pe_batch_stride, int B, int nH, int S, float scale, int out_mode,
+                          void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    if (B < 0 || nH < 1 || S < 0) return set_error(WS_ERR_INVALID_ARG, "mla_decode: bad shape");
+    if (B == 0) return WS_OK;
+    if (!q_proj || !q_pe || !out || (S > 0 && (!c_kv || !k_pe))) return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    if (out_mode < WS_OUT_NORM_BF16 || out_mode > WS_OUT_NORM_F32) return set_error(WS_ERR_INVALID_ARG, "bad out_mode");
+    if (c_batch_stride < 0 || pe_batch_stride < 0) return set_error(WS_ERR_INVALID_ARG, "mla_decode: negative stride");
+    return mla_launch(q_proj, q_pe, c_kv, k_pe, B, nH, S, scale, out_mode, out, out_max, out_sum, out_lse, workspace,
+                      workspace_bytes, static_cast<cudaStream_t>(stream), /*after_primary=*/true,
+                      /*kv_after_primary=*/true, c_batch_stride, pe_batch_stride);
+}
+
 size_t ws_mla_decode_absorbed_workspace_size(int B, int nH, int S) { return mla_absorbed_workspace_bytes(B, nH, S); }
 
 int ws_mla_decode_absorbed(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,

@@ -83,7 +83,8 @@ struct Maps {
 };
 
 struct Params {
-    int B, S, tpb;          // batches, tokens, tiles per batch
+    int B, S, tpb;          // query sequences (head groups of NH heads), tokens, tiles per sequence
+    int hg;                 // head groups per latent sequence: query sequence b reads latent row b / hg
     float scale_log2;       // softmax scale * log2(e)
     int c_tok_in_dim2, pe_tok_in_dim2;   // tensor-map axis order (see make_kv_map)
     float* ws_part;         // pieces, slot = cta + batch
@@ -165,13 +166,14 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
     auto issue_tile = [&]() -> bool {
         const int64_t i = pi;
         const bool new_seg = pb != seg;   // this tile starts a sequence: its q follows the tile's latent
+        const int lb = pb / p.hg;         // the latent sequence this query sequence's heads read
         for (int pr = 0; pr < 4; ++pr) {
             const int64_t n = 4 * i + pr;
             const int sl = (int)(n % NP);
             const uint32_t u = (uint32_t)(n / NP);
             if (u > 0 && !wait_bar(s, bar(s, B_PAIR_EMPTY + sl), (u - 1) & 1, p.status)) return false;
             mbar_arrive_expect_tx(bar(s, B_PAIR_FULL + sl), PAIR_BYTES);
-            const int c1 = p.c_tok_in_dim2 ? pb : ptl * TT, c2 = p.c_tok_in_dim2 ? ptl * TT : pb;
+            const int c1 = p.c_tok_in_dim2 ? lb : ptl * TT, c2 = p.c_tok_in_dim2 ? ptl * TT : lb;
             tma_load_3d(pairs + sl * PAIR_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr, c1, c2);
             tma_load_3d(pairs + sl * PAIR_BYTES + BOX_BYTES, &maps.c, bar(s, B_PAIR_FULL + sl), 128 * pr + 64,
                         c1, c2);
@@ -192,8 +194,8 @@ mla_decode_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Par
         const uint32_t ue = (uint32_t)(i / NE);
         if (ue > 0 && !wait_bar(s, bar(s, B_PE_EMPTY + e), (ue - 1) & 1, p.status)) return false;
         mbar_arrive_expect_tx(bar(s, B_PE_FULL + e), BOX_BYTES);
-        tma_load_3d(pes + e * BOX_BYTES, &maps.pe, bar(s, B_PE_FULL + e), 0, p.pe_tok_in_dim2 ? pb : ptl * TT,
-                    p.pe_tok_in_dim2 ? ptl * TT : pb);
+        tma_load_3d(pes + e * BOX_BYTES, &maps.pe, bar(s, B_PE_FULL + e), 0, p.pe_tok_in_dim2 ? lb : ptl * TT,
+                    p.pe_tok_in_dim2 ? ptl * TT : lb);
         if (++ptl == p.tpb) {
             ptl = 0;
             ++pb;
@@ -715,16 +717,27 @@ __global__ void __launch_bounds__(128) mla_absorb_kernel(const __nv_bfloat16* __
 size_t mla_workspace_bytes(int B, int nH, int S) {
     (void)S;
     const int nsm = device_sm_count();
-    return kCounterHeaderBytes + size_t(nsm + B) * mla::SLOT_FLOATS * 4 + (nH > 0 ? 0 : 0);
+    const int hg = std::max(1, (nH + mla::NH - 1) / mla::NH);   // query sequences per latent sequence
+    return kCounterHeaderBytes + size_t(nsm + (size_t)B * hg) * mla::SLOT_FLOATS * 4;
 }
 
 int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
                float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
-               size_t workspace_bytes, cudaStream_t st, bool after_primary, bool kv_after_primary) {
+               size_t workspace_bytes, cudaStream_t st, bool after_primary, bool kv_after_primary,
+               int64_t c_bstride, int64_t pe_bstride) {
     using namespace mla;
-    if (nH != NH) return set_error(WS_ERR_UNSUPPORTED, "mla_decode: this build supports 16 heads per sequence");
+    // nH = hg * 16 heads per sequence run as hg query sequences of 16 heads that read the same latent
+    // sequence (query rows b*nH + h are already laid out that way: query sequence b*hg + h/16)
+    if (nH < NH || nH % NH) return set_error(WS_ERR_UNSUPPORTED, "mla_decode: heads per sequence must be a multiple of 16");
     if (B < 0 || S < 0) return set_error(WS_ERR_INVALID_ARG, "mla_decode: bad shape");
     if (B == 0) return WS_OK;
+    const int hg = nH / NH;
+    if (c_bstride < 0) c_bstride = (int64_t)S * CLR;
+    if (pe_bstride < 0) pe_bstride = (int64_t)S * QRD;
+    if (c_bstride < (int64_t)S * CLR || pe_bstride < (int64_t)S * QRD || c_bstride % 8 || pe_bstride % 8)
+        return set_error(WS_ERR_INVALID_ARG, "mla_decode: batch strides must cover S tokens and be 16-byte multiples");
+    const int BL = B;   // latent sequences
+    B *= hg;            // query sequences from here on
     const int tpb = (S + TT - 1) / TT;
     const int64_t total = (int64_t)B * tpb;
     const int nsm = device_sm_count();
@@ -737,8 +750,8 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
         Maps maps;
         memset(&maps, 0, sizeof(maps));
         int fc = 0, fpe = 0, fq = 0, rc;
-        if ((rc = make_kv_map(&maps.c, c_kv, CLR, (int64_t)S * CLR, CLR, S, B, TT, &fc)) != WS_OK) return rc;
-        if ((rc = make_kv_map(&maps.pe, k_pe, QRD, (int64_t)S * QRD, QRD, S, B, TT, &fpe)) != WS_OK) return rc;
+        if ((rc = make_kv_map(&maps.c, c_kv, CLR, c_bstride, CLR, S, BL, TT, &fc)) != WS_OK) return rc;
+        if ((rc = make_kv_map(&maps.pe, k_pe, QRD, pe_bstride, QRD, S, BL, TT, &fpe)) != WS_OK) return rc;
         if ((rc = make_kv_map(&maps.q, q_proj, CLR, (int64_t)B * NH * CLR, CLR, (int64_t)B * NH, 1, NH, &fq)) != WS_OK)
             return rc;
         if (fq) return set_error(WS_ERR_INVALID_ARG, "mla_decode: unexpected query layout");
@@ -749,6 +762,7 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
         prm.c_tok_in_dim2 = fc;
         prm.pe_tok_in_dim2 = fpe;
         prm.B = B;
+        prm.hg = hg;
         prm.S = S;
         prm.tpb = tpb;
         prm.scale_log2 = scale * kLog2e;

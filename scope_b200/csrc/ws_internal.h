@@ -72,10 +72,12 @@ size_t mla_workspace_bytes(int B, int nH, int S);
 // after_primary: the decode grid is a programmatic dependent of the previous launch on the stream (its
 // setup overlaps that grid; its producer waits for it before loading q, and with kv_after_primary before
 // the first latent load too, for a previous grid that may append to the cache)
+// nH: a multiple of 16 (groups of 16 heads share one latent read); c_bstride / pe_bstride: elements between
+// latent sequences (-1: contiguous [B, S, *])
 int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const void* k_pe, int B, int nH, int S,
                float scale, int out_mode, void* out, float* out_max, float* out_sum, float* out_lse, void* workspace,
                size_t workspace_bytes, cudaStream_t st, bool after_primary = false,
-               bool kv_after_primary = false);
+               bool kv_after_primary = false, int64_t c_bstride = -1, int64_t pe_bstride = -1);
 size_t mla_absorbed_workspace_bytes(int B, int nH, int S);
 int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
                         const void* c_kv, const void* k_pe, const void* w_uv, int64_t w_uv_head_stride, int B, int nH,

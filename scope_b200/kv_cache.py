@@ -116,9 +116,9 @@ class ShardedKVCache:
             return out.reshape(B, H, D), lse.reshape(B, H)
         if exchange is None:
             raise RuntimeError("decode: a PartialExchange is required when world > 1")
-        o, l = gqa_decode(qv, k, v, scale, out_dtype=torch.float32)
-        exchange.part_o.copy_(o.reshape(B * H, D))
-        exchange.part_l.copy_(l.reshape(B * H))
+        # the kernel writes this rank's partial straight into the exchange block
+        gqa_decode(qv, k, v, scale, out_dtype=torch.float32, out=exchange.part_o.view(self._bkv, H // self._kv_h, D),
+                   lse=exchange.part_l.view(self._bkv, H // self._kv_h))
         out, lse = exchange.step(torch.bfloat16)
         return out.reshape(B, H, D), lse.reshape(B, H)
 
@@ -170,3 +170,19 @@ class ShardedKVCacheCompressed:
     def reset(self):
         for i in range(self._nl):
             self._filled[i] = 0
+
+    def decode(self, li, q_proj, q_pe, scale, exchange=None):
+        """Absorbed-MLA decode over all tokens of the layer: q_proj [B*nH, 512],
+        q_pe [B*nH, 64] -> (out [B*nH, 512] bf16 normalised, lse [B*nH] fp32).
+        With world > 1 pass the rank's PartialExchange(B*nH, 512, world): the
+        kernel writes this rank's fp32 partial into its block, then one
+        exchange merges the shards (a rank holding no token of the layer
+        contributes lse = -inf)."""
+        from .cpu_attn import mla_decode
+        c, pe = self.get(li)   # views of the [B, cap, *] buffers: the kernel reads them in place by batch stride
+        if self.world == 1:
+            return mla_decode(q_proj, q_pe, c, pe, scale)
+        if exchange is None:
+            raise RuntimeError("decode: a PartialExchange is required when world > 1")
+        mla_decode(q_proj, q_pe, c, pe, scale, out_dtype=torch.float32, out=exchange.part_o, lse=exchange.part_l)
+        return exchange.step(torch.bfloat16)

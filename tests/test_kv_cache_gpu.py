@@ -106,3 +106,26 @@ def test_mla_compressed_cache(world):
     ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, C, P)), scale)
     assert np.abs(out.cpu().numpy() - ro / rs[:, None]).max() < 2e-2
     assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < 1e-3
+
+
+def test_mla_compressed_cache_decode():
+    """ShardedKVCacheCompressed.decode at world 1: the cache buffers ([B, cap, *],
+    cap > filled tokens) are read in place."""
+    g = torch.Generator().manual_seed(29)
+    B, nH, total = 2, 16, 700
+    ca = ShardedKVCacheCompressed(1, B, 1024, 512, 64, device=DEV)
+    cs, ps = [], []
+    for n in steps_of(total, 300):
+        c = torch.randn(B, n, 512, generator=g).bfloat16()
+        p = torch.randn(B, n, 64, generator=g).bfloat16()
+        ca.append(0, c.to(DEV), p.to(DEV))
+        cs.append(c)
+        ps.append(p)
+    C, P = torch.cat(cs, 1), torch.cat(ps, 1)
+    qp = torch.randn(B * nH, 512, generator=g).bfloat16()
+    qpe = torch.randn(B * nH, 64, generator=g).bfloat16()
+    out, lse = ca.decode(0, qp.to(DEV), qpe.to(DEV), 192 ** -0.5)
+    torch.cuda.synchronize()
+    ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, C, P)), 192 ** -0.5)
+    assert np.abs(out.float().cpu().numpy() - ro / rs[:, None]).max() < 2e-2
+    assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < 1e-3

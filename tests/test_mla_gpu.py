@@ -174,3 +174,29 @@ def test_decode_steps_after_appends_without_host_sync():
         ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, c[:, :S], p[:, :S])), scale)
         assert np.abs(out.float().cpu().numpy() - ro / rs[:, None]).max() < TOL_OUT, s
         assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < TOL_LSE, s
+
+
+@pytest.mark.parametrize("nH,B,S", [(32, 3, 700), (128, 2, 1500), (8, 4, 300), (20, 2, 257)])
+def test_head_counts(ext, nH, B, S):
+    """Any heads per sequence (the reference takes nH = q_proj.size(0) / B,
+    kernel/cpu_attn.cpp:858-862): multiples of 16 run as head groups that
+    share the latent, other counts on zero-padded query rows."""
+    check_against_oracle(ext, *rand_inputs(B, S, nH=nH, seed=nH + S), 192 ** -0.5)
+
+
+def test_strided_latent_views(ext):
+    """c_kv / k_pe as views of a larger cache ([B, cap, *] read for S tokens)
+    are read in place through the batch stride."""
+    from scope_b200.cpu_attn import mla_decode
+    B, nH, S, cap = 3, 16, 900, 1280
+    qp, qpe, c, p = rand_inputs(B, S, nH=nH, seed=5)
+    cbuf = torch.zeros(B, cap, 512, dtype=torch.bfloat16, device=DEV)
+    pbuf = torch.zeros(B, cap, 64, dtype=torch.bfloat16, device=DEV)
+    cbuf[:, :S] = c.to(DEV)
+    pbuf[:, :S] = p.to(DEV)
+    cbuf[:, S:] = 30.0   # garbage past the filled tokens must not be read
+    out, lse = mla_decode(qp.to(DEV), qpe.to(DEV), cbuf[:, :S], pbuf[:, :S], 192 ** -0.5)
+    torch.cuda.synchronize()
+    ro, rm, rs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, c, p)), 192 ** -0.5)
+    assert np.abs(out.float().cpu().numpy() - ro / rs[:, None]).max() < TOL_OUT
+    assert np.abs(lse.cpu().numpy() - (rm + np.log(rs))).max() < TOL_LSE
