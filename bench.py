@@ -772,7 +772,7 @@ class Csa(Workload):
 
 
 class Indexer(Workload):
-    """idx: the CSA indexer top-k that produces cfg5's ids (SURVEY "next" row):
+    """idx: the CSA indexer top-k that produces cfg5's ids (the step before the CSA decode):
     bs=16 sequences, 64 index heads x 128 dims over nc=65536 compressed entries,
     bf16 q/kv (the dtype the DeepSeek-V4 runtime passes, system/ds4offload.py:95-125),
     fp32 weights, top-2048 by descending score (ws_indexer_topk: scoring kernel +

@@ -25,6 +25,7 @@
 //   * the merge counters are cleared with cudaMemsetAsync on the caller's
 //     stream before each launch; the partials need no clearing.
 // Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
+#include <atomic>
 #include <cstdio>
 
 #include "common.cuh"
@@ -36,17 +37,20 @@ constexpr size_t kScratchBytes = size_t(4) << 20;   // 4 MiB per device
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kScratchBytes];
 
-// Device address of g_noalloc_scratch for the current device (nullptr on failure).
+// Device address of g_noalloc_scratch for the current device (nullptr on failure), looked up on the first
+// call per device and kept in an atomic slot, so calls from several host threads read it safely (two threads
+// racing on the first call both store the same address).  A cudaDeviceReset() discards the module and with
+// it this address: a process that resets a device must not call this entry point on it afterwards.
 static void* scratch_address() {
-    static void* cache[64];
+    static std::atomic<void*> cache[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!cache[dev]) {
-        void* ptr = nullptr;
+    void* ptr = cache[dev].load(std::memory_order_acquire);
+    if (!ptr) {
         if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess) return nullptr;
-        cache[dev] = ptr;
+        cache[dev].store(ptr, std::memory_order_release);
     }
-    return cache[dev];
+    return ptr;
 }
 
 }  // namespace ws

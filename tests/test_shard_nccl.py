@@ -11,7 +11,6 @@ otherwise.
 """
 import datetime
 import multiprocessing as mp
-import os
 import socket
 
 import numpy as np
