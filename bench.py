@@ -227,9 +227,10 @@ class GqaDense(Workload):
 
     kernel_name = "gqa_decode_kernel<128,128,1,4>"
 
-    def __init__(self, world, rank, name, B, H, Hkv, D, L, seed):
+    def __init__(self, world, rank, name, B, H, Hkv, D, L, seed, exchange="peer"):
         from scope_b200 import _lib
         self.name = name
+        self.exchange = exchange if world > 1 else "none"
         self.world, self.rank = world, rank
         self.B, self.H, self.Hkv, self.D, self.L = B, H, Hkv, D, L
         self.G = H // Hkv
@@ -253,9 +254,12 @@ class GqaDense(Workload):
             self.out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(B, H, dtype=torch.float32, device=dev)
         else:
-            from scope_b200.shard import PartialExchange
-            self.ex = PartialExchange(B * H, D, world, dev)
-            self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
+            from scope_b200.shard import PartialExchange, PeerExchange
+            if self.exchange == "peer":
+                self.ex = PeerExchange(B * H, D, world, rank, dev)
+            else:
+                self.ex = PartialExchange(B * H, D, world, dev)
+                self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
             self.out = torch.empty(B * H, D, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(B * H, dtype=torch.float32, device=dev)
         nbytes = self.lib.ws_gqa_decode_workspace_size(rows, self.G, D, self.Lloc)
@@ -289,20 +293,28 @@ class GqaDense(Workload):
         st = torch.cuda.current_stream().cuda_stream
         rows = self.B * self.Hkv
         if self.world == 1:
-            out, lse, mode = self.out, self.lse, self._lib.WS_OUT_NORM_BF16
+            out, lse, mode = self.out.data_ptr(), self.lse.data_ptr(), self._lib.WS_OUT_NORM_BF16
+        elif self.exchange == "peer":   # this rank's partial goes straight into rank 0's slot (NVLink stores)
+            (out, lse), mode = self.ex.slot(), self._lib.WS_OUT_NORM_F32
         else:
-            out, lse, mode = self.part_o, self.part_l, self._lib.WS_OUT_NORM_F32
+            out, lse, mode = self.part_o.data_ptr(), self.part_l.data_ptr(), self._lib.WS_OUT_NORM_F32
         rc = L_.ws_gqa_decode(self.qv.data_ptr(), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
                               v.stride(0), v.stride(1), rows, self.G, self.D, self.D, self.Lloc, self.scale,
-                              self._lib.WS_DTYPE_BF16, mode, out.data_ptr(), None, None, lse.data_ptr(),
+                              self._lib.WS_DTYPE_BF16, mode, out, None, None, lse,
                               self.ws.data_ptr(), self.ws.numel(), st)
         if rc != 0:
             raise RuntimeError(L_.ws_last_error().decode())
 
     def step(self, i):
         self.kernel(i)
-        if self.world > 1:
+        if self.exchange == "peer":
+            self.ex.step(out=self.out if self.rank == 0 else None, out_lse=self.lse if self.rank == 0 else None)
+        elif self.world > 1:
             self.ex.step(torch.bfloat16, out=self.out, out_lse=self.lse)
+
+    def close(self):
+        if self.exchange == "peer":
+            self.ex.close()
 
     def e2e_step(self, i):
         c = i % self.copies
@@ -376,7 +388,10 @@ class GqaDense(Workload):
                 "l2": (f"inputs {2 * self.B * self.Hkv * self.Lloc * self.D * 2 / 1e9:.2f} GB per GPU > L2"
                        if self.copies == 1 else f"{self.copies} rotating input copies > 3x L2"),
                 "timing": "cuda-graph replay" if self.graph else "stream launches",
-                "exchange": "nccl all_gather of (o fp32, lse) + lse_merge kernel" if self.world > 1 else "none"}
+                "exchange": {"peer": "partials stored by the decode into rank 0's IPC-mapped slots over NVLink, a "
+                                     "release flag per rank, rank 0's merge kernel after a bounded acquire wait",
+                             "nccl": "nccl all_gather of (o fp32, lse) + lse_merge kernel on every rank",
+                             "none": "none"}[self.exchange]}
 
     def cpu_reference(self, budget_s, max_calls, warm=1):
         return cpu_ref_dense(self.B, self.Hkv, self.G, self.D, self.L, budget_s, max_calls, warm)
@@ -1029,7 +1044,8 @@ def cpu_reference_for(name, args, budget_s, max_calls, warm):
 
 def make_workload(name, world, rank, args):
     if name == "cfg4":
-        return GqaDense(world, rank, "cfg4", 32, 32, 4, 128, args.kv_len or 131072, SEEDS["cfg4"])
+        return GqaDense(world, rank, "cfg4", 32, 32, 4, 128, args.kv_len or 131072, SEEDS["cfg4"],
+                        exchange=args.exchange)
     if name == "cfg1":
         return GqaDense(world, rank, "cfg1", 1, 32, 4, 128, args.kv_len or 4096, SEEDS["cfg1"])
     if name == "cfg2":
@@ -1165,6 +1181,8 @@ def main():
     ap.add_argument("--kv-len", type=int, default=0, help="override KV length (profiling on a small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="cfg4 at N > 1: partials over NVLink peer stores to rank 0, or an NCCL all_gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1222,6 +1240,11 @@ def main():
         if parity is not None:
             line["parity"] = parity
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
+    status = scope_b200.status_take()
+    if status != 0:
+        raise RuntimeError(f"rank {rank}: a kernel reported a device-side failure (status {status})")
     if world > 1:
         import torch.distributed as dist
         barrier(world)

@@ -10,7 +10,8 @@
  *   - launches asynchronously on that stream and never synchronises;
  *   - returns WS_OK (0) or a WS_ERR_* code; ws_last_error() then returns a
  *     message (thread-local).
- * No entry point allocates device memory: callers pass a workspace whose
+ * No decode entry point allocates device memory (ws_peer_buffer_create is
+ * the one allocating entry, for the multi-GPU exchange): callers pass a workspace whose
  * size the matching *_workspace_size() returns.  A workspace must be zeroed
  * once when it is allocated (its counters reset themselves after every
  * launch) and must not be shared by launches that may overlap in time.
@@ -185,6 +186,13 @@ int ws_mla_decode_absorbed(const void* q_nope, const void* w_uk, int64_t w_uk_he
                            int nH, int S, int nop, int vhd, float scale, void* out, float* out_lse, void* workspace,
                            size_t workspace_bytes, void* stream);
 size_t ws_mla_decode_absorbed_workspace_size(int B, int nH, int S);
+/* The same step over a latent cache read in place: latent sequences
+ * c_batch_stride / pe_batch_stride elements apart (multiples of 8). */
+int ws_mla_decode_absorbed_strided(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
+                                   const void* c_kv, int64_t c_batch_stride, const void* k_pe, int64_t pe_batch_stride,
+                                   const void* w_uv, int64_t w_uv_head_stride, int B, int nH, int S, int nop, int vhd,
+                                   float scale, void* out, float* out_lse, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 /* ---- CSA index modes (ws_csa_decode with an id list) */
 #define WS_CSA_IDX_ALL 0            /* every id must lie in this buffer's range; others are skipped and
@@ -254,6 +262,40 @@ int ws_csa_decode_qcodes(const uint8_t* q_u8, const float* q_scales, int bs, int
 int ws_csa_kv_quantize_s8(const void* kv, int64_t rows, int hd, void* out, float* scales, int32_t* sums,
                           void* stream);
 int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float* scales, void* stream);
+
+/*
+ * Exchange of sequence-shard partials over NVLink peer memory (root gather):
+ * the device-side form of the runtime's share merge (system/qwenoffload.py:1606-1617,
+ * system/mixoffload.py:1456-1464) across GPUs of one box.
+ * Rank 0 allocates the exchange buffer (ws_peer_buffer_create: the one entry
+ * point that allocates device memory; ws_peer_exchange_bytes gives its size)
+ * and hands the 64-byte CUDA IPC handle to the other ranks, which map it with
+ * ws_peer_buffer_open.  For step `epoch` (1, 2, ... in the same order on
+ * every rank):
+ *   - rank r's decode writes its partial -- o fp32 [rows, dim] normalised,
+ *     then lse fp32 [rows] -- at base + ws_peer_slot_offset(world, rows, dim,
+ *     epoch & 1, r) (for ws_gqa_decode: out_mode WS_OUT_NORM_F32, out at
+ *     that address, out_lse right after the rows x dim floats);
+ *   - ranks r > 0 then call ws_peer_signal(base, r, epoch): a release store of
+ *     the epoch into rank 0's flag for r, then a bounded wait until rank 0 has
+ *     merged step epoch - 1 (its buffer is the one the next step writes);
+ *   - rank 0 calls ws_peer_merge(base, world, rows, dim, epoch, ...): a
+ *     bounded wait for every flag, the log-sum-exp merge into out [rows, dim]
+ *     (bf16 or fp32) and out_lse [rows], then "consumed = epoch".
+ * A wait that gives up (2 s) records WS_ERR_DEVICE for ws_status_take; the
+ * exchange must then be rebuilt.  Launches are asynchronous on `stream`; the
+ * epoch is a launch argument, so a captured CUDA graph would replay a stale
+ * epoch.  world <= 32, dim % 4 == 0.
+ */
+size_t ws_peer_exchange_bytes(int world, int64_t rows, int dim);
+size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int parity, int rank);
+int ws_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle);
+int ws_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
+int ws_peer_buffer_close(void* dev_ptr);
+int ws_peer_buffer_free(void* dev_ptr);
+int ws_peer_signal(void* root_base, int rank, int64_t epoch, void* stream);
+int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, int64_t epoch, void* out, int out_dtype,
+                  float* out_lse, void* stream);
 
 /* ---- indexer top-k orders */
 #define WS_TOPK_BY_SCORE 0   /* descending score, ties: lower id first (the reference's partial_sort order) */

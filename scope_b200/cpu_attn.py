@@ -248,15 +248,25 @@ def mla_decode_absorbed(q_nope: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Te
     if vhd < 1:
         raise RuntimeError("kv_b_proj_weight must hold nH x (nop + vhd) rows of 512")
     hs = (nop + vhd) * 512   # W_UK and W_UV are read in place: head blocks at this stride
-    c_kv, k_pe = c_kv.contiguous(), k_pe.contiguous()
+    # the latent may be a view of a [B, cap, *] cache: read in place through its batch stride when the
+    # tokens of each sequence are contiguous, else copied
+    def seq_contiguous(t, w):
+        return t.stride(2) == 1 and (S <= 1 or t.stride(1) == w) and (B <= 1 or (t.stride(0) % 8 == 0
+                                                                                   and t.stride(0) >= S * w))
+    if not seq_contiguous(c_kv, 512):
+        c_kv = c_kv.contiguous()
+    if not seq_contiguous(k_pe, 64):
+        k_pe = k_pe.contiguous()
+    c_bs = c_kv.stride(0) if B > 1 else S * 512
+    pe_bs = k_pe.stride(0) if B > 1 else S * 64
     out = torch.empty(B, nH, vhd, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, nH, dtype=torch.float32, device=dev) if return_lse else None
     L_ = lib()
     with torch.cuda.device(dev):
         ws = workspaces.get(L_.ws_mla_decode_absorbed_workspace_size(B, nH, S), dev)
-        rc = L_.ws_mla_decode_absorbed(ptr(qn), w.data_ptr(), hs, ptr(qpe), ptr(c_kv), ptr(k_pe),
-                                       w.data_ptr() + nop * 512 * 2, hs, B, nH, S, nop, vhd, float(scale), ptr(out),
-                                       ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
+        rc = L_.ws_mla_decode_absorbed_strided(ptr(qn), w.data_ptr(), hs, ptr(qpe), ptr(c_kv), c_bs, ptr(k_pe), pe_bs,
+                                               w.data_ptr() + nop * 512 * 2, hs, B, nH, S, nop, vhd, float(scale),
+                                               ptr(out), ptr(lse), ptr(ws), ws.numel(), stream_ptr(dev))
     check(rc, "ws_mla_decode_absorbed")
     return (out, lse) if return_lse else out
 

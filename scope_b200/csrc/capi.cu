@@ -271,6 +271,21 @@ int ws_mla_decode_absorbed(const void* q_nope, const void* w_uk, int64_t w_uk_he
                                vhd, scale, out, out_lse, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int ws_mla_decode_absorbed_strided(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
+                                   const void* c_kv, int64_t c_batch_stride, const void* k_pe, int64_t pe_batch_stride,
+                                   const void* w_uv, int64_t w_uv_head_stride, int B, int nH, int S, int nop, int vhd,
+                                   float scale, void* out, float* out_lse, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    if (B < 0 || nH < 1 || S < 0 || c_batch_stride < 0 || pe_batch_stride < 0)
+        return set_error(WS_ERR_INVALID_ARG, "mla_decode_absorbed: bad shape");
+    if (B == 0) return WS_OK;
+    if (!q_nope || !w_uk || !q_pe || !w_uv || !out || (S > 0 && (!c_kv || !k_pe)))
+        return set_error(WS_ERR_INVALID_ARG, "null pointer");
+    return mla_absorbed_launch(q_nope, w_uk, w_uk_head_stride, q_pe, c_kv, k_pe, w_uv, w_uv_head_stride, B, nH, S, nop,
+                               vhd, scale, out, out_lse, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                               c_batch_stride, pe_batch_stride);
+}
+
 size_t ws_csa_decode_workspace_size(int bs, int nq, int q_dtype) {
     return csa_workspace_bytes(std::max(bs, 0), std::max(nq, 1), q_dtype == WS_DTYPE_F32);
 }

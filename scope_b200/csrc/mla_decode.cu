@@ -829,7 +829,7 @@ size_t mla_absorbed_workspace_bytes(int B, int nH, int S) {
 int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
                         const void* c_kv, const void* k_pe, const void* w_uv, int64_t w_uv_head_stride, int B, int nH,
                         int S, int nop, int vhd, float scale, void* out, float* out_lse, void* workspace,
-                        size_t workspace_bytes, cudaStream_t st) {
+                        size_t workspace_bytes, cudaStream_t st, int64_t c_bstride, int64_t pe_bstride) {
     using namespace mla;
     if (nH != NH) return set_error(WS_ERR_UNSUPPORTED, "mla_decode_absorbed: this build supports 16 heads per sequence");
     if (B < 0 || S < 0 || nop < 4 || nop > 256 || nop % 4 || vhd < 1 || w_uk_head_stride < (int64_t)nop * CLR ||
@@ -861,7 +861,7 @@ int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
     int rc = mla_launch(q_proj, q_pe, c_kv, k_pe, B, nH, S, scale, WS_OUT_NORM_BF16, o_n, nullptr, nullptr, out_lse,
-                        workspace, dec, st, /*after_primary=*/true, /*kv_after_primary=*/false);
+                        workspace, dec, st, /*after_primary=*/true, /*kv_after_primary=*/false, c_bstride, pe_bstride);
     if (rc != WS_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(NH, (unsigned)((vhd + kUpV - 1) / kUpV));

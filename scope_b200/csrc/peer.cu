@@ -1,0 +1,233 @@
+// Exchange of sequence-shard partials over NVLink peer memory (root gather).
+//
+// The reference's runtimes merge the partials of their KV shares on the host
+// (system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464); across
+// GPUs of one box the merge input is each rank's (o fp32, lse fp32) block.
+// Instead of an all_gather collective, every rank's decode kernel writes its
+// block straight into rank 0's receive slot (rank 0's buffer is mapped into
+// every rank's address space with CUDA IPC, so the epilogue's stores cross
+// NVLink), then:
+//   * ranks 1..N-1 run peer_signal_kernel: a system-scope fence, then the step's
+//     epoch stored with release semantics into rank 0's flag word for that rank;
+//     it then waits (bounded) until rank 0 has consumed the step before last,
+//     whose buffer the next step's decode overwrites (two buffers, by epoch
+//     parity);
+//   * rank 0 runs peer_merge_kernel: each CTA waits (bounded, acquire loads)
+//     for every rank's flag to reach the epoch, merges its rows by log-sum-exp
+//     from the slots, and the CTA that takes the last ticket publishes the
+//     epoch as consumed.
+// Buffer layout (rank 0's allocation): a 1 KB control block -- flags[64]
+// (int64, one per rank), consumed (int64), the CTA ticket (int32), the last
+// epoch whose merge gave up (int64) -- then
+// 2 x world slots of slot_floats floats each, slot (parity, rank) holding
+// o [rows, dim] then lse [rows].
+// Every wait gives up after kWaitNs, records kDevTimeout in the status word
+// and skips its work; the exchange is then unusable and must be rebuilt.
+// No cluster multicast and no multimem: plain stores and loads only.
+#include <cstdio>
+
+#include "common.cuh"
+#include "ws_internal.h"
+
+namespace ws {
+namespace peer {
+
+constexpr int kMaxRanks = 64;
+constexpr size_t kCtrlBytes = 1024;
+constexpr int kConsumed = kMaxRanks;            // int64 index of the consumed word
+constexpr int kTicketByte = (kMaxRanks + 1) * 8;
+constexpr int kFailed = kMaxRanks + 2;          // int64 index: the last epoch a merge CTA gave up in
+constexpr uint64_t kWaitNs = 2000000000ull;     // 2 s
+constexpr int kRowsPerCta = 8;                  // one warp per row
+
+__device__ __forceinline__ void st_release_sys(int64_t* p, int64_t v) {
+    asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
+    int64_t v;
+    asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// slot floats: o [rows, dim] + lse [rows], rounded up to 64 floats (256 bytes) so every slot and its o
+// block start 16-byte aligned
+inline int64_t slot_floats(int64_t rows, int dim) { return (int64_t)align_up((size_t)(rows * dim + rows), 64); }
+
+__global__ void peer_signal_kernel(int64_t* root_ctrl, int rank, int64_t epoch, int* status) {
+    if (threadIdx.x != 0) return;
+    // this rank's block was written by the previous kernel on the stream (complete at its boundary); the
+    // fence orders those stores before the flag for any observer on another GPU
+    __threadfence_system();
+    st_release_sys(root_ctrl + rank, epoch);
+    // the next step writes the buffer of epoch - 1: wait until rank 0 has merged that step
+    const int64_t need = epoch - 1;
+    if (need <= 0) return;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(root_ctrl + kConsumed) < need) {
+        if (globaltimer_ns() - t0 > kWaitNs) {
+            atomicExch(status, kDevTimeout);
+            return;
+        }
+        __nanosleep(256);
+    }
+}
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(32 * kRowsPerCta) peer_merge_kernel(const float* __restrict__ slots,
+                                                                      int64_t slot_stride, int P, int64_t R, int D,
+                                                                      int64_t* ctrl, int64_t epoch, void* out,
+                                                                      float* out_lse, int* status) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint64_t t0 = globaltimer_ns();
+        for (int r = 1; r < P && ok; ++r) {   // rank 0's own block is ordered by the stream
+            while (ld_acquire_sys(ctrl + r) < epoch) {
+                if (globaltimer_ns() - t0 > kWaitNs) {
+                    atomicExch(status, kDevTimeout);
+                    atomicExch(reinterpret_cast<unsigned long long*>(ctrl + kFailed), (unsigned long long)epoch);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * kRowsPerCta + warp;
+    if (s_ok && row < R) {
+        // lane p < P holds partial p's lse (P <= 32); the weights follow from the row's log-sum-exp
+        const float lp = lane < P ? __ldcg(slots + lane * slot_stride + R * D + row) : -INFINITY;
+        float M = lp;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float w = (M == -INFINITY || lp == -INFINITY) ? 0.f : expf(lp - M);
+        float s = w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float lse = M == -INFINITY ? -INFINITY : M + logf(s);
+        const float wp = M == -INFINITY ? 0.f : w / s;   // exp(lp - lse)
+        for (int c = lane * 4; c < D; c += 128) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < P; ++p) {
+                const float e = __shfl_sync(0xffffffffu, wp, p);
+                if (e == 0.f) continue;
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(slots + p * slot_stride + row * D + c));
+                acc.x = fmaf(e, v.x, acc.x);
+                acc.y = fmaf(e, v.y, acc.y);
+                acc.z = fmaf(e, v.z, acc.z);
+                acc.w = fmaf(e, v.w, acc.w);
+            }
+            if (OUT_BF16) {
+                uint2 pk = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + row * D + c) = pk;
+            } else {
+                *reinterpret_cast<float4*>(static_cast<float*>(out) + row * D + c) = acc;
+            }
+        }
+        if (lane == 0 && out_lse) out_lse[row] = lse;
+    }
+    // the last CTA to finish publishes the epoch as consumed (its slots may be overwritten from now on)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        int* ticket = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ctrl) + kTicketByte);
+        if (atomicAdd(ticket, 1) == (int)gridDim.x - 1) {
+            atomicExch(ticket, 0);
+            // publish only when no CTA of this launch gave up waiting
+            if (atomicAdd(reinterpret_cast<unsigned long long*>(ctrl + kFailed), 0ull) != (unsigned long long)epoch) {
+                __threadfence_system();
+                st_release_sys(ctrl + kConsumed, epoch);
+            }
+        }
+    }
+}
+
+}  // namespace peer
+}  // namespace ws
+
+using namespace ws;
+using namespace ws::peer;
+
+extern "C" {
+
+size_t ws_peer_exchange_bytes(int world, int64_t rows, int dim) {
+    if (world < 1 || world > kMaxRanks || rows < 0 || dim < 1) return 0;
+    return kCtrlBytes + 2 * (size_t)world * (size_t)slot_floats(rows, dim) * sizeof(float);
+}
+
+size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int parity, int rank) {
+    return kCtrlBytes + ((size_t)(parity & 1) * world + (size_t)rank) * (size_t)slot_floats(rows, dim) * sizeof(float);
+}
+
+int ws_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle) {
+    if (!dev_ptr || !ipc_handle || bytes < kCtrlBytes) return set_error(WS_ERR_INVALID_ARG, "peer_buffer_create: bad argument");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *dev_ptr = p;
+    return WS_OK;
+}
+
+int ws_peer_buffer_open(const void* ipc_handle, void** dev_ptr) {
+    if (!ipc_handle || !dev_ptr) return set_error(WS_ERR_INVALID_ARG, "peer_buffer_open: bad argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int ws_peer_buffer_close(void* dev_ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int ws_peer_buffer_free(void* dev_ptr) {
+    const cudaError_t e = cudaFree(dev_ptr);
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int ws_peer_signal(void* root_base, int rank, int64_t epoch, void* stream) {
+    if (!root_base || rank < 1 || rank >= kMaxRanks || epoch < 1)
+        return set_error(WS_ERR_INVALID_ARG, "peer_signal: bad argument");
+    peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int64_t*>(root_base), rank,
+                                                                       epoch, device_status_word());
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, int64_t epoch, void* out, int out_dtype,
+                  float* out_lse, void* stream) {
+    if (!root_base || world < 1 || world > 32 || rows < 0 || dim < 4 || dim % 4 || epoch < 1 || (rows > 0 && !out))
+        return set_error(WS_ERR_INVALID_ARG, "peer_merge: bad argument (world <= 32, dim % 4 == 0)");
+    if (out_dtype != WS_DTYPE_BF16 && out_dtype != WS_DTYPE_F32)
+        return set_error(WS_ERR_INVALID_ARG, "peer_merge: out dtype");
+    if (reinterpret_cast<uintptr_t>(out) % 16) return set_error(WS_ERR_INVALID_ARG, "peer_merge: out must be 16-byte aligned");
+    const int64_t sf = slot_floats(rows, dim);
+    const float* slots = reinterpret_cast<const float*>(static_cast<uint8_t*>(root_base) +
+                                                        ws_peer_slot_offset(world, rows, dim, (int)(epoch & 1), 0));
+    const int64_t ctas = std::max<int64_t>(1, (rows + kRowsPerCta - 1) / kRowsPerCta);
+    if (ctas > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "peer_merge: too many rows");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int64_t* ctrl = static_cast<int64_t*>(root_base);
+    if (out_dtype == WS_DTYPE_BF16)
+        peer_merge_kernel<true><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, epoch,
+                                                                          out, out_lse, device_status_word());
+    else
+        peer_merge_kernel<false><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, epoch,
+                                                                           out, out_lse, device_status_word());
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+}  // extern "C"

@@ -82,7 +82,7 @@ size_t mla_absorbed_workspace_bytes(int B, int nH, int S);
 int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_stride, const void* q_pe,
                         const void* c_kv, const void* k_pe, const void* w_uv, int64_t w_uv_head_stride, int B, int nH,
                         int S, int nop, int vhd, float scale, void* out, float* out_lse, void* workspace,
-                        size_t workspace_bytes, cudaStream_t st);
+                        size_t workspace_bytes, cudaStream_t st, int64_t c_bstride = -1, int64_t pe_bstride = -1);
 
 struct CsaLaunch {
     const void* q;

@@ -78,3 +78,82 @@ class PartialExchange:
     def step(self, out_dtype=torch.bfloat16, out=None, out_lse=None, merge_fn: Callable | None = None):
         self.gather()
         return self.merge(out_dtype, out=out, out_lse=out_lse, merge_fn=merge_fn)
+
+
+class PeerExchange:
+    """The exchange over NVLink peer memory: rank 0 gathers, merges and holds
+    the result (see ws_peer_merge in include/scope_b200.h).
+
+    Rank 0 allocates the buffer and broadcasts its CUDA IPC handle; the other
+    ranks map it.  Before a step, a rank's decode writes its partial at
+    ``slot()`` -- (o pointer, lse pointer) into rank 0's buffer, by the next
+    epoch's parity -- then ``step()`` signals (ranks > 0) or waits, merges and
+    returns (out, out_lse) (rank 0; None elsewhere).  Every rank must call
+    ``step()`` once per step, in the same order.  The epoch is a launch
+    argument, so steps are not replayable from a captured CUDA graph.
+    """
+
+    def __init__(self, rows: int, dim: int, world: int, rank: int, device, group=None):
+        import ctypes
+
+        from ._lib import check, lib
+        self.rows, self.dim, self.world, self.rank, self.group = rows, dim, world, rank, group
+        self.device = torch.device(device)
+        L = lib()
+        nbytes = L.ws_peer_exchange_bytes(world, rows, dim)
+        if nbytes == 0:
+            raise ValueError("PeerExchange: bad world / rows / dim")
+        handle = ctypes.create_string_buffer(64)
+        base = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            if rank == 0:
+                check(L.ws_peer_buffer_create(nbytes, ctypes.byref(base), handle), "ws_peer_buffer_create")
+            objs = [handle.raw if rank == 0 else None]
+            dist.broadcast_object_list(objs, src=0, group=group)
+            if rank != 0:
+                check(L.ws_peer_buffer_open(ctypes.create_string_buffer(objs[0], 64), ctypes.byref(base)),
+                      "ws_peer_buffer_open")
+        self.base = base.value
+        self.epoch = 0
+        self._closed = False
+
+    def slot(self):
+        """(o, lse) device addresses where this rank's partial of the next step goes."""
+        from ._lib import lib
+        off = lib().ws_peer_slot_offset(self.world, self.rows, self.dim, (self.epoch + 1) & 1, self.rank)
+        o = self.base + off
+        return o, o + 4 * self.rows * self.dim
+
+    def step(self, out=None, out_lse=None, out_dtype=torch.bfloat16):
+        from . import _lib
+        from ._lib import check, lib, stream_ptr
+        e = self.epoch + 1
+        with torch.cuda.device(self.device):
+            st = stream_ptr(self.device)
+            if self.rank == 0:
+                if out is None:
+                    out = torch.empty(self.rows, self.dim, dtype=out_dtype, device=self.device)
+                if out_lse is None:
+                    out_lse = torch.empty(self.rows, dtype=torch.float32, device=self.device)
+                code = _lib.WS_DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.WS_DTYPE_F32
+                check(lib().ws_peer_merge(self.base, self.world, self.rows, self.dim, e, out.data_ptr(), code,
+                                          out_lse.data_ptr(), st), "ws_peer_merge")
+            else:
+                check(lib().ws_peer_signal(self.base, self.rank, e, st), "ws_peer_signal")
+                out = out_lse = None
+        self.epoch = e
+        return out, out_lse
+
+    def close(self) -> None:
+        """Collective: unmap on ranks > 0, then free on rank 0."""
+        from ._lib import lib
+        if self._closed:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        if self.rank != 0:
+            lib().ws_peer_buffer_close(self.base)
+        dist.barrier(group=self.group)
+        if self.rank == 0:
+            lib().ws_peer_buffer_free(self.base)
+        self._closed = True

@@ -214,3 +214,62 @@ def test_sharded_caches_decode_over_nccl():
     mro, mrm, mrs = oracle.mla_compressed(*(oracle.bf16_bits(t) for t in (qp, qpe, c, p)), 192 ** -0.5)
     assert np.abs(mo - mro / mrs[:, None]).max() < TOL_OUT
     assert np.abs(ml - (mrm + np.log(mrs))).max() < TOL_LSE
+
+
+def _peer_rank(rank, port, qs, ks, vs, scale):
+    """Steps of a sharded GQA decode whose partials go over NVLink peer stores
+    into rank 0's slots (PeerExchange); rank 0 returns every step's merge."""
+    import torch.distributed as dist
+
+    import scope_b200
+    from scope_b200 import _lib
+    from scope_b200.shard import PeerExchange, shard_bounds
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", world_size=WORLD, rank=rank,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        scope_b200.build()
+        rows, G, D = qs[0].shape
+        L = ks[0].shape[1]
+        lo, hi = shard_bounds(L, WORLD, rank)
+        ex = PeerExchange(rows * G, D, WORLD, rank, dev)
+        L_ = _lib.lib()
+        ws = torch.zeros(L_.ws_gqa_decode_workspace_size(rows, G, D, hi - lo), dtype=torch.uint8, device=dev)
+        outs = []
+        for q, k, v in zip(qs, ks, vs):   # back to back on one stream, no host synchronisation between steps
+            qd = q.to(dev)
+            kd, vd = k[:, lo:hi].contiguous().to(dev), v[:, lo:hi].contiguous().to(dev)
+            o_ptr, l_ptr = ex.slot()
+            rc = L_.ws_gqa_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kd.stride(0), kd.stride(1),
+                                  vd.stride(0), vd.stride(1), rows, G, D, D, hi - lo, scale, _lib.WS_DTYPE_BF16,
+                                  _lib.WS_OUT_NORM_F32, o_ptr, None, None, l_ptr, ws.data_ptr(), ws.numel(),
+                                  torch.cuda.current_stream().cuda_stream)
+            assert rc == 0, L_.ws_last_error()
+            out, lse = ex.step()
+            if rank == 0:
+                outs.append((out.float(), lse.clone()))
+        torch.cuda.synchronize()
+        status = scope_b200.status_take()
+        ex.close()
+        assert status == 0, status
+        return [(o.cpu().numpy(), l_.cpu().numpy()) for o, l_ in outs]
+    finally:
+        dist.destroy_process_group()
+
+
+@needs_two
+def test_peer_exchange_steps():
+    import oracle
+    g = torch.Generator().manual_seed(53)
+    rows, G, D, L, steps = 8, 8, 128, 6001, 5
+    qs = [torch.randn(rows, G, D, generator=g).bfloat16() for _ in range(steps)]
+    ks = [torch.randn(rows, L, D, generator=g).bfloat16() for _ in range(steps)]
+    vs = [torch.randn(rows, L, D, generator=g).bfloat16() for _ in range(steps)]
+    scale = D ** -0.5
+    res = _run_two_ranks(_peer_rank, (qs, ks, vs, scale))
+    assert len(res) == steps
+    for (out, lse), q, k, v in zip(res, qs, ks, vs):
+        ro, rm, rs = oracle.gqa_decode(oracle.bf16_bits(q), oracle.bf16_bits(k), oracle.bf16_bits(v), scale)
+        assert np.abs(out - ro.reshape(rows * G, D)).max() < TOL_OUT
+        assert np.abs(lse - (rm + np.log(rs)).reshape(rows * G)).max() < TOL_LSE
