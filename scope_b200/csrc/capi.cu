@@ -124,6 +124,7 @@ int ws_status_take(void* stream) {
 
 size_t ws_gqa_decode_workspace_size(int B_kv, int G, int Dv, int L) {
     B_kv = std::min(B_kv, kMaxGroupsPerLaunch);   // larger calls run in chunks of rows
+    G = std::min(G, kMaxHeadsPerLaunch);          // and of 16 query heads
     const int64_t tiles = (int64_t)B_kv * ((L + 63) / 64);
     const int nctas = (int)std::min<int64_t>(device_sm_count(), std::max<int64_t>(tiles, 1));
     return gqa_workspace_bytes(G, Dv, B_kv, B_kv, nctas);
@@ -164,25 +165,36 @@ int ws_gqa_decode(const void* q, const void* k, const void* v, int64_t k_stride_
         }
         return WS_OK;
     }
-    GqaLaunch a;
-    memset(&a, 0, sizeof(a));
-    a.q = q;
-    a.q_row_stride = (int64_t)G * Dk;
-    a.G = G; a.Dk = Dk; a.Dv = Dv; a.scale = scale;
-    a.varlen = 0;
-    a.n_rows = B_kv; a.L = L;
-    a.nshare = 1;
-    a.shares[0].k = k; a.shares[0].v = v;
-    a.shares[0].n_tok = L; a.shares[0].n_rows = B_kv;
-    a.shares[0].k_stride_tok = k_stride_t; a.shares[0].k_stride_row = k_stride_b;
-    a.shares[0].v_stride_tok = v_stride_t; a.shares[0].v_stride_row = v_stride_b;
-    a.out_mode = out_mode;
-    a.out = out; a.out_max = out_max; a.out_sum = out_sum; a.out_lse = out_lse;
-    a.out_row_stride = (int64_t)G * Dv; a.ml_row_stride = G;
-    a.workspace = workspace; a.workspace_bytes = workspace_bytes;
-    a.status = device_status_word();
-    a.stream = stream;
-    return gqa_launch(a);
+    // more than 16 query heads per kv row: chunks of 16 heads, each a launch over the same rows (the kv rows
+    // are read once per chunk); the chunks address q and the outputs through their row strides
+    const size_t ob = out_mode == WS_OUT_NORM_BF16 ? 2 : 4;
+    for (int g0 = 0; g0 < G; g0 += kMaxHeadsPerLaunch) {
+        const int gc = std::min(kMaxHeadsPerLaunch, G - g0);
+        GqaLaunch a;
+        memset(&a, 0, sizeof(a));
+        a.q = static_cast<const uint16_t*>(q) + (int64_t)g0 * Dk;
+        a.q_row_stride = (int64_t)G * Dk;
+        a.G = gc; a.Dk = Dk; a.Dv = Dv; a.scale = scale;
+        a.varlen = 0;
+        a.n_rows = B_kv; a.L = L;
+        a.nshare = 1;
+        a.shares[0].k = k; a.shares[0].v = v;
+        a.shares[0].n_tok = L; a.shares[0].n_rows = B_kv;
+        a.shares[0].k_stride_tok = k_stride_t; a.shares[0].k_stride_row = k_stride_b;
+        a.shares[0].v_stride_tok = v_stride_t; a.shares[0].v_stride_row = v_stride_b;
+        a.out_mode = out_mode;
+        a.out = static_cast<uint8_t*>(out) + (size_t)g0 * Dv * ob;
+        a.out_max = out_max ? static_cast<uint8_t*>(out_max) + (size_t)g0 * ob : nullptr;
+        a.out_sum = out_sum ? static_cast<uint8_t*>(out_sum) + (size_t)g0 * ob : nullptr;
+        a.out_lse = out_lse ? out_lse + g0 : nullptr;
+        a.out_row_stride = (int64_t)G * Dv; a.ml_row_stride = G;
+        a.workspace = workspace; a.workspace_bytes = workspace_bytes;
+        a.status = device_status_word();
+        a.stream = stream;
+        const int rc = gqa_launch(a);
+        if (rc != WS_OK) return rc;
+    }
+    return WS_OK;
 }
 
 size_t ws_gqa_decode_shares_workspace_size(int B, int Hkv, int G, int Dv, int n_shares) {

@@ -840,6 +840,13 @@ static int dispatch(const GqaMaps& maps, const GqaParams& p, int Dk, int Dv, int
     WS_GQA_CASE(192, 128, 1, 4)
     WS_GQA_CASE(192, 128, 2, 3)
     WS_GQA_CASE(128, 64, 1, 4)
+    // the other head sizes the reference accepts (any multiple of 16): dims up to 256, rounded up to 64
+    WS_GQA_CASE(64, 128, 1, 6)
+    WS_GQA_CASE(64, 128, 2, 5)
+    WS_GQA_CASE(192, 192, 1, 3)
+    WS_GQA_CASE(192, 192, 2, 3)
+    WS_GQA_CASE(256, 256, 1, 2)
+    WS_GQA_CASE(256, 256, 2, 2)
 #undef WS_GQA_CASE
     return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: unsupported (Dk, Dv, G) combination");
 }

@@ -27,6 +27,7 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // them to zero, and partials never land on them.
 constexpr size_t kCounterHeaderBytes = size_t(256) << 10;
 constexpr int kMaxGroupsPerLaunch = int(kCounterHeaderBytes / 4);
+constexpr int kMaxHeadsPerLaunch = 16;   // query heads per kv row one GQA launch takes (two MMA column tiles)
 
 struct KvShare {
     const void* k;

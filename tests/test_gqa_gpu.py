@@ -281,3 +281,28 @@ def test_split_merge_equals_unsplit_large(ext):
     ro, rm, rs = oracle_of(q[:1].cpu(), k[:1].cpu(), v[:1].cpu(), sc)
     assert np.abs((full_o[:1] / full_s[:1]).cpu().numpy() - ro).max() < TOL_OUT
     assert np.abs((full_m[:1] + full_s[:1].log()).cpu().numpy()[..., 0] - (rm + np.log(rs))).max() < TOL_LSE
+
+
+@pytest.mark.parametrize("B,G,Dk,Dv,L", [
+    (3, 8, 32, 32, 500), (2, 4, 80, 80, 1300), (2, 8, 96, 96, 777), (2, 8, 256, 256, 1500),
+    (3, 12, 256, 256, 900), (2, 4, 192, 192, 1000), (2, 10, 192, 192, 600), (2, 8, 64, 128, 900),
+    (2, 12, 48, 112, 333), (2, 24, 128, 128, 2000), (2, 32, 128, 128, 700), (1, 40, 64, 64, 300)])
+def test_head_sizes_and_groups(ext, B, G, Dk, Dv, L):
+    """The head sizes and group counts the reference accepts (any D % 16 == 0,
+    any G; kernel/cpu_attn.cpp:578-583): dims up to 256 run on the tile sizes
+    rounded up to 64, G > 16 as chunks of 16 query heads over the same rows."""
+    g = torch.Generator().manual_seed(B * 1000 + G * 10 + Dk + Dv + L)
+    q = rand_bf16(B, G, Dk, gen=g)
+    k = rand_bf16(B, L, Dk, gen=g)
+    v = rand_bf16(B, L, Dv, gen=g)
+    scale = Dk ** -0.5
+    o, m, s = ext.fused_cpu_attn_mla(q.to(DEV), k.to(DEV), v.to(DEV), scale)
+    torch.cuda.synchronize()
+    ro, rm, rs = oracle_of(q, k, v, scale)
+    o, m, s = o.cpu().numpy(), m.cpu().numpy()[..., 0], s.cpu().numpy()[..., 0]
+    assert np.abs(o / s[..., None] - ro).max() < TOL_OUT
+    assert np.abs((m + np.log(s)) - (rm + np.log(rs))).max() < TOL_LSE
+    if Dk == Dv:   # the public bf16 form too (bf16 out, max, sum)
+        po, pm, ps = ext.fused_cpu_attn(q.to(DEV), k.to(DEV), v.to(DEV), scale)
+        torch.cuda.synchronize()
+        assert np.abs(po.float().cpu().numpy() - ro).max() < TOL_OUT
