@@ -925,13 +925,22 @@ int gqa_launch(const GqaLaunch& a) {
         p.defer_merge = (tpr + per_cta - 1) / per_cta + 1 > 8;
     }
     cudaStream_t st = static_cast<cudaStream_t>(a.stream);
+    const int DVP = (a.Dv + 63) / 64 * 64, NG = (a.G <= 8 ? 1 : 2) * 8;
+    if (p.defer_merge && DVP > 256)   // checked before the decode is launched
+        return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: unsupported value width for the deferred merge");
     int rc = dispatch(maps, p, a.Dk, a.Dv, nctas, extra_smem, st);
     if (rc != WS_OK || !p.defer_merge) return rc;
-    const int DVP = (a.Dv + 63) / 64 * 64, NG = (a.G <= 8 ? 1 : 2) * 8;
-    if (DVP == 64 && NG == 8) return launch_merge<64, 8>(p, tpr, total_tiles, nctas, st);
-    if (DVP == 64 && NG == 16) return launch_merge<64, 16>(p, tpr, total_tiles, nctas, st);
-    if (DVP == 128 && NG == 8) return launch_merge<128, 8>(p, tpr, total_tiles, nctas, st);
-    if (DVP == 128 && NG == 16) return launch_merge<128, 16>(p, tpr, total_tiles, nctas, st);
+#define WS_GQA_MERGE(dvp, ng) \
+    if (DVP == dvp && NG == ng) return launch_merge<dvp, ng>(p, tpr, total_tiles, nctas, st);
+    WS_GQA_MERGE(64, 8)
+    WS_GQA_MERGE(64, 16)
+    WS_GQA_MERGE(128, 8)
+    WS_GQA_MERGE(128, 16)
+    WS_GQA_MERGE(192, 8)
+    WS_GQA_MERGE(192, 16)
+    WS_GQA_MERGE(256, 8)
+    WS_GQA_MERGE(256, 16)
+#undef WS_GQA_MERGE
     return set_error(WS_ERR_UNSUPPORTED, "gqa_decode: unsupported value width for the deferred merge");
 }
 
