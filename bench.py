@@ -1061,7 +1061,7 @@ def make_workload(name, world, rank, args):
     raise ValueError(name)
 
 
-WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "idx", "mla_abs")
+WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "idx", "mla_abs", "aux")
 SEEDS = {"cfg4": 4000, "cfg1": 1000, "cfg5": 5}
 
 
@@ -1153,6 +1153,117 @@ def time_e2e(wl, steps, warmup, world):
     return max_over_ranks(e0.elapsed_time(e1) / 1e3 / steps, world)
 
 
+def run_aux(args):
+    """--workload aux: the auxiliary kernels of the path, each timed alone on
+    inputs larger than L2 (CUDA events, mean over --steps launches after
+    --warmup), with its algorithmic bytes per launch: the int8 / u8
+    quantisers, the fp32 GQA decode, the two log-sum-exp merges (the strided
+    one at a sharded-exchange shape) and the KV-cache append (one token; a
+    latency-bound launch).  One JSON line; per-kernel results in "ops"."""
+    from scope_b200 import _lib
+    L_ = _lib.lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = lambda: torch.cuda.current_stream().cuda_stream   # noqa: E731
+    g = torch.Generator(device=dev).manual_seed(77)
+    hbm, peak_src = peaks()
+
+    def chk(rc):
+        if rc != 0:
+            raise RuntimeError(L_.ws_last_error().decode())
+
+    def timed(fn, nbytes):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        return {"us": us, "bytes": nbytes, "GB/s": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / hbm}
+
+    ops = {}
+    # kv_quantize_bf16_to_int8 over [8, 32768, 512] bf16 (two copies, alternating)
+    rows, hd = 8 * 32768, 512
+    kvs = [bf16_randn((rows, hd), g, dev) for _ in range(2)]
+    k8 = torch.empty(rows, hd, dtype=torch.int8, device=dev)
+    ksc = torch.empty(rows, dtype=torch.float32, device=dev)
+    ksm = torch.empty(rows, dtype=torch.int32, device=dev)
+    ops["csa_kv_quantize_s8"] = timed(lambda i: chk(L_.ws_csa_kv_quantize_s8(
+        kvs[i % 2].data_ptr(), rows, hd, k8.data_ptr(), ksc.data_ptr(), ksm.data_ptr(), st())), rows * hd * 3 + rows * 8)
+    del kvs, k8, ksc, ksm
+    # q_quantize_fp32_to_u8 over [131072, 512] fp32
+    rows = 131072
+    qs = [torch.randn(rows, hd, generator=g, device=dev) for _ in range(2)]
+    qu = torch.empty(rows, hd, dtype=torch.uint8, device=dev)
+    qsc = torch.empty(rows, dtype=torch.float32, device=dev)
+    ops["csa_q_quantize_u8"] = timed(lambda i: chk(L_.ws_csa_q_quantize_u8(
+        qs[i % 2].data_ptr(), rows, hd, qu.data_ptr(), qsc.data_ptr(), st())), rows * hd * 5 + rows * 4)
+    del qs, qu, qsc
+    # fp32 GQA decode (gqa_f32_kernel): 32 kv rows x 16384 tokens x 128, G = 8
+    B_kv, G, D, L = 32, 8, 128, 16384
+    q = torch.randn(B_kv, G, D, generator=g, device=dev)
+    k = torch.randn(B_kv, L, D, generator=g, device=dev)
+    v = torch.randn(B_kv, L, D, generator=g, device=dev)
+    out = torch.empty(B_kv, G, D, device=dev)
+    lse = torch.empty(B_kv, G, device=dev)
+    ws = torch.zeros(L_.ws_gqa_decode_workspace_size(B_kv, G, D, L), dtype=torch.uint8, device=dev)
+    ops["gqa_f32_decode"] = timed(lambda i: chk(L_.ws_gqa_decode(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), v.stride(0), v.stride(1), B_kv, G, D, D,
+        L, D ** -0.5, _lib.WS_DTYPE_F32, _lib.WS_OUT_NORM_F32, out.data_ptr(), None, None, lse.data_ptr(),
+        ws.data_ptr(), ws.numel(), st())), 2 * B_kv * L * D * 4 + B_kv * G * (2 * D * 4 + 4))
+    del q, k, v, out, lse, ws
+    # strided merge of 8 gathered [o, lse] blocks (the NCCL exchange's merge), 131072 rows x 128
+    P, R, D = 8, 131072, 128
+    blk = R * D + R
+    parts = torch.randn(P, blk, generator=g, device=dev)
+    out = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(R, device=dev)
+    ops["lse_merge_strided"] = timed(lambda i: chk(L_.ws_lse_merge_strided(
+        parts.data_ptr(), blk, parts.data_ptr() + 4 * R * D, blk, P, R, D, out.data_ptr(), _lib.WS_DTYPE_BF16,
+        lse.data_ptr(), st())), P * blk * 4 + R * (D * 2 + 4))
+    del parts, out, lse
+    # vectorised merge of 9 split partials (the CSA split merge shape), 16384 rows x 512
+    P, R, D = 9, 16384, 512
+    po = torch.randn(P, R, D, generator=g, device=dev)
+    pl = torch.randn(P, R, generator=g, device=dev)
+    out = torch.empty(R, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(R, device=dev)
+    ops["lse_merge"] = timed(lambda i: chk(L_.ws_lse_merge(
+        po.data_ptr(), pl.data_ptr(), P, R, D, out.data_ptr(), _lib.WS_DTYPE_BF16, lse.data_ptr(), st())),
+        P * R * (D + 1) * 4 + R * (D * 2 + 4))
+    del po, pl, out, lse
+    # KV-cache append of one decode token into [128 rows, 8192, 128] (one launch per token)
+    rows, cap, D = 128, 8192, 128
+    cache = torch.zeros(rows, cap, D, dtype=torch.bfloat16, device=dev)
+    new = bf16_randn((rows, 1, D), g, dev)
+    # one launch per token is far shorter than a Python-side launch: the launches are captured in a CUDA
+    # graph (args.steps appends at successive positions) and the graph is timed, so the events see device time
+    gs = torch.cuda.Stream()
+    gs.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
+        for i in range(args.steps):
+            chk(L_.ws_kv_append(cache.data_ptr(), cache.stride(0), cache.stride(1), cap, new.data_ptr(),
+                                new.stride(0), new.stride(1), rows, 1, D, _lib.WS_DTYPE_BF16, i % cap,
+                                torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    r = timed(lambda i: graph.replay(), 2 * rows * D * 2 * args.steps)
+    ops["kv_append_1tok"] = {"us": r["us"] / args.steps, "bytes": 2 * rows * D * 2, "GB/s": r["GB/s"],
+                             "frac": r["frac"], "note": "per launch, from a CUDA graph of back-to-back appends"}
+    tot_b = sum(o["bytes"] for o in ops.values())
+    tot_us = sum(o["us"] for o in ops.values())
+    line = {"metric": METRIC, "value": tot_b / tot_us / 1e6, "unit": "TB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": tot_us / 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16/fp32", "data": "synthetic (seeded normal)",
+            "config": {"workload": "aux_kernels", "peak_GBps": hbm, "peak_source": peak_src,
+                       "l2": "every input but the append's is larger than L2"},
+            "ops": ops, "gpu_launches": len(ops) * args.steps}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference_arm(args):
     """The reference's own CPU kernel on this host's cores, one bounded sample
     of the workload per step.  Touches no GPU and loads nothing of scope_b200."""
@@ -1199,6 +1310,11 @@ def main():
                                 device_id=torch.device("cuda", local))
     import scope_b200
     scope_b200.build()
+    if args.workload == "aux":
+        if world > 1:
+            raise SystemExit("--workload aux runs on one GPU")
+        run_aux(args)
+        return
     wl = make_workload(args.workload, world, rank, args)
     parity = wl.parity_check(SEEDS[args.workload]) if hasattr(wl, "parity_check") else None
 

@@ -294,6 +294,12 @@ int ws_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
 int ws_peer_buffer_close(void* dev_ptr);
 int ws_peer_buffer_free(void* dev_ptr);
 int ws_peer_signal(void* root_base, int rank, int64_t epoch, void* stream);
+/* Ranks > 0, the faster form: the decode writes its block ([rows, dim] o then
+ * [rows] lse, 16-byte aligned) to local memory and ws_peer_push copies it into
+ * rank 0's slot, then does what ws_peer_signal does, in one launch.  `ticket`
+ * is one device int of this rank, zeroed once (the launch leaves it zero). */
+int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, int dim, int rank, int64_t epoch,
+                 int* ticket, void* stream);
 int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, int64_t epoch, void* out, int out_dtype,
                   float* out_lse, void* stream);
 

@@ -91,6 +91,7 @@ SIGNATURES = {
     "ws_peer_buffer_close": (_i, [_V]),
     "ws_peer_buffer_free": (_i, [_V]),
     "ws_peer_signal": (_i, [_V, _i, _i64, _V]),
+    "ws_peer_push": (_i, [_V, _V, _i, _i64, _i, _i, _i64, _V, _V]),
     "ws_peer_merge": (_i, [_V, _i, _i64, _i, _i64, _V, _i, _V, _V]),
 }
 

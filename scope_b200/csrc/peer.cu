@@ -73,6 +73,35 @@ __global__ void peer_signal_kernel(int64_t* root_ctrl, int rank, int64_t epoch, 
     }
 }
 
+// Ranks > 0: copy this rank's block (written locally by its decode) into rank 0's slot with 16-byte
+// stores spread over the grid, then the CTA that takes the last ticket publishes the epoch and waits for
+// rank 0 to have consumed epoch - 1 (as peer_signal_kernel does).  Keeping the decode's own stores local
+// matters: its merge tickets fence every prior store, and a fence behind stores to another GPU waits for
+// the NVLink round trip.
+__global__ void __launch_bounds__(256) peer_push_kernel(const float4* __restrict__ src, float4* dst, int64_t n16,
+                                                        int64_t* root_ctrl, int* ticket, int rank, int64_t epoch,
+                                                        int* status) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __ldcg(src + i);
+    __threadfence_system();   // every thread's copies are performed before its CTA takes the ticket
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
+    atomicExch(ticket, 0);
+    __threadfence_system();
+    st_release_sys(root_ctrl + rank, epoch);
+    const int64_t need = epoch - 1;
+    if (need <= 0) return;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(root_ctrl + kConsumed) < need) {
+        if (globaltimer_ns() - t0 > kWaitNs) {
+            atomicExch(status, kDevTimeout);
+            return;
+        }
+        __nanosleep(256);
+    }
+}
+
 template <bool OUT_BF16>
 __global__ void __launch_bounds__(32 * kRowsPerCta) peer_merge_kernel(const float* __restrict__ slots,
                                                                       int64_t slot_stride, int P, int64_t R, int D,
@@ -202,6 +231,24 @@ int ws_peer_signal(void* root_base, int rank, int64_t epoch, void* stream) {
         return set_error(WS_ERR_INVALID_ARG, "peer_signal: bad argument");
     peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int64_t*>(root_base), rank,
                                                                        epoch, device_status_word());
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, int dim, int rank, int64_t epoch,
+                 int* ticket, void* stream) {
+    if (!block || !root_base || !ticket || rank < 1 || rank >= world || world > kMaxRanks || rows < 0 || dim < 1 ||
+        epoch < 1)
+        return set_error(WS_ERR_INVALID_ARG, "peer_push: bad argument");
+    if (reinterpret_cast<uintptr_t>(block) % 16) return set_error(WS_ERR_INVALID_ARG, "peer_push: block must be 16-byte aligned");
+    const int64_t floats = rows * dim + rows;
+    const int64_t n16 = (floats + 3) / 4;   // the slot holds slot_floats >= floats rounded up to 64
+    float4* dst = reinterpret_cast<float4*>(static_cast<uint8_t*>(root_base) +
+                                            ws_peer_slot_offset(world, rows, dim, (int)(epoch & 1), rank));
+    const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(128, (n16 + 255) / 256));
+    peer_push_kernel<<<ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float4*>(block), dst, n16, static_cast<int64_t*>(root_base), ticket, rank, epoch,
+        device_status_word());
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }

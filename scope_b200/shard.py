@@ -86,8 +86,9 @@ class PeerExchange:
 
     Rank 0 allocates the buffer and broadcasts its CUDA IPC handle; the other
     ranks map it.  Before a step, a rank's decode writes its partial at
-    ``slot()`` -- (o pointer, lse pointer) into rank 0's buffer, by the next
-    epoch's parity -- then ``step()`` signals (ranks > 0) or waits, merges and
+    ``slot()`` -- (o pointer, lse pointer): rank 0's own slot, or a local
+    block on the other ranks -- then ``step()`` pushes the block into rank 0's
+    slot and signals (ranks > 0, one ws_peer_push launch) or waits, merges and
     returns (out, out_lse) (rank 0; None elsewhere).  Every rank must call
     ``step()`` once per step, in the same order.  The epoch is a launch
     argument, so steps are not replayable from a captured CUDA graph.
@@ -116,12 +117,21 @@ class PeerExchange:
         self.base = base.value
         self.epoch = 0
         self._closed = False
+        if rank != 0:
+            # ranks > 0: the decode writes here (local memory), ws_peer_push copies it into rank 0's slot
+            n = -(-(rows * dim + rows) // 64) * 64
+            self.block = torch.empty(n, dtype=torch.float32, device=self.device)
+            self.ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     def slot(self):
-        """(o, lse) device addresses where this rank's partial of the next step goes."""
+        """(o, lse) device addresses where this rank's decode writes its partial of the next
+        step: rank 0's own slot in its buffer (by the next epoch's parity), or, on other
+        ranks, a local block that step() pushes into rank 0's slot."""
         from ._lib import lib
-        off = lib().ws_peer_slot_offset(self.world, self.rows, self.dim, (self.epoch + 1) & 1, self.rank)
-        o = self.base + off
+        if self.rank != 0:
+            o = self.block.data_ptr()
+        else:
+            o = self.base + lib().ws_peer_slot_offset(self.world, self.rows, self.dim, (self.epoch + 1) & 1, 0)
         return o, o + 4 * self.rows * self.dim
 
     def step(self, out=None, out_lse=None, out_dtype=torch.bfloat16):
@@ -139,7 +149,8 @@ class PeerExchange:
                 check(lib().ws_peer_merge(self.base, self.world, self.rows, self.dim, e, out.data_ptr(), code,
                                           out_lse.data_ptr(), st), "ws_peer_merge")
             else:
-                check(lib().ws_peer_signal(self.base, self.rank, e, st), "ws_peer_signal")
+                check(lib().ws_peer_push(self.block.data_ptr(), self.base, self.world, self.rows, self.dim, self.rank,
+                                         e, self.ticket.data_ptr(), st), "ws_peer_push")
                 out = out_lse = None
         self.epoch = e
         return out, out_lse

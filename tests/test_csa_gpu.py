@@ -439,3 +439,35 @@ def test_workspace_pool_shared_with_gqa():
         ro, rm, rs = oracle.gqa_decode(oracle.bf16_bits(qg), oracle.bf16_bits(k), oracle.bf16_bits(v), 128 ** -0.5)
         assert np.abs((o / s).cpu().numpy() - ro).max() < TOL_OUT
         scope_b200.csa_attn.csa_sparse_decode(q.to(DEV), kv.to(DEV), idx.to(DEV), 0.05, sc.to(DEV))
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_split_merge_unaligned_output(out_dtype):
+    """Split partials are merged inside the decode launch when the output rows
+    take 16-byte stores; an output that starts off a 16-byte boundary goes
+    through the separate merge grid instead.  Both against the oracle, with the
+    workspace reused across the two."""
+    from scope_b200 import _lib
+    bs, nq, nc, k = 4, 64, 6000, 1500
+    q, kv, sc, idx = rand_case(bs, nq, nc, k, seed=88, int8=True, q_bf16=True)
+    L = _lib.lib()
+    qd, kvd, scd, idd = q.to(DEV), kv.to(DEV), sc.to(DEV), idx.to(DEV)
+    ro, rl, _ = oracle_of(q, kv, sc, 512 ** -0.5, idx=idx)
+    esz = 4 if out_dtype == torch.float32 else 2
+    for shift in (0, 1):   # elements: 0 -> aligned rows, 1 -> rows 4 or 2 bytes off a 16-byte boundary
+        buf = torch.full((bs * nq * 512 + 8,), float("nan"), dtype=out_dtype, device=DEV)
+        out = buf[shift:shift + bs * nq * 512]
+        lse = torch.empty(bs, nq, device=DEV)
+        ws = scope_b200._lib.workspaces.get(L.ws_csa_decode_workspace_size(bs, nq, _lib.WS_DTYPE_BF16), qd.device)
+        rc = L.ws_csa_decode(qd.data_ptr(), _lib.WS_DTYPE_BF16, bs, nq, 512, kvd.data_ptr(), _lib.WS_DTYPE_I8,
+                             scd.data_ptr(), nc, 0, idd.data_ptr(), k, _lib.WS_CSA_IDX_ALL, 0, 0, 512 ** -0.5,
+                             out.data_ptr(), _lib.WS_DTYPE_F32 if esz == 4 else _lib.WS_DTYPE_BF16, lse.data_ptr(),
+                             ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        if shift and rc != 0:   # the C ABI wants 16-byte aligned outputs: nothing to compare then
+            assert rc == _lib.WS_ERR_INVALID_ARG
+            continue
+        assert rc == 0, L.ws_last_error()
+        torch.cuda.synchronize()
+        assert np.abs(out.float().cpu().numpy().reshape(bs, nq, 512) - ro).max() < TOL_OUT
+        assert np.abs(lse.cpu().numpy() - rl).max() < TOL_LSE
+    assert scope_b200.status_take() == 0
