@@ -126,8 +126,13 @@ size_t ws_gqa_decode_workspace_size(int B_kv, int G, int Dv, int L) {
     B_kv = std::min(B_kv, kMaxGroupsPerLaunch);   // larger calls run in chunks of rows
     G = std::min(G, kMaxHeadsPerLaunch);          // and of 16 query heads
     const int64_t tiles = (int64_t)B_kv * ((L + 63) / 64);
-    const int nctas = (int)std::min<int64_t>(device_sm_count(), std::max<int64_t>(tiles, 1));
-    return gqa_workspace_bytes(G, Dv, B_kv, B_kv, nctas);
+    const int nsm = device_sm_count();
+    const int nctas = (int)std::min<int64_t>(nsm, std::max<int64_t>(tiles, 1));
+    // the fp32 path (same entry, WS_DTYPE_F32) splits each row over up to 2 x SMs / rows blocks of >= 256
+    // tokens, one slot of G x Dv + 2G floats each: size for that too, so its split is not cut short
+    const int64_t f32_splits = std::max<int64_t>(1, std::min<int64_t>((L + 255) / 256, (2 * nsm + B_kv - 1) / B_kv));
+    const size_t f32 = kCounterHeaderBytes + (size_t)B_kv * f32_splits * ((size_t)G * Dv + 2 * G) * sizeof(float);
+    return std::max(gqa_workspace_bytes(G, Dv, B_kv, B_kv, nctas), f32);
 }
 
 int ws_gqa_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_t,

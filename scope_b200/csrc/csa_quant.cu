@@ -7,7 +7,8 @@
 // inv = 127 / maxv (IEEE division); q = rne(x * inv), saturated to int8, or
 // rne(x * inv) + 128 saturated to uint8.  The int8 form also returns the
 // row sum of the quantised values (int32).
-// One warp per row, 8 elements per lane per step; HBM-bound.
+// One warp per row, 8 elements per lane per step (rows up to 512 wide are held
+// in registers and read once); HBM-bound.
 #include "common.cuh"
 #include "ws_internal.h"
 
@@ -30,23 +31,16 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_quant_s8_kernel(const _
     const int64_t row = (int64_t)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     if (row >= rows) return;
     const __nv_bfloat16* x = kv + row * hd;
-    float maxv = 0.f;
-    for (int d = lane * 8; d < hd; d += 256) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + d));
+    auto absmax8 = [](const uint4& v, float m) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const float2 f = __bfloat1622float2(h[u]);
-            maxv = fmaxf(maxv, fmaxf(fabsf(f.x), fabsf(f.y)));
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
         }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) maxv = fmaxf(maxv, __shfl_xor_sync(0xffffffffu, maxv, o));
-    float sc;
-    const float inv = row_scale_inv(maxv, &sc);
-    int32_t sum = 0;
-    for (int d = lane * 8; d < hd; d += 256) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + d));
+        return m;
+    };
+    auto quant8 = [&](const uint4& v, float inv, int d, int32_t& sum) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
         uint32_t packed[2] = {0u, 0u};
 #pragma unroll
@@ -58,6 +52,26 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_quant_s8_kernel(const _
             packed[u >> 1] |= ((uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8)) << ((u & 1) * 16);
         }
         *reinterpret_cast<uint2*>(out + row * hd + d) = make_uint2(packed[0], packed[1]);
+    };
+    float maxv = 0.f, sc, inv;
+    int32_t sum = 0;
+    if (hd <= 512) {
+        // the row stays in registers: two 16-byte loads per lane, issued together, read once
+        const int d0 = lane * 8, d1 = lane * 8 + 256;
+        const uint4 v0 = d0 < hd ? __ldg(reinterpret_cast<const uint4*>(x + d0)) : make_uint4(0, 0, 0, 0);
+        const uint4 v1 = d1 < hd ? __ldg(reinterpret_cast<const uint4*>(x + d1)) : make_uint4(0, 0, 0, 0);
+        maxv = absmax8(v1, absmax8(v0, 0.f));   // zero padding leaves the max unchanged
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) maxv = fmaxf(maxv, __shfl_xor_sync(0xffffffffu, maxv, o));
+        inv = row_scale_inv(maxv, &sc);
+        if (d0 < hd) quant8(v0, inv, d0, sum);
+        if (d1 < hd) quant8(v1, inv, d1, sum);
+    } else {
+        for (int d = lane * 8; d < hd; d += 256) maxv = absmax8(__ldg(reinterpret_cast<const uint4*>(x + d)), maxv);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) maxv = fmaxf(maxv, __shfl_xor_sync(0xffffffffu, maxv, o));
+        inv = row_scale_inv(maxv, &sc);
+        for (int d = lane * 8; d < hd; d += 256) quant8(__ldg(reinterpret_cast<const uint4*>(x + d)), inv, d, sum);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
