@@ -294,7 +294,7 @@ class GqaDense(Workload):
         rows = self.B * self.Hkv
         if self.world == 1:
             out, lse, mode = self.out.data_ptr(), self.lse.data_ptr(), self._lib.WS_OUT_NORM_BF16
-        elif self.exchange == "peer":   # this rank's partial goes straight into rank 0's slot (NVLink stores)
+        elif self.exchange == "peer":   # rank 0's own slot, or the local block that the push copies to rank 0
             (out, lse), mode = self.ex.slot(), self._lib.WS_OUT_NORM_F32
         else:
             out, lse, mode = self.part_o.data_ptr(), self.part_l.data_ptr(), self._lib.WS_OUT_NORM_F32
@@ -388,8 +388,8 @@ class GqaDense(Workload):
                 "l2": (f"inputs {2 * self.B * self.Hkv * self.Lloc * self.D * 2 / 1e9:.2f} GB per GPU > L2"
                        if self.copies == 1 else f"{self.copies} rotating input copies > 3x L2"),
                 "timing": "cuda-graph replay" if self.graph else "stream launches",
-                "exchange": {"peer": "partials stored by the decode into rank 0's IPC-mapped slots over NVLink, a "
-                                     "release flag per rank, rank 0's merge kernel after a bounded acquire wait",
+                "exchange": {"peer": "partials pushed into rank 0's IPC-mapped slots over NVLink (one launch per rank), "
+                                     "rank 0's merge kernel after a bounded acquire wait on the ranks' flags",
                              "nccl": "nccl all_gather of (o fp32, lse) + lse_merge kernel on every rank",
                              "none": "none"}[self.exchange]}
 
@@ -607,9 +607,10 @@ class Csa(Workload):
     profile_name = "csa_decode_cfg5"
     graph = True
 
-    def __init__(self, world, rank, bs=16, nH=64, nc=65536, k=2048, seed=5):
+    def __init__(self, world, rank, bs=16, nH=64, nc=65536, k=2048, seed=5, exchange="peer"):
         from scope_b200 import _lib
         self.world, self.rank = world, rank
+        self.exchange = exchange if world > 1 else "none"
         self.bs, self.nH, self.nc, self.k = bs, nH, nc, k
         self.scale = 512 ** -0.5
         self.workload = f"csa_ds4_b{bs}_h{nH}_nc{nc}_top{k}_int8"
@@ -650,9 +651,12 @@ class Csa(Workload):
             self.out = torch.empty(bs, nH, 512, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(bs, nH, dtype=torch.float32, device=dev)
         else:
-            from scope_b200.shard import PartialExchange
-            self.ex = PartialExchange(bs * nH, 512, world, dev)
-            self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
+            from scope_b200.shard import PartialExchange, PeerExchange
+            if self.exchange == "peer":
+                self.ex = PeerExchange(bs * nH, 512, world, rank, dev)
+            else:
+                self.ex = PartialExchange(bs * nH, 512, world, dev)
+                self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
             self.out = torch.empty(bs * nH, 512, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(bs * nH, dtype=torch.float32, device=dev)
         self.ws = torch.zeros(self.lib.ws_csa_decode_workspace_size(bs, nH, self._lib.WS_DTYPE_BF16),
@@ -728,22 +732,29 @@ class Csa(Workload):
         st = torch.cuda.current_stream().cuda_stream
         c, kvc = i % self.n_sets, i % self.n_kv
         if self.world == 1:
-            out, lse, odt, mode, lo = self.out, self.lse, self._lib.WS_DTYPE_BF16, self._lib.WS_CSA_IDX_ALL, 0
+            out, lse = self.out.data_ptr(), self.lse.data_ptr()
+            odt, mode, lo = self._lib.WS_DTYPE_BF16, self._lib.WS_CSA_IDX_ALL, 0
         else:
-            out, lse, odt, mode, lo = (self.part_o, self.part_l, self._lib.WS_DTYPE_F32,
-                                       self._lib.WS_CSA_IDX_SORTED_SHARD, self.lo)
+            out, lse = self.ex.slot() if self.exchange == "peer" else (self.part_o.data_ptr(), self.part_l.data_ptr())
+            odt, mode, lo = self._lib.WS_DTYPE_F32, self._lib.WS_CSA_IDX_SORTED_SHARD, self.lo
         kv = self.kv[kvc]
         rc = L_.ws_csa_decode(self.q[c].data_ptr(), self._lib.WS_DTYPE_BF16, self.bs, self.nH, 512, kv.data_ptr(),
                               self._lib.WS_DTYPE_I8, self.kv_scales[kvc].data_ptr(), kv.shape[1], lo,
-                              self.idx[c].data_ptr(), self.k, mode, 0, 0, self.scale, out.data_ptr(), odt,
-                              lse.data_ptr(), self.ws.data_ptr(), self.ws.numel(), st)
+                              self.idx[c].data_ptr(), self.k, mode, 0, 0, self.scale, out, odt,
+                              lse, self.ws.data_ptr(), self.ws.numel(), st)
         if rc != 0:
             raise RuntimeError(L_.ws_last_error().decode())
 
     def step(self, i):
         self.kernel(i)
-        if self.world > 1:
+        if self.exchange == "peer":
+            self.ex.step(out=self.out if self.rank == 0 else None, out_lse=self.lse if self.rank == 0 else None)
+        elif self.world > 1:
             self.ex.step(torch.bfloat16, out=self.out, out_lse=self.lse)
+
+    def close(self):
+        if self.exchange == "peer":
+            self.ex.close()
 
     def e2e_step(self, i):
         """Through the public API: q and the step's top-k ids come from host
@@ -755,6 +766,9 @@ class Csa(Workload):
         idx.copy_(self.idx_host, non_blocking=True)
         if self.world == 1:
             out, lse = csa_attn.csa_sparse_decode(q, self.kv[kvc], idx, self.scale, self.kv_scales[kvc])
+        elif self.exchange == "peer":   # the C-ABI decode into the exchange slot, then the exchange
+            self.step(i)
+            out, lse = self.out, self.lse
         else:
             po, pl = csa_attn.csa_sparse_decode(q, self.kv[kvc], idx, self.scale, self.kv_scales[kvc],
                                                 shard_lo=self.lo, idx_mode="sorted_shard", out_dtype=torch.float32)
@@ -780,7 +794,10 @@ class Csa(Workload):
                 "l2": (f"{self.n_sets} rotating top-k sets and q copies, {self.n_kv} KV shard copies "
                        f"({self.n_kv * self.kv[0].numel() / 2 ** 20:.0f} MiB) > 3x L2"),
                 "timing": "cuda-graph replay",
-                "exchange": "nccl all_gather of (o fp32, lse) + lse_merge kernel" if self.world > 1 else "none"}
+                "exchange": {"peer": "partials pushed into rank 0's IPC-mapped slots over NVLink (one launch per rank), "
+                                     "rank 0's merge kernel after a bounded acquire wait on the ranks' flags",
+                             "nccl": "nccl all_gather of (o fp32, lse) + lse_merge kernel",
+                             "none": "none"}[self.exchange]}
 
     def cpu_reference(self, budget_s, max_calls, warm=1):
         return cpu_ref_csa(self.bs, self.nH, self.nc, self.k, budget_s, max_calls, warm)
@@ -1055,7 +1072,7 @@ def make_workload(name, world, rank, args):
     if name == "mla_abs":
         return MlaAbsorbed(world, rank, S=args.kv_len or 16384)
     if name == "cfg5":
-        return Csa(world, rank, nc=args.kv_len or 65536, seed=SEEDS["cfg5"])
+        return Csa(world, rank, nc=args.kv_len or 65536, seed=SEEDS["cfg5"], exchange=args.exchange)
     if name == "idx":
         return Indexer(world, rank, nc=args.kv_len or 65536)
     raise ValueError(name)
@@ -1293,7 +1310,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
-                    help="cfg4 at N > 1: partials over NVLink peer stores to rank 0, or an NCCL all_gather")
+                    help="cfg4 / cfg5 at N > 1: partials pushed over NVLink to rank 0, or an NCCL all_gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -270,38 +270,33 @@ int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float*
  * Rank 0 allocates the exchange buffer (ws_peer_buffer_create: the one entry
  * point that allocates device memory; ws_peer_exchange_bytes gives its size)
  * and hands the 64-byte CUDA IPC handle to the other ranks, which map it with
- * ws_peer_buffer_open.  For step `epoch` (1, 2, ... in the same order on
- * every rank):
- *   - rank r's decode writes its partial -- o fp32 [rows, dim] normalised,
- *     then lse fp32 [rows] -- at base + ws_peer_slot_offset(world, rows, dim,
- *     epoch & 1, r) (for ws_gqa_decode: out_mode WS_OUT_NORM_F32, out at
- *     that address, out_lse right after the rows x dim floats);
- *   - ranks r > 0 then call ws_peer_signal(base, r, epoch): a release store of
- *     the epoch into rank 0's flag for r, then a bounded wait until rank 0 has
- *     merged step epoch - 1 (its buffer is the one the next step writes);
- *   - rank 0 calls ws_peer_merge(base, world, rows, dim, epoch, ...): a
- *     bounded wait for every flag, the log-sum-exp merge into out [rows, dim]
- *     (bf16 or fp32) and out_lse [rows], then "consumed = epoch".
- * A wait that gives up (2 s) records WS_ERR_DEVICE for ws_status_take; the
- * exchange must then be rebuilt.  Launches are asynchronous on `stream`; the
- * epoch is a launch argument, so a captured CUDA graph would replay a stale
- * epoch.  world <= 32, dim % 4 == 0.
+ * ws_peer_buffer_open.  Each rank's partial is o fp32 [rows, dim] normalised,
+ * then lse fp32 [rows] (for ws_gqa_decode: out_mode WS_OUT_NORM_F32, out_lse
+ * right after the rows x dim floats).  Per step, on every rank in the same order:
+ *   - rank 0's decode writes its partial at base + ws_peer_slot_offset(.., 0),
+ *     then ws_peer_merge: a bounded wait until every rank's flag reaches this
+ *     step, the log-sum-exp merge into out [rows, dim] (bf16 or fp32) and
+ *     out_lse [rows], then the step is published as consumed;
+ *   - rank r > 0's decode writes its partial to a local, 16-byte aligned block
+ *     (rounded up to a multiple of 64 floats), then ws_peer_push: a bounded
+ *     wait until rank 0 has consumed the previous step, the copy into rank r's
+ *     slot over NVLink, and the release of rank r's flag.  `state` is two
+ *     int64 words of rank r's memory, zeroed once (its step count and a ticket).
+ * The step counts live on the devices and every pointer is fixed, so the steps
+ * can be captured in a CUDA graph.  A wait that gives up (2 s) records
+ * WS_ERR_DEVICE for ws_status_take; the exchange must then be rebuilt.
+ * world <= 32, dim % 4 == 0.
  */
 size_t ws_peer_exchange_bytes(int world, int64_t rows, int dim);
-size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int parity, int rank);
+size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int rank);
 int ws_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle);
 int ws_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
 int ws_peer_buffer_close(void* dev_ptr);
 int ws_peer_buffer_free(void* dev_ptr);
-int ws_peer_signal(void* root_base, int rank, int64_t epoch, void* stream);
-/* Ranks > 0, the faster form: the decode writes its block ([rows, dim] o then
- * [rows] lse, 16-byte aligned) to local memory and ws_peer_push copies it into
- * rank 0's slot, then does what ws_peer_signal does, in one launch.  `ticket`
- * is one device int of this rank, zeroed once (the launch leaves it zero). */
-int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, int dim, int rank, int64_t epoch,
-                 int* ticket, void* stream);
-int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, int64_t epoch, void* out, int out_dtype,
-                  float* out_lse, void* stream);
+int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, int dim, int rank, int64_t* state,
+                 void* stream);
+int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, void* out, int out_dtype, float* out_lse,
+                  void* stream);
 
 /* ---- indexer top-k orders */
 #define WS_TOPK_BY_SCORE 0   /* descending score, ties: lower id first (the reference's partial_sort order) */

@@ -85,14 +85,13 @@ SIGNATURES = {
     "ws_indexer_topk_workspace_size": (_sz, [_i, _i64]),
     "ws_kv_append": (_i, [_V, _i64, _i64, _i64, _V, _i64, _i64, _i64, _i64, _i, _i, _i64, _V]),
     "ws_peer_exchange_bytes": (_sz, [_i, _i64, _i]),
-    "ws_peer_slot_offset": (_sz, [_i, _i64, _i, _i, _i]),
+    "ws_peer_slot_offset": (_sz, [_i, _i64, _i, _i]),
     "ws_peer_buffer_create": (_i, [_sz, ctypes.POINTER(_V), _V]),
     "ws_peer_buffer_open": (_i, [_V, ctypes.POINTER(_V)]),
     "ws_peer_buffer_close": (_i, [_V]),
     "ws_peer_buffer_free": (_i, [_V]),
-    "ws_peer_signal": (_i, [_V, _i, _i64, _V]),
-    "ws_peer_push": (_i, [_V, _V, _i, _i64, _i, _i, _i64, _V, _V]),
-    "ws_peer_merge": (_i, [_V, _i, _i64, _i, _i64, _V, _i, _V, _V]),
+    "ws_peer_push": (_i, [_V, _V, _i, _i64, _i, _i, _V, _V]),
+    "ws_peer_merge": (_i, [_V, _i, _i64, _i, _V, _i, _V, _V]),
 }
 
 _lib = None

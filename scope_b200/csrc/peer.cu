@@ -3,24 +3,26 @@
 // The reference's runtimes merge the partials of their KV shares on the host
 // (system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464); across
 // GPUs of one box the merge input is each rank's (o fp32, lse fp32) block.
-// Instead of an all_gather collective, every rank's decode kernel writes its
-// block straight into rank 0's receive slot (rank 0's buffer is mapped into
-// every rank's address space with CUDA IPC, so the epilogue's stores cross
-// NVLink), then:
-//   * ranks 1..N-1 run peer_signal_kernel: a system-scope fence, then the step's
-//     epoch stored with release semantics into rank 0's flag word for that rank;
-//     it then waits (bounded) until rank 0 has consumed the step before last,
-//     whose buffer the next step's decode overwrites (two buffers, by epoch
-//     parity);
+// Instead of an all_gather collective, rank 0's buffer is mapped into every
+// rank's address space with CUDA IPC, and per step:
+//   * every rank's decode writes its block: rank 0 straight into its own slot,
+//     the other ranks into a local block;
+//   * ranks 1..N-1 run peer_push_kernel: wait (bounded) until rank 0 has merged
+//     the previous step (its slot is free again), copy the block into rank 0's
+//     slot with 16-byte stores over NVLink, fence at system scope, and the CTA
+//     that takes the last ticket stores this step's epoch into rank 0's flag
+//     word for the rank with release semantics;
 //   * rank 0 runs peer_merge_kernel: each CTA waits (bounded, acquire loads)
 //     for every rank's flag to reach the epoch, merges its rows by log-sum-exp
 //     from the slots, and the CTA that takes the last ticket publishes the
 //     epoch as consumed.
+// The epochs live on the devices -- each rank's push counts its own steps in
+// its state word, rank 0's merge counts through `consumed` -- and every
+// pointer is fixed, so a captured CUDA graph may replay the steps.
 // Buffer layout (rank 0's allocation): a 1 KB control block -- flags[64]
-// (int64, one per rank), consumed (int64), the CTA ticket (int32), the last
-// epoch whose merge gave up (int64) -- then
-// 2 x world slots of slot_floats floats each, slot (parity, rank) holding
-// o [rows, dim] then lse [rows].
+// (int64, one per rank), consumed (int64), the merge's CTA ticket (int32), the
+// last epoch whose merge gave up (int64) -- then `world` slots of slot_floats
+// floats each, slot r holding o [rows, dim] then lse [rows].
 // Every wait gives up after kWaitNs, records kDevTimeout in the status word
 // and skips its work; the exchange is then unusable and must be rebuilt.
 // No cluster multicast and no multimem: plain stores and loads only.
@@ -54,60 +56,53 @@ __device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
 // block start 16-byte aligned
 inline int64_t slot_floats(int64_t rows, int dim) { return (int64_t)align_up((size_t)(rows * dim + rows), 64); }
 
-__global__ void peer_signal_kernel(int64_t* root_ctrl, int rank, int64_t epoch, int* status) {
-    if (threadIdx.x != 0) return;
-    // this rank's block was written by the previous kernel on the stream (complete at its boundary); the
-    // fence orders those stores before the flag for any observer on another GPU
-    __threadfence_system();
-    st_release_sys(root_ctrl + rank, epoch);
-    // the next step writes the buffer of epoch - 1: wait until rank 0 has merged that step
-    const int64_t need = epoch - 1;
-    if (need <= 0) return;
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_sys(root_ctrl + kConsumed) < need) {
-        if (globaltimer_ns() - t0 > kWaitNs) {
-            atomicExch(status, kDevTimeout);
-            return;
-        }
-        __nanosleep(256);
-    }
-}
-
-// Ranks > 0: copy this rank's block (written locally by its decode) into rank 0's slot with 16-byte
-// stores spread over the grid, then the CTA that takes the last ticket publishes the epoch and waits for
-// rank 0 to have consumed epoch - 1 (as peer_signal_kernel does).  Keeping the decode's own stores local
-// matters: its merge tickets fence every prior store, and a fence behind stores to another GPU waits for
-// the NVLink round trip.
+// Ranks > 0, one launch per step: wait until rank 0 has consumed the previous step (the slot is free), copy
+// this rank's block (written locally by its decode) into rank 0's slot with 16-byte stores spread over the
+// grid, then the CTA that takes the last ticket advances this rank's epoch and publishes it as the rank's
+// flag.  state: [0] this rank's epoch (int64), [1] the CTA ticket (int32).  Keeping the decode's own stores
+// local matters: its merge tickets fence every prior store, and a fence behind stores to another GPU waits
+// for the NVLink round trip.
 __global__ void __launch_bounds__(256) peer_push_kernel(const float4* __restrict__ src, float4* dst, int64_t n16,
-                                                        int64_t* root_ctrl, int* ticket, int rank, int64_t epoch,
-                                                        int* status) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
-        dst[i] = __ldcg(src + i);
+                                                        int64_t* root_ctrl, int64_t* state, int rank, int* status) {
+    __shared__ int s_go;
+    const int64_t epoch = state[0] + 1;   // the last CTA advances it only after every CTA has read it
+    if (threadIdx.x == 0) {
+        int go = 1;
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_sys(root_ctrl + kConsumed) < epoch - 1) {
+            if (globaltimer_ns() - t0 > kWaitNs) {
+                atomicExch(status, kDevTimeout);
+                go = 0;
+                break;
+            }
+            __nanosleep(128);
+        }
+        s_go = go;
+    }
+    __syncthreads();
+    if (s_go)
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+            dst[i] = __ldcg(src + i);
     __threadfence_system();   // every thread's copies are performed before its CTA takes the ticket
     __syncthreads();
     if (threadIdx.x != 0) return;
+    int* ticket = reinterpret_cast<int*>(state + 1);
     if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
     atomicExch(ticket, 0);
+    state[0] = epoch;
     __threadfence_system();
     st_release_sys(root_ctrl + rank, epoch);
-    const int64_t need = epoch - 1;
-    if (need <= 0) return;
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_sys(root_ctrl + kConsumed) < need) {
-        if (globaltimer_ns() - t0 > kWaitNs) {
-            atomicExch(status, kDevTimeout);
-            return;
-        }
-        __nanosleep(256);
-    }
 }
 
 template <bool OUT_BF16>
 __global__ void __launch_bounds__(32 * kRowsPerCta) peer_merge_kernel(const float* __restrict__ slots,
                                                                       int64_t slot_stride, int P, int64_t R, int D,
-                                                                      int64_t* ctrl, int64_t epoch, void* out,
-                                                                      float* out_lse, int* status) {
+                                                                      int64_t* ctrl, void* out, float* out_lse,
+                                                                      int* status) {
     __shared__ int s_ok;
+    // this step's epoch: one past the last consumed one (the last CTA advances `consumed` only after every
+    // CTA has read it)
+    const int64_t epoch = *reinterpret_cast<volatile int64_t*>(ctrl + kConsumed) + 1;
     if (threadIdx.x == 0) {
         int ok = 1;
         const uint64_t t0 = globaltimer_ns();
@@ -185,11 +180,12 @@ extern "C" {
 
 size_t ws_peer_exchange_bytes(int world, int64_t rows, int dim) {
     if (world < 1 || world > kMaxRanks || rows < 0 || dim < 1) return 0;
-    return kCtrlBytes + 2 * (size_t)world * (size_t)slot_floats(rows, dim) * sizeof(float);
+    return kCtrlBytes + (size_t)world * (size_t)slot_floats(rows, dim) * sizeof(float);
 }
 
-size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int parity, int rank) {
-    return kCtrlBytes + ((size_t)(parity & 1) * world + (size_t)rank) * (size_t)slot_floats(rows, dim) * sizeof(float);
+size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int rank) {
+    (void)world;
+    return kCtrlBytes + (size_t)rank * (size_t)slot_floats(rows, dim) * sizeof(float);
 }
 
 int ws_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle) {
@@ -226,53 +222,41 @@ int ws_peer_buffer_free(void* dev_ptr) {
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
-int ws_peer_signal(void* root_base, int rank, int64_t epoch, void* stream) {
-    if (!root_base || rank < 1 || rank >= kMaxRanks || epoch < 1)
-        return set_error(WS_ERR_INVALID_ARG, "peer_signal: bad argument");
-    peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int64_t*>(root_base), rank,
-                                                                       epoch, device_status_word());
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
-}
-
-int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, int dim, int rank, int64_t epoch,
-                 int* ticket, void* stream) {
-    if (!block || !root_base || !ticket || rank < 1 || rank >= world || world > kMaxRanks || rows < 0 || dim < 1 ||
-        epoch < 1)
+int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, int dim, int rank, int64_t* state,
+                 void* stream) {
+    if (!block || !root_base || !state || rank < 1 || rank >= world || world > kMaxRanks || rows < 0 || dim < 1)
         return set_error(WS_ERR_INVALID_ARG, "peer_push: bad argument");
-    if (reinterpret_cast<uintptr_t>(block) % 16) return set_error(WS_ERR_INVALID_ARG, "peer_push: block must be 16-byte aligned");
-    const int64_t floats = rows * dim + rows;
-    const int64_t n16 = (floats + 3) / 4;   // the slot holds slot_floats >= floats rounded up to 64
-    float4* dst = reinterpret_cast<float4*>(static_cast<uint8_t*>(root_base) +
-                                            ws_peer_slot_offset(world, rows, dim, (int)(epoch & 1), rank));
+    if (reinterpret_cast<uintptr_t>(block) % 16 || reinterpret_cast<uintptr_t>(state) % 8)
+        return set_error(WS_ERR_INVALID_ARG, "peer_push: block must be 16-byte and state 8-byte aligned");
+    const int64_t n16 = (rows * dim + rows + 3) / 4;   // the block and the slot are rounded up to 64 floats
+    float4* dst = reinterpret_cast<float4*>(static_cast<uint8_t*>(root_base) + ws_peer_slot_offset(world, rows, dim, rank));
     const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(128, (n16 + 255) / 256));
     peer_push_kernel<<<ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const float4*>(block), dst, n16, static_cast<int64_t*>(root_base), ticket, rank, epoch,
+        reinterpret_cast<const float4*>(block), dst, n16, static_cast<int64_t*>(root_base), state, rank,
         device_status_word());
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
-int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, int64_t epoch, void* out, int out_dtype,
-                  float* out_lse, void* stream) {
-    if (!root_base || world < 1 || world > 32 || rows < 0 || dim < 4 || dim % 4 || epoch < 1 || (rows > 0 && !out))
+int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, void* out, int out_dtype, float* out_lse,
+                  void* stream) {
+    if (!root_base || world < 1 || world > 32 || rows < 0 || dim < 4 || dim % 4 || (rows > 0 && !out))
         return set_error(WS_ERR_INVALID_ARG, "peer_merge: bad argument (world <= 32, dim % 4 == 0)");
     if (out_dtype != WS_DTYPE_BF16 && out_dtype != WS_DTYPE_F32)
         return set_error(WS_ERR_INVALID_ARG, "peer_merge: out dtype");
     if (reinterpret_cast<uintptr_t>(out) % 16) return set_error(WS_ERR_INVALID_ARG, "peer_merge: out must be 16-byte aligned");
     const int64_t sf = slot_floats(rows, dim);
-    const float* slots = reinterpret_cast<const float*>(static_cast<uint8_t*>(root_base) +
-                                                        ws_peer_slot_offset(world, rows, dim, (int)(epoch & 1), 0));
+    const float* slots = reinterpret_cast<const float*>(static_cast<uint8_t*>(root_base) + kCtrlBytes);
     const int64_t ctas = std::max<int64_t>(1, (rows + kRowsPerCta - 1) / kRowsPerCta);
     if (ctas > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "peer_merge: too many rows");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int64_t* ctrl = static_cast<int64_t*>(root_base);
     if (out_dtype == WS_DTYPE_BF16)
-        peer_merge_kernel<true><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, epoch,
-                                                                          out, out_lse, device_status_word());
+        peer_merge_kernel<true><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, out,
+                                                                          out_lse, device_status_word());
     else
-        peer_merge_kernel<false><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, epoch,
-                                                                           out, out_lse, device_status_word());
+        peer_merge_kernel<false><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, out,
+                                                                           out_lse, device_status_word());
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }

@@ -82,16 +82,17 @@ class PartialExchange:
 
 class PeerExchange:
     """The exchange over NVLink peer memory: rank 0 gathers, merges and holds
-    the result (see ws_peer_merge in include/scope_b200.h).
+    the result (ws_peer_push / ws_peer_merge in include/scope_b200.h).
 
     Rank 0 allocates the buffer and broadcasts its CUDA IPC handle; the other
     ranks map it.  Before a step, a rank's decode writes its partial at
     ``slot()`` -- (o pointer, lse pointer): rank 0's own slot, or a local
     block on the other ranks -- then ``step()`` pushes the block into rank 0's
-    slot and signals (ranks > 0, one ws_peer_push launch) or waits, merges and
-    returns (out, out_lse) (rank 0; None elsewhere).  Every rank must call
-    ``step()`` once per step, in the same order.  The epoch is a launch
-    argument, so steps are not replayable from a captured CUDA graph.
+    slot and raises the rank's flag (ranks > 0, one launch) or waits for every
+    flag, merges and returns (out, out_lse) (rank 0; None elsewhere).  Every
+    rank must call ``step()`` once per step, in the same order.  The step
+    counts live on the devices and the pointers never change, so the steps may
+    be captured in a CUDA graph.
     """
 
     def __init__(self, rows: int, dim: int, world: int, rank: int, device, group=None):
@@ -115,29 +116,25 @@ class PeerExchange:
                 check(L.ws_peer_buffer_open(ctypes.create_string_buffer(objs[0], 64), ctypes.byref(base)),
                       "ws_peer_buffer_open")
         self.base = base.value
-        self.epoch = 0
         self._closed = False
         if rank != 0:
-            # ranks > 0: the decode writes here (local memory), ws_peer_push copies it into rank 0's slot
+            # the decode writes here (local memory); ws_peer_push copies it into rank 0's slot
             n = -(-(rows * dim + rows) // 64) * 64
             self.block = torch.empty(n, dtype=torch.float32, device=self.device)
-            self.ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.state = torch.zeros(2, dtype=torch.int64, device=self.device)   # step count, CTA ticket
 
     def slot(self):
-        """(o, lse) device addresses where this rank's decode writes its partial of the next
-        step: rank 0's own slot in its buffer (by the next epoch's parity), or, on other
-        ranks, a local block that step() pushes into rank 0's slot."""
+        """(o, lse) device addresses where this rank's decode writes its partial."""
         from ._lib import lib
         if self.rank != 0:
             o = self.block.data_ptr()
         else:
-            o = self.base + lib().ws_peer_slot_offset(self.world, self.rows, self.dim, (self.epoch + 1) & 1, 0)
+            o = self.base + lib().ws_peer_slot_offset(self.world, self.rows, self.dim, 0)
         return o, o + 4 * self.rows * self.dim
 
     def step(self, out=None, out_lse=None, out_dtype=torch.bfloat16):
         from . import _lib
         from ._lib import check, lib, stream_ptr
-        e = self.epoch + 1
         with torch.cuda.device(self.device):
             st = stream_ptr(self.device)
             if self.rank == 0:
@@ -146,14 +143,12 @@ class PeerExchange:
                 if out_lse is None:
                     out_lse = torch.empty(self.rows, dtype=torch.float32, device=self.device)
                 code = _lib.WS_DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.WS_DTYPE_F32
-                check(lib().ws_peer_merge(self.base, self.world, self.rows, self.dim, e, out.data_ptr(), code,
+                check(lib().ws_peer_merge(self.base, self.world, self.rows, self.dim, out.data_ptr(), code,
                                           out_lse.data_ptr(), st), "ws_peer_merge")
-            else:
-                check(lib().ws_peer_push(self.block.data_ptr(), self.base, self.world, self.rows, self.dim, self.rank,
-                                         e, self.ticket.data_ptr(), st), "ws_peer_push")
-                out = out_lse = None
-        self.epoch = e
-        return out, out_lse
+                return out, out_lse
+            check(lib().ws_peer_push(self.block.data_ptr(), self.base, self.world, self.rows, self.dim, self.rank,
+                                     self.state.data_ptr(), st), "ws_peer_push")
+        return None, None
 
     def close(self) -> None:
         """Collective: unmap on ranks > 0, then free on rank 0."""

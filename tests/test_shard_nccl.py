@@ -216,9 +216,10 @@ def test_sharded_caches_decode_over_nccl():
     assert np.abs(ml - (mrm + np.log(mrs))).max() < TOL_LSE
 
 
-def _peer_rank(rank, port, qs, ks, vs, scale):
-    """Steps of a sharded GQA decode whose partials go over NVLink peer stores
-    into rank 0's slots (PeerExchange); rank 0 returns every step's merge."""
+def _peer_rank(rank, port, qs, ks, vs, scale, n_graph=3):
+    """Steps of a sharded GQA decode whose partials go over NVLink into rank 0's
+    slots (PeerExchange): eager steps, then replays of a captured CUDA graph of
+    decode + exchange; rank 0 returns every step's merge."""
     import torch.distributed as dist
 
     import scope_b200
@@ -237,18 +238,43 @@ def _peer_rank(rank, port, qs, ks, vs, scale):
         L_ = _lib.lib()
         ws = torch.zeros(L_.ws_gqa_decode_workspace_size(rows, G, D, hi - lo), dtype=torch.uint8, device=dev)
         outs = []
-        for q, k, v in zip(qs, ks, vs):   # back to back on one stream, no host synchronisation between steps
-            qd = q.to(dev)
-            kd, vd = k[:, lo:hi].contiguous().to(dev), v[:, lo:hi].contiguous().to(dev)
+        # static buffers: the first steps run eagerly, the last ones replay a captured CUDA graph of the same
+        # decode + exchange after their inputs are copied in (the exchange counts its steps on the devices)
+        qd = torch.empty_like(qs[0], device=dev)
+        kd = torch.empty(rows, hi - lo, D, dtype=torch.bfloat16, device=dev)
+        vd = torch.empty_like(kd)
+        out0 = torch.empty(rows * G, D, dtype=torch.bfloat16, device=dev)
+        lse0 = torch.empty(rows * G, dtype=torch.float32, device=dev)
+
+        def one_step():
             o_ptr, l_ptr = ex.slot()
             rc = L_.ws_gqa_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kd.stride(0), kd.stride(1),
                                   vd.stride(0), vd.stride(1), rows, G, D, D, hi - lo, scale, _lib.WS_DTYPE_BF16,
                                   _lib.WS_OUT_NORM_F32, o_ptr, None, None, l_ptr, ws.data_ptr(), ws.numel(),
                                   torch.cuda.current_stream().cuda_stream)
             assert rc == 0, L_.ws_last_error()
-            out, lse = ex.step()
+            ex.step(out=out0 if rank == 0 else None, out_lse=lse0 if rank == 0 else None)
+
+        n_eager = len(qs) - n_graph
+        graph = None
+        for s, (q, k, v) in enumerate(zip(qs, ks, vs)):
+            qd.copy_(q)
+            kd.copy_(k[:, lo:hi])
+            vd.copy_(v[:, lo:hi])
+            if s < n_eager:   # back to back on one stream, no host synchronisation between steps
+                one_step()
+            else:
+                if graph is None:
+                    torch.cuda.synchronize()
+                    side = torch.cuda.Stream()
+                    side.wait_stream(torch.cuda.current_stream())
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=side):
+                        one_step()   # captured, not run
+                    torch.cuda.synchronize()
+                graph.replay()
             if rank == 0:
-                outs.append((out.float(), lse.clone()))
+                outs.append((out0.float().clone(), lse0.clone()))
         torch.cuda.synchronize()
         status = scope_b200.status_take()
         ex.close()
@@ -262,7 +288,7 @@ def _peer_rank(rank, port, qs, ks, vs, scale):
 def test_peer_exchange_steps():
     import oracle
     g = torch.Generator().manual_seed(53)
-    rows, G, D, L, steps = 8, 8, 128, 6001, 5
+    rows, G, D, L, steps = 8, 8, 128, 6001, 7   # 4 eager steps, then 3 replays of a captured graph
     qs = [torch.randn(rows, G, D, generator=g).bfloat16() for _ in range(steps)]
     ks = [torch.randn(rows, L, D, generator=g).bfloat16() for _ in range(steps)]
     vs = [torch.randn(rows, L, D, generator=g).bfloat16() for _ in range(steps)]
