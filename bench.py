@@ -254,9 +254,11 @@ class GqaDense(Workload):
             self.out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(B, H, dtype=torch.float32, device=dev)
         else:
-            from scope_b200.shard import PartialExchange, PeerExchange
+            from scope_b200.shard import PartialExchange, PeerExchange, ScatterExchange
             if self.exchange == "peer":
                 self.ex = PeerExchange(B * H, D, world, rank, dev)
+            elif self.exchange == "scatter":
+                self.ex = ScatterExchange(B * H, D, world, rank, dev)
             else:
                 self.ex = PartialExchange(B * H, D, world, dev)
                 self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
@@ -294,7 +296,7 @@ class GqaDense(Workload):
         rows = self.B * self.Hkv
         if self.world == 1:
             out, lse, mode = self.out.data_ptr(), self.lse.data_ptr(), self._lib.WS_OUT_NORM_BF16
-        elif self.exchange == "peer":   # rank 0's own slot, or the local block that the push copies to rank 0
+        elif self.exchange in ("peer", "scatter"):   # rank 0's own slot, or a local block the exchange copies
             (out, lse), mode = self.ex.slot(), self._lib.WS_OUT_NORM_F32
         else:
             out, lse, mode = self.part_o.data_ptr(), self.part_l.data_ptr(), self._lib.WS_OUT_NORM_F32
@@ -305,15 +307,19 @@ class GqaDense(Workload):
         if rc != 0:
             raise RuntimeError(L_.ws_last_error().decode())
 
-    def step(self, i):
-        self.kernel(i)
-        if self.exchange == "peer":
+    def exchange_step(self, i):
+        """The exchange of one step alone (N > 1): the partials already sit in their blocks."""
+        if self.exchange in ("peer", "scatter"):
             self.ex.step(out=self.out if self.rank == 0 else None, out_lse=self.lse if self.rank == 0 else None)
         elif self.world > 1:
             self.ex.step(torch.bfloat16, out=self.out, out_lse=self.lse)
 
+    def step(self, i):
+        self.kernel(i)
+        self.exchange_step(i)
+
     def close(self):
-        if self.exchange == "peer":
+        if self.exchange in ("peer", "scatter"):
             self.ex.close()
 
     def e2e_step(self, i):
@@ -390,6 +396,8 @@ class GqaDense(Workload):
                 "timing": "cuda-graph replay" if self.graph else "stream launches",
                 "exchange": {"peer": "partials pushed into rank 0's IPC-mapped slots over NVLink (one launch per rank), "
                                      "rank 0's merge kernel after a bounded acquire wait on the ranks' flags",
+                             "scatter": "each rank merges its share of the rows from its peers' copies (IPC-mapped "
+                                        "buffers over NVLink) and stores the merged share in rank 0's gather area",
                              "nccl": "nccl all_gather of (o fp32, lse) + lse_merge kernel on every rank",
                              "none": "none"}[self.exchange]}
 
@@ -651,9 +659,11 @@ class Csa(Workload):
             self.out = torch.empty(bs, nH, 512, dtype=torch.bfloat16, device=dev)
             self.lse = torch.empty(bs, nH, dtype=torch.float32, device=dev)
         else:
-            from scope_b200.shard import PartialExchange, PeerExchange
+            from scope_b200.shard import PartialExchange, PeerExchange, ScatterExchange
             if self.exchange == "peer":
                 self.ex = PeerExchange(bs * nH, 512, world, rank, dev)
+            elif self.exchange == "scatter":
+                self.ex = ScatterExchange(bs * nH, 512, world, rank, dev)
             else:
                 self.ex = PartialExchange(bs * nH, 512, world, dev)
                 self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
@@ -735,7 +745,8 @@ class Csa(Workload):
             out, lse = self.out.data_ptr(), self.lse.data_ptr()
             odt, mode, lo = self._lib.WS_DTYPE_BF16, self._lib.WS_CSA_IDX_ALL, 0
         else:
-            out, lse = self.ex.slot() if self.exchange == "peer" else (self.part_o.data_ptr(), self.part_l.data_ptr())
+            out, lse = (self.ex.slot() if self.exchange in ("peer", "scatter")
+                        else (self.part_o.data_ptr(), self.part_l.data_ptr()))
             odt, mode, lo = self._lib.WS_DTYPE_F32, self._lib.WS_CSA_IDX_SORTED_SHARD, self.lo
         kv = self.kv[kvc]
         rc = L_.ws_csa_decode(self.q[c].data_ptr(), self._lib.WS_DTYPE_BF16, self.bs, self.nH, 512, kv.data_ptr(),
@@ -745,15 +756,19 @@ class Csa(Workload):
         if rc != 0:
             raise RuntimeError(L_.ws_last_error().decode())
 
-    def step(self, i):
-        self.kernel(i)
-        if self.exchange == "peer":
+    def exchange_step(self, i):
+        """The exchange of one step alone (N > 1): the partials already sit in their blocks."""
+        if self.exchange in ("peer", "scatter"):
             self.ex.step(out=self.out if self.rank == 0 else None, out_lse=self.lse if self.rank == 0 else None)
         elif self.world > 1:
             self.ex.step(torch.bfloat16, out=self.out, out_lse=self.lse)
 
+    def step(self, i):
+        self.kernel(i)
+        self.exchange_step(i)
+
     def close(self):
-        if self.exchange == "peer":
+        if self.exchange in ("peer", "scatter"):
             self.ex.close()
 
     def e2e_step(self, i):
@@ -766,7 +781,7 @@ class Csa(Workload):
         idx.copy_(self.idx_host, non_blocking=True)
         if self.world == 1:
             out, lse = csa_attn.csa_sparse_decode(q, self.kv[kvc], idx, self.scale, self.kv_scales[kvc])
-        elif self.exchange == "peer":   # the C-ABI decode into the exchange slot, then the exchange
+        elif self.exchange in ("peer", "scatter"):   # the C-ABI decode into the exchange slot, then the exchange
             self.step(i)
             out, lse = self.out, self.lse
         else:
@@ -796,6 +811,8 @@ class Csa(Workload):
                 "timing": "cuda-graph replay",
                 "exchange": {"peer": "partials pushed into rank 0's IPC-mapped slots over NVLink (one launch per rank), "
                                      "rank 0's merge kernel after a bounded acquire wait on the ranks' flags",
+                             "scatter": "each rank merges its share of the rows from its peers' copies (IPC-mapped "
+                                        "buffers over NVLink) and stores the merged share in rank 0's gather area",
                              "nccl": "nccl all_gather of (o fp32, lse) + lse_merge kernel",
                              "none": "none"}[self.exchange]}
 
@@ -1309,8 +1326,9 @@ def main():
     ap.add_argument("--kv-len", type=int, default=0, help="override KV length (profiling on a small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
-                    help="cfg4 / cfg5 at N > 1: partials pushed over NVLink to rank 0, or an NCCL all_gather")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "scatter", "nccl"],
+                    help="cfg4 / cfg5 at N > 1: partials pushed over NVLink to rank 0 (peer), merged in shares "
+                         "by every rank and gathered on rank 0 (scatter), or an NCCL all_gather (nccl)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1342,6 +1360,9 @@ def main():
         t_step, n_timed = time_steps(wl, wl.step, args.steps, args.warmup, world)
     clocks = clk.summary()
     t_e2e = time_e2e(wl, min(args.steps, 500), args.warmup, world)
+    # N > 1: the exchange alone (push + merge, or all_gather + merge), every rank in step
+    t_ex = (time_steps(wl, wl.exchange_step, min(args.steps, 200), args.warmup, world)[0]
+            if world > 1 and hasattr(wl, "exchange_step") else None)
 
     hbm, peak_src = peaks()
     kb = wl.kernel_bytes()
@@ -1372,6 +1393,8 @@ def main():
                 "clocks": clocks, "cpu_baseline": cpu}
         if parity is not None:
             line["parity"] = parity
+        if t_ex is not None:
+            line["exchange_us"] = t_ex * 1e6
         print(json.dumps(line), flush=True)
     if hasattr(wl, "close"):
         wl.close()

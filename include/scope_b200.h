@@ -298,6 +298,35 @@ int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, i
 int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, void* out, int out_dtype, float* out_lse,
                   void* stream);
 
+/*
+ * The same exchange in scatter-merge form, for partials large against the
+ * NVLink time of one block: every rank owns the contiguous share of rows
+ * [rows*q/world, rows*(q+1)/world) and merges it, so a rank sends and receives
+ * (world - 1) / world of one block, and only the merged shares (in the out
+ * dtype) travel to rank 0, which returns the whole result.
+ * Every rank allocates ws_peer_rs_bytes(world, rows, dim) with
+ * ws_peer_buffer_create, the ranks exchange their IPC handles, and each maps
+ * every other rank's buffer with ws_peer_buffer_open.  `bases` is a device
+ * array of `world` int64 addresses, entry q this rank's address of rank q's
+ * buffer (its own at entry `rank`).  Per step, on every rank in the same order:
+ * the decode writes this rank's partial into a local 16-byte aligned `block`
+ * (o fp32 [rows, dim] normalised, then lse [rows]); ws_peer_rs_scatter (a
+ * bounded wait until every peer has read the previous step, the copies, the
+ * release of this rank's flag in every peer's buffer); ws_peer_rs_merge (a
+ * bounded wait for every flag, the log-sum-exp merge of this rank's share;
+ * rank 0 writes out [rows, dim] (bf16 or fp32, the same out_dtype on every
+ * rank) and out_lse [rows] (may be NULL), the other ranks ignore out).
+ * `state` is two int64 words of this rank's memory, zeroed once.  The step
+ * counts live on the devices, so the steps can be captured in a CUDA graph.
+ * A wait that gives up (2 s) records WS_ERR_DEVICE; the exchange must then be
+ * rebuilt.  world <= 32, dim % 4 == 0.
+ */
+size_t ws_peer_rs_bytes(int world, int64_t rows, int dim);
+int ws_peer_rs_scatter(const float* block, const int64_t* bases, int world, int64_t rows, int dim, int rank,
+                       int64_t* state, void* stream);
+int ws_peer_rs_merge(const float* block, const int64_t* bases, int world, int64_t rows, int dim, int rank,
+                     const int64_t* state, void* out, int out_dtype, float* out_lse, void* stream);
+
 /* ---- indexer top-k orders */
 #define WS_TOPK_BY_SCORE 0   /* descending score, ties: lower id first (the reference's partial_sort order) */
 #define WS_TOPK_BY_ID 1      /* ascending id: the layout WS_CSA_IDX_SORTED_SHARD wants */

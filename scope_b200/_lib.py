@@ -92,6 +92,9 @@ SIGNATURES = {
     "ws_peer_buffer_free": (_i, [_V]),
     "ws_peer_push": (_i, [_V, _V, _i, _i64, _i, _i, _V, _V]),
     "ws_peer_merge": (_i, [_V, _i, _i64, _i, _V, _i, _V, _V]),
+    "ws_peer_rs_bytes": (_sz, [_i, _i64, _i]),
+    "ws_peer_rs_scatter": (_i, [_V, _V, _i, _i64, _i, _i, _V, _V]),
+    "ws_peer_rs_merge": (_i, [_V, _V, _i, _i64, _i, _i, _V, _V, _i, _V, _V]),
 }
 
 _lib = None

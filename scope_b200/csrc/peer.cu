@@ -27,6 +27,7 @@
 // and skips its work; the exchange is then unusable and must be rebuilt.
 // No cluster multicast and no multimem: plain stores and loads only.
 #include <cstdio>
+#include <type_traits>
 
 #include "common.cuh"
 #include "ws_internal.h"
@@ -59,19 +60,22 @@ inline int64_t slot_floats(int64_t rows, int dim) { return (int64_t)align_up((si
 // Ranks > 0, one launch per step: wait until rank 0 has consumed the previous step (the slot is free), copy
 // this rank's block (written locally by its decode) into rank 0's slot with 16-byte stores spread over the
 // grid, then the CTA that takes the last ticket advances this rank's epoch and publishes it as the rank's
-// flag.  state: [0] this rank's epoch (int64), [1] the CTA ticket (int32).  Keeping the decode's own stores
+// flag (not when a CTA gave up waiting).  state: [0] this rank's epoch (int64), [1] the CTA ticket and the
+// last epoch a CTA gave up in (int32 each).  Keeping the decode's own stores
 // local matters: its merge tickets fence every prior store, and a fence behind stores to another GPU waits
 // for the NVLink round trip.
 __global__ void __launch_bounds__(256) peer_push_kernel(const float4* __restrict__ src, float4* dst, int64_t n16,
                                                         int64_t* root_ctrl, int64_t* state, int rank, int* status) {
     __shared__ int s_go;
     const int64_t epoch = state[0] + 1;   // the last CTA advances it only after every CTA has read it
+    int* ticket = reinterpret_cast<int*>(state + 1);   // [0] the CTA ticket, [1] the last step a CTA gave up in
     if (threadIdx.x == 0) {
         int go = 1;
         const uint64_t t0 = globaltimer_ns();
         while (ld_acquire_sys(root_ctrl + kConsumed) < epoch - 1) {
             if (globaltimer_ns() - t0 > kWaitNs) {
                 atomicExch(status, kDevTimeout);
+                atomicExch(ticket + 1, (int)epoch);
                 go = 0;
                 break;
             }
@@ -86,10 +90,10 @@ __global__ void __launch_bounds__(256) peer_push_kernel(const float4* __restrict
     __threadfence_system();   // every thread's copies are performed before its CTA takes the ticket
     __syncthreads();
     if (threadIdx.x != 0) return;
-    int* ticket = reinterpret_cast<int*>(state + 1);
     if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
     atomicExch(ticket, 0);
-    state[0] = epoch;
+    state[0] = epoch;   // advanced even after a failed wait, so the ranks' step counts stay in line
+    if (atomicAdd(ticket + 1, 0) == (int)epoch) return;   // a CTA gave up: its share was not copied
     __threadfence_system();
     st_release_sys(root_ctrl + rank, epoch);
 }
@@ -170,6 +174,215 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) peer_merge_kernel(const floa
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Scatter-merge form.  Gathering every block on rank 0 puts world - 1 blocks through rank 0's inbound links;
+// here every rank owns one contiguous share of the rows and merges it, so each rank sends and receives
+// (world - 1) / world of one block, and only the merged shares (out dtype, no lse weights) go to rank 0.
+// Every rank allocates a buffer of ws_peer_rs_bytes and maps every other rank's:
+//   control block (2 KB, int64 words): flags[64] -- flag[r] = the last step rank r scattered into this
+//   buffer; gflags[64] (rank 0's buffer) -- gflag[q] = the last step rank q stored its merged share;
+//   consumed -- the last step whose slots this rank's merge has read; gconsumed (rank 0's buffer) -- the
+//   last step whose gathered shares rank 0 has copied out; the merge's CTA ticket; the last step a merge
+//   CTA gave up in.
+//   then `world` slots: slot r holds rank r's partial of this rank's share, o [share, dim] then lse [share];
+//   then the gather area (used in rank 0's buffer): out [rows, dim] in the out dtype, lse [rows] at a fixed
+//   offset of rows * dim floats.
+// Per step, every rank: rs_scatter_kernel (wait until each peer has read the previous step's slot, copy
+// the peer's rows of this rank's block into it, release flag[rank] in the peer's buffer), then
+// rs_merge_kernel (wait for every flag, merge this rank's share from the slots and its own block; rank 0
+// writes its rows to out, the others store theirs in rank 0's gather area and release their gflag after
+// a bounded wait for rank 0 to have copied out the previous step; rank 0 then waits for every gflag and
+// copies the gathered rows to out).
+namespace rs {
+
+constexpr size_t kCtrl = 2048;
+constexpr int kFlags = 0, kGFlags = 64, kConsumedW = 128, kGConsumed = 129, kTicketW = 130, kFailedW = 131;
+
+__host__ __device__ inline int64_t share_lo(int64_t rows, int world, int q) { return rows * q / world; }
+__host__ __device__ inline int64_t slot_floats(int64_t rows, int world, int dim) {
+    const int64_t sm = (rows + world - 1) / world;   // the largest share
+    return (sm * dim + sm + 63) / 64 * 64;
+}
+__host__ __device__ inline int64_t area_offset(int64_t rows, int world, int dim) {
+    return (int64_t)kCtrl + (int64_t)world * slot_floats(rows, world, dim) * 4;
+}
+
+// Bounded wait of one lane for *p >= v; false (and the status recorded) when it gives up.
+__device__ __forceinline__ bool wait_at_least(const int64_t* p, int64_t v, uint64_t t0, int* status) {
+    while (ld_acquire_sys(p) < v) {
+        if (globaltimer_ns() - t0 > kWaitNs) {
+            atomicExch(status, kDevTimeout);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(256) rs_scatter_kernel(const float* __restrict__ block,
+                                                         const int64_t* __restrict__ bases, int world, int64_t rows,
+                                                         int dim, int rank, int64_t* state, int* status) {
+    __shared__ int s_go;
+    const int64_t epoch = state[0] + 1;   // the last CTA advances it only after every CTA has read it
+    int* ticket = reinterpret_cast<int*>(state + 1);   // [0] the CTA ticket, [1] the last step a CTA gave up in
+    const int64_t sf = slot_floats(rows, world, dim);
+    if (threadIdx.x < 32) {   // lane q: peer q has read its slots of the previous step
+        const int q = threadIdx.x;
+        bool ok = true;
+        if (q < world && q != rank)
+            ok = wait_at_least(reinterpret_cast<const int64_t*>(bases[q]) + kConsumedW, epoch - 1, globaltimer_ns(),
+                               status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (q == 0) {
+            if (!ok) atomicExch(ticket + 1, (int)epoch);
+            s_go = ok;
+        }
+    }
+    __syncthreads();
+    if (s_go) {
+        const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+        const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        for (int p = 1; p < world; ++p) {
+            const int q = (rank + p) % world;   // the ranks start on different peers
+            const int64_t lo = share_lo(rows, world, q), n = share_lo(rows, world, q + 1) - lo;
+            float* slot = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bases[q]) + kCtrl) + (int64_t)rank * sf;
+            const float4* src = reinterpret_cast<const float4*>(block + lo * dim);
+            float4* dst = reinterpret_cast<float4*>(slot);
+            const int64_t n16 = n * dim / 4;
+            for (int64_t i = t; i < n16; i += nth) dst[i] = __ldcg(src + i);
+            for (int64_t i = t; i < n; i += nth) slot[n * dim + i] = __ldcg(block + rows * dim + lo + i);
+        }
+    }
+    __threadfence_system();   // every thread's stores are performed before its CTA takes the ticket
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    if (atomicAdd(ticket, 1) != (int)gridDim.x - 1) return;
+    atomicExch(ticket, 0);
+    state[0] = epoch;   // advanced even after a failed wait, so the ranks' step counts stay in line
+    if (atomicAdd(ticket + 1, 0) == (int)epoch) return;
+    __threadfence_system();
+    for (int p = 1; p < world; ++p) {
+        const int q = (rank + p) % world;
+        st_release_sys(reinterpret_cast<int64_t*>(bases[q]) + kFlags + rank, epoch);
+    }
+}
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(32 * kRowsPerCta) rs_merge_kernel(const float* __restrict__ block,
+                                                                    const int64_t* __restrict__ bases, int world,
+                                                                    int64_t rows, int dim, int rank,
+                                                                    const int64_t* state, void* out, float* out_lse,
+                                                                    int* status) {
+    using OutT = typename std::conditional<OUT_BF16, __nv_bfloat16, float>::type;
+    __shared__ int s_ok;
+    const int64_t epoch = *reinterpret_cast<const volatile int64_t*>(state);   // advanced by this step's scatter
+    int64_t* ctrl = reinterpret_cast<int64_t*>(bases[rank]);
+    int64_t* root = reinterpret_cast<int64_t*>(bases[0]);
+    const int64_t sf = slot_floats(rows, world, dim);
+    const float* slots = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(ctrl) + kCtrl);
+    const int64_t lo = share_lo(rows, world, rank), n = share_lo(rows, world, rank + 1) - lo;
+    uint8_t* area = reinterpret_cast<uint8_t*>(root) + area_offset(rows, world, dim);   // rank 0's gather area
+    OutT* area_o = reinterpret_cast<OutT*>(area);
+    float* area_l = reinterpret_cast<float*>(area) + rows * dim;
+    if (threadIdx.x < 32) {   // lane q: flag q reached this step; lane `rank` (> 0): rank 0 copied out the last one
+        const int q = threadIdx.x;
+        const uint64_t t0 = globaltimer_ns();
+        bool ok = true;
+        if (q < world && q != rank) ok = wait_at_least(ctrl + kFlags + q, epoch, t0, status);
+        if (q == rank && rank != 0) ok = wait_at_least(root + kGConsumed, epoch - 1, t0, status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (q == 0) {
+            if (!ok) atomicExch(reinterpret_cast<unsigned long long*>(ctrl + kFailedW), (unsigned long long)epoch);
+            s_ok = ok;
+        }
+    }
+    __syncthreads();
+    const bool ok1 = s_ok;   // read once by every thread: s_ok is written again below
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * kRowsPerCta + warp;   // row within this rank's share
+    if (ok1 && r < n) {
+        // lane p < world holds partial p's lse; this rank's own partial is read from its block
+        const float lp = lane < world ? __ldcg(lane == rank ? block + rows * dim + lo + r : slots + lane * sf + n * dim + r)
+                                      : -INFINITY;
+        float M = lp;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float w = (M == -INFINITY || lp == -INFINITY) ? 0.f : expf(lp - M);
+        float s = w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float lse = M == -INFINITY ? -INFINITY : M + logf(s);
+        const float wp = M == -INFINITY ? 0.f : w / s;   // exp(lp - lse)
+        OutT* dst = (rank == 0 ? static_cast<OutT*>(out) : area_o) + (lo + r) * dim;
+        for (int c = lane * 4; c < dim; c += 128) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < world; ++p) {
+                const float e = __shfl_sync(0xffffffffu, wp, p);
+                if (e == 0.f) continue;
+                const float* src = p == rank ? block + (lo + r) * dim : slots + p * sf + r * dim;
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + c));
+                acc.x = fmaf(e, v.x, acc.x);
+                acc.y = fmaf(e, v.y, acc.y);
+                acc.z = fmaf(e, v.z, acc.z);
+                acc.w = fmaf(e, v.w, acc.w);
+            }
+            if (OUT_BF16)
+                *reinterpret_cast<uint2*>(dst + c) = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+            else
+                *reinterpret_cast<float4*>(dst + c) = acc;
+        }
+        if (lane == 0) {
+            if (rank != 0) area_l[lo + r] = lse;
+            else if (out_lse) out_lse[lo + r] = lse;
+        }
+    }
+    if (rank == 0 && world > 1 && ok1) {
+        // the other ranks' merged rows [share_lo(1), rows) arrive in the gather area; copy them to out
+        __syncthreads();   // every thread has read s_ok before it is written again
+        if (threadIdx.x < 32) {
+            const int q = threadIdx.x;
+            bool ok = true;
+            if (q >= 1 && q < world) ok = wait_at_least(ctrl + kGFlags + q, epoch, globaltimer_ns(), status);
+            ok = __all_sync(0xffffffffu, ok);
+            if (q == 0) {
+                if (!ok)
+                    atomicExch(reinterpret_cast<unsigned long long*>(ctrl + kFailedW), (unsigned long long)epoch);
+                s_ok = ok;
+            }
+        }
+        __syncthreads();
+        if (s_ok) {
+            const int64_t r1 = share_lo(rows, world, 1);
+            const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+            const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+            // rows * dim elements of 2 or 4 bytes with dim % 4 == 0: 8-byte units from any row start
+            const uint2* src = reinterpret_cast<const uint2*>(area_o + r1 * dim);
+            uint2* dst = reinterpret_cast<uint2*>(static_cast<OutT*>(out) + r1 * dim);
+            const int64_t n8 = (rows - r1) * dim * (int64_t)sizeof(OutT) / 8;
+            for (int64_t i = t; i < n8; i += nth) dst[i] = __ldcg(src + i);
+            if (out_lse)
+                for (int64_t i = t; i < rows - r1; i += nth) out_lse[r1 + i] = __ldcg(area_l + r1 + i);
+        }
+    }
+    // the last CTA publishes this step: slots read (consumed); rank 0: gathered rows copied out; the others:
+    // the merged share stored in rank 0's gather area (gflag)
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int* ticket = reinterpret_cast<int*>(ctrl + kTicketW);
+        if (atomicAdd(ticket, 1) == (int)gridDim.x - 1) {
+            atomicExch(ticket, 0);
+            if (atomicAdd(reinterpret_cast<unsigned long long*>(ctrl + kFailedW), 0ull) != (unsigned long long)epoch) {
+                __threadfence_system();
+                st_release_sys(ctrl + kConsumedW, epoch);
+                if (rank == 0) st_release_sys(ctrl + kGConsumed, epoch);
+                else st_release_sys(root + kGFlags + rank, epoch);
+            }
+        }
+    }
+}
+
+}  // namespace rs
 }  // namespace peer
 }  // namespace ws
 
@@ -193,6 +406,7 @@ int ws_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle) {
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, bytes);
     if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();   // zeroed before any peer maps it
     cudaIpcMemHandle_t h;
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
     if (e != cudaSuccess) {
@@ -257,6 +471,52 @@ int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, void* out, 
     else
         peer_merge_kernel<false><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, out,
                                                                            out_lse, device_status_word());
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+size_t ws_peer_rs_bytes(int world, int64_t rows, int dim) {
+    if (world < 1 || world > 32 || rows < 0 || dim < 4 || dim % 4) return 0;
+    return (size_t)rs::area_offset(rows, world, dim) + align_up((size_t)(rows * dim + rows), 64) * sizeof(float);
+}
+
+int ws_peer_rs_scatter(const float* block, const int64_t* bases, int world, int64_t rows, int dim, int rank,
+                       int64_t* state, void* stream) {
+    if (!block || !bases || !state || world < 1 || world > 32 || rank < 0 || rank >= world || rows < 0 || dim < 4 ||
+        dim % 4)
+        return set_error(WS_ERR_INVALID_ARG, "peer_rs_scatter: bad argument (world <= 32, dim % 4 == 0)");
+    if (reinterpret_cast<uintptr_t>(block) % 16 || reinterpret_cast<uintptr_t>(bases) % 8 ||
+        reinterpret_cast<uintptr_t>(state) % 8)
+        return set_error(WS_ERR_INVALID_ARG, "peer_rs_scatter: block must be 16-byte, bases and state 8-byte aligned");
+    // (world - 1) / world of the block leaves this rank: one 16-byte copy per thread per pass
+    const int64_t n16 = (rows - rows / std::max(world, 1)) * dim / 4 + 1;
+    const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(128, (n16 + 255) / 256));
+    rs::rs_scatter_kernel<<<ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(block, bases, world, rows, dim, rank,
+                                                                             state, device_status_word());
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int ws_peer_rs_merge(const float* block, const int64_t* bases, int world, int64_t rows, int dim, int rank,
+                     const int64_t* state, void* out, int out_dtype, float* out_lse, void* stream) {
+    if (!block || !bases || !state || world < 1 || world > 32 || rank < 0 || rank >= world || rows < 0 || dim < 4 ||
+        dim % 4 || (rank == 0 && rows > 0 && !out))
+        return set_error(WS_ERR_INVALID_ARG, "peer_rs_merge: bad argument (world <= 32, dim % 4 == 0, out on rank 0)");
+    if (out_dtype != WS_DTYPE_BF16 && out_dtype != WS_DTYPE_F32)
+        return set_error(WS_ERR_INVALID_ARG, "peer_rs_merge: out dtype");
+    if (reinterpret_cast<uintptr_t>(block) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+        return set_error(WS_ERR_INVALID_ARG, "peer_rs_merge: block and out must be 16-byte aligned");
+    const int64_t share = (rows + world - 1) / world;
+    // rank 0 also copies the gathered rows out: at least 64 CTAs there, and the same grid on every rank
+    const int64_t ctas = std::max<int64_t>(64, (share + kRowsPerCta - 1) / kRowsPerCta);
+    if (ctas > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "peer_rs_merge: too many rows");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (out_dtype == WS_DTYPE_BF16)
+        rs::rs_merge_kernel<true><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(block, bases, world, rows, dim, rank,
+                                                                            state, out, out_lse, device_status_word());
+    else
+        rs::rs_merge_kernel<false><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(block, bases, world, rows, dim, rank,
+                                                                             state, out, out_lse, device_status_word());
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }

@@ -6,10 +6,18 @@ CSA compressed entries [r*nc/N, (r+1)*nc/N) of every sequence (a rank attends
 to the ids of the global top-k list that fall in its range, rebased to its
 local rows).  Each rank produces a normalised partial per query row, o fp32
 and lse fp32; a rank whose range holds nothing of a row gives o = 0 and
-lse = -inf.  The ranks then exchange the partials with one all_gather and merge
-them by log-sum-exp -- the merge the reference's runtimes do on the host
-(system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464) -- here on
-the device with ws_lse_merge_strided, straight from the gathered blocks.
+lse = -inf.  The ranks then exchange the partials once and merge them by
+log-sum-exp -- the merge the reference's runtimes do on the host
+(system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464) -- on the
+device.  Three forms of that one exchange:
+
+* PartialExchange: one NCCL all_gather of the blocks, then ws_lse_merge_strided
+  on every rank (the result on every rank);
+* PeerExchange: the blocks pushed into rank 0's slots over NVLink peer memory,
+  merged there (the result on rank 0);
+* ScatterExchange: each rank merges one share of the rows from its peers'
+  copies and sends the merged share to rank 0 (the result on rank 0).
+
 There is no other collective on the path.
 """
 from __future__ import annotations
@@ -157,9 +165,107 @@ class PeerExchange:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
-        if self.rank != 0:
-            lib().ws_peer_buffer_close(self.base)
+        with torch.cuda.device(self.device):
+            if self.rank != 0:
+                lib().ws_peer_buffer_close(self.base)
         dist.barrier(group=self.group)
-        if self.rank == 0:
-            lib().ws_peer_buffer_free(self.base)
+        with torch.cuda.device(self.device):
+            if self.rank == 0:
+                lib().ws_peer_buffer_free(self.base)
+        self._closed = True
+
+
+class ScatterExchange:
+    """The exchange over NVLink peer memory in scatter-merge form
+    (ws_peer_rs_scatter / ws_peer_rs_merge in include/scope_b200.h).
+
+    Every rank allocates a buffer, the ranks all-gather their CUDA IPC handles
+    and each maps every other rank's.  Each rank owns the share of rows
+    ``shard_bounds(rows, world, rank)`` and merges it: its decode writes its
+    whole partial at ``slot()`` (a local block), ``step()`` copies every
+    peer's rows into that peer's buffer, waits for the peers' rows of its own
+    share, merges them, and sends the merged share to rank 0 in ``out_dtype``.
+    Rank 0 returns (out, out_lse) for all rows; the others (None, None).  A
+    rank sends and receives (world - 1) / world of one block per step, against
+    (world - 1) blocks into rank 0 for PeerExchange, so it pays when the
+    partials are large (many query rows, wide latents) or world is large.
+    Every rank calls ``step()`` once per step, in the same order; the step
+    counts live on the devices, so the steps may be captured in a CUDA graph.
+    """
+
+    def __init__(self, rows: int, dim: int, world: int, rank: int, device, out_dtype=torch.bfloat16, group=None):
+        import ctypes
+
+        from ._lib import check, lib
+        self.rows, self.dim, self.world, self.rank, self.group = rows, dim, world, rank, group
+        self.device = torch.device(device)
+        if out_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("ScatterExchange: out_dtype bf16 or fp32")
+        self.out_dtype = out_dtype
+        L = lib()
+        nbytes = L.ws_peer_rs_bytes(world, rows, dim)
+        if nbytes == 0:
+            raise ValueError("ScatterExchange: bad world / rows / dim (world <= 32, dim % 4 == 0)")
+        handle = ctypes.create_string_buffer(64)
+        own = ctypes.c_void_p()
+        self._closed = False
+        with torch.cuda.device(self.device):
+            check(L.ws_peer_buffer_create(nbytes, ctypes.byref(own), handle), "ws_peer_buffer_create")
+            handles = [None] * world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            ptrs, self._mapped = [], []
+            for q in range(world):
+                if q == rank:
+                    ptrs.append(own.value)
+                    continue
+                b = ctypes.c_void_p()
+                check(L.ws_peer_buffer_open(ctypes.create_string_buffer(handles[q], 64), ctypes.byref(b)),
+                      "ws_peer_buffer_open")
+                ptrs.append(b.value)
+                self._mapped.append(b.value)
+        self.own = own.value
+        self.bases = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        n = -(-(rows * dim + rows) // 64) * 64
+        self.block = torch.empty(n, dtype=torch.float32, device=self.device)   # this rank's partial, local
+        self.state = torch.zeros(2, dtype=torch.int64, device=self.device)     # step count; ticket + failure mark
+
+    def slot(self):
+        """(o, lse) device addresses where this rank's decode writes its partial."""
+        o = self.block.data_ptr()
+        return o, o + 4 * self.rows * self.dim
+
+    def step(self, out=None, out_lse=None):
+        from . import _lib
+        from ._lib import check, lib, stream_ptr
+        code = _lib.WS_DTYPE_BF16 if self.out_dtype == torch.bfloat16 else _lib.WS_DTYPE_F32
+        with torch.cuda.device(self.device):
+            st = stream_ptr(self.device)
+            if self.rank == 0:
+                if out is None:
+                    out = torch.empty(self.rows, self.dim, dtype=self.out_dtype, device=self.device)
+                if out.dtype != self.out_dtype or out.numel() != self.rows * self.dim or not out.is_contiguous():
+                    raise ValueError("ScatterExchange.step: out must be contiguous [rows, dim] of out_dtype")
+                if out_lse is None:
+                    out_lse = torch.empty(self.rows, dtype=torch.float32, device=self.device)
+            L = lib()
+            check(L.ws_peer_rs_scatter(self.block.data_ptr(), self.bases.data_ptr(), self.world, self.rows,
+                                       self.dim, self.rank, self.state.data_ptr(), st), "ws_peer_rs_scatter")
+            check(L.ws_peer_rs_merge(self.block.data_ptr(), self.bases.data_ptr(), self.world, self.rows, self.dim,
+                                     self.rank, self.state.data_ptr(), out.data_ptr() if self.rank == 0 else None,
+                                     code, out_lse.data_ptr() if self.rank == 0 else None, st), "ws_peer_rs_merge")
+        return (out, out_lse) if self.rank == 0 else (None, None)
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free this rank's."""
+        from ._lib import lib
+        if self._closed:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for b in self._mapped:
+                lib().ws_peer_buffer_close(b)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            lib().ws_peer_buffer_free(self.own)
         self._closed = True

@@ -216,15 +216,16 @@ def test_sharded_caches_decode_over_nccl():
     assert np.abs(ml - (mrm + np.log(mrs))).max() < TOL_LSE
 
 
-def _peer_rank(rank, port, qs, ks, vs, scale, n_graph=3):
-    """Steps of a sharded GQA decode whose partials go over NVLink into rank 0's
-    slots (PeerExchange): eager steps, then replays of a captured CUDA graph of
-    decode + exchange; rank 0 returns every step's merge."""
+def _peer_rank(rank, port, qs, ks, vs, scale, kind="push", n_graph=3):
+    """Steps of a sharded GQA decode whose partials go over NVLink peer memory
+    (kind "push": PeerExchange, into rank 0's slots; "scatter": ScatterExchange,
+    each rank merging its share of the rows): eager steps, then replays of a
+    captured CUDA graph of decode + exchange; rank 0 returns every step's merge."""
     import torch.distributed as dist
 
     import scope_b200
     from scope_b200 import _lib
-    from scope_b200.shard import PeerExchange, shard_bounds
+    from scope_b200.shard import PeerExchange, ScatterExchange, shard_bounds
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", world_size=WORLD, rank=rank,
@@ -234,7 +235,8 @@ def _peer_rank(rank, port, qs, ks, vs, scale, n_graph=3):
         rows, G, D = qs[0].shape
         L = ks[0].shape[1]
         lo, hi = shard_bounds(L, WORLD, rank)
-        ex = PeerExchange(rows * G, D, WORLD, rank, dev)
+        ex = (PeerExchange(rows * G, D, WORLD, rank, dev) if kind == "push"
+              else ScatterExchange(rows * G, D, WORLD, rank, dev))
         L_ = _lib.lib()
         ws = torch.zeros(L_.ws_gqa_decode_workspace_size(rows, G, D, hi - lo), dtype=torch.uint8, device=dev)
         outs = []
@@ -285,15 +287,17 @@ def _peer_rank(rank, port, qs, ks, vs, scale, n_graph=3):
 
 
 @needs_two
-def test_peer_exchange_steps():
+@pytest.mark.parametrize("kind,rows,G", [("push", 8, 8), ("scatter", 8, 8), ("scatter", 35, 1)])
+def test_peer_exchange_steps(kind, rows, G):
+    """35 x 1 query rows split 17 / 18 between the scatter form's two shares."""
     import oracle
     g = torch.Generator().manual_seed(53)
-    rows, G, D, L, steps = 8, 8, 128, 6001, 7   # 4 eager steps, then 3 replays of a captured graph
+    D, L, steps = 128, 6001, 7   # 4 eager steps, then 3 replays of a captured graph
     qs = [torch.randn(rows, G, D, generator=g).bfloat16() for _ in range(steps)]
     ks = [torch.randn(rows, L, D, generator=g).bfloat16() for _ in range(steps)]
     vs = [torch.randn(rows, L, D, generator=g).bfloat16() for _ in range(steps)]
     scale = D ** -0.5
-    res = _run_two_ranks(_peer_rank, (qs, ks, vs, scale))
+    res = _run_two_ranks(_peer_rank, (qs, ks, vs, scale, kind))
     assert len(res) == steps
     for (out, lse), q, k, v in zip(res, qs, ks, vs):
         ro, rm, rs = oracle.gqa_decode(oracle.bf16_bits(q), oracle.bf16_bits(k), oracle.bf16_bits(v), scale)
