@@ -11,8 +11,8 @@
  *   - returns WS_OK (0) or a WS_ERR_* code; ws_last_error() then returns a
  *     message (thread-local).
  * No decode entry point allocates device memory (ws_peer_buffer_create is
- * the one allocating entry, for the multi-GPU exchange): callers pass a workspace whose
- * size the matching *_workspace_size() returns.  A workspace must be zeroed
+ * the one allocating entry, for the multi-GPU exchange): callers pass a 16-byte
+ * aligned workspace whose size the matching *_workspace_size() returns.  A workspace must be zeroed
  * once when it is allocated (its counters reset themselves after every
  * launch) and must not be shared by launches that may overlap in time.
  * Exception: when ws_status_take() returns WS_ERR_DEVICE, a launch may have

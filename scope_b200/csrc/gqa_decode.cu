@@ -430,23 +430,53 @@ gqa_decode_kernel(const __grid_constant__ GqaMaps maps, const __grid_constant__ 
         }
         const int slot = cta + sg.j;
         float* part = p.ws_part + (int64_t)slot * C::SLOT_FLOATS;
-        for (int e = ctid; e < NG * DVP; e += kConsumerWarps * 32) {
-            const int grp = e / DVP, d = e - grp * DVP;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, rm[w * NG + grp]);
-            const float Mu = (M == -INFINITY) ? 0.f : M;
-            float acc = 0.f, L = 0.f;
+        // the warps' weights per query group, once: thread g < NG turns column g of rm into the weights
+        // 2^(m_w - M) and column g of rl into (M, L) -- rl[g] = M, rl[NG + g] = L
+        if (ctid < NG) {
+            float mw[kConsumerWarps], M = -INFINITY;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) {
-                const float wt = ex2(rm[w * NG + grp] - Mu);
-                acc += wt * ro[(w * NG + grp) * DVP + d];
-                L += wt * rl[w * NG + grp];
+                mw[w] = rm[w * NG + ctid];
+                M = fmaxf(M, mw[w]);
             }
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            float L = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float wt = ex2(mw[w] - Mu);
+                L += wt * rl[w * NG + ctid];
+                rm[w * NG + ctid] = wt;
+            }
+            rl[ctid] = M;
+            rl[NG + ctid] = L;
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        // the weighted sum, four values per thread and step (every warp's float4 load issued together)
+        for (int ch = ctid; ch < NG * DVP / 4; ch += kConsumerWarps * 32) {
+            const int e = ch * 4, grp = e / DVP, d = e - grp * DVP;
+            float4 v[kConsumerWarps];
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w)
+                v[w] = *reinterpret_cast<const float4*>(ro + (w * NG + grp) * DVP + d);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float wt = rm[w * NG + grp];
+                acc.x += wt * v[w].x;
+                acc.y += wt * v[w].y;
+                acc.z += wt * v[w].z;
+                acc.w += wt * v[w].w;
+            }
+            const float M = rl[grp], L = rl[NG + grp];
             if (np == 1) {
-                if (grp < p.G && d < p.Dv) store_final(p, sg.group, grp, d, acc, M, L);
+                if (grp < p.G) {
+                    if (d < p.Dv) store_final(p, sg.group, grp, d, acc.x, M, L);
+                    if (d + 1 < p.Dv) store_final(p, sg.group, grp, d + 1, acc.y, M, L);
+                    if (d + 2 < p.Dv) store_final(p, sg.group, grp, d + 2, acc.z, M, L);
+                    if (d + 3 < p.Dv) store_final(p, sg.group, grp, d + 3, acc.w, M, L);
+                }
             } else {
-                part[e] = acc;
+                *reinterpret_cast<float4*>(part + e) = acc;
                 if (d == 0) {
                     part[NG * DVP + grp] = M;
                     part[NG * DVP + NG + grp] = L;
@@ -907,6 +937,8 @@ int gqa_launch(const GqaLaunch& a) {
     const size_t need = base_need + (a.varlen ? gqa_varlen_extra_bytes(a.B) : 0);
     if (a.workspace_bytes < need || (need && !a.workspace))
         return set_error(WS_ERR_WORKSPACE, "gqa_decode: workspace too small (see ws_gqa_workspace_size)");
+    if (reinterpret_cast<uintptr_t>(a.workspace) % 16)
+        return set_error(WS_ERR_WORKSPACE, "gqa_decode: workspace must be 16-byte aligned");
     p.ws_cnt = static_cast<int*>(a.workspace);
     p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + kCounterHeaderBytes);
     if (a.varlen) {

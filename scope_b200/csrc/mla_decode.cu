@@ -745,6 +745,8 @@ int mla_launch(const void* q_proj, const void* q_pe, const void* c_kv, const voi
     const size_t need = kCounterHeaderBytes + size_t(nctas + B) * SLOT_FLOATS * 4;
     if (workspace_bytes < need || !workspace)
         return set_error(WS_ERR_WORKSPACE, "mla_decode: workspace too small (see ws_mla_decode_workspace_size)");
+    if (reinterpret_cast<uintptr_t>(workspace) % 16)
+        return set_error(WS_ERR_WORKSPACE, "mla_decode: workspace must be 16-byte aligned");
     float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterHeaderBytes);
     if (total > 0) {
         Maps maps;
@@ -838,6 +840,8 @@ int mla_absorbed_launch(const void* q_nope, const void* w_uk, int64_t w_uk_head_
     if (B == 0) return WS_OK;
     if (!workspace || workspace_bytes < mla_absorbed_workspace_bytes(B, nH, S))
         return set_error(WS_ERR_WORKSPACE, "mla_decode_absorbed: workspace too small (see ws_mla_decode_absorbed_workspace_size)");
+    if (reinterpret_cast<uintptr_t>(workspace) % 16)
+        return set_error(WS_ERR_WORKSPACE, "mla_decode_absorbed: workspace must be 16-byte aligned");
     if (reinterpret_cast<uintptr_t>(w_uk) % 16 || reinterpret_cast<uintptr_t>(w_uv) % 16 || w_uk_head_stride % 8 ||
         w_uv_head_stride % 8)
         return set_error(WS_ERR_INVALID_ARG, "mla_decode_absorbed: weights and head strides must be 16-byte aligned");
