@@ -1100,10 +1100,10 @@ SEEDS = {"cfg4": 4000, "cfg1": 1000, "cfg5": 5}
 
 
 # -------------------------------------------------------------------- main
-def make_runner(wl, fn):
+def make_runner(wl, fn, graph=None):
     """Returns run(n) that issues n steps.  Small workloads are captured once
     (one pass over all input copies) in a CUDA graph and replayed."""
-    if not wl.graph:
+    if not (wl.graph if graph is None else graph):
         state = {"i": 0}
 
         def run(n):
@@ -1150,10 +1150,10 @@ def time_steps_flushed(wl, fn, steps, warmup, world):
     return max_over_ranks(total / steps, world), steps
 
 
-def time_steps(wl, fn, steps, warmup, world):
+def time_steps(wl, fn, steps, warmup, world, graph=None):
     if getattr(wl, "flush_l2", False):
         return time_steps_flushed(wl, fn, steps, warmup, world)
-    run, per = make_runner(wl, fn)
+    run, per = make_runner(wl, fn, graph)
     run(max(warmup, per))
     barrier(world)
     torch.cuda.synchronize()
@@ -1360,8 +1360,10 @@ def main():
         t_step, n_timed = time_steps(wl, wl.step, args.steps, args.warmup, world)
     clocks = clk.summary()
     t_e2e = time_e2e(wl, min(args.steps, 500), args.warmup, world)
-    # N > 1: the exchange alone (push + merge, or all_gather + merge), every rank in step
-    t_ex = (time_steps(wl, wl.exchange_step, min(args.steps, 200), args.warmup, world)[0]
+    # N > 1: the exchange alone, back to back (push + merge, or all_gather + merge), every rank in step; the
+    # peer forms from a CUDA graph, so that host launch overhead is not what is timed
+    t_ex = (time_steps(wl, wl.exchange_step, min(args.steps, 200), args.warmup, world,
+                       graph=True if getattr(wl, "exchange", "") in ("peer", "scatter") else None)[0]
             if world > 1 and hasattr(wl, "exchange_step") else None)
 
     hbm, peak_src = peaks()

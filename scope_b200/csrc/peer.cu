@@ -53,6 +53,20 @@ __device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
     return v;
 }
 
+// A launch that may start while the previous grid on the stream drains (programmatic stream serialization);
+// the kernel calls griddepcontrol.wait before it reads anything that grid writes.
+inline void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[1], dim3 grid, dim3 block,
+                       cudaStream_t st) {
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+}
+
 // slot floats: o [rows, dim] + lse [rows], rounded up to 64 floats (256 bytes) so every slot and its o
 // block start 16-byte aligned
 inline int64_t slot_floats(int64_t rows, int dim) { return (int64_t)align_up((size_t)(rows * dim + rows), 64); }
@@ -67,26 +81,47 @@ inline int64_t slot_floats(int64_t rows, int dim) { return (int64_t)align_up((si
 __global__ void __launch_bounds__(256) peer_push_kernel(const float4* __restrict__ src, float4* dst, int64_t n16,
                                                         int64_t* root_ctrl, int64_t* state, int rank, int* status) {
     __shared__ int s_go;
-    const int64_t epoch = state[0] + 1;   // the last CTA advances it only after every CTA has read it
     int* ticket = reinterpret_cast<int*>(state + 1);   // [0] the CTA ticket, [1] the last step a CTA gave up in
-    if (threadIdx.x == 0) {
-        int go = 1;
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_sys(root_ctrl + kConsumed) < epoch - 1) {
+    // A programmatic dependent of the decode: the wait for rank 0 to free the slot (a read over NVLink) runs
+    // while the decode finishes.  The step count read before griddepcontrol.wait is a guess (a previous push
+    // may still be in flight when the grid before this one started early); it is read again after the wait
+    // and the slot wait repeated if it changed.
+    const int64_t guess = *reinterpret_cast<volatile int64_t*>(state) + 1;
+    auto slot_free = [&](int64_t e, uint64_t t0) {
+        while (ld_acquire_sys(root_ctrl + kConsumed) < e - 1) {
             if (globaltimer_ns() - t0 > kWaitNs) {
                 atomicExch(status, kDevTimeout);
-                atomicExch(ticket + 1, (int)epoch);
-                go = 0;
-                break;
+                atomicExch(ticket + 1, (int)e);
+                return 0;
             }
             __nanosleep(128);
         }
+        return 1;
+    };
+    int go = 1;
+    const uint64_t t0 = globaltimer_ns();
+    if (threadIdx.x == 0) go = slot_free(guess, t0);
+    pdl_wait_primary();   // the decode's block (and every grid before it) is complete
+    // the last CTA advances the count only after every CTA has read it
+    const int64_t epoch = *reinterpret_cast<volatile int64_t*>(state) + 1;
+    if (threadIdx.x == 0) {
+        if (go && epoch != guess) go = slot_free(epoch, t0);
+        else if (!go) atomicExch(ticket + 1, (int)epoch);
         s_go = go;
     }
     __syncthreads();
-    if (s_go)
-        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
-            dst[i] = __ldcg(src + i);
+    if (s_go) {   // four 16-byte loads in flight per thread, then their stores
+        const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += 4 * nth) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (i + u * nth < n16) v[u] = __ldcg(src + i + u * nth);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (i + u * nth < n16) dst[i + u * nth] = v[u];
+        }
+    }
     __threadfence_system();   // every thread's copies are performed before its CTA takes the ticket
     __syncthreads();
     if (threadIdx.x != 0) return;
@@ -104,23 +139,32 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) peer_merge_kernel(const floa
                                                                       int64_t* ctrl, void* out, float* out_lse,
                                                                       int* status) {
     __shared__ int s_ok;
-    // this step's epoch: one past the last consumed one (the last CTA advances `consumed` only after every
-    // CTA has read it)
-    const int64_t epoch = *reinterpret_cast<volatile int64_t*>(ctrl + kConsumed) + 1;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        const uint64_t t0 = globaltimer_ns();
-        for (int r = 1; r < P && ok; ++r) {   // rank 0's own block is ordered by the stream
-            while (ld_acquire_sys(ctrl + r) < epoch) {
+    // A programmatic dependent of rank 0's decode: the waits for the other ranks' flags run while that decode
+    // finishes; its own slot is read only after griddepcontrol.wait.  This step's epoch is one past the last
+    // consumed one (the last CTA advances `consumed` only after every CTA has read it); the value read before
+    // the wait is a guess, read again after it, and the flag waits are repeated if it changed.
+    const int64_t guess = *reinterpret_cast<volatile int64_t*>(ctrl + kConsumed) + 1;
+    auto flags_up = [&](int64_t e, uint64_t t0) {
+        for (int r = 1; r < P; ++r) {
+            while (ld_acquire_sys(ctrl + r) < e) {
                 if (globaltimer_ns() - t0 > kWaitNs) {
                     atomicExch(status, kDevTimeout);
-                    atomicExch(reinterpret_cast<unsigned long long*>(ctrl + kFailed), (unsigned long long)epoch);
-                    ok = 0;
-                    break;
+                    atomicExch(reinterpret_cast<unsigned long long*>(ctrl + kFailed), (unsigned long long)e);
+                    return 0;
                 }
                 __nanosleep(64);
             }
         }
+        return 1;
+    };
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    if (threadIdx.x == 0) ok = flags_up(guess, t0);
+    pdl_wait_primary();
+    const int64_t epoch = *reinterpret_cast<volatile int64_t*>(ctrl + kConsumed) + 1;
+    if (threadIdx.x == 0) {
+        if (ok && epoch != guess) ok = flags_up(epoch, t0);
+        else if (!ok) atomicExch(reinterpret_cast<unsigned long long*>(ctrl + kFailed), (unsigned long long)epoch);
         s_ok = ok;
     }
     __syncthreads();
@@ -140,14 +184,21 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) peer_merge_kernel(const floa
         const float wp = M == -INFINITY ? 0.f : w / s;   // exp(lp - lse)
         for (int c = lane * 4; c < D; c += 128) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int p = 0; p < P; ++p) {
-                const float e = __shfl_sync(0xffffffffu, wp, p);
-                if (e == 0.f) continue;
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(slots + p * slot_stride + row * D + c));
-                acc.x = fmaf(e, v.x, acc.x);
-                acc.y = fmaf(e, v.y, acc.y);
-                acc.z = fmaf(e, v.z, acc.z);
-                acc.w = fmaf(e, v.w, acc.w);
+            for (int p0 = 0; p0 < P; p0 += 8) {   // eight partials' loads in flight, then their sums
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (p0 + u < P)
+                        v[u] = __ldcg(reinterpret_cast<const float4*>(slots + (p0 + u) * slot_stride + row * D + c));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float e = __shfl_sync(0xffffffffu, wp, (p0 + u) & 31);
+                    if (p0 + u >= P || e == 0.f) continue;   // an empty partial may hold anything: skipped
+                    acc.x = fmaf(e, v[u].x, acc.x);
+                    acc.y = fmaf(e, v[u].y, acc.y);
+                    acc.z = fmaf(e, v[u].z, acc.z);
+                    acc.w = fmaf(e, v[u].w, acc.w);
+                }
             }
             if (OUT_BF16) {
                 uint2 pk = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
@@ -316,15 +367,25 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) rs_merge_kernel(const float*
         OutT* dst = (rank == 0 ? static_cast<OutT*>(out) : area_o) + (lo + r) * dim;
         for (int c = lane * 4; c < dim; c += 128) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int p = 0; p < world; ++p) {
-                const float e = __shfl_sync(0xffffffffu, wp, p);
-                if (e == 0.f) continue;
-                const float* src = p == rank ? block + (lo + r) * dim : slots + p * sf + r * dim;
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + c));
-                acc.x = fmaf(e, v.x, acc.x);
-                acc.y = fmaf(e, v.y, acc.y);
-                acc.z = fmaf(e, v.z, acc.z);
-                acc.w = fmaf(e, v.w, acc.w);
+            for (int p0 = 0; p0 < world; p0 += 8) {   // eight partials' loads in flight, then their sums
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int p = p0 + u;
+                    if (p < world) {
+                        const float* src = p == rank ? block + (lo + r) * dim : slots + p * sf + r * dim;
+                        v[u] = __ldcg(reinterpret_cast<const float4*>(src + c));
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float e = __shfl_sync(0xffffffffu, wp, (p0 + u) & 31);
+                    if (p0 + u >= world || e == 0.f) continue;
+                    acc.x = fmaf(e, v[u].x, acc.x);
+                    acc.y = fmaf(e, v[u].y, acc.y);
+                    acc.z = fmaf(e, v[u].z, acc.z);
+                    acc.w = fmaf(e, v[u].w, acc.w);
+                }
             }
             if (OUT_BF16)
                 *reinterpret_cast<uint2*>(dst + c) = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
@@ -445,10 +506,11 @@ int ws_peer_push(const float* block, void* root_base, int world, int64_t rows, i
     const int64_t n16 = (rows * dim + rows + 3) / 4;   // the block and the slot are rounded up to 64 floats
     float4* dst = reinterpret_cast<float4*>(static_cast<uint8_t*>(root_base) + ws_peer_slot_offset(world, rows, dim, rank));
     const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(128, (n16 + 255) / 256));
-    peer_push_kernel<<<ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const float4*>(block), dst, n16, static_cast<int64_t*>(root_base), state, rank,
-        device_status_word());
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    pdl_config(cfg, attr, dim3(ctas), dim3(256), static_cast<cudaStream_t>(stream));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, peer_push_kernel, reinterpret_cast<const float4*>(block), dst, n16,
+                                             static_cast<int64_t*>(root_base), state, rank, device_status_word());
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -463,15 +525,16 @@ int ws_peer_merge(void* root_base, int world, int64_t rows, int dim, void* out, 
     const float* slots = reinterpret_cast<const float*>(static_cast<uint8_t*>(root_base) + kCtrlBytes);
     const int64_t ctas = std::max<int64_t>(1, (rows + kRowsPerCta - 1) / kRowsPerCta);
     if (ctas > INT32_MAX) return set_error(WS_ERR_UNSUPPORTED, "peer_merge: too many rows");
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     int64_t* ctrl = static_cast<int64_t*>(root_base);
-    if (out_dtype == WS_DTYPE_BF16)
-        peer_merge_kernel<true><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, out,
-                                                                          out_lse, device_status_word());
-    else
-        peer_merge_kernel<false><<<(unsigned)ctas, 32 * kRowsPerCta, 0, st>>>(slots, sf, world, rows, dim, ctrl, out,
-                                                                           out_lse, device_status_word());
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    pdl_config(cfg, attr, dim3((unsigned)ctas), dim3(32 * kRowsPerCta), static_cast<cudaStream_t>(stream));
+    const cudaError_t e =
+        out_dtype == WS_DTYPE_BF16
+            ? cudaLaunchKernelEx(&cfg, peer_merge_kernel<true>, slots, sf, world, rows, dim, ctrl, out, out_lse,
+                                 device_status_word())
+            : cudaLaunchKernelEx(&cfg, peer_merge_kernel<false>, slots, sf, world, rows, dim, ctrl, out, out_lse,
+                                 device_status_word());
     return e == cudaSuccess ? WS_OK : set_error(WS_ERR_CUDA, cudaGetErrorString(e));
 }
 
