@@ -283,9 +283,11 @@ int ws_csa_q_quantize_u8(const float* q, int64_t rows, int hd, void* out, float*
  *     slot over NVLink, and the release of rank r's flag.  `state` is two
  *     int64 words of rank r's memory, zeroed once (its step count and a ticket).
  * The step counts live on the devices and every pointer is fixed, so the steps
- * can be captured in a CUDA graph.  A wait that gives up (2 s) records
- * WS_ERR_DEVICE for ws_status_take; the exchange must then be rebuilt.
- * world <= 32, dim % 4 == 0.
+ * can be captured in a CUDA graph.  Both are programmatic dependent launches:
+ * they poll the other ranks while the kernel before them drains and read its
+ * output only after it completes.  A wait that gives up (2 s from the launch's
+ * start) records WS_ERR_DEVICE for ws_status_take; the exchange must then be
+ * rebuilt.  world <= 32, dim % 4 == 0.
  */
 size_t ws_peer_exchange_bytes(int world, int64_t rows, int dim);
 size_t ws_peer_slot_offset(int world, int64_t rows, int dim, int rank);
