@@ -68,3 +68,30 @@ def test_error_string_and_version(built_lib):
     assert built_lib.ws_version() >= 100
     built_lib.ws_last_error.restype = ctypes.c_char_p
     assert isinstance(built_lib.ws_last_error(), bytes)
+
+
+def test_exchange_sizes_and_argument_checks():
+    """Host-only parts of the NVLink exchange entries: buffer sizes, and the
+    argument checks that return before any CUDA call."""
+    L = _lib.lib()
+    # gather form: 1 KB control block + one slot per rank of rows*dim + rows floats, rounded to 64 floats
+    slot = -(-(1024 * 128 + 1024) // 64) * 64
+    assert L.ws_peer_exchange_bytes(8, 1024, 128) == 1024 + 8 * slot * 4
+    assert L.ws_peer_slot_offset(8, 1024, 128, 3) == 1024 + 3 * slot * 4
+    assert L.ws_peer_exchange_bytes(0, 1024, 128) == 0 and L.ws_peer_exchange_bytes(65, 16, 128) == 0
+    # scatter-merge form: 2 KB control block, one slot per rank of the largest share, then the gather area
+    for world, rows, dim in ((8, 2048, 128), (2, 35, 128), (3, 1024, 512), (32, 1, 4)):
+        share = -(-rows // world)
+        sf = -(-(share * dim + share) // 64) * 64
+        area = -(-(rows * dim + rows) // 64) * 64
+        assert L.ws_peer_rs_bytes(world, rows, dim) == 2048 + world * sf * 4 + area * 4
+    assert L.ws_peer_rs_bytes(33, 64, 128) == 0          # world > 32
+    assert L.ws_peer_rs_bytes(2, 64, 6) == 0             # dim % 4 != 0
+    # rejected before any launch: a rank 0 push, null pointers, an output dtype that is not bf16 / fp32
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    assert L.ws_peer_push(p, p, 2, 16, 128, 0, p, None) == 1
+    assert L.ws_peer_rs_scatter(None, p, 2, 16, 128, 0, p, None) == 1
+    assert L.ws_peer_rs_merge(p, p, 2, 16, 128, 0, p, None, 0, None, None) == 1   # rank 0 without out
+    assert L.ws_peer_rs_merge(p, p, 2, 16, 128, 1, p, None, 7, None, None) == 1   # bad out dtype
+    assert b"peer" in L.ws_last_error()
