@@ -1,4 +1,6 @@
-// Exchange of sequence-shard partials over NVLink peer memory (root gather).
+// Exchange of sequence-shard partials over NVLink peer memory: the root-gather
+// form (peer_push_kernel / peer_merge_kernel) and, further down, the
+// scatter-merge form (rs_scatter_kernel / rs_merge_kernel).
 //
 // The reference's runtimes merge the partials of their KV shares on the host
 // (system/qwenoffload.py:1606-1617, system/mixoffload.py:1456-1464); across
@@ -18,7 +20,9 @@
 //     epoch as consumed.
 // The epochs live on the devices -- each rank's push counts its own steps in
 // its state word, rank 0's merge counts through `consumed` -- and every
-// pointer is fixed, so a captured CUDA graph may replay the steps.
+// pointer is fixed, so a captured CUDA graph may replay the steps.  Both
+// kernels are programmatic dependent launches: their polls of the other
+// ranks' words run while the decode before them drains.
 // Buffer layout (rank 0's allocation): a 1 KB control block -- flags[64]
 // (int64, one per rank), consumed (int64), the merge's CTA ticket (int32), the
 // last epoch whose merge gave up (int64) -- then `world` slots of slot_floats
