@@ -21,7 +21,12 @@ and replace its three code paths with the library's kernels:
 * ``MlaDecodeLayer``: the single-token branch of ``_mla_compressed_forward``
   (system/deepseek.py:326-407: absorb, attention over the cache, merge,
   up-projection) over a ShardedKVCacheCompressed, with the new token appended
-  first (:250-252) -- one call per decode step, nothing copied to the host.
+  first (:250-252) -- one call per decode step, nothing copied to the host;
+* ``ds4_window_compressed_decode``: the DeepSeek-V4 decode step's attention
+  over the sliding-window cache and the compressed cache
+  (system/ds4offload.py:280-342), with the compressed cache resident in HBM
+  instead of pinned host memory: two CSA launches and one log-sum-exp merge,
+  the attention sink entering that merge as a partial with no value.
 
 Layouts follow the harness: q [B*NH, GROUPS, QHD] bf16 (kv row r = b*NH + h,
 query head r*GROUPS + g); a share's k, v [B*NH, len, QHD / VHD] bf16; outputs
@@ -33,7 +38,7 @@ from typing import Sequence
 
 import torch
 
-from .ops import Share, gqa_decode_shares
+from .ops import Share, gqa_decode_shares, lse_merge
 
 
 def _rows_of(q: torch.Tensor) -> tuple[int, int, int]:
@@ -107,7 +112,6 @@ def pairwise_merge(o1, m1, s1, o2, m2, s2):
     o_i [R..., D] un-normalised, m_i / s_i [R..., 1] max and sum, all fp32 CUDA
     tensors.  Returns (o, m, s) of the union in the same form, computed by the
     device log-sum-exp merge (ws_lse_merge) on the normalised partials."""
-    from .ops import lse_merge
     for t in (o1, m1, s1, o2, m2, s2):
         if not t.is_cuda or t.dtype != torch.float32:
             raise RuntimeError("pairwise_merge: fp32 CUDA tensors")
@@ -154,3 +158,71 @@ class MlaDecodeLayer:
         B = q_nope.shape[0]
         out = mla_decode_absorbed(q_nope, q_pe, c, pe, self.w, self.scale)   # [B, nH, vhd]
         return out.reshape(B, 1, self.nH * self.vhd)
+
+
+def ds4_window_compressed_decode(q: torch.Tensor, kv_window: torch.Tensor, kv_compressed: torch.Tensor,
+                                 scale: float, *, window_len: int | None = None, n_compress: int | None = None,
+                                 topk_idxs: torch.Tensor | None = None, attn_sink: torch.Tensor | None = None,
+                                 return_lse: bool = False):
+    """The DeepSeek-V4 decode step's attention over its two caches (system/ds4offload.py:280-342).
+
+    q [bsz, 1, nH, hd] (bf16 or fp32, after rope); kv_window [bsz, win, hd]
+    bf16, the sliding-window cache, whose first ``window_len`` entries (all
+    by default) are attended; kv_compressed [bsz, nc, hd] bf16, the
+    compressed cache, resident here (the reference keeps it in pinned host
+    memory and attends to it on the CPU).  K = V = the entry, as in the
+    reference (MQA over one latent).
+
+    * ``topk_idxs`` None: the reference's parallel branch (:286-327): every
+      window entry and the first ``n_compress`` compressed entries (all by
+      default), two partials merged by the pairwise formula.  That branch
+      applies no attention sink.
+    * ``topk_idxs`` int32 [bsz, k]: the gather branch (:328-342): the window
+      entries plus the compressed entries the indexer selected, in one
+      softmax.  Ids are compressed-cache positions (the reference's
+      ``topk_idxs[..., win:] - win``); ids outside [0, nc) are skipped (the
+      reference clamps them to entry 0).
+    * ``attn_sink`` [nH] (the gather branch's ``sparse_attn`` sink): a
+      per-head logit that joins each head's softmax denominator and carries
+      no value.  ``sparse_attn`` is a DeepSeek-V4 kernel that the reference
+      imports from the model's own code, not shipped with it; this follows
+      that published definition of a sink.
+
+    Returns o [bsz, 1, nH, hd] in q's dtype (and lse fp32 [bsz, nH] with
+    ``return_lse``).  Two ws_csa_decode launches and one ws_lse_merge.
+    """
+    from .csa_attn import _launch
+    if q.dim() != 4 or q.shape[1] != 1 or not q.is_cuda:
+        raise RuntimeError("q must be a CUDA tensor [bsz, 1, nH, hd] (one decode token)")
+    bsz, _, nH, hd = q.shape
+    if q.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("q must be bf16 or fp32")
+    for name, t in (("kv_window", kv_window), ("kv_compressed", kv_compressed)):
+        if t.dim() != 3 or t.shape[0] < bsz or t.shape[2] != hd or t.dtype != torch.bfloat16 or not t.is_cuda:
+            raise RuntimeError(f"{name} must be a bf16 CUDA tensor [>= bsz, entries, hd]")
+    kv_w, kv_c = kv_window[:bsz].contiguous(), kv_compressed[:bsz].contiguous()
+    win, nc = kv_w.shape[1], kv_c.shape[1]
+    wl = win if window_len is None else int(window_len)
+    ncomp = nc if n_compress is None else int(n_compress)
+    if not 0 <= wl <= win or not 0 <= ncomp <= nc:
+        raise RuntimeError("window_len / n_compress out of range")
+    dev = q.device
+    q3 = q.reshape(bsz, nH, hd).contiguous()
+    n_parts = 3 if attn_sink is not None else 2
+    parts_o = torch.zeros(n_parts, bsz, nH, hd, dtype=torch.float32, device=dev)
+    parts_l = torch.full((n_parts, bsz, nH), float("-inf"), dtype=torch.float32, device=dev)
+    if wl > 0:   # the window share: entries [0, window_len)
+        _launch(q3, kv_w, scale, parts_o[0], parts_l[0], kv_range=(0, wl))
+    if topk_idxs is not None:   # the indexer's compressed entries
+        if topk_idxs.dtype != torch.int32 or topk_idxs.dim() != 2 or topk_idxs.shape[0] != bsz:
+            raise RuntimeError("topk_idxs must be int32 [bsz, k]")
+        _launch(q3, kv_c, scale, parts_o[1], parts_l[1], idx=topk_idxs.contiguous(), shard_lo=0, idx_mode="shard")
+    elif ncomp > 0:   # every compressed entry so far
+        _launch(q3, kv_c, scale, parts_o[1], parts_l[1], kv_range=(0, ncomp))
+    if attn_sink is not None:   # the sink: a partial whose lse is the head's logit and whose value is zero
+        if attn_sink.numel() != nH:
+            raise RuntimeError("attn_sink must hold one logit per head")
+        parts_l[2].copy_(attn_sink.to(device=dev, dtype=torch.float32).view(1, nH).expand(bsz, nH))
+    out, lse = lse_merge(parts_o, parts_l, out_dtype=q.dtype)
+    out = out.view(bsz, 1, nH, hd)
+    return (out, lse) if return_lse else out

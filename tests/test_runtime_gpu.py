@@ -143,3 +143,68 @@ def test_mla_layer_decode_steps():
         # relative to the output's scale: bf16 rounding of o_n and of the output is ~4e-3 of it
         assert (out.float().cpu() - want).abs().max().item() < TOL_OUT * want.abs().max().item()
     assert cache.seq_len(0) == prefill + steps
+
+
+def _ds4_case(seed, bsz=2, nH=16, hd=512, win=128, nc=700):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(bsz, 1, nH, hd, generator=g).bfloat16()
+    kw = torch.randn(bsz, win, hd, generator=g).bfloat16()
+    kc = torch.randn(bsz, nc, hd, generator=g).bfloat16()
+    return q, kw, kc
+
+
+def test_ds4_parallel_branch():
+    """system/ds4offload.py:286-327 (the 'parallel' branch): window attention over the
+    whole window cache, compressed attention over the first n_compress entries, merged
+    by the pairwise formula -- restated here in float64 as the reference writes it."""
+    scope_b200.build()
+    q, kw, kc = _ds4_case(21)
+    scale, n_compress = 512 ** -0.5, 650
+    out, lse = runtime.ds4_window_compressed_decode(q.to(DEV), kw.to(DEV), kc.to(DEV), scale,
+                                                    n_compress=n_compress, return_lse=True)
+    torch.cuda.synchronize()
+    qf, kwf, kcf = q.squeeze(1).double(), kw.double(), kc[:, :n_compress].double()
+
+    def part(kv):
+        sc = torch.einsum("bnh,bsh->bns", qf, kv) * scale
+        m = sc.amax(-1, keepdim=True)
+        e = torch.exp(sc - m)
+        return torch.einsum("bns,bsh->bnh", e, kv), m, e.sum(-1, keepdim=True)
+
+    o_c, m_c, s_c = part(kcf)
+    o_w, m_w, s_w = part(kwf)
+    m_g = torch.maximum(m_w, m_c)
+    w_w, w_c = torch.exp(m_w - m_g), torch.exp(m_c - m_g)
+    denom = w_w * s_w + w_c * s_c
+    want = (o_w * w_w + o_c * w_c) / denom
+    assert out.shape == q.shape and out.dtype == torch.bfloat16
+    assert (out.squeeze(1).double().cpu() - want).abs().max().item() < TOL_OUT
+    assert (lse.double().cpu() - (m_g + denom.log())[..., 0]).abs().max().item() < TOL_LSE
+
+
+def test_ds4_gather_branch_with_sink():
+    """system/ds4offload.py:328-342: the valid window entries plus the indexer's
+    compressed entries in one softmax, with a per-head sink logit in the denominator.
+    Padding ids (-1) and ids past the cache are skipped."""
+    scope_b200.build()
+    q, kw, kc = _ds4_case(22)
+    bsz, _, nH, hd = q.shape
+    scale, window_len, k = 512 ** -0.5, 100, 256
+    g = torch.Generator().manual_seed(23)
+    ids = torch.stack([torch.randperm(kc.shape[1], generator=g)[:k] for _ in range(bsz)]).int()
+    ids[:, -5:] = -1                       # padding
+    ids[0, 0] = kc.shape[1] + 3            # past the cache
+    sink = torch.randn(nH, generator=g) * 2.0
+    out, lse = runtime.ds4_window_compressed_decode(q.to(DEV), kw.to(DEV), kc.to(DEV), scale, window_len=window_len,
+                                                    topk_idxs=ids.to(DEV), attn_sink=sink.to(DEV), return_lse=True)
+    torch.cuda.synchronize()
+    for b in range(bsz):
+        sel = ids[b][(ids[b] >= 0) & (ids[b] < kc.shape[1])].long()
+        kv = torch.cat([kw[b, :window_len], kc[b, sel]]).double()            # [n, hd]
+        sc = (q[b, 0].double() @ kv.T) * scale                                # [nH, n]
+        logits = torch.cat([sc, sink.double()[:, None]], dim=1)              # the sink column carries no value
+        p = torch.softmax(logits, dim=1)[:, :-1]
+        want = p @ kv
+        want_lse = torch.logsumexp(logits, dim=1)
+        assert (out[b, 0].double().cpu() - want).abs().max().item() < TOL_OUT
+        assert (lse[b].double().cpu() - want_lse).abs().max().item() < TOL_LSE
