@@ -869,7 +869,7 @@ __device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, volatile 
     return false;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) indexer_score_tc_kernel(const __grid_constant__ CUtensorMap map_kv,
+__global__ void __launch_bounds__(kThreads, 2) indexer_score_tc_kernel(const __grid_constant__ CUtensorMap map_kv,
                                                                        const __nv_bfloat16* __restrict__ q,
                                                                        const float* __restrict__ w,
                                                                        const TcParams p) {
@@ -1099,13 +1099,22 @@ int indexer_topk_launch(const void* q, const void* kv, int bf16, const float* w,
         tp.nH = nH;
         tp.kb = hd / 64;
         const size_t fixed = 1024 + (size_t)tp.kb * QBOX + NHP * 4 + NBARS * 8 + 16;
-        tp.stages = (int)std::min<size_t>(kMaxStages, (200 * 1024 - fixed) / ((size_t)tp.kb * BOX));
+        // Two CTAs per SM, each with a two-stage ring, when the shared memory allows it (hd <= 128): their
+        // pipelines cover each other's per-tile hand-offs, which one CTA with a deeper ring does not (the
+        // bench's idx step went from 66.6 to 64.2 us; a ring of 3 instead of 5 stages at one CTA per SM
+        // measured the same as 5).  Otherwise one CTA per SM with the deepest ring that fits.
+        int per_sm = 2;
+        tp.stages = (int)std::min<size_t>(kMaxStages, (112 * 1024 - fixed) / ((size_t)tp.kb * BOX));
+        if (tp.stages < 2) {
+            per_sm = 1;
+            tp.stages = (int)std::min<size_t>(kMaxStages, (200 * 1024 - fixed) / ((size_t)tp.kb * BOX));
+        }
         tp.nc = nc;
         tp.scores = scores;
         tp.status = device_status_word();
         const int sms = device_sm_count();
         const int64_t tiles = (nc + TT - 1) / TT;
-        tp.ctas_per_seq = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms / std::max(bs, 1)));
+        tp.ctas_per_seq = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * per_sm / std::max(bs, 1)));
         CUtensorMap map;
         int tok_in_dim2 = 0;
         int rc = make_kv_map(&map, kv, hd, nc * hd, hd, nc, bs, TT, &tok_in_dim2);
