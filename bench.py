@@ -1298,6 +1298,57 @@ def run_aux(args):
     print(json.dumps(line), flush=True)
 
 
+OTHER_WORKLOADS = ("cfg1", "cfg2", "cfg3", "cfg5", "idx", "mla_abs")
+
+
+def run_others(args, hbm):
+    """The other BASELINE configs (and the indexer / absorbed-MLA steps), one GPU each, measured in the
+    same process after the headline: per workload the device-timed step and its dominant kernel (inputs
+    rotated past L2 as in their own runs), the step through the public API with host buffers, and the
+    reference's CPU kernel on a bounded number of calls.  Returns {name: summary}."""
+    import argparse as _ap
+    steps = min(max(args.steps, 200), 2000)
+    warm = max(args.warmup, 10)
+    res = {}
+    gpu_index = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[0]) if os.environ.get("CUDA_VISIBLE_DEVICES") \
+        else torch.cuda.current_device()
+    with ClockSampler(gpu_index) as clk:
+        for name in OTHER_WORKLOADS:
+            sub = _ap.Namespace(**vars(args))
+            sub.kv_len, sub.workload = 0, name
+            wl = None
+            try:
+                wl = make_workload(name, 1, 0, sub)
+                t_kernel, _ = time_steps(wl, wl.kernel, steps, warm, 1)
+                t_step, n_timed = time_steps(wl, wl.step, steps, warm, 1)
+                t_e2e = time_e2e(wl, min(steps, 200), warm, 1)
+                kb = wl.kernel_bytes()
+                r = {"workload": wl.config()["workload"], "us_per_step": t_step * 1e6,
+                     "value": wl.step_bytes() / t_step / 1e12, "unit": "TB/s", "timed_steps": n_timed,
+                     "kernel": wl.kernel_name, "kernel_us": t_kernel * 1e6, "algorithmic_bytes_per_launch": kb,
+                     "achieved_gbs": kb / t_kernel / 1e9, "frac": kb / t_kernel / 1e9 / hbm,
+                     "e2e_us": t_e2e * 1e6, "e2e_value": wl.step_bytes() / t_e2e / 1e12,
+                     "gpu_launches_per_step": wl.kernels_per_step}
+                tr = tensor_roofline(wl, t_kernel)
+                if tr is not None:
+                    r["tensor_frac"] = tr["frac"]
+                if not args.no_cpu_baseline:
+                    bps, info = wl.cpu_reference(budget_s=2.0, max_calls=20)
+                    r["cpu_reference"] = {"value": bps / 1e12, "unit": "TB/s", "us_per_call": info["sec_per_call"] * 1e6,
+                                          "calls": info["calls"], "cores": info["cores"], "kind": info["kind"],
+                                          "sample": info["sample"]}
+                res[name] = r
+            except Exception as e:   # one workload's failure leaves the headline line intact
+                res[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            if wl is not None and hasattr(wl, "close"):
+                wl.close()
+            del wl
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+    res["clocks"] = clk.summary()
+    return res
+
+
 def run_reference_arm(args):
     """The reference's own CPU kernel on this host's cores, one bounded sample
     of the workload per step.  Touches no GPU and loads nothing of scope_b200."""
@@ -1326,6 +1377,8 @@ def main():
     ap.add_argument("--kv-len", type=int, default=0, help="override KV length (profiling on a small case)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-others", action="store_true",
+                    help="N = 1, cfg4: skip the other workloads measured after the headline ('workloads' key)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "scatter", "nccl"],
                     help="cfg4 / cfg5 at N > 1: partials pushed over NVLink to rank 0 (peer), merged in shares "
                          "by every rank and gathered on rank 0 (scatter), or an NCCL all_gather (nccl)")
@@ -1397,6 +1450,14 @@ def main():
             line["parity"] = parity
         if t_ex is not None:
             line["exchange_us"] = t_ex * 1e6
+        if world == 1 and args.workload == "cfg4" and not args.kv_len and not args.no_others:
+            # the headline's buffers go before the other workloads allocate theirs
+            if hasattr(wl, "close"):
+                wl.close()
+            wl = None
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            line["workloads"] = run_others(args, hbm)
         print(json.dumps(line), flush=True)
     if hasattr(wl, "close"):
         wl.close()
