@@ -247,12 +247,19 @@ class GqaDense(Workload):
         self.k = [bf16_randn((rows, self.Lloc, D), g, dev) for _ in range(self.copies)]
         self.v = [bf16_randn((rows, self.Lloc, D), g, dev) for _ in range(self.copies)]
         gq = torch.Generator(device=dev).manual_seed(seed)
-        self.q = bf16_randn((B, H, D), gq, dev)
+        # q, then the new token's K and V rows, in one device block that a public-API step fills from one
+        # pinned host block with one copy; out, then lse, in one block read back with one copy
+        self.nq, self.nkv = B * H * D, rows * D
+        self.in_dev = torch.empty(self.nq + 2 * self.nkv, dtype=torch.bfloat16, device=dev)
+        self.q = self.in_dev[:self.nq].view(B, H, D)
+        self.q.copy_(bf16_randn((B, H, D), gq, dev))
         self.qv = self.q.view(rows, self.G, D)
         self.lib, self._lib = _lib.lib(), _lib
+        ob, lb = B * H * D * 2, B * H * 4
+        self.out_dev = torch.empty(ob + lb, dtype=torch.uint8, device=dev)
+        out_v, lse_v = self.out_dev[:ob].view(torch.bfloat16), self.out_dev[ob:].view(torch.float32)
         if world == 1:
-            self.out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
-            self.lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+            self.out, self.lse = out_v.view(B, H, D), lse_v.view(B, H)
         else:
             from scope_b200.shard import PartialExchange, PeerExchange, ScatterExchange
             if self.exchange == "peer":
@@ -262,15 +269,11 @@ class GqaDense(Workload):
             else:
                 self.ex = PartialExchange(B * H, D, world, dev)
                 self.part_o, self.part_l = self.ex.part_o, self.ex.part_l
-            self.out = torch.empty(B * H, D, dtype=torch.bfloat16, device=dev)
-            self.lse = torch.empty(B * H, dtype=torch.float32, device=dev)
+            self.out, self.lse = out_v.view(B * H, D), lse_v.view(B * H)
         nbytes = self.lib.ws_gqa_decode_workspace_size(rows, self.G, D, self.Lloc)
         self.ws = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=dev)
-        self.q_host = torch.randn(B, H, D).bfloat16().pin_memory()
-        self.knew_host = torch.randn(rows, D).bfloat16().pin_memory()
-        self.vnew_host = torch.randn(rows, D).bfloat16().pin_memory()
-        self.out_host = torch.empty(B * H * D, dtype=torch.bfloat16).pin_memory()
-        self.lse_host = torch.empty(B * H, dtype=torch.float32).pin_memory()
+        self.in_host = torch.randn(self.nq + 2 * self.nkv).bfloat16().pin_memory()
+        self.out_host = torch.empty(ob + lb, dtype=torch.uint8).pin_memory()
         # the decode, its deferred merge when a row's tiles span more than eight CTAs (the rule in
         # gqa_decode.cu's host code), and with N > 1 the merge of the exchanged partials
         tpr = -(-self.Lloc // 64)
@@ -323,19 +326,28 @@ class GqaDense(Workload):
             self.ex.close()
 
     def e2e_step(self, i):
+        """Through the public API with host buffers: q (and, on the rank holding the last shard, the new
+        token's K and V rows) arrive in one copy from pinned memory, the token is appended to the cache
+        with ws_kv_append, the decode (and exchange) runs, and out + lse leave in one copy."""
         c = i % self.copies
-        self.q.copy_(self.q_host, non_blocking=True)
-        if self.rank == self.world - 1:   # the new token lands in the last shard
-            self.k[c][:, self.Lloc - 1].copy_(self.knew_host, non_blocking=True)
-            self.v[c][:, self.Lloc - 1].copy_(self.vnew_host, non_blocking=True)
+        last = self.rank == self.world - 1   # the new token lands in the last shard
+        n = self.nq + 2 * self.nkv if last else self.nq
+        self.in_dev[:n].copy_(self.in_host[:n], non_blocking=True)
+        if last:
+            st = torch.cuda.current_stream().cuda_stream
+            rows = self.B * self.Hkv
+            for cache, off in ((self.k[c], self.nq), (self.v[c], self.nq + self.nkv)):
+                rc = self.lib.ws_kv_append(cache.data_ptr(), cache.stride(0), cache.stride(1), self.Lloc,
+                                           self.in_dev[off:].data_ptr(), self.D, self.D, rows, 1, self.D,
+                                           self._lib.WS_DTYPE_BF16, self.Lloc - 1, st)
+                if rc != 0:
+                    raise RuntimeError(self.lib.ws_last_error().decode())
         self.step(i)
         if self.rank == 0:
-            self.out_host.copy_(self.out.view(-1), non_blocking=True)
-            self.lse_host.copy_(self.lse.view(-1), non_blocking=True)
+            self.out_host.copy_(self.out_dev, non_blocking=True)
 
     def e2e_bytes(self):
-        return (self.world * self.q.numel() * 2 + 2 * self.knew_host.numel() * 2,
-                self.out.numel() * 2 + self.lse.numel() * 4)
+        return ((self.world * self.nq + 2 * self.nkv) * 2, self.out_dev.numel())
 
     def parity_check(self, seed):
         """N > 1, before timing: one step on input copy 0, then rank 0 rebuilds
