@@ -306,3 +306,54 @@ def test_head_sizes_and_groups(ext, B, G, Dk, Dv, L):
         po, pm, ps = ext.fused_cpu_attn(q.to(DEV), k.to(DEV), v.to(DEV), scale)
         torch.cuda.synchronize()
         assert np.abs(po.float().cpu().numpy() - ro).max() < TOL_OUT
+
+
+def _f64_decode(q, k, v, scale):
+    """float64 attention per row: q [B, G, D], k/v [B, L, D] -> (normalised out, lse)."""
+    q, k, v = q.double(), k.double(), v.double()
+    s = torch.einsum("bgd,bld->bgl", q, k) * scale
+    lse = torch.logsumexp(s, dim=-1)
+    return torch.einsum("bgl,bld->bgd", torch.softmax(s, dim=-1), v), lse
+
+
+@pytest.mark.parametrize("B,G,D,L", [
+    (3, 8, 128, 1), (2, 8, 128, 31), (2, 8, 128, 33), (4, 8, 128, 1000), (2, 16, 128, 2049), (3, 1, 64, 777),
+    (2, 12, 256, 1500), (2, 16, 256, 300), (2, 8, 80, 500), (5, 3, 16, 64), (40, 8, 128, 3000),
+    (2, 4, 192, 999),
+])
+@pytest.mark.parametrize("aligned", [True, False])
+def test_fp32_path_shapes(ext, B, G, D, L, aligned):
+    """The fp32 path of fused_cpu_attn: 16-byte aligned K/V rows run the tiled kernels (the register-blocked
+    one for G <= 8 and D <= 128), rows that are not (a view starting one float into its buffer) the per-token
+    kernel.  Both against a float64 reference."""
+    gen = torch.Generator().manual_seed(B * 31 + G * 7 + D + L)
+    q = torch.randn(B, G, D, generator=gen)
+    kb = torch.randn(B, L, D + 4, generator=gen)
+    vb = torch.randn(B, L, D + 4, generator=gen)
+    k, v = (kb[..., :D], vb[..., :D]) if aligned else (kb[..., 1:D + 1], vb[..., 1:D + 1])
+    ro, rl = _f64_decode(q, k, v, D ** -0.5)
+    kd, vd = kb.to(DEV), vb.to(DEV)
+    kd, vd = (kd[..., :D], vd[..., :D]) if aligned else (kd[..., 1:D + 1], vd[..., 1:D + 1])
+    o, m, s = ext.fused_cpu_attn(q.to(DEV), kd, vd, D ** -0.5)
+    torch.cuda.synchronize()
+    assert o.dtype == torch.float32
+    assert (o.cpu().double() - ro).abs().max().item() < 1e-4
+    assert ((m + s.log())[..., 0].cpu().double() - rl).abs().max().item() < 1e-4
+
+
+def test_fp32_path_token_major_and_long(ext):
+    """A token-major [L, Hkv, D] fp32 cache seen per head, and 16384-token rows split over many CTAs; repeated
+    launches on one workspace give identical results."""
+    gen = torch.Generator(device=DEV).manual_seed(12)
+    L, Hkv, G, D = 16384, 4, 8, 128
+    kc = torch.randn(L, Hkv, D, device=DEV, generator=gen)
+    vc = torch.randn(L, Hkv, D, device=DEV, generator=gen)
+    q = torch.randn(Hkv, G, D, device=DEV, generator=gen)
+    o, m, s = ext.fused_cpu_attn(q, kc.permute(1, 0, 2), vc.permute(1, 0, 2), D ** -0.5)
+    for _ in range(3):
+        o2, m2, s2 = ext.fused_cpu_attn(q, kc.permute(1, 0, 2), vc.permute(1, 0, 2), D ** -0.5)
+        assert torch.equal(o2, o) and torch.equal(m2, m) and torch.equal(s2, s)
+    ro, rl = _f64_decode(q.cpu(), kc.permute(1, 0, 2).cpu(), vc.permute(1, 0, 2).cpu(), D ** -0.5)
+    assert (o.cpu().double() - ro).abs().max().item() < 1e-4
+    assert ((m + s.log())[..., 0].cpu().double() - rl).abs().max().item() < 1e-4
+    assert scope_b200.status_take() == 0
