@@ -239,6 +239,7 @@ class GqaDense(Workload):
         self.scale = D ** -0.5
         self.workload = (f"gqa_qwen3_b{B}_l{L}" + ("_sharded" if name == "cfg4" else ""))
         dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
         rows = B * Hkv
         per_copy = 2 * rows * self.Lloc * D * 2
         self.copies = max(1, -(-3 * L2_BYTES // per_copy)) if per_copy < 3 * L2_BYTES else 1
@@ -295,7 +296,7 @@ class GqaDense(Workload):
     def kernel(self, i):
         L_, c = self.lib, i % self.copies
         k, v = self.k[c], self.v[c]
-        st = torch.cuda.current_stream().cuda_stream
+        st = self._lib.stream_ptr(self.dev)
         rows = self.B * self.Hkv
         if self.world == 1:
             out, lse, mode = self.out.data_ptr(), self.lse.data_ptr(), self._lib.WS_OUT_NORM_BF16
@@ -334,7 +335,7 @@ class GqaDense(Workload):
         n = self.nq + 2 * self.nkv if last else self.nq
         self.in_dev[:n].copy_(self.in_host[:n], non_blocking=True)
         if last:
-            st = torch.cuda.current_stream().cuda_stream
+            st = self._lib.stream_ptr(self.dev)
             rows = self.B * self.Hkv
             for cache, off in ((self.k[c], self.nq), (self.v[c], self.nq + self.nkv)):
                 rc = self.lib.ws_kv_append(cache.data_ptr(), cache.stride(0), cache.stride(1), self.Lloc,

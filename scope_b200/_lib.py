@@ -5,6 +5,7 @@ instead of falling back to anything else.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -129,8 +130,23 @@ def check(rc: int, what: str) -> None:
         raise ScopeError(f"{what} failed (status {rc}): {msg}")
 
 
+# The current stream's raw handle without building a Stream object (2 us per call on the host otherwise, and
+# every launch asks for it).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def on_device(device: torch.device):
+    """Context that makes `device` current for a launch: nothing to do (and no device switch paid for) when
+    it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def ptr(t: torch.Tensor | None):

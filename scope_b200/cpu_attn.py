@@ -17,7 +17,7 @@ import math
 import torch
 
 from . import _lib
-from ._lib import check, lib, ptr, stream_ptr, workspaces
+from ._lib import check, lib, ptr, on_device, stream_ptr, workspaces
 
 _num_threads = [0]
 
@@ -55,7 +55,7 @@ def _run_gqa(q, k, v, scale, dtype_code, out_mode, out, mx, sm, lse):
     B, G, Dk = q.shape
     L, Dv = k.shape[1], v.shape[2]
     L_ = lib()
-    with torch.cuda.device(dev):
+    with on_device(dev):
         nbytes = L_.ws_gqa_decode_workspace_size(B, G, Dv, L)
         ws = workspaces.get(nbytes, dev)
         rc = L_.ws_gqa_decode(ptr(q), ptr(k), ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
@@ -174,7 +174,7 @@ def _run_mla(q_proj, q_pe, c_kv, k_pe, scale, out_mode, out, mx, sm, lse):
                 dst.view(B, nH).copy_(src[:, :nH])
         return
     L_ = lib()
-    with torch.cuda.device(dev):
+    with on_device(dev):
         ws = workspaces.get(L_.ws_mla_decode_workspace_size(B, nH, S), dev)
         rc = L_.ws_mla_decode_strided(ptr(q_proj), ptr(q_pe), ptr(c_kv), c_bs, ptr(k_pe), pe_bs, B, nH, S,
                                       float(scale), out_mode, ptr(out), ptr(mx), ptr(sm), ptr(lse), ptr(ws),
@@ -262,7 +262,7 @@ def mla_decode_absorbed(q_nope: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Te
     out = torch.empty(B, nH, vhd, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, nH, dtype=torch.float32, device=dev) if return_lse else None
     L_ = lib()
-    with torch.cuda.device(dev):
+    with on_device(dev):
         ws = workspaces.get(L_.ws_mla_decode_absorbed_workspace_size(B, nH, S), dev)
         rc = L_.ws_mla_decode_absorbed_strided(ptr(qn), w.data_ptr(), hs, ptr(qpe), ptr(c_kv), c_bs, ptr(k_pe), pe_bs,
                                                w.data_ptr() + nop * 512 * 2, hs, B, nH, S, nop, vhd, float(scale),

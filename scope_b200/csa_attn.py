@@ -27,7 +27,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import check, lib, ptr, stream_ptr, workspaces
+from ._lib import check, lib, ptr, on_device, stream_ptr, workspaces
 from .cpu_attn import _require_cuda, get_num_threads, set_num_threads  # noqa: F401
 
 HD = 512
@@ -92,7 +92,7 @@ def _launch(q, kv, scale, out, lse, *, idx=None, kv_scales=None, kv_range=None, 
     kv_s, kv_e = kv_range if kv_range is not None else (shard_lo, shard_lo + nc)
     if bs == 0 or nq == 0:
         return
-    with torch.cuda.device(dev):
+    with on_device(dev):
         L_ = lib()
         ws = workspaces.get(L_.ws_csa_decode_workspace_size(bs, nq, q_code), dev)
         rc = L_.ws_csa_decode(ptr(q), q_code, bs, nq, hd, ptr(kv), kv_code, ptr(kv_scales), nc, int(shard_lo),
@@ -249,7 +249,7 @@ def _launch_qcodes(q_u8, q_scales, kv_i8, kv_scales, kv_sums, kv_vals, scale, o_
     kp = _pad_dims(kv_i8, HD)
     vp = None if kv_vals is None else _pad_dims(kv_vals, HD)
     out = o_out if hd == HD else torch.empty(bs, nq, HD, dtype=o_out.dtype, device=dev)
-    with torch.cuda.device(dev):
+    with on_device(dev):
         L_ = lib()
         ws = workspaces.get(L_.ws_csa_decode_workspace_size(bs, nq, _lib.WS_DTYPE_BF16), dev)
         rc = L_.ws_csa_decode_qcodes(ptr(qp), ptr(q_scales.contiguous()), bs, nq, HD, ptr(kp),
@@ -293,7 +293,7 @@ def kv_quantize_bf16_to_int8(kv: torch.Tensor, n_threads: int = 0):
     out = torch.empty((bs, nc, hd), dtype=torch.int8, device=kv.device)
     scales = torch.empty((bs, nc), dtype=torch.float32, device=kv.device)
     sums = torch.empty((bs, nc), dtype=torch.int32, device=kv.device)
-    with torch.cuda.device(kv.device):
+    with on_device(kv.device):
         rc = lib().ws_csa_kv_quantize_s8(ptr(kv), bs * nc, hd, ptr(out), ptr(scales), ptr(sums),
                                          stream_ptr(kv.device))
     check(rc, "ws_csa_kv_quantize_s8")
@@ -310,7 +310,7 @@ def q_quantize_fp32_to_u8(q: torch.Tensor, n_threads: int = 0):
     rows = q.numel() // hd if hd else 0
     out = torch.empty(q.shape, dtype=torch.uint8, device=q.device)
     scales = torch.empty(q.shape[:-1], dtype=torch.float32, device=q.device)
-    with torch.cuda.device(q.device):
+    with on_device(q.device):
         rc = lib().ws_csa_q_quantize_u8(ptr(q), rows, hd, ptr(out), ptr(scales), stream_ptr(q.device))
     check(rc, "ws_csa_q_quantize_u8")
     return out, scales
@@ -426,7 +426,7 @@ def indexer_topk(q_idx, kv_idx, weights, k: int, order: str = "score", return_sc
     ids = torch.empty(bs, k, dtype=torch.int32, device=dev)
     scores = torch.empty(bs, nc, dtype=torch.float32, device=dev) if return_scores else None
     code = _lib.WS_DTYPE_F32 if q_idx.dtype == torch.float32 else _lib.WS_DTYPE_BF16
-    with torch.cuda.device(dev):
+    with on_device(dev):
         L_ = lib()
         ws = workspaces.get(L_.ws_indexer_topk_workspace_size(bs, nc), dev)
         rc = L_.ws_indexer_topk(ptr(q_idx), ptr(kv_idx), code, ptr(weights), bs, nH, hd, nc, k,

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import check, lib, ptr, stream_ptr
+from ._lib import check, lib, ptr, on_device, stream_ptr
 
 
 def shard_capacity(max_seq: int, world: int) -> int:
@@ -43,7 +43,7 @@ def _append(dst: torch.Tensor, src: torch.Tensor, t0: int) -> None:
     if src.stride(2) != 1:
         src = src.contiguous()
     rows, n, D = src.shape
-    with torch.cuda.device(dst.device):
+    with on_device(dst.device):
         rc = lib().ws_kv_append(ptr(dst), dst.stride(0), dst.stride(1), dst.shape[1], ptr(src), src.stride(0),
                                 src.stride(1), rows, n, D, code, t0, stream_ptr(dst.device))
     check(rc, "ws_kv_append")

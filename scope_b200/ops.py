@@ -13,7 +13,7 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from ._lib import KvShare, check, lib, ptr, stream_ptr, workspaces
+from ._lib import KvShare, check, lib, ptr, on_device, stream_ptr, workspaces
 
 
 class Share:
@@ -94,7 +94,7 @@ def gqa_decode_shares(q: torch.Tensor, shares: Sequence[Share], scale: float,
     if lse is None:
         lse = torch.empty(B, H, dtype=torch.float32, device=dev)
     L_ = lib()
-    with torch.cuda.device(dev):
+    with on_device(dev):
         nbytes = L_.ws_gqa_decode_shares_workspace_size(B, Hkv, G, Dv, len(shares))
         ws = workspaces.get(nbytes, dev)
         rc = L_.ws_gqa_decode_shares(ptr(q), B, Hkv, G, Dk, Dv, float(scale), arr, len(shares),
@@ -128,7 +128,7 @@ def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor, out_dtype: torch.d
     if out_lse is None:
         out_lse = torch.empty(*lead, dtype=torch.float32, device=dev)
     code = _lib.WS_DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.WS_DTYPE_F32
-    with torch.cuda.device(dev):
+    with on_device(dev):
         rc = lib().ws_lse_merge(ptr(o_c), ptr(l_c), P, R, D, ptr(out), code, ptr(out_lse), stream_ptr(dev))
     check(rc, "ws_lse_merge")
     return out, out_lse
