@@ -31,6 +31,7 @@ struct F32Params {
     const float* v;
     int64_t k_sb, k_st, v_sb, v_st;
     int G, D, L, splits;
+    int GR;          // query heads per kv row in q and the outputs (this launch takes G of them, G <= GR)
     float scale;
     int out_mode;
     void* out;
@@ -43,11 +44,11 @@ struct F32Params {
 
 __device__ __forceinline__ void f32_store(const F32Params& p, int row, int g, int d, float o_un, float m, float l) {
     const bool empty = !(l > 0.f);
-    const int64_t oi = ((int64_t)row * p.G + g) * p.D + d;
+    const int64_t oi = ((int64_t)row * p.GR + g) * p.D + d;
     float* out = static_cast<float*>(p.out);
     out[oi] = empty ? 0.f : (p.out_mode == WS_OUT_UNNORM_F32 ? o_un : o_un / l);
     if (d == 0) {
-        const int64_t mi = (int64_t)row * p.G + g;
+        const int64_t mi = (int64_t)row * p.GR + g;
         if (p.out_max) {
             static_cast<float*>(p.out_max)[mi] = empty ? -INFINITY : m;
             static_cast<float*>(p.out_sum)[mi] = empty ? 0.f : l;
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(128) gqa_f32_kernel(const F32Params p) {
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
             const int d = lane + 32 * i;
-            qr[g][i] = (g < p.G && d < p.D) ? p.q[((int64_t)row * p.G + g) * p.D + d] : 0.f;
+            qr[g][i] = (g < p.G && d < p.D) ? p.q[((int64_t)row * p.GR + g) * p.D + d] : 0.f;
             o[g][i] = 0.f;
         }
     }
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(kF32Threads, 2) gqa_f32_rb_kernel(const F32Par
     };
     int issued = min(ntiles, kF32Stages - 1);
     for (int i = 0; i < issued; ++i) load_tile(i);
-    for (int e = tid; e < G * D; e += kF32Threads) s_q[e] = p.q[(int64_t)row * G * D + e];
+    for (int e = tid; e < G * D; e += kF32Threads) s_q[e] = p.q[(int64_t)row * p.GR * D + e];
     for (int e = tid; e < TT * GB; e += kF32Threads) s_pt[e] = 0.f;   // heads >= G stay 0
     if (tid < GB) {
         s_alpha[tid] = 0.f;
@@ -447,7 +448,7 @@ __global__ void __launch_bounds__(kF32Threads, 2) gqa_f32_tile_kernel(const F32P
     };
     int issued = min(ntiles, kF32Stages - 1);
     for (int i = 0; i < issued; ++i) load_tile(i);
-    for (int e = tid; e < p.G * D; e += kF32Threads) s_q[e] = p.q[(int64_t)row * p.G * D + e];
+    for (int e = tid; e < p.G * D; e += kF32Threads) s_q[e] = p.q[(int64_t)row * p.GR * D + e];
     if (tid < kF32MaxG) {
         s_alpha[tid] = 0.f;
         s_mx[tid] = -INFINITY;
@@ -529,19 +530,45 @@ __global__ void __launch_bounds__(kF32Threads, 2) gqa_f32_tile_kernel(const F32P
     f32_finish(p, row, split, tid, s_mx, s_sum, [&](int g, int d) { return red[g * D + d]; });
 }
 
+static int gqa_f32_heads(const void* q, const void* k, const void* v, int64_t k_sb, int64_t k_st, int64_t v_sb,
+                         int64_t v_st, int B_kv, int G, int GR, int g0, int D, int L, float scale, int out_mode,
+                         void* out, void* out_max, void* out_sum, float* out_lse, void* workspace,
+                         size_t workspace_bytes, cudaStream_t st);
+
 int gqa_f32_launch(const void* q, const void* k, const void* v, int64_t k_sb, int64_t k_st, int64_t v_sb,
                       int64_t v_st, int B_kv, int G, int D, int L, float scale, int out_mode, void* out,
                       void* out_max, void* out_sum, float* out_lse, void* workspace, size_t workspace_bytes,
                       cudaStream_t st) {
-    if (G > kF32MaxG) return set_error(WS_ERR_UNSUPPORTED, "fp32 path: groups must be <= 16");
     if (D > 32 * kF32MaxDPerLane) return set_error(WS_ERR_UNSUPPORTED, "fp32 path: head_dim must be <= 256");
+    if (G > kF32MaxG) {
+        // more query heads per kv row than one launch takes: launches of 16 heads over the same rows, q and
+        // the outputs addressed through their rows of G heads (the kv rows are read once per launch)
+        for (int g0 = 0; g0 < G; g0 += kF32MaxG) {
+            const int rc = gqa_f32_heads(q, k, v, k_sb, k_st, v_sb, v_st, B_kv, std::min(kF32MaxG, G - g0), G, g0, D, L,
+                                         scale, out_mode, out, out_max, out_sum, out_lse, workspace, workspace_bytes, st);
+            if (rc != WS_OK) return rc;
+        }
+        return WS_OK;
+    }
+    return gqa_f32_heads(q, k, v, k_sb, k_st, v_sb, v_st, B_kv, G, G, 0, D, L, scale, out_mode, out, out_max, out_sum,
+                         out_lse, workspace, workspace_bytes, st);
+}
+
+// One launch over heads g0 .. g0 + G - 1 of rows that hold GR heads each.
+static int gqa_f32_heads(const void* q, const void* k, const void* v, int64_t k_sb, int64_t k_st, int64_t v_sb,
+                         int64_t v_st, int B_kv, int G, int GR, int g0, int D, int L, float scale, int out_mode,
+                         void* out, void* out_max, void* out_sum, float* out_lse, void* workspace,
+                         size_t workspace_bytes, cudaStream_t st) {
     F32Params p;
-    p.q = static_cast<const float*>(q);
+    p.q = static_cast<const float*>(q) + (int64_t)g0 * D;
     p.k = static_cast<const float*>(k);
     p.v = static_cast<const float*>(v);
     p.k_sb = k_sb; p.k_st = k_st; p.v_sb = v_sb; p.v_st = v_st;
-    p.G = G; p.D = D; p.L = L; p.scale = scale; p.out_mode = out_mode;
-    p.out = out; p.out_max = out_max; p.out_sum = out_sum; p.out_lse = out_lse;
+    p.G = G; p.GR = GR; p.D = D; p.L = L; p.scale = scale; p.out_mode = out_mode;
+    p.out = static_cast<float*>(out) + (int64_t)g0 * D;
+    p.out_max = out_max ? static_cast<float*>(out_max) + g0 : nullptr;
+    p.out_sum = out_sum ? static_cast<float*>(out_sum) + g0 : nullptr;
+    p.out_lse = out_lse ? out_lse + g0 : nullptr;
     const int DPL = (D + 31) / 32 <= 4 ? 4 : 8;
     const int slot_floats = G * D + 2 * G;
     // splits: enough blocks to cover the SMs twice, at most one per 256 tokens

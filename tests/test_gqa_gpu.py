@@ -319,13 +319,13 @@ def _f64_decode(q, k, v, scale):
 @pytest.mark.parametrize("B,G,D,L", [
     (3, 8, 128, 1), (2, 8, 128, 31), (2, 8, 128, 33), (4, 8, 128, 1000), (2, 16, 128, 2049), (3, 1, 64, 777),
     (2, 12, 256, 1500), (2, 16, 256, 300), (2, 8, 80, 500), (5, 3, 16, 64), (40, 8, 128, 3000),
-    (2, 4, 192, 999),
+    (2, 4, 192, 999), (2, 24, 128, 700), (1, 40, 64, 300),
 ])
 @pytest.mark.parametrize("aligned", [True, False])
 def test_fp32_path_shapes(ext, B, G, D, L, aligned):
     """The fp32 path of fused_cpu_attn: 16-byte aligned K/V rows run the tiled kernels (the register-blocked
     one for G <= 8 and D <= 128), rows that are not (a view starting one float into its buffer) the per-token
-    kernel.  Both against a float64 reference."""
+    kernel; more than 16 query heads per kv row run as launches of 16.  All against a float64 reference."""
     gen = torch.Generator().manual_seed(B * 31 + G * 7 + D + L)
     q = torch.randn(B, G, D, generator=gen)
     kb = torch.randn(B, L, D + 4, generator=gen)
