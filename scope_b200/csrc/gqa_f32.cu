@@ -581,7 +581,7 @@ static int gqa_f32_heads(const void* q, const void* k, const void* v, int64_t k_
     if (splits > 1 && !workspace) splits = 1;
     p.ws_cnt = static_cast<int*>(workspace);
     p.ws_part = workspace ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + cnt_bytes) : nullptr;
-    // the tiled forms when every K and V row starts 16-byte aligned (one bulk copy per row)
+    // the tiled forms when every K and V row starts 16-byte aligned (16-byte cp.async copies)
     const bool aligned = reinterpret_cast<uintptr_t>(k) % 16 == 0 && reinterpret_cast<uintptr_t>(v) % 16 == 0 &&
                          k_sb % 4 == 0 && k_st % 4 == 0 && v_sb % 4 == 0 && v_st % 4 == 0 && D % 4 == 0;
     if (aligned) {
